@@ -1,0 +1,203 @@
+/*
+ * need_scan.h -- C ABI of the B200 (sm_100a) recurrent-scan library
+ * (need_b200/_lib/libneed_scan.so).
+ *
+ * The library implements NEED's gated linear recurrence
+ *
+ *     h[t] = a[t] * h[t-1] + b[t]        (element-wise per channel)
+ *
+ * and the gate arithmetic its callers wrap around it.  Every entry point takes
+ * plain device pointers, element strides and sizes, launches on the given
+ * stream, never synchronises and never allocates device memory; scratch comes
+ * from a caller-owned workspace (see need_scan_workspace_size).
+ *
+ * Reference interfaces replaced (NEED, file:line):
+ *   need_affine_recurrence_scan  <- need_kernels.affine_recurrence_scan   need_kernels.py:229-264
+ *   need_ssd_scan                <- need_kernels.ssd_scan                 need_kernels.py:302-339
+ *   need_recurrent_retention_scan<- need_kernels.recurrent_retention_scan need_kernels.py:342-345
+ *   need_gated_scan              <- the sigmoid-gated scan its callers compose from
+ *                                   torch ops (need_core.py:1630-1638 with a sigmoid decay)
+ *   need_ragged_verify           <- the one-token recurrent step applied k times
+ *                                   (need_core.py:6410-6431, :1653-1686) for a ragged
+ *                                   batch of drafted tokens (generate.py:885-1001)
+ *   need_commit_states           <- keeping the state at the accepted prefix
+ *                                   (generate.py:1078-1083 appends the accepted tokens)
+ *   need_sp_fixup                <- no counterpart (sequence-parallel extension)
+ *
+ * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
+ * message for the calling thread's last failure.  All entry points are
+ * reentrant and may be called from several host threads on distinct streams.
+ */
+#ifndef NEED_SCAN_H
+#define NEED_SCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEED_SCAN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define NEED_API __attribute__((visibility("default")))
+#else
+#define NEED_API
+#endif
+
+typedef struct CUstream_st* need_stream_t; /* == cudaStream_t */
+
+typedef enum {
+    NEED_OK = 0,
+    NEED_ERR_INVALID = 1,     /* bad argument: null pointer, negative size, bad form */
+    NEED_ERR_UNSUPPORTED = 2, /* dtype / alignment / stride the kernels do not take */
+    NEED_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed */
+    NEED_ERR_WORKSPACE = 4    /* workspace missing or smaller than required */
+} need_status;
+
+typedef enum { NEED_F32 = 0, NEED_BF16 = 1, NEED_F16 = 2 } need_dtype;
+
+/* What the streamed inputs in[] hold, and what `out` receives.
+ *   NEED_FORM_AFFINE    in[0]=decay a (dtype decay_dtype, or one value per row
+ *                       when decay_per_row), in[1]=update b          out = h
+ *   NEED_FORM_GATED     in[0]=decay logit z, in[1]=input-gate logit g, in[2]=x
+ *                       a = sigmoid(z), b = (1-a)*(sigmoid(g)*x)    out = h
+ *   NEED_FORM_SSD       in[0]=dt_raw, in[1]=b_gate, in[2]=u, in[3]=c_gate,
+ *                       in[4]=out_gate; a = exp(-(dt_min + dt_scale*sigmoid(dt_raw))),
+ *                       b = (1-a)*(sigmoid(b_gate)*u)
+ *                       out = (sigmoid(c_gate)*h + d_skip*u) * sigmoid(out_gate)
+ *   NEED_FORM_RETENTION in[0]=decay (as AFFINE), in[1]=kv, in[2]=q
+ *                       out = q * h
+ * Resets: where seg_start[b, t] != 0 the state is zeroed before step t
+ * (a[t] := 0; b[t] unchanged).
+ *
+ * Precision: the state is carried in fp32.  With 16-bit inputs every gate op
+ * is rounded to the input dtype at the points where the reference's torch path
+ * rounds (need_kernels.py:330-339), and the state is rounded to the input dtype
+ * before the SSD / retention epilogue, as the reference's `state_seq` is. */
+typedef enum {
+    NEED_FORM_AFFINE = 0,
+    NEED_FORM_GATED = 1,
+    NEED_FORM_SSD = 2,
+    NEED_FORM_RETENTION = 3
+} need_form;
+
+/* A streamed tensor viewed as [nb, nh, T, C] with channel stride 1.
+ * Strides are in elements.  The base must be 16-byte aligned and every stride
+ * times the element size a multiple of 16 bytes (dims of size 1 excepted). */
+typedef struct {
+    const void* ptr;
+    int64_t stride_b, stride_h, stride_t;
+} need_view;
+
+typedef struct {
+    int32_t form;        /* need_form */
+    int32_t dtype;       /* need_dtype of in[] other than an AFFINE/RETENTION decay, and of out */
+    int32_t decay_dtype; /* AFFINE / RETENTION: need_dtype of in[0] */
+    int32_t decay_per_row; /* AFFINE / RETENTION: 1 = in[0] holds one value per (b, h, t),
+                              broadcast over C (its view's stride_* index [nb, nh, T]) */
+    int64_t nb, nh, T, C;  /* sequence = (b, h); nb * nh independent recurrences of C channels */
+    need_view in[5];
+    void* out;             /* [nb, nh, T, C], dtype `dtype` */
+    int64_t out_stride_b, out_stride_h, out_stride_t;
+    const float* d_skip;   /* SSD: [C] fp32 */
+    double dt_min, dt_max; /* SSD: dt = dt_min + (dt_max - dt_min) * sigmoid(dt_raw) */
+    const float* h0;       /* optional [nb*nh, C] fp32 initial state (contiguous) */
+    float* h_final;        /* optional [nb*nh, C] fp32 state after the last token */
+    const uint8_t* seg_start; /* optional reset mask indexed [b, t] (shared by the nh heads) */
+    int64_t seg_stride_b, seg_stride_t;
+    float* summary;        /* optional [nb*nh, C, 2] fp32: (prod of a over T, h_final), the
+                              per-slice summary the sequence-parallel combine exchanges */
+    float* tile_prod;      /* optional [nb*nh, ceil(T/L), C] fp32: product of a over
+                              [0, start of chunk), L = need_scan_chunk_len(form, dtype, ...) */
+    void* workspace;       /* >= need_scan_workspace_size(...) bytes, zero-filled before its
+                              first use; reusable by later calls on the same stream without
+                              clearing; never used by two launches at once */
+    size_t workspace_bytes;
+} need_scan_args;
+
+/* Version of this header the library was built from. */
+NEED_API int need_abi_version(void);
+
+/* Message for the calling thread's most recent failure ("" if none). */
+NEED_API const char* need_last_error(void);
+
+/* Tokens per tile along T for a call (the chunk length tile_prod is indexed by). */
+NEED_API int64_t need_scan_chunk_len(int32_t form, int32_t dtype, int32_t decay_dtype, int32_t decay_per_row);
+
+/* Workspace bytes a call with these sizes needs. */
+NEED_API size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t decay_dtype,
+                                int32_t decay_per_row, int64_t nb, int64_t nh, int64_t T,
+                                int64_t C);
+
+/* Reads (and clears) the workspace's device-side error word: bit 0 = a look-back
+ * wait gave up, bit 1 = a tile load wait gave up.  Synchronises `stream`. */
+NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream);
+
+/* need_kernels.affine_recurrence_scan (need_kernels.py:229-264): args->form must be
+ * NEED_FORM_AFFINE. */
+NEED_API int need_affine_recurrence_scan(const need_scan_args* args, need_stream_t stream);
+
+/* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
+NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);
+
+/* need_kernels.recurrent_retention_scan (need_kernels.py:342-345):
+ * args->form == NEED_FORM_RETENTION. */
+NEED_API int need_recurrent_retention_scan(const need_scan_args* args, need_stream_t stream);
+
+/* The sigmoid-gated scan (need_core.py:1630-1638 with decay = sigmoid(z)):
+ * args->form == NEED_FORM_GATED. */
+NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Ragged decode / speculative verify                                        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    int32_t form;          /* NEED_FORM_GATED or NEED_FORM_SSD */
+    int32_t dtype;         /* NEED_BF16, NEED_F16 or NEED_F32: states, inputs and outputs */
+    int64_t nseq, C;
+    void* states;          /* [nslots, C] state pool, read only here */
+    const int32_t* slot;   /* optional [nseq]: pool row of sequence i (default i) */
+    const int32_t* cu_k;   /* [nseq + 1] offsets of each sequence's drafted tokens */
+    int64_t total_k;       /* cu_k[nseq] (rows of the packed inputs) */
+    const void* in[5];     /* packed [total_k, C] contiguous: GATED z, g, x;
+                              SSD dt_raw, b_gate, u, c_gate, out_gate */
+    const float* d_skip;   /* SSD: [C] fp32 */
+    double dt_min, dt_max;
+    void* y;               /* [total_k, C] output of each drafted token */
+    void* states_k;        /* [total_k, C] state after each drafted token */
+} need_verify_args;
+
+/* k_i one-token steps per sequence from its pooled state, in the model dtype's
+ * arithmetic (need_core.py:6420-6428).  The pool is not modified. */
+NEED_API int need_ragged_verify(const need_verify_args* args, need_stream_t stream);
+
+/* states[slot[i]] := states_k[cu_k[i] + accept_len[i] - 1] when accept_len[i] > 0;
+ * accept_len[i] must lie in [0, cu_k[i+1] - cu_k[i]] (clamped on device). */
+NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* states,
+                       const int32_t* slot, const void* states_k, const int32_t* cu_k,
+                       const int32_t* accept_len, need_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Sequence parallelism (T sharded over ranks)                               */
+/* ------------------------------------------------------------------------ */
+
+/* After a rank scanned its T-slice from a zero state (with `summary` and
+ * `tile_prod` requested) and gathered every rank's summary into
+ * `all_summary` [nranks, nb*nh, C, 2], this adds the carry from ranks < rank:
+ *     carry = compose(summary[0..rank-1]);  h[t] += (prod_{s<=t} a[s]) * carry
+ * over the leading tiles of the slice, stopping at the first tile where the
+ * product has fallen to 2^-24 or below for every channel of the tile (the
+ * correction is then below fp32 resolution of the carry).  It also corrects
+ * h_final / summary when given.  `args` is the same description the local scan
+ * got (form AFFINE or GATED); `args->out` is read and rewritten. */
+NEED_API int need_sp_fixup(const need_scan_args* args, const float* all_summary, int32_t nranks,
+                  int32_t rank, need_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEED_SCAN_H */

@@ -1,0 +1,104 @@
+"""ctypes binding of the C ABI in include/need_scan.h (libneed_scan.so).
+
+The structures mirror the header field for field; ``load()`` opens the in-tree
+library and declares every entry point.  Nothing here touches the GPU: the
+first CUDA call happens inside an entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import (POINTER, Structure, c_char_p, c_double, c_int32, c_int64, c_size_t, c_uint32,
+                    c_void_p)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libneed_scan.so")
+ABI_VERSION = 1
+
+# need_status
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3, 4
+# need_dtype
+F32, BF16, F16 = 0, 1, 2
+# need_form
+FORM_AFFINE, FORM_GATED, FORM_SSD, FORM_RETENTION = 0, 1, 2, 3
+
+
+class NeedView(Structure):
+    _fields_ = [("ptr", c_void_p), ("stride_b", c_int64), ("stride_h", c_int64), ("stride_t", c_int64)]
+
+
+class NeedScanArgs(Structure):
+    _fields_ = [
+        ("form", c_int32), ("dtype", c_int32), ("decay_dtype", c_int32), ("decay_per_row", c_int32),
+        ("nb", c_int64), ("nh", c_int64), ("T", c_int64), ("C", c_int64),
+        ("in_", NeedView * 5),
+        ("out", c_void_p), ("out_stride_b", c_int64), ("out_stride_h", c_int64), ("out_stride_t", c_int64),
+        ("d_skip", c_void_p), ("dt_min", c_double), ("dt_max", c_double),
+        ("h0", c_void_p), ("h_final", c_void_p),
+        ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
+        ("summary", c_void_p), ("tile_prod", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
+class NeedVerifyArgs(Structure):
+    _fields_ = [
+        ("form", c_int32), ("dtype", c_int32), ("nseq", c_int64), ("C", c_int64),
+        ("states", c_void_p), ("slot", c_void_p), ("cu_k", c_void_p), ("total_k", c_int64),
+        ("in_", c_void_p * 5), ("d_skip", c_void_p), ("dt_min", c_double), ("dt_max", c_double),
+        ("y", c_void_p), ("states_k", c_void_p),
+    ]
+
+
+# every symbol the header declares, with (restype, argtypes)
+SIGNATURES = {
+    "need_abi_version": (c_int32, []),
+    "need_last_error": (c_char_p, []),
+    "need_scan_chunk_len": (c_int64, [c_int32, c_int32, c_int32, c_int32]),
+    "need_scan_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int64, c_int64, c_int64, c_int64]),
+    "need_workspace_error": (c_int32, [c_void_p, POINTER(c_uint32), c_void_p]),
+    "need_affine_recurrence_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_ragged_verify": (c_int32, [POINTER(NeedVerifyArgs), c_void_p]),
+    "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p]),
+    "need_sp_fixup": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_int32, c_void_p]),
+}
+
+_LIB = None
+
+
+class NeedError(RuntimeError):
+    """A C-ABI call returned a non-zero need_status."""
+
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed (status {code}): {msg}")
+        self.code = code
+
+
+def load(path: str = LIB_PATH):
+    """Opens libneed_scan.so (raises if it has not been built) and declares its entry points."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `python -m need_b200.build` "
+                           "(there is no CPU fallback for the scan kernels)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    ver = lib.need_abi_version()
+    if ver != ABI_VERSION:
+        raise RuntimeError(f"libneed_scan ABI version {ver}, expected {ABI_VERSION}")
+    _LIB = lib
+    return lib
+
+
+def check(fn: str, code: int) -> None:
+    if code != OK:
+        msg = _LIB.need_last_error().decode(errors="replace") if _LIB is not None else ""
+        raise NeedError(fn, code, msg)

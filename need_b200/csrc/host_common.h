@@ -1,0 +1,59 @@
+// host_common.h -- shared host-side helpers of the C ABI: error reporting,
+// per-device one-time kernel attributes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <atomic>
+#include <string>
+
+#include "need_scan.h"
+
+namespace need {
+
+// Message of the calling thread's last failure.
+inline std::string& last_error_slot() {
+    static thread_local std::string msg;
+    return msg;
+}
+
+inline int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    last_error_slot() = buf;
+    return code;
+}
+
+inline int ok() {
+    last_error_slot().clear();
+    return NEED_OK;
+}
+
+inline int cuda_fail(cudaError_t e, const char* what) {
+    return fail(NEED_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device.
+template <typename Kern>
+inline cudaError_t ensure_smem(Kern kern, int bytes, std::atomic<uint64_t>& done_mask) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+    if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
+inline int dtype_bytes(int dt) { return dt == NEED_F32 ? 4 : 2; }
+inline bool dtype_ok(int dt) { return dt == NEED_F32 || dt == NEED_BF16 || dt == NEED_F16; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace need

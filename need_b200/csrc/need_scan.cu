@@ -1,0 +1,319 @@
+// need_scan.cu -- C ABI of the chunked-scan kernels (need_scan.h): argument
+// validation, TMA descriptor encoding, tile planning and launch.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <mutex>
+
+#include "host_common.h"
+#include "need_scan.h"
+#include "scan_kernel.cuh"
+
+using namespace need;
+using bf16 = __nv_bfloat16;
+using f16 = __half;
+
+namespace {
+
+// ------------------------------------------------------------------ plans
+// One instantiation of scan_kernel per (form, stream dtype, decay dtype,
+// row-broadcast decay).  Tile lengths keep each CTA's staged tile near 96 KB
+// so two CTAs fit an SM's 228 KB of shared memory.
+template <typename T>
+using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? 64 : 32, sizeof(T) == 2 ? 8 : 4>;
+template <typename T>
+using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? 32 : 16, sizeof(T) == 2 ? 8 : 4>;
+
+template <typename TS, typename TD, bool RD>
+struct AffL {
+    static constexpr int L = RD ? (sizeof(TS) == 2 ? 64 : 32) : ((sizeof(TS) == 2 && sizeof(TD) == 2) ? 64 : 32);
+};
+template <typename TS, typename TD, bool RD>
+using AffCfg = ScanCfg<FORM_AFFINE, TS, TD, RD, AffL<TS, TD, RD>::L, 8>;
+
+template <typename TS, typename TD, bool RD>
+struct RetL {
+    static constexpr bool SMALL = !RD && sizeof(TS) == 4;
+    static constexpr int L = RD ? (sizeof(TS) == 2 ? 64 : 32) : (SMALL ? 16 : 32);
+    static constexpr int NW = SMALL ? 4 : 8;
+};
+template <typename TS, typename TD, bool RD>
+using RetCfg = ScanCfg<FORM_RETENTION, TS, TD, RD, RetL<TS, TD, RD>::L, RetL<TS, TD, RD>::NW>;
+
+struct Plan {
+    int L = 0, nin = 0, in0 = 0;
+    bool dstream = false, split = false;
+    int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
+};
+
+template <class K>
+int launch_cfg(const ScanParams& prm, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_done{0};
+    cudaError_t e = ensure_smem(scan_kernel<K>, K::SMEM, smem_done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel)");
+    scan_kernel<K><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch");
+    return NEED_OK;
+}
+
+template <class K>
+Plan plan_of() {
+    Plan p;
+    p.L = K::L;
+    p.nin = K::NIN;
+    p.in0 = K::IN0;
+    p.dstream = K::HAS_DSTREAM;
+    p.split = K::SPLIT;
+    p.launch = &launch_cfg<K>;
+    return p;
+}
+
+template <template <typename, typename, bool> class CFG>
+bool plan_decay(int dt, int ddt, int rd, Plan* out) {
+    // decay dtype either equals the stream dtype or is fp32
+    if (dt == NEED_F32 && ddt == NEED_F32) *out = rd ? plan_of<CFG<float, float, true>>() : plan_of<CFG<float, float, false>>();
+    else if (dt == NEED_BF16 && ddt == NEED_BF16) *out = rd ? plan_of<CFG<bf16, bf16, true>>() : plan_of<CFG<bf16, bf16, false>>();
+    else if (dt == NEED_BF16 && ddt == NEED_F32) *out = rd ? plan_of<CFG<bf16, float, true>>() : plan_of<CFG<bf16, float, false>>();
+    else if (dt == NEED_F16 && ddt == NEED_F16) *out = rd ? plan_of<CFG<f16, f16, true>>() : plan_of<CFG<f16, f16, false>>();
+    else if (dt == NEED_F16 && ddt == NEED_F32) *out = rd ? plan_of<CFG<f16, float, true>>() : plan_of<CFG<f16, float, false>>();
+    else return false;
+    return true;
+}
+
+bool select_plan(int form, int dt, int ddt, int rd, Plan* out) {
+    if (!dtype_ok(dt)) return false;
+    switch (form) {
+        case NEED_FORM_GATED:
+            if (dt == NEED_F32) *out = plan_of<GatedCfg<float>>();
+            else if (dt == NEED_BF16) *out = plan_of<GatedCfg<bf16>>();
+            else *out = plan_of<GatedCfg<f16>>();
+            return true;
+        case NEED_FORM_SSD:
+            if (dt == NEED_F32) *out = plan_of<SsdCfg<float>>();
+            else if (dt == NEED_BF16) *out = plan_of<SsdCfg<bf16>>();
+            else *out = plan_of<SsdCfg<f16>>();
+            return true;
+        case NEED_FORM_AFFINE:
+            return plan_decay<AffCfg>(dt, ddt, rd ? 1 : 0, out);
+        case NEED_FORM_RETENTION:
+            return plan_decay<RetCfg>(dt, ddt, rd ? 1 : 0, out);
+        default:
+            return false;
+    }
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct Geometry {
+    int64_t ncb, nchains, nchunks, ntiles;
+};
+
+Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) {
+    Geometry g;
+    g.ncb = cdiv(C, CB);
+    g.nchains = nb * nh * g.ncb;
+    g.nchunks = cdiv(T, pl.L);
+    g.ntiles = g.nchains * g.nchunks;
+    return g;
+}
+
+size_t ws_bytes(int64_t ntiles) {
+    const size_t hdr = WS_HDR_WORDS * 4;
+    const size_t flags = ((size_t(ntiles) * 4 + 255) / 256) * 256;
+    return hdr + flags + size_t(ntiles) * 256 * sizeof(float2) * 2;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t nh, int64_t T, int64_t C,
+                int L, int which) {
+    if (v.ptr == nullptr) return fail(NEED_ERR_INVALID, "in[%d] is null", which);
+    if (!aligned16(v.ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[%d] is not 16-byte aligned", which);
+    const int64_t es = dtype_bytes(dt);
+    const int64_t sizes[3] = {T, nh, nb};
+    const int64_t strides[3] = {v.stride_t, v.stride_h, v.stride_b};
+    cuuint64_t gs[3];
+    int64_t prev = ((C * es + 15) / 16) * 16;  // packed stride for size-1 dims
+    for (int i = 0; i < 3; ++i) {
+        if (sizes[i] == 1) {
+            gs[i] = static_cast<cuuint64_t>(prev);
+        } else {
+            const int64_t b = strides[i] * es;
+            if (strides[i] <= 0 || (b % 16) != 0 || b >= (int64_t(1) << 40))
+                return fail(NEED_ERR_UNSUPPORTED,
+                            "in[%d]: stride %lld (dim %d) must be positive and a multiple of 16 bytes", which,
+                            static_cast<long long>(strides[i]), i);
+            gs[i] = static_cast<cuuint64_t>(b);
+        }
+        prev = static_cast<int64_t>(gs[i]) * sizes[i];
+    }
+    const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(T), cuuint64_t(nh), cuuint64_t(nb)};
+    const cuuint32_t box[4] = {cuuint32_t(CB), cuuint32_t(L), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUtensorMapDataType ty = dt == NEED_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : dt == NEED_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    auto fn = encode_fn();
+    if (fn == nullptr) return fail(NEED_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const CUresult r = fn(tm, ty, 4, const_cast<void*>(v.ptr), dims, gs, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NEED_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled(in[%d]) failed: %d", which, int(r));
+    return NEED_OK;
+}
+
+int check_sizes(const need_scan_args* a) {
+    if (a->nb < 1 || a->nh < 1 || a->T < 1 || a->C < 1)
+        return fail(NEED_ERR_INVALID, "sizes must be >= 1 (nb=%lld nh=%lld T=%lld C=%lld)", (long long)a->nb,
+                    (long long)a->nh, (long long)a->T, (long long)a->C);
+    if (a->T > INT32_MAX / 2 || a->C > INT32_MAX / 2 || a->nb * a->nh > INT32_MAX / 2)
+        return fail(NEED_ERR_UNSUPPORTED, "sizes exceed the 32-bit tile index range");
+    return NEED_OK;
+}
+
+// Validates `a` and fills the kernel parameters.
+int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
+    if (a == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (a->form != expect_form) return fail(NEED_ERR_INVALID, "args->form %d does not match the entry point", a->form);
+    if (int rc = check_sizes(a)) return rc;
+    const bool rowdec_form = a->form == NEED_FORM_AFFINE || a->form == NEED_FORM_RETENTION;
+    const int ddt = rowdec_form ? a->decay_dtype : a->dtype;
+    const int rd = rowdec_form ? (a->decay_per_row ? 1 : 0) : 0;
+    if (!select_plan(a->form, a->dtype, ddt, rd, pl))
+        return fail(NEED_ERR_UNSUPPORTED, "no kernel for form %d dtype %d decay dtype %d", a->form, a->dtype, ddt);
+    const Geometry g = geometry(*pl, a->nb, a->nh, a->T, a->C);
+    if (g.ntiles > INT32_MAX) return fail(NEED_ERR_UNSUPPORTED, "too many tiles (%lld)", (long long)g.ntiles);
+    const int group = pl->split ? 4 : 8;
+    if (a->C % group != 0)
+        return fail(NEED_ERR_UNSUPPORTED, "C=%lld must be a multiple of %d for this dtype", (long long)a->C, group);
+
+    memset(P, 0, sizeof(*P));
+    for (int k = 0; k < pl->nin; ++k) {
+        const int dt = (pl->dstream && k == 0) ? ddt : a->dtype;
+        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->L, pl->in0 + k))
+            return rc;
+    }
+    if (rowdec_form && rd) {
+        if (a->in[0].ptr == nullptr) return fail(NEED_ERR_INVALID, "in[0] (row decay) is null");
+        P->rowdec = a->in[0].ptr;
+        P->dsb = a->in[0].stride_b;
+        P->dsh = a->in[0].stride_h;
+        P->dst = a->in[0].stride_t;
+    }
+    if (a->out == nullptr) return fail(NEED_ERR_INVALID, "out is null");
+    if (!aligned16(a->out)) return fail(NEED_ERR_UNSUPPORTED, "out is not 16-byte aligned");
+    const int64_t ostr[3] = {a->out_stride_t, a->out_stride_h, a->out_stride_b};
+    const int64_t osz[3] = {a->T, a->nh, a->nb};
+    for (int i = 0; i < 3; ++i)
+        if (osz[i] > 1 && (ostr[i] <= 0 || ostr[i] % group != 0))
+            return fail(NEED_ERR_UNSUPPORTED, "out stride %lld must be a positive multiple of %d elements",
+                        (long long)ostr[i], group);
+    if (a->form == NEED_FORM_SSD && a->d_skip == nullptr) return fail(NEED_ERR_INVALID, "d_skip is null");
+    if (a->workspace == nullptr) return fail(NEED_ERR_WORKSPACE, "workspace is null");
+    if (!aligned16(a->workspace)) return fail(NEED_ERR_WORKSPACE, "workspace is not 16-byte aligned");
+    const size_t need = ws_bytes(g.ntiles);
+    if (a->workspace_bytes < need)
+        return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, need);
+
+    P->nb = int32_t(a->nb);
+    P->nh = int32_t(a->nh);
+    P->T = int32_t(a->T);
+    P->C = int32_t(a->C);
+    P->ncb = int32_t(g.ncb);
+    P->nchains = int32_t(g.nchains);
+    P->nchunks = int32_t(g.nchunks);
+    P->ntiles = int32_t(g.ntiles);
+    P->out = a->out;
+    P->osb = a->out_stride_b;
+    P->osh = a->out_stride_h;
+    P->ost = a->out_stride_t;
+    P->dskip = a->d_skip;
+    // need_kernels.py:331: the Python floats enter fp32 arithmetic as fp32
+    P->dt_min = static_cast<float>(a->dt_min);
+    P->dt_scale = static_cast<float>(a->dt_max - a->dt_min);
+    P->h0 = a->h0;
+    P->h_final = a->h_final;
+    P->seg = a->seg_start;
+    P->sgb = a->seg_stride_b;
+    P->sgt = a->seg_stride_t;
+    P->summary = a->summary;
+    P->tile_prod = a->tile_prod;
+    unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+    P->hdr = reinterpret_cast<uint32_t*>(ws);
+    P->flags = reinterpret_cast<uint32_t*>(ws + WS_HDR_WORDS * 4);
+    const size_t flag_bytes = ((size_t(g.ntiles) * 4 + 255) / 256) * 256;
+    P->agg = reinterpret_cast<float2*>(ws + WS_HDR_WORDS * 4 + flag_bytes);
+    P->incl = P->agg + size_t(g.ntiles) * 256;
+    return NEED_OK;
+}
+
+int run(const need_scan_args* a, int form, cudaStream_t s) {
+    Plan pl;
+    ScanParams P;
+    if (int rc = prepare(a, form, &pl, &P)) return rc;
+    if (int rc = pl.launch(P, s)) return rc;
+    return ok();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ exported
+extern "C" {
+
+int need_abi_version(void) { return NEED_SCAN_ABI_VERSION; }
+
+const char* need_last_error(void) { return last_error_slot().c_str(); }
+
+int64_t need_scan_chunk_len(int32_t form, int32_t dtype, int32_t decay_dtype, int32_t decay_per_row) {
+    Plan pl;
+    const bool rf = form == NEED_FORM_AFFINE || form == NEED_FORM_RETENTION;
+    if (!select_plan(form, dtype, rf ? decay_dtype : dtype, rf ? decay_per_row : 0, &pl)) return -1;
+    return pl.L;
+}
+
+size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t decay_dtype, int32_t decay_per_row, int64_t nb,
+                                int64_t nh, int64_t T, int64_t C) {
+    Plan pl;
+    const bool rf = form == NEED_FORM_AFFINE || form == NEED_FORM_RETENTION;
+    if (!select_plan(form, dtype, rf ? decay_dtype : dtype, rf ? decay_per_row : 0, &pl)) return 0;
+    if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(0);
+    return ws_bytes(geometry(pl, nb, nh, T, C).ntiles);
+}
+
+int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream) {
+    if (workspace == nullptr || error_out == nullptr) return fail(NEED_ERR_INVALID, "null argument");
+    uint32_t* word = static_cast<uint32_t*>(workspace) + WS_ERROR;
+    cudaError_t e = cudaMemcpyAsync(error_out, word, 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(word, 0, 4, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "need_workspace_error");
+    return ok();
+}
+
+int need_affine_recurrence_scan(const need_scan_args* args, need_stream_t stream) {
+    return run(args, NEED_FORM_AFFINE, stream);
+}
+
+int need_ssd_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_SSD, stream); }
+
+int need_recurrent_retention_scan(const need_scan_args* args, need_stream_t stream) {
+    return run(args, NEED_FORM_RETENTION, stream);
+}
+
+int need_gated_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_GATED, stream); }
+
+}  // extern "C"

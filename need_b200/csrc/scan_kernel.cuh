@@ -1,0 +1,658 @@
+// scan_kernel.cuh -- single-pass chunked scan of h[t] = a[t]*h[t-1] + b[t] for
+// sm_100a (B200).
+//
+// Work decomposition.  A call scans nseq = nb*nh independent sequences of C
+// channels over T steps.  A tile is (sequence, 256-channel block, L-token
+// chunk).  Tiles are processed in ticket order (an atomic counter), chunk-major,
+// so every tile's predecessor along T was handed out earlier and is resident or
+// finished: waiting on it cannot deadlock.
+//
+// Per tile (one CTA, NW warps):
+//   1. TMA (cp.async.bulk.tensor, no multicast) stages the tile's input rows
+//      [L x 256] of every streamed tensor into shared memory (zero fill past
+//      T and C), completion on one mbarrier.
+//   2. Phase 1: warp w owns rows [w*R, (w+1)*R), lane owns 8 channels.  Each
+//      thread computes a, b for its rows (gate math per form; 16-bit inputs
+//      are rounded where the reference's torch path rounds), writes them back
+//      in place where later phases need them, and reduces its rows to one
+//      affine map (A, B): h_out = A*h_in + B.
+//   3. The warps' maps are composed through shared memory: each warp gets the
+//      map of the rows before it, the last warp the tile's whole map.
+//   4. Decoupled look-back (last warp): publish the tile map (AGG), walk back
+//      over predecessors composing their maps until one that has published its
+//      inclusive state (INCL), publish our own inclusive state.  Every wait is
+//      bounded; on give-up an error bit is set and the tile continues.
+//   5. Phase 2: every thread restarts its rows from the exact carry, writes
+//      the outputs straight to global memory (16-byte stores, a warp writes
+//      512 contiguous bytes per row).
+// HBM traffic is the algorithmic minimum (inputs read once, outputs written
+// once) plus a 4 KB workspace record per tile.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+
+namespace need {
+
+enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
+
+constexpr int CB = 256;  // channels per tile (32 lanes x 8 channels)
+
+// workspace header words (uint32)
+enum { WS_TICKET = 0, WS_DONE = 1, WS_EPOCH = 2, WS_ERROR = 3, WS_HDR_WORDS = 32 };
+enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
+enum { ST_AGG = 1u, ST_INCL = 2u };
+
+constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~100 ns sleeps: < 1 s worst case
+constexpr uint32_t kTmaPolls = 1u << 22;
+
+struct ScanParams {
+    CUtensorMap tm[5];  // streamed inputs (64-byte aligned members)
+    int32_t nb, nh, T, C;
+    int32_t ncb, nchains, nchunks, ntiles;
+    void* out;
+    int64_t osb, osh, ost;
+    const void* rowdec;  // decay per (b, h, t) when broadcast over C
+    int64_t dsb, dsh, dst;
+    const float* dskip;
+    float dt_min, dt_scale;
+    const float* h0;
+    float* h_final;
+    const uint8_t* seg;
+    int64_t sgb, sgt;
+    float* summary;
+    float* tile_prod;
+    uint32_t* hdr;
+    uint32_t* flags;
+    float2* agg;   // [ntiles][8][32]
+    float2* incl;  // [ntiles][8][32]
+};
+
+// ------------------------------------------------------------------ types
+template <typename T>
+struct Ops;
+
+template <>
+struct Ops<__nv_bfloat16> {
+    using P = __nv_bfloat162;
+    static constexpr int BYTES = 2;
+    static __device__ __forceinline__ P pack(float x, float y) { return __floats2bfloat162_rn(x, y); }
+    static __device__ __forceinline__ float2 unpack(P p) { return __bfloat1622float2(p); }
+    static __device__ __forceinline__ P mul(P a, P b) { return __hmul2_rn(a, b); }
+    static __device__ __forceinline__ P add(P a, P b) { return __hadd2_rn(a, b); }
+    static __device__ __forceinline__ P sub(P a, P b) { return __hsub2_rn(a, b); }
+    static __device__ __forceinline__ P one() { return __floats2bfloat162_rn(1.0f, 1.0f); }
+    static __device__ __forceinline__ P zero() { return __floats2bfloat162_rn(0.0f, 0.0f); }
+};
+
+template <>
+struct Ops<__half> {
+    using P = __half2;
+    static constexpr int BYTES = 2;
+    static __device__ __forceinline__ P pack(float x, float y) { return __floats2half2_rn(x, y); }
+    static __device__ __forceinline__ float2 unpack(P p) { return __half22float2(p); }
+    static __device__ __forceinline__ P mul(P a, P b) { return __hmul2_rn(a, b); }
+    static __device__ __forceinline__ P add(P a, P b) { return __hadd2_rn(a, b); }
+    static __device__ __forceinline__ P sub(P a, P b) { return __hsub2_rn(a, b); }
+    static __device__ __forceinline__ P one() { return __floats2half2_rn(1.0f, 1.0f); }
+    static __device__ __forceinline__ P zero() { return __floats2half2_rn(0.0f, 0.0f); }
+};
+
+template <>
+struct Ops<float> {
+    using P = float2;
+    static constexpr int BYTES = 4;
+    static __device__ __forceinline__ P pack(float x, float y) { return make_float2(x, y); }
+    static __device__ __forceinline__ float2 unpack(P p) { return p; }
+    // separately rounded fp32 ops (no contraction into fma), as torch computes
+    static __device__ __forceinline__ P mul(P a, P b) {
+        return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+    }
+    static __device__ __forceinline__ P add(P a, P b) {
+        return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+    }
+    static __device__ __forceinline__ P sub(P a, P b) {
+        return make_float2(__fsub_rn(a.x, b.x), __fsub_rn(a.y, b.y));
+    }
+    static __device__ __forceinline__ P one() { return make_float2(1.0f, 1.0f); }
+    static __device__ __forceinline__ P zero() { return make_float2(0.0f, 0.0f); }
+};
+
+// sigmoid(x) = 1 / (1 + 2^(-x * log2 e)).  16-bit paths round the result to
+// bf16/fp16 afterwards, so the hardware ex2/rcp approximations (a few fp32 ulp)
+// only move a rounded gate when it lies within those ulp of a rounding tie.
+__device__ __forceinline__ float sigmoid_approx(float x) {
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+    return r;
+}
+__device__ __forceinline__ float exp_approx(float x) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * 1.4426950408889634f));
+    return e;
+}
+// fp32 paths: library expf and IEEE division, as the reference's fp32 ops.
+__device__ __forceinline__ float sigmoid_exact(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
+
+template <typename T>
+__device__ __forceinline__ float sigm(float x) {
+    if constexpr (Ops<T>::BYTES == 4) return sigmoid_exact(x);
+    else return sigmoid_approx(x);
+}
+template <typename T>
+__device__ __forceinline__ float expo(float x) {
+    if constexpr (Ops<T>::BYTES == 4) return expf(x);
+    else return exp_approx(x);
+}
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
+// ------------------------------------------------------------------ 8-channel rows
+// A thread's 8 channels: with SPLIT (any 4-byte stream) they are two groups of
+// four, channels [lane*4, +4) and [128 + lane*4, +4); otherwise one group of
+// eight, [lane*8, +8).  Pair i holds channels (2i, 2i+1) of that list.
+template <bool SPLIT>
+__device__ __forceinline__ int chan(int e, int lane) {
+    return SPLIT ? ((e >> 2) * 128 + lane * 4 + (e & 3)) : (lane * 8 + e);
+}
+
+template <typename T, bool SPLIT>
+struct Row8 {
+    using P = typename Ops<T>::P;
+    // shared -> 4 pairs
+    static __device__ __forceinline__ void lds(const T* row, int lane, P (&p)[4]) {
+        if constexpr (Ops<T>::BYTES == 4) {
+            const float4 v0 = *reinterpret_cast<const float4*>(row + lane * 4);
+            const float4 v1 = *reinterpret_cast<const float4*>(row + 128 + lane * 4);
+            p[0] = make_float2(v0.x, v0.y);
+            p[1] = make_float2(v0.z, v0.w);
+            p[2] = make_float2(v1.x, v1.y);
+            p[3] = make_float2(v1.z, v1.w);
+        } else if constexpr (SPLIT) {
+            const uint2 v0 = *reinterpret_cast<const uint2*>(row + lane * 4);
+            const uint2 v1 = *reinterpret_cast<const uint2*>(row + 128 + lane * 4);
+            const uint32_t w[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = *reinterpret_cast<const P*>(&w[i]);
+        } else {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + lane * 8);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = *reinterpret_cast<const P*>(&w[i]);
+        }
+    }
+    static __device__ __forceinline__ void sts(T* row, int lane, const P (&p)[4]) {
+        if constexpr (Ops<T>::BYTES == 4) {
+            *reinterpret_cast<float4*>(row + lane * 4) = make_float4(p[0].x, p[0].y, p[1].x, p[1].y);
+            *reinterpret_cast<float4*>(row + 128 + lane * 4) = make_float4(p[2].x, p[2].y, p[3].x, p[3].y);
+        } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(&p[i]);
+            if constexpr (SPLIT) {
+                *reinterpret_cast<uint2*>(row + lane * 4) = make_uint2(w[0], w[1]);
+                *reinterpret_cast<uint2*>(row + 128 + lane * 4) = make_uint2(w[2], w[3]);
+            } else {
+                *reinterpret_cast<uint4*>(row + lane * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    }
+    // registers -> global row (channel 0 of the tile at `row`); group g is
+    // stored only when ok[g] (channels past C are never written)
+    static __device__ __forceinline__ void stg(T* row, int lane, const P (&p)[4], bool ok0, bool ok1) {
+        if constexpr (Ops<T>::BYTES == 4) {
+            if (ok0) *reinterpret_cast<float4*>(row + lane * 4) = make_float4(p[0].x, p[0].y, p[1].x, p[1].y);
+            if (ok1) *reinterpret_cast<float4*>(row + 128 + lane * 4) = make_float4(p[2].x, p[2].y, p[3].x, p[3].y);
+        } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(&p[i]);
+            if constexpr (SPLIT) {
+                if (ok0) *reinterpret_cast<uint2*>(row + lane * 4) = make_uint2(w[0], w[1]);
+                if (ok1) *reinterpret_cast<uint2*>(row + 128 + lane * 4) = make_uint2(w[2], w[3]);
+            } else {
+                if (ok0) *reinterpret_cast<uint4*>(row + lane * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    }
+};
+
+// ------------------------------------------------------------------ config
+template <int FORM_, typename TS_, typename TD_, bool ROWDEC_, int L_, int NW_>
+struct ScanCfg {
+    static constexpr int FORM = FORM_;
+    using TS = TS_;  // streamed dtype (inputs other than a separate decay, and the output)
+    using TD = TD_;  // decay dtype (AFFINE / RETENTION)
+    static constexpr bool ROWDEC = ROWDEC_;
+    static constexpr int L = L_, NW = NW_, NT = NW * 32, R = L / NW;
+    static_assert(L % NW == 0, "rows must split evenly over warps");
+    static constexpr bool HAS_DSTREAM = (FORM == FORM_AFFINE || FORM == FORM_RETENTION) && !ROWDEC;
+    static constexpr bool SPLIT = (Ops<TS>::BYTES == 4) || (HAS_DSTREAM && Ops<TD>::BYTES == 4);
+    // streamed inputs, in[] order of the C ABI
+    static constexpr int NIN = FORM == FORM_AFFINE      ? (ROWDEC ? 1 : 2)
+                               : FORM == FORM_GATED     ? 3
+                               : FORM == FORM_SSD       ? 5
+                                                        : (ROWDEC ? 2 : 3);
+    // in[] index of the first streamed tensor (AFFINE/RETENTION with a row decay skip in[0])
+    static constexpr int IN0 = ((FORM == FORM_AFFINE || FORM == FORM_RETENTION) && ROWDEC) ? 1 : 0;
+    __host__ __device__ static constexpr int slot_bytes(int k) {
+        return L * CB * ((HAS_DSTREAM && k == 0) ? Ops<TD>::BYTES : Ops<TS>::BYTES);
+    }
+    __host__ __device__ static constexpr int slots_bytes() {
+        int s = 0;
+        for (int k = 0; k < NIN; ++k) s += slot_bytes(k);
+        return s;
+    }
+    // GATED frees its input-gate slot after phase 1: the warp maps live there.
+    static constexpr int AGG_SLOT = FORM == FORM_GATED ? 1 : -1;
+    static constexpr int AGG_BYTES = NW * 8 * 32 * 8;
+    static constexpr int OFF_AGG = slots_bytes();
+    static constexpr int OFF_CARRY = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
+    static constexpr int OFF_ROWDEC = OFF_CARRY + 8 * 32 * 4;
+    static constexpr int OFF_RESET = OFF_ROWDEC + (ROWDEC ? L * 4 : 0);
+    static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
+    static constexpr int SMEM = OFF_MISC + 32 + 128;  // + alignment slack
+    // resident CTAs per SM: bounded by shared memory (228 KB per SM, 1 KB
+    // reserved per CTA) and by 128 registers per thread at 256 threads
+    static constexpr int MINB_SMEM = (228 * 1024) / (SMEM + 1024);
+    static constexpr int MINB_CAP = NT >= 256 ? 2 : 4;
+    static constexpr int MINB = MINB_SMEM < 1 ? 1 : (MINB_SMEM < MINB_CAP ? MINB_SMEM : MINB_CAP);
+};
+
+template <class K>
+__device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
+    int off = 0;
+#pragma unroll
+    for (int j = 0; j < 5; ++j)
+        if (j < k) off += K::slot_bytes(j);
+    return base + off;
+}
+
+// ------------------------------------------------------------------ the kernel
+template <class K>
+__global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
+    using TS = typename K::TS;
+    using TD = typename K::TD;
+    using OS = Ops<TS>;
+    using PS = typename OS::P;
+    constexpr bool SPLIT = K::SPLIT;
+    constexpr int L = K::L, NW = K::NW, R = K::R;
+
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    float2* s_agg = reinterpret_cast<float2*>(K::AGG_SLOT >= 0 ? slot_ptr<K>(base, K::AGG_SLOT)
+                                                                 : base + K::OFF_AGG);
+    float* s_carry = reinterpret_cast<float*>(base + K::OFF_CARRY);
+    float* s_rowdec = reinterpret_cast<float*>(base + K::OFF_ROWDEC);
+    uint8_t* s_reset = base + K::OFF_RESET;
+    uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(base + K::OFF_MISC + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        s_misc[0] = atomicAdd(&p.hdr[WS_TICKET], 1u);
+        s_misc[1] = ld_volatile_u32(&p.hdr[WS_EPOCH]);
+        mbar_init(s_bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int tile = static_cast<int>(s_misc[0]);
+    const uint32_t epoch = s_misc[1] & 0x3fffffffu;
+    const int chunk = tile / p.nchains;
+    const int chain = tile - chunk * p.nchains;
+    const int seq = chain / p.ncb;
+    const int cblk = chain - seq * p.ncb;
+    const int bi = seq / p.nh, hi = seq - bi * p.nh;
+    const int t0 = chunk * L, c0 = cblk * CB;
+
+    if (tid == 0) {
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k);
+        mbar_arrive_expect_tx(s_bar, bytes);
+#pragma unroll
+        for (int k = 0; k < K::NIN; ++k)
+            tma_load_4d(slot_ptr<K>(base, k), &p.tm[k], c0, t0, hi, bi, s_bar);
+    }
+    // reset flags and per-row decay while the tile is in flight
+    for (int r = tid; r < L; r += K::NT) {
+        const int t = t0 + r;
+        uint8_t rs = 0;
+        if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
+        s_reset[r] = rs;
+        if constexpr (K::ROWDEC) {
+            float d = 1.0f;
+            if (t < p.T) d = to_f(reinterpret_cast<const TD*>(p.rowdec)[bi * p.dsb + hi * p.dsh + (int64_t)t * p.dst]);
+            s_rowdec[r] = d;
+        }
+    }
+    if (!mbar_wait_bounded(s_bar, 0, kTmaPolls)) {
+        atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+        mbar_wait_bounded(s_bar, 0, kTmaPolls);
+    }
+    __syncthreads();
+
+    // per-thread constants
+    const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
+    float dsk[8];
+    if constexpr (K::FORM == FORM_SSD) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int c = c0 + chan<SPLIT>(e, lane);
+            dsk[e] = c < p.C ? p.dskip[c] : 0.0f;
+        }
+    }
+
+    // ---------------------------------------------------------- phase 1
+    // a, b for row r of this thread; `write` stores the rounded a, b back for phase 2.
+    auto gates = [&](int r, bool write, float (&a)[8], float (&b)[8]) {
+        const bool reset = s_reset[r] != 0;
+        if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
+            if constexpr (K::ROWDEC) {
+                const float d = reset ? 0.0f : s_rowdec[r];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) a[e] = d;
+            } else {
+                typename Ops<TD>::P dp[4];
+                Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CB, lane, dp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = Ops<TD>::unpack(dp[i]);
+                    a[2 * i] = reset ? 0.0f : f.x;
+                    a[2 * i + 1] = reset ? 0.0f : f.y;
+                }
+            }
+            PS up[4];
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CB, lane, up);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = OS::unpack(up[i]);
+                b[2 * i] = f.x;
+                b[2 * i + 1] = f.y;
+            }
+        } else {
+            // GATED: slots z, g, x.  SSD: slots dt, bg, u (cg, og used in phase 2)
+            TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CB;
+            TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CB;
+            TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CB;
+            PS p0[4], p1[4], p2[4], ap[4], bp[4];
+            Row8<TS, SPLIT>::lds(s0, lane, p0);
+            Row8<TS, SPLIT>::lds(s1, lane, p1);
+            Row8<TS, SPLIT>::lds(s2, lane, p2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f0 = OS::unpack(p0[i]);
+                const float2 f1 = OS::unpack(p1[i]);
+                PS dec;
+                if constexpr (K::FORM == FORM_GATED) {
+                    dec = OS::pack(sigm<TS>(f0.x), sigm<TS>(f0.y));
+                } else {
+                    // need_kernels.py:330-332: fp32 dt, decay rounded to the input dtype
+                    const float dx = __fadd_rn(__fmul_rn(sigm<TS>(f0.x), p.dt_scale), p.dt_min);
+                    const float dy = __fadd_rn(__fmul_rn(sigm<TS>(f0.y), p.dt_scale), p.dt_min);
+                    dec = OS::pack(expo<TS>(-dx), expo<TS>(-dy));
+                }
+                const PS gs = OS::pack(sigm<TS>(f1.x), sigm<TS>(f1.y));
+                const PS gx = OS::mul(gs, p2[i]);
+                const PS om = OS::sub(OS::one(), dec);
+                bp[i] = OS::mul(om, gx);
+                ap[i] = reset ? OS::zero() : dec;
+                const float2 af = OS::unpack(ap[i]);
+                const float2 bf = OS::unpack(bp[i]);
+                a[2 * i] = af.x;
+                a[2 * i + 1] = af.y;
+                b[2 * i] = bf.x;
+                b[2 * i + 1] = bf.y;
+            }
+            if (write) {
+                Row8<TS, SPLIT>::sts(s0, lane, ap);  // a over the decay input
+                if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, lane, bp);  // b over x
+                else Row8<TS, SPLIT>::sts(s1, lane, bp);  // b over b_gate
+            }
+        }
+        if (r >= nvalid) {  // rows past T: identity map
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                a[e] = 1.0f;
+                b[e] = 0.0f;
+            }
+        }
+    };
+    // a, b written back by phase 1
+    auto reload = [&](int r, float (&a)[8], float (&b)[8]) {
+        if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
+            gates(r, false, a, b);
+        } else {
+            PS ap[4], bp[4];
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CB, lane, ap);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CB, lane, bp);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 af = OS::unpack(ap[i]);
+                const float2 bf = OS::unpack(bp[i]);
+                a[2 * i] = af.x;
+                a[2 * i + 1] = af.y;
+                b[2 * i] = bf.x;
+                b[2 * i + 1] = bf.y;
+            }
+        }
+    };
+
+    float A[8], B[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        A[e] = 1.0f;
+        B[e] = 0.0f;
+    }
+#pragma unroll 2
+    for (int j = 0; j < R; ++j) {
+        float a[8], b[8];
+        gates(warp * R + j, true, a, b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            B[e] = fmaf(a[e], B[e], b[e]);
+            A[e] = a[e] * A[e];
+        }
+    }
+    if constexpr (K::AGG_SLOT >= 0) __syncthreads();  // the slot's last readers are done
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_agg[(warp * 8 + e) * 32 + lane] = make_float2(A[e], B[e]);
+    __syncthreads();
+
+    // ---------------------------------------------------------- compose warps
+    float EA[8], EB[8];  // map of the rows before this warp
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        EA[e] = 1.0f;
+        EB[e] = 0.0f;
+    }
+    for (int w = 0; w < warp; ++w) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float2 m = s_agg[(w * 8 + e) * 32 + lane];
+            EB[e] = fmaf(m.x, EB[e], m.y);
+            EA[e] = m.x * EA[e];
+        }
+    }
+
+    // ---------------------------------------------------------- look-back
+    if (warp == NW - 1) {
+        float TA[8], TB[8];  // the whole tile's map
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            TA[e] = A[e] * EA[e];
+            TB[e] = fmaf(A[e], EB[e], B[e]);
+        }
+        const int seqC = seq;  // row of h0 / h_final / summary
+        float carry[8], carryP[8];
+        if (chunk == 0) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int c = c0 + chan<SPLIT>(e, lane);
+                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seqC * p.C + c] : 0.0f;
+                carryP[e] = 1.0f;
+            }
+        } else {
+            // publish this tile's map
+            float2* my = p.agg + (int64_t)tile * 256;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) __stcg(&my[e * 32 + lane], make_float2(TA[e], TB[e]));
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) st_release_gpu(&p.flags[tile], (epoch << 2) | ST_AGG);
+            // walk back along the chain
+            float accA[8], accB[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                accA[e] = 1.0f;
+                accB[e] = 0.0f;
+            }
+            int k = tile - p.nchains;
+            for (;;) {
+                uint32_t f = 0;
+                bool ok = false;
+                for (uint32_t it = 0; it < kLookbackPolls; ++it) {
+                    uint32_t v = 0;
+                    if (lane == 0) v = ld_acquire_gpu(&p.flags[k]);
+                    v = __shfl_sync(0xffffffffu, v, 0);
+                    if ((v >> 2) == epoch && (v & 3u) != 0) {
+                        f = v;
+                        ok = true;
+                        break;
+                    }
+                    if (it >= 4) __nanosleep(100);
+                }
+                if (!ok) {
+                    if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        carry[e] = accB[e];
+                        carryP[e] = accA[e];
+                    }
+                    break;
+                }
+                (void)ld_acquire_gpu(&p.flags[k]);  // every lane acquires before reading the record
+                if ((f & 3u) == ST_INCL) {
+                    const float2* src = p.incl + (int64_t)k * 256;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 m = __ldcg(&src[e * 32 + lane]);  // (prod, h)
+                        carry[e] = fmaf(accA[e], m.y, accB[e]);
+                        carryP[e] = accA[e] * m.x;
+                    }
+                    break;
+                }
+                const float2* src = p.agg + (int64_t)k * 256;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float2 m = __ldcg(&src[e * 32 + lane]);  // (A, B)
+                    accB[e] = fmaf(accA[e], m.y, accB[e]);
+                    accA[e] = accA[e] * m.x;
+                }
+                k -= p.nchains;
+            }
+        }
+        // publish the inclusive state
+        float inclP[8], inclH[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            inclP[e] = TA[e] * carryP[e];
+            inclH[e] = fmaf(TA[e], carry[e], TB[e]);
+        }
+        if (chunk + 1 < p.nchunks) {
+            float2* mi = p.incl + (int64_t)tile * 256;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) __stcg(&mi[e * 32 + lane], make_float2(inclP[e], inclH[e]));
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) st_release_gpu(&p.flags[tile], (epoch << 2) | ST_INCL);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            s_carry[e * 32 + lane] = carry[e];
+            const int c = c0 + chan<SPLIT>(e, lane);
+            if (c < p.C) {
+                if (p.tile_prod != nullptr)
+                    p.tile_prod[((int64_t)seqC * p.nchunks + chunk) * p.C + c] = carryP[e];
+                if (chunk + 1 == p.nchunks) {
+                    if (p.h_final != nullptr) p.h_final[(int64_t)seqC * p.C + c] = inclH[e];
+                    if (p.summary != nullptr)
+                        reinterpret_cast<float2*>(p.summary)[(int64_t)seqC * p.C + c] = make_float2(inclP[e], inclH[e]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---------------------------------------------------------- phase 2
+    float h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = fmaf(EA[e], s_carry[e * 32 + lane], EB[e]);
+    const bool ok0 = c0 + chan<SPLIT>(0, lane) < p.C;
+    const bool ok1 = c0 + chan<SPLIT>(4, lane) < p.C;
+    TS* orow0 = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + c0;
+    PS dsp[4];
+    if constexpr (K::FORM == FORM_SSD) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dsp[i] = OS::pack(dsk[2 * i], dsk[2 * i + 1]);
+    }
+#pragma unroll 2
+    for (int j = 0; j < R; ++j) {
+        const int r = warp * R + j;
+        float a[8], b[8];
+        reload(r, a, b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = fmaf(a[e], h[e], b[e]);
+        if (r < nvalid) {
+            PS o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = OS::pack(h[2 * i], h[2 * i + 1]);  // state in the input dtype
+            if constexpr (K::FORM == FORM_SSD) {
+                PS up[4], cp[4], gp[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CB, lane, up);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CB, lane, cp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CB, lane, gp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 cf = OS::unpack(cp[i]);
+                    const float2 gf = OS::unpack(gp[i]);
+                    const PS cgs = OS::pack(sigm<TS>(cf.x), sigm<TS>(cf.y));
+                    const PS ogs = OS::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
+                    // (cg * state + D * u) * og, each op in the input dtype
+                    o[i] = OS::mul(OS::add(OS::mul(cgs, o[i]), OS::mul(dsp[i], up[i])), ogs);
+                }
+            } else if constexpr (K::FORM == FORM_RETENTION) {
+                PS qp[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CB, lane, qp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
+            }
+            Row8<TS, SPLIT>::stg(orow0 + (int64_t)(t0 + r) * p.ost, lane, o, ok0, ok1);
+        }
+    }
+
+    // ---------------------------------------------------------- retire
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const uint32_t d = atomicAdd(&p.hdr[WS_DONE], 1u);
+        if (d == static_cast<uint32_t>(p.ntiles) - 1u) {
+            atomicExch(&p.hdr[WS_TICKET], 0u);
+            atomicExch(&p.hdr[WS_DONE], 0u);
+            __threadfence();
+            atomicAdd(&p.hdr[WS_EPOCH], 1u);
+        }
+    }
+}
+
+}  // namespace need

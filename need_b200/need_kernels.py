@@ -1,0 +1,478 @@
+"""Drop-in replacement for NEED's ``need_kernels`` module on B200.
+
+``need_core.py`` imports ``need_kernels`` (need_core.py:33-36) and calls
+``affine_recurrence_scan`` (:1566-1567, :1637-1638), ``ssd_scan`` (:1624-1629),
+``rms_norm`` and ``swiglu`` on it.  This module keeps those names, signatures
+and conventions (need_kernels.py:229-345):
+
+* the result is a new tensor in ``update.dtype`` / ``u.dtype``; inputs are
+  never modified;
+* ``update.numel() == 0`` returns ``update``; a bad ``dim`` raises
+  ``IndexError``; ``decay`` broadcasts to ``update``'s shape;
+* ``backend`` is accepted and ignored: there is one implementation, the
+  sm_100a kernels of ``libneed_scan.so``.
+
+The scan itself runs only on CUDA tensors through the C ABI.  There is no CPU
+or eager-PyTorch fallback: a CPU tensor, a missing library or a request for
+gradients raises.  ``rms_norm``, ``swiglu``, ``residual_scale_add``,
+``sparse_moe_combine`` and ``sample_from_logits`` are outside the scan path;
+they are plain PyTorch expressions so that ``need_core`` keeps working.
+
+New entry points (no reference counterpart): ``gated_scan`` (sigmoid-gated
+scan with packed-segment resets, initial and final state), ``ragged_verify`` /
+``commit_states`` (speculative-decode state update), and the pieces of the
+sequence-parallel scan used by ``need_b200.sp``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import threading
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from . import abi
+
+HAS_TRITON = False  # the reference's flag: this module uses no Triton
+
+_DT = {torch.float32: abi.F32, torch.bfloat16: abi.BF16, torch.float16: abi.F16}
+_ws_lock = threading.Lock()
+_workspaces = {}
+
+
+# --------------------------------------------------------------------------
+# helpers
+# --------------------------------------------------------------------------
+
+def _lib():
+    return abi.load()
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("need_b200 kernels take CUDA tensors only (no CPU fallback); got a "
+                               f"{t.device} tensor")
+    dev = ts[0].device
+    for t in ts:
+        if t is not None and t.device != dev:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+
+
+def _no_grad(*ts: torch.Tensor) -> None:
+    if torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in ts):
+        raise NotImplementedError(
+            "need_b200: the scan has no backward yet; call it under torch.no_grad() or with tensors "
+            "that do not require grad")
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch for the look-back records, one per (device, stream).
+
+    The kernels leave it ready for the next launch on the same stream, so it is
+    allocated (and zeroed) only when a larger one is needed.
+    """
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=dev)
+            _workspaces[key] = ws
+        return ws
+
+
+def workspace_error(dev: Optional[torch.device] = None) -> int:
+    """Reads and clears the device error word of this stream's workspace (synchronises)."""
+    dev = dev or torch.device("cuda", torch.cuda.current_device())
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        return 0
+    out = ctypes.c_uint32(0)
+    abi.check("need_workspace_error", _lib().need_workspace_error(ws.data_ptr(), ctypes.byref(out), _stream(dev)))
+    return int(out.value)
+
+
+def _fill_common(a: abi.NeedScanArgs, form: int, dtype: torch.dtype, nb: int, nh: int, T: int, C: int,
+                 out: torch.Tensor) -> None:
+    """Form, dtype, sizes and the output of a [B, T, C] (nh == 1) call."""
+    a.form = form
+    a.dtype = _DT[dtype]
+    a.decay_dtype = _DT[dtype]
+    a.nb, a.nh, a.T, a.C = nb, nh, T, C
+    a.out = out.data_ptr()
+    if out.dim() == 3:
+        a.out_stride_b, a.out_stride_h, a.out_stride_t = out.stride(0), 0, out.stride(1)
+
+
+def _fill_state(a: abi.NeedScanArgs, dev, nb: int, nh: int, C: int, seg_start, h0, h_final) -> list:
+    keep = []
+    if seg_start is not None:
+        seg = seg_start.to(device=dev, dtype=torch.uint8)
+        if seg.dim() != 2 or seg.shape[0] != nb:
+            raise ValueError(f"seg_start must be [B, T] = [{nb}, T]; got {tuple(seg_start.shape)}")
+        a.seg_start = seg.data_ptr()
+        a.seg_stride_b, a.seg_stride_t = seg.stride()
+        keep.append(seg)
+    if h0 is not None:
+        h0f = h0.to(device=dev, dtype=torch.float32).reshape(nb * nh, C).contiguous()
+        a.h0 = h0f.data_ptr()
+        keep.append(h0f)
+    if h_final is not None:
+        a.h_final = h_final.data_ptr()
+    return keep
+
+
+def _launch(fn_name: str, a: abi.NeedScanArgs, dev: torch.device, rowdec: int = 0) -> None:
+    lib = _lib()
+    nbytes = lib.need_scan_workspace_size(a.form, a.dtype, a.decay_dtype, rowdec, a.nb, a.nh, a.T, a.C)
+    if nbytes == 0:
+        raise abi.NeedError(fn_name, abi.ERR_UNSUPPORTED, "unsupported dtype combination")
+    ws = workspace(dev, nbytes)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel()
+    abi.check(fn_name, getattr(lib, fn_name)(ctypes.byref(a), _stream(dev)))
+
+
+def _channel_ok(C: int, split: bool) -> bool:
+    return C % (4 if split else 8) == 0
+
+
+# --------------------------------------------------------------------------
+# affine_recurrence_scan  (need_kernels.py:229-264)
+# --------------------------------------------------------------------------
+
+def _bhtc(t: torch.Tensor, dim: int) -> torch.Tensor:
+    """``t`` (at most two dims before ``dim``) laid out so the dims after ``dim``
+    form one contiguous channel run with 16-byte aligned rows; copies if not."""
+    es = t.element_size()
+    trail_ok = True
+    expect = 1
+    for n, s in zip(reversed(t.shape[dim + 1:]), reversed(t.stride()[dim + 1:])):
+        if n != 1 and s != expect:
+            trail_ok = False
+        expect *= n
+    rows_ok = all(n == 1 or (s > 0 and (s * es) % 16 == 0) for n, s in zip(t.shape[:dim + 1], t.stride()[:dim + 1]))
+    if not (trail_ok and rows_ok and t.data_ptr() % 16 == 0):
+        t = t.contiguous()
+    return t
+
+
+def _lead(t: torch.Tensor, dim: int) -> Tuple[int, int, int, int]:
+    """(nb, nh, stride_b, stride_h) of the (at most two) dims before ``dim``."""
+    if dim == 0:
+        return 1, 1, 0, 0
+    if dim == 1:
+        return t.shape[0], 1, t.stride(0), 0
+    return t.shape[0], t.shape[1], t.stride(0), t.stride(1)
+
+
+def affine_recurrence_scan(decay: torch.Tensor, update: torch.Tensor, *, dim: int = 1,
+                           backend: str = "auto") -> torch.Tensor:
+    """``state_t = decay_t * state_{t-1} + update_t`` along ``dim`` (need_kernels.py:229-264).
+
+    The scan is carried in fp32 and returned in ``update.dtype``; ``backend`` is
+    ignored.
+    """
+    del backend
+    if update.numel() == 0:
+        return update
+    dim = dim if dim >= 0 else update.ndim + dim
+    if dim < 0 or dim >= update.ndim:
+        raise IndexError(f"scan dim {dim} out of range for rank {update.ndim}")
+    if decay.shape != update.shape:
+        decay = torch.broadcast_to(decay, update.shape)
+    _require_cuda(decay, update)
+    _no_grad(decay, update)
+    return _affine(decay, update, dim)
+
+
+def _affine(decay: torch.Tensor, update: torch.Tensor, dim: int, *, q: Optional[torch.Tensor] = None,
+            seg_start=None, h0=None, h_final=None) -> torch.Tensor:
+    """The kernel call behind affine_recurrence_scan / recurrent_retention_scan.
+
+    ``update`` is scanned along ``dim``; the dims after it are the channels, the
+    (at most two) dims before it are independent sequences.  A decay constant
+    over the channels (a broadcast [..., T, 1]) is read as one value per row.
+    """
+    dev = update.device
+    out_dtype = update.dtype
+    ts = out_dtype if out_dtype in _DT else torch.float32
+    u = update if update.dtype == ts else update.to(ts)
+    td = decay.dtype if decay.dtype in (ts, torch.float32) else torch.float32
+    d = decay if decay.dtype == td else decay.to(td)
+    if q is not None and q.dtype != ts:
+        q = q.to(ts)
+    C = math.prod(u.shape[dim + 1:]) if dim + 1 < u.ndim else 1
+    rowdec = all(s == 0 or n == 1 for n, s in zip(d.shape[dim + 1:], d.stride()[dim + 1:]))
+    split = ts == torch.float32 or (not rowdec and td == torch.float32)
+    if dim > 2 or dim == u.ndim - 1 or not _channel_ok(C, split):
+        if seg_start is not None or h0 is not None or h_final is not None:
+            raise ValueError("resets / initial / final state need a [B, T, C] or [B, H, T, C] layout "
+                             "with C a multiple of 8")
+        return _affine_generic(d, u, dim, out_dtype, q=q)
+    u = _bhtc(u, dim)
+    nb, nh, sb, sh = _lead(u, dim)
+    T = u.shape[dim]
+    out = torch.empty(u.shape, dtype=ts, device=dev)
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_RETENTION if q is not None else abi.FORM_AFFINE, ts, nb, nh, T, C, out)
+    ob, oh, osb, osh = _lead(out, dim)
+    a.out_stride_b, a.out_stride_h, a.out_stride_t = osb, osh, out.stride(dim)
+    a.decay_dtype = _DT[td]
+    a.decay_per_row = 1 if rowdec else 0
+    if rowdec:
+        _, _, dsb, dsh = _lead(d, dim)
+        a.in_[0] = abi.NeedView(d.data_ptr(), dsb, dsh, d.stride(dim))
+    else:
+        d = _bhtc(d, dim)
+        _, _, dsb, dsh = _lead(d, dim)
+        a.in_[0] = abi.NeedView(d.data_ptr(), dsb, dsh, d.stride(dim))
+    a.in_[1] = abi.NeedView(u.data_ptr(), sb, sh, u.stride(dim))
+    keep = [d, u, out]
+    if q is not None:
+        q = _bhtc(q, dim)
+        _, _, qsb, qsh = _lead(q, dim)
+        a.in_[2] = abi.NeedView(q.data_ptr(), qsb, qsh, q.stride(dim))
+        keep.append(q)
+    keep += _fill_state(a, dev, nb, nh, C, seg_start, h0, h_final)
+    _launch("need_recurrent_retention_scan" if q is not None else "need_affine_recurrence_scan", a, dev,
+            rowdec=a.decay_per_row)
+    return out if ts == out_dtype else out.to(out_dtype)
+
+
+def _affine_generic(decay, update, dim, out_dtype, q=None):
+    """Any other layout: scanned dim first, every other dim flattened into
+    channels (padded to a multiple of 8), scanned as one [1, T, M] sequence."""
+    T = update.shape[dim]
+    u2 = update.movedim(dim, 0).reshape(T, -1)
+    d2 = torch.broadcast_to(decay, update.shape).movedim(dim, 0).reshape(T, -1)
+    M = u2.shape[1]
+    pad = (-M) % 8
+    u3 = F.pad(u2, (0, pad)).contiguous().unsqueeze(0)
+    d3 = F.pad(d2, (0, pad)).contiguous().unsqueeze(0)
+    q3 = None
+    if q is not None:
+        q3 = F.pad(q.movedim(dim, 0).reshape(T, -1), (0, pad)).contiguous().unsqueeze(0)
+    out = _affine(d3, u3, 1, q=q3)[0, :, :M]
+    moved = list(update.movedim(dim, 0).shape)
+    return out.reshape(moved).movedim(0, dim).to(out_dtype)
+
+
+# --------------------------------------------------------------------------
+# recurrent_retention_scan  (need_kernels.py:342-345)
+# --------------------------------------------------------------------------
+
+def recurrent_retention_scan(q: torch.Tensor, kv: torch.Tensor, decay: torch.Tensor,
+                             backend: str = "auto") -> torch.Tensor:
+    """``q * affine_recurrence_scan(decay, kv, dim=2)``, fused: the scan state is
+    rounded to ``kv.dtype`` and multiplied by ``q`` in the kernel epilogue."""
+    del backend
+    if kv.numel() == 0:
+        return q * kv
+    if decay.shape != kv.shape:
+        decay = torch.broadcast_to(decay, kv.shape)
+    _require_cuda(q, kv, decay)
+    _no_grad(q, kv, decay)
+    if q.shape != kv.shape or q.dtype != kv.dtype or kv.dtype not in _DT:
+        return q * _affine(decay, kv, 2)
+    return _affine(decay, kv, 2, q=q)
+
+
+# --------------------------------------------------------------------------
+# gated scan (the sigmoid-gated form of need_core.py:1630-1638)
+# --------------------------------------------------------------------------
+
+def _bt_c_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() != 3:
+        raise ValueError(f"{name} must be [B, T, C]; got {tuple(t.shape)}")
+    if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any((s * t.element_size()) % 16 for s in t.stride()[:2]):
+        t = t.contiguous()
+    return t
+
+
+def gated_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Tensor, *,
+               seg_start: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+               return_final_state: bool = False):
+    """``a = sigmoid(decay_logit)``, ``b = (1 - a) * (sigmoid(gate_logit) * x)``,
+    ``h_t = a_t h_{t-1} + b_t`` over [B, T, C]; ``h`` in ``x.dtype``.
+
+    ``seg_start`` [B, T] (bool/uint8): the state is zeroed before every marked
+    token (a packed-segment boundary).  ``h0`` [B, C]: initial state.  With
+    ``return_final_state`` also returns the fp32 state after the last token.
+    Gate arithmetic is rounded to ``x.dtype`` where the reference's torch path
+    rounds (need_kernels.py:330-336).
+    """
+    _require_cuda(x, decay_logit, gate_logit)
+    _no_grad(x, decay_logit, gate_logit)
+    if not (x.shape == decay_logit.shape == gate_logit.shape):
+        raise ValueError("x, decay_logit and gate_logit must have the same [B, T, C] shape")
+    ts = x.dtype if x.dtype in _DT else torch.float32
+    xs, zs, gs = (_bt_c_tensor(t if t.dtype == ts else t.to(ts), n)
+                  for t, n in ((x, "x"), (decay_logit, "decay_logit"), (gate_logit, "gate_logit")))
+    B, T, C = xs.shape
+    if B * T * C == 0:
+        out = torch.empty_like(xs)
+        return (out, torch.zeros(B, C, device=x.device)) if return_final_state else out
+    if not _channel_ok(C, ts == torch.float32):
+        pad = (-C) % 8
+        res = gated_scan(F.pad(xs, (0, pad)), F.pad(zs, (0, pad)), F.pad(gs, (0, pad)), seg_start=seg_start,
+                         h0=None if h0 is None else F.pad(h0.float(), (0, pad)), return_final_state=True)
+        out, hf = res[0][..., :C], res[1][:, :C]
+        return (out, hf) if return_final_state else out
+    out = torch.empty((B, T, C), dtype=ts, device=x.device)
+    hf = torch.empty((B, C), dtype=torch.float32, device=x.device) if return_final_state else None
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_GATED, ts, B, 1, T, C, out)
+    for k, t in enumerate((zs, gs, xs)):
+        a.in_[k] = abi.NeedView(t.data_ptr(), t.stride(0), 0, t.stride(1))
+    keep = _fill_state(a, x.device, B, 1, C, seg_start, h0, hf)
+    _launch("need_gated_scan", a, x.device)
+    del keep
+    out = out if out.dtype == x.dtype else out.to(x.dtype)
+    return (out, hf) if return_final_state else out
+
+
+# --------------------------------------------------------------------------
+# ssd_scan  (need_kernels.py:302-339)
+# --------------------------------------------------------------------------
+
+def ssd_scan(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tensor, dt_raw: torch.Tensor,
+             out_gate: torch.Tensor, d_skip: torch.Tensor, dt_min: float, dt_max: float,
+             backend: str = "auto", *, seg_start: Optional[torch.Tensor] = None,
+             h0: Optional[torch.Tensor] = None, h_final: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused SSD-style diagonal scan (need_kernels.py:302-339), all [B, T, D]:
+
+    ``a = exp(-(dt_min + (dt_max - dt_min) * sigmoid(dt_raw)))``,
+    ``h = scan(a, (1 - a) * sigmoid(b_gate) * u)``,
+    ``y = (sigmoid(c_gate) * h + d_skip * u) * sigmoid(out_gate)``.
+    ``backend`` is ignored.  Keyword-only extensions: packed-segment resets,
+    initial state, fp32 final state written into ``h_final`` [B, D].
+    """
+    del backend
+    b, t, d = u.shape
+    tensors = (u, b_gate, c_gate, dt_raw, out_gate)
+    _require_cuda(*tensors, d_skip)
+    _no_grad(*tensors, d_skip)
+    ts = u.dtype if u.dtype in _DT else torch.float32
+    if u.numel() == 0:
+        return torch.empty_like(u)
+    xs = [_bt_c_tensor(x if x.dtype == ts else x.to(ts), n)
+          for x, n in zip(tensors, ("u", "b_gate", "c_gate", "dt_raw", "out_gate"))]
+    if not _channel_ok(d, ts == torch.float32):
+        pad = (-d) % 8
+        hf = None if h_final is None else torch.empty(b, d + pad, device=u.device)
+        y = ssd_scan(*[F.pad(x, (0, pad)) for x in xs], F.pad(d_skip.float(), (0, pad)), dt_min, dt_max,
+                     seg_start=seg_start, h0=None if h0 is None else F.pad(h0.float(), (0, pad)), h_final=hf)
+        if h_final is not None:
+            h_final.copy_(hf[:, :d])
+        return y[..., :d].to(u.dtype)
+    out = torch.empty((b, t, d), dtype=ts, device=u.device)
+    ds = d_skip.to(device=u.device, dtype=torch.float32).reshape(-1).contiguous()
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_SSD, ts, b, 1, t, d, out)
+    xu, xbg, xcg, xdt, xog = xs
+    for k, x in enumerate((xdt, xbg, xu, xcg, xog)):
+        a.in_[k] = abi.NeedView(x.data_ptr(), x.stride(0), 0, x.stride(1))
+    a.d_skip = ds.data_ptr()
+    a.dt_min, a.dt_max = float(dt_min), float(dt_max)
+    keep = _fill_state(a, u.device, b, 1, d, seg_start, h0, h_final)
+    _launch("need_ssd_scan", a, u.device)
+    del keep
+    return out if out.dtype == u.dtype else out.to(u.dtype)
+
+
+# --------------------------------------------------------------------------
+# ragged decode / speculative verify
+# --------------------------------------------------------------------------
+
+def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str = "gated",
+                  slot: Optional[torch.Tensor] = None, d_skip: Optional[torch.Tensor] = None,
+                  dt_min: float = 0.001, dt_max: float = 0.2,
+                  out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+    """k_i one-token recurrent steps for each sequence, from its pooled state.
+
+    ``states`` [S, C] pool (not modified); ``cu_k`` int32 [N+1] offsets of each
+    sequence's drafted tokens in the packed inputs; ``inputs`` is
+    (decay_logit, gate_logit, x) for ``form="gated"`` or
+    (dt_raw, b_gate, u, c_gate, out_gate) for ``form="ssd"``, each [sum k, C].
+    Arithmetic follows the reference's streaming step (need_core.py:6420-6428),
+    every op in the state dtype.  Returns (y, states_k), both [sum k, C].
+    """
+    _require_cuda(states, cu_k, *inputs)
+    nseq = cu_k.numel() - 1
+    total = inputs[0].shape[0]
+    C = states.shape[1]
+    y, sk = out if out is not None else (torch.empty(total, C, dtype=states.dtype, device=states.device),
+                                         torch.empty(total, C, dtype=states.dtype, device=states.device))
+    a = abi.NeedVerifyArgs()
+    a.form = abi.FORM_GATED if form == "gated" else abi.FORM_SSD
+    a.dtype = _DT[states.dtype]
+    a.nseq, a.C = nseq, C
+    a.states = states.data_ptr()
+    a.slot = slot.data_ptr() if slot is not None else None
+    a.cu_k = cu_k.data_ptr()
+    a.total_k = total
+    for k, t in enumerate(inputs):
+        a.in_[k] = t.data_ptr()
+    ds = None
+    if d_skip is not None:
+        ds = d_skip.to(device=states.device, dtype=torch.float32).contiguous()
+        a.d_skip = ds.data_ptr()
+    a.dt_min, a.dt_max = float(dt_min), float(dt_max)
+    a.y, a.states_k = y.data_ptr(), sk.data_ptr()
+    abi.check("need_ragged_verify", _lib().need_ragged_verify(ctypes.byref(a), _stream(states.device)))
+    return y, sk
+
+
+def commit_states(states: torch.Tensor, states_k: torch.Tensor, cu_k: torch.Tensor,
+                  accept_len: torch.Tensor, slot: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """In place: ``states[slot[i]] = states_k[cu_k[i] + L_i - 1]`` where ``L_i > 0``."""
+    _require_cuda(states, states_k, cu_k, accept_len)
+    nseq = cu_k.numel() - 1
+    abi.check("need_commit_states", _lib().need_commit_states(
+        _DT[states.dtype], nseq, states.shape[1], states.data_ptr(),
+        slot.data_ptr() if slot is not None else None, states_k.data_ptr(), cu_k.data_ptr(),
+        accept_len.data_ptr(), _stream(states.device)))
+    return states
+
+
+# --------------------------------------------------------------------------
+# outside the scan path: plain PyTorch, same contracts as need_kernels.py:266-371
+# --------------------------------------------------------------------------
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, backend: str = "auto") -> torch.Tensor:
+    inv = torch.rsqrt(x.float().pow(2).mean(dim=-1, keepdim=True) + eps).to(x.dtype)
+    return x * inv * weight
+
+
+def swiglu(a: torch.Tensor, b: torch.Tensor, backend: str = "auto") -> torch.Tensor:
+    return F.silu(a) * b
+
+
+def residual_scale_add(x: torch.Tensor, y: torch.Tensor, scale: float, backend: str = "auto") -> torch.Tensor:
+    return x + float(scale) * y
+
+
+def sparse_moe_combine(expert_outputs: torch.Tensor, topk_idx: torch.Tensor, topk_weight: torch.Tensor,
+                       backend: str = "auto") -> torch.Tensor:
+    n_exp = expert_outputs.shape[0]
+    onehot = F.one_hot(topk_idx.long(), n_exp).to(topk_weight.dtype)          # [B, T, k, E]
+    w = (onehot * topk_weight.unsqueeze(-1)).sum(dim=-2)                       # [B, T, E]
+    return torch.einsum("ebtd,bte->btd", expert_outputs, w.to(expert_outputs.dtype))
+
+
+def sample_from_logits(logits: torch.Tensor, temperature: float = 1.0, backend: str = "auto") -> torch.Tensor:
+    z = logits.float() / max(float(temperature), 1e-8)
+    z = torch.where(torch.isfinite(z), z, torch.full_like(z, -1.0e9))
+    p = torch.softmax(z, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0, posinf=0.0, neginf=0.0).clamp_min(0.0)
+    s = p.sum(dim=-1, keepdim=True)
+    p = torch.where(s > 0, p / s.clamp_min(1e-12), torch.full_like(p, 1.0 / max(1, p.shape[-1])))
+    return torch.multinomial(p, 1)

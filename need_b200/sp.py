@@ -1,0 +1,97 @@
+"""Sequence-parallel (T-sharded) gated scan over ranks of one node.
+
+Rank r holds tokens [r*T/P, (r+1)*T/P) of every sequence.  The exchange is one
+step:
+
+1. each rank scans its slice from a zero state with ``need_gated_scan``,
+   also recording the slice map (prod a, h at the slice end) per channel and
+   the product of ``a`` at every tile start;
+2. the slice maps (``[B, C, 2]`` fp32 per rank, 2*B*C*4 bytes) are
+   all-gathered with NCCL into local memory;
+3. ``need_sp_fixup`` composes the maps of ranks < r into the carry entering
+   slice r and adds ``prod(a) * carry`` to the leading tiles of the slice
+   until that correction is below 2^-24 of the carry on every channel.
+
+Batch/channel sharding needs no exchange at all; only the T split does.  The
+oracle for this path is the whole-T scan on one device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import abi
+from . import need_kernels as nk
+
+
+@dataclass
+class LocalScan:
+    """One rank's local scan and what the fix-up needs from it."""
+    args: abi.NeedScanArgs
+    out: torch.Tensor
+    summary: torch.Tensor    # [B, C, 2] fp32 (prod a, h_end) of this slice
+    tile_prod: torch.Tensor  # [B, nchunks, C] fp32
+    h_final: torch.Tensor    # [B, C] fp32
+    keep: List[torch.Tensor] = field(default_factory=list)
+
+
+def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Tensor, *,
+               seg_start: Optional[torch.Tensor] = None) -> LocalScan:
+    """Scan this rank's [B, T_r, C] slice from a zero state (step 1)."""
+    nk._require_cuda(x, decay_logit, gate_logit)
+    ts = x.dtype
+    if ts not in nk._DT:
+        raise TypeError(f"unsupported dtype {ts}")
+    xs, zs, gs = (nk._bt_c_tensor(t.to(ts), n) for t, n in ((x, "x"), (decay_logit, "z"), (gate_logit, "g")))
+    B, T, C = xs.shape
+    if C % 8 != 0:
+        raise ValueError("the sequence-parallel scan needs C to be a multiple of 8")
+    lib = nk._lib()
+    L = lib.need_scan_chunk_len(abi.FORM_GATED, nk._DT[ts], nk._DT[ts], 0)
+    nchunks = (T + L - 1) // L
+    dev = x.device
+    out = torch.empty((B, T, C), dtype=ts, device=dev)
+    summary = torch.empty((B, C, 2), dtype=torch.float32, device=dev)
+    tile_prod = torch.empty((B, nchunks, C), dtype=torch.float32, device=dev)
+    hf = torch.empty((B, C), dtype=torch.float32, device=dev)
+    a = abi.NeedScanArgs()
+    nk._fill_common(a, abi.FORM_GATED, ts, B, 1, T, C, out)
+    for k, t in enumerate((zs, gs, xs)):
+        a.in_[k] = abi.NeedView(t.data_ptr(), t.stride(0), 0, t.stride(1))
+    keep = [xs, zs, gs] + nk._fill_state(a, dev, B, 1, C, seg_start, None, hf)
+    a.summary = summary.data_ptr()
+    a.tile_prod = tile_prod.data_ptr()
+    nk._launch("need_gated_scan", a, dev)
+    return LocalScan(a, out, summary, tile_prod, hf, keep)
+
+
+def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> None:
+    """Step 3: add the carry from ranks < rank to ``loc.out``, ``loc.h_final`` and
+    ``loc.summary``.  ``all_summary`` is [nranks, B, C, 2] fp32 on this device."""
+    all_summary = all_summary.contiguous()
+    dev = loc.out.device
+    abi.check("need_sp_fixup", nk._lib().need_sp_fixup(
+        ctypes.byref(loc.args), all_summary.data_ptr(), int(nranks), int(rank), nk._stream(dev)))
+
+
+def sp_gated_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Tensor, *,
+                  group: Optional[dist.ProcessGroup] = None, seg_start: Optional[torch.Tensor] = None,
+                  return_final_state: bool = False):
+    """The gated scan of a sequence whose T is split over the ranks of ``group``.
+
+    Every rank passes its own contiguous [B, T/P, C] slice (ranks in T order);
+    each gets back the exact outputs of its slice, and with
+    ``return_final_state`` the fp32 state after its slice's last token.
+    """
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    loc = local_scan(x, decay_logit, gate_logit, seg_start=seg_start)
+    if world > 1:
+        gathered = torch.empty((world,) + tuple(loc.summary.shape), dtype=torch.float32, device=x.device)
+        dist.all_gather_into_tensor(gathered, loc.summary, group=group)
+        fixup(loc, gathered, world, rank)
+    return (loc.out, loc.h_final) if return_final_state else loc.out

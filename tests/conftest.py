@@ -1,0 +1,31 @@
+"""pytest configuration: the ``gpu`` marker and shared helpers.
+
+``-m "not gpu"`` runs on any host (oracle vs. golden fixtures, the C ABI's
+symbols and argument checks, the sequence-parallel exchange on gloo ranks).
+``-m gpu`` needs a B200: the CUDA kernels against the oracle.
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+if GOLDEN not in sys.path:
+    sys.path.insert(0, GOLDEN)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from need_b200 import build
+    build.build()
+    return torch.device("cuda", 0)

@@ -1,0 +1,166 @@
+#!/usr/bin/env python3
+"""Generate golden fixtures by running the reference's own functions on CPU.
+
+Run in a container that has the reference checked out (default
+/root/reference; override with NEED_REFERENCE):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+
+Each fixture ``<case>.npz`` holds the reference outputs for the seeded inputs
+of ``cases.py`` (inputs are regenerated from their seed; ``input_sha256``
+guards against drift).  Reference entry points used (file:line in NEED):
+
+  need_kernels.affine_recurrence_scan       need_kernels.py:229-264 (CPU -> :177-226)
+  need_core.affine_recurrence_scan_torch    need_core.py:1419-1461
+  need_kernels.recurrent_retention_scan     need_kernels.py:342-345
+  need_kernels.ssd_scan (torch path)        need_kernels.py:302-339
+  StructuredDualRetention.stream_step       need_core.py:1653-1686
+  the one-token formula of                  need_core.py:6420-6428
+
+The gated form (decay = sigmoid(z), update = (1 - decay)*(sigmoid(g)*x)) is the
+gate arithmetic of need_kernels.py:330-336 with a sigmoid decay; it is built
+here from torch ops in the model dtype exactly as the reference's callers do.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import cases  # noqa: E402
+
+REF = os.environ.get("NEED_REFERENCE", "/root/reference")
+sys.dont_write_bytecode = True
+sys.path.insert(0, REF)
+import need_core  # noqa: E402
+import need_kernels  # noqa: E402
+
+TD = {"fp32": torch.float32, "bf16": torch.bfloat16}
+
+
+def T(x: np.ndarray, dtype: str) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x)).to(TD[dtype])
+
+
+def npf(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().numpy().astype(np.float32)
+
+
+def ref_gated(inp, dtype):
+    x, z, g = T(inp["x"], dtype), T(inp["z"], dtype), T(inp["g"], dtype)
+    decay = torch.sigmoid(z)
+    gate = torch.sigmoid(g)
+    update = (1.0 - decay) * (gate * x)
+    if inp["seg"] is not None:
+        decay = decay.masked_fill(torch.from_numpy(inp["seg"].astype(bool))[..., None], 0.0)
+    h = need_kernels.affine_recurrence_scan(decay, update, dim=1)
+    h2 = need_core.affine_recurrence_scan_torch(decay, update, dim=1, chunk_size=64)
+    assert torch.equal(h, h2), "need_kernels and need_core CPU scans disagree"
+    # fp32 carry after the last token (the reference's chunk `state`)
+    hf = need_kernels.affine_recurrence_scan(decay.float(), update.float(), dim=1)[:, -1]
+    return {"h": npf(h), "h_final": npf(hf), "decay": npf(decay), "update": npf(update)}
+
+
+def ref_retention(inp, dtype):
+    q, kv = T(inp["q"], dtype), T(inp["kv"], dtype)
+    decay = torch.from_numpy(inp["decay"])  # fp32, broadcast over head_dim
+    s = need_kernels.affine_recurrence_scan(decay, kv, dim=2)
+    y = need_kernels.recurrent_retention_scan(q, kv, decay)
+    return {"state_seq": npf(s), "y": npf(y)}
+
+
+def ref_ssd(inp, dtype):
+    args = [T(inp[k], dtype) for k in ("u", "bg", "cg", "dt", "og")]
+    dskip = torch.from_numpy(inp["dskip"])
+    y = need_kernels.ssd_scan(*args, dskip, inp["dt_min"], inp["dt_max"], backend="auto")
+    return {"y": npf(y)}
+
+
+def ref_stream(inp, form, dtype):
+    """k_i one-token steps per sequence, the arithmetic of need_core.py:6420-6428."""
+    dt = TD[dtype]
+    states = T(inp["states"], dtype)
+    cu = inp["cu_k"]
+    tot = int(cu[-1])
+    c = states.shape[1]
+    ys = torch.zeros(tot, c, dtype=dt)
+    sk = torch.zeros(tot, c, dtype=dt)
+    dmin, dmax = 0.001, 0.2
+    for i in range(states.shape[0]):
+        rec = states[i:i + 1].clone()
+        for j in range(int(cu[i]), int(cu[i + 1])):
+            if form == "gated":
+                decay = torch.sigmoid(T(inp["p0"][j:j + 1], dtype))
+                bg = torch.sigmoid(T(inp["p1"][j:j + 1], dtype))
+                u_act = T(inp["p2"][j:j + 1], dtype)
+                rec = decay * rec + (1.0 - decay) * (bg * u_act)
+                y = rec
+            else:
+                dt_raw, b_gate, u_act, c_gate, out_gate = (T(inp[f"p{k}"][j:j + 1], dtype) for k in range(5))
+                d = torch.sigmoid(dt_raw.float())
+                d = dmin + (dmax - dmin) * d
+                decay = torch.exp(-d).to(dt)
+                bg = torch.sigmoid(b_gate).to(dt)
+                cg = torch.sigmoid(c_gate).to(dt)
+                og = torch.sigmoid(out_gate).to(dt)
+                rec = decay * rec + (1.0 - decay) * (bg * u_act)
+                D = torch.from_numpy(inp["dskip"])
+                y = (cg * rec + D.to(dt).view(1, -1) * u_act) * og
+            ys[j] = y[0]
+            sk[j] = rec[0]
+    return {"y": npf(ys), "states_k": npf(sk)}
+
+
+def check_module_stream_step():
+    """The formula above against the real StructuredDualRetention.stream_step."""
+    torch.manual_seed(0)
+    cfg = need_core.NeedConfig(d_model=16, n_heads=2, n_layers=1, block_size=32)
+    mod = need_core.StructuredDualRetention(cfg).to(torch.bfloat16).eval()
+    state = {}
+    x = torch.randn(3, 4, 16).to(torch.bfloat16)
+    rec = torch.zeros(3, 16, dtype=torch.bfloat16)
+    hist = torch.zeros(3, 16, 3, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for t in range(4):
+            xt = x[:, t:t + 1]
+            mod.stream_step(xt, state)
+            u, bg, cg, dt, og = mod.in_proj(xt).chunk(5, dim=-1)
+            hist = torch.cat([hist[:, :, 1:], u[:, 0].unsqueeze(-1)], dim=-1)
+            w = mod.dwconv.weight.squeeze(1).to(torch.bfloat16)
+            uc = (hist * w.unsqueeze(0)).sum(dim=-1) + mod.dwconv.bias.to(torch.bfloat16).view(1, -1)
+            ua = torch.nn.functional.silu(uc)
+            d = torch.sigmoid(dt[:, 0].float())
+            d = cfg.ssd_dt_min + (cfg.ssd_dt_max - cfg.ssd_dt_min) * d
+            decay = torch.exp(-d).to(torch.bfloat16)
+            b = torch.sigmoid(bg[:, 0]).to(torch.bfloat16)
+            rec = decay * rec + (1.0 - decay) * (b * ua)
+            assert torch.equal(rec, state["scan_state"]), f"stream_step formula mismatch at t={t}"
+
+
+def main():
+    check_module_stream_step()
+    for name, spec in cases.CASES.items():
+        inp = cases.make_inputs(name)
+        kind, dtype = spec["kind"], spec["dtype"]
+        if kind == "gated":
+            out = ref_gated(inp, dtype)
+        elif kind == "retention":
+            out = ref_retention(inp, dtype)
+        elif kind == "ssd":
+            out = ref_ssd(inp, dtype)
+        else:
+            out = ref_stream(inp, spec["form"], dtype)
+        if inp.get("x") is not None and inp["x"].size > 250_000:
+            # large case: keep outputs only (decay/update are pinned by the small cases)
+            out = {k: v for k, v in out.items() if k in ("h", "h_final")}
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, input_sha256=np.array(cases.input_digest(inp)), **out)
+        print(f"{name}: {', '.join(f'{k}{list(v.shape)}' for k, v in out.items())}")
+
+
+if __name__ == "__main__":
+    main()

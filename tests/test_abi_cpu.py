@@ -1,0 +1,96 @@
+"""The C ABI without a GPU: the library builds and loads, exports every symbol
+include/need_scan.h declares, the ctypes mirror has the header's layout, and
+argument errors come back as status codes (these paths make no CUDA call)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from need_b200 import abi, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "need_scan.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return abi.load()
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"NEED_API\s+[\w\s\*]+?\b(need_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ("need_gated_scan", "need_affine_recurrence_scan", "need_ssd_scan", "need_recurrent_retention_scan",
+              "need_ragged_verify", "need_commit_states", "need_sp_fixup", "need_scan_workspace_size"):
+        assert s in syms
+    assert set(syms) == set(abi.SIGNATURES), "ctypes binding and header disagree"
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", build.LIB], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (need_\w+)", out))
+    missing = set(declared_symbols()) - exported
+    assert not missing, f"not exported: {missing}"
+    assert lib.need_abi_version() == abi.ABI_VERSION
+
+
+def test_struct_layout_matches_header(tmp_path):
+    """Compile a C program against the header and compare sizes/offsets with ctypes."""
+    fields = {
+        "need_scan_args": (abi.NeedScanArgs, [f[0] for f in abi.NeedScanArgs._fields_]),
+        "need_verify_args": (abi.NeedVerifyArgs, [f[0] for f in abi.NeedVerifyArgs._fields_]),
+        "need_view": (abi.NeedView, [f[0] for f in abi.NeedView._fields_]),
+    }
+    lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
+    for cname, (_, names) in fields.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for n in names:
+            cn = "in" if n == "in_" else n
+            lines.append(f'printf("{cname}.{n} %zu\\n", offsetof({cname}, {cn}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                        check=True).stdout.splitlines())
+    for cname, (cls, names) in fields.items():
+        assert int(got[cname]) == ctypes.sizeof(cls), cname
+        for n in names:
+            assert int(got[f"{cname}.{n}"]) == getattr(cls, n).offset, f"{cname}.{n}"
+
+
+def test_sizes_and_chunk_lengths(lib):
+    L = lib.need_scan_chunk_len(abi.FORM_GATED, abi.BF16, abi.BF16, 0)
+    assert L == 64
+    ws = lib.need_scan_workspace_size(abi.FORM_GATED, abi.BF16, abi.BF16, 0, 16, 1, 4096, 1024)
+    ntiles = 16 * 4 * 64
+    assert ws >= ntiles * 4096
+    assert lib.need_scan_workspace_size(abi.FORM_GATED, 7, 7, 0, 1, 1, 1, 8) == 0  # unknown dtype
+    assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
+
+
+def test_argument_errors_return_status(lib):
+    a = abi.NeedScanArgs()
+    assert lib.need_gated_scan(None, None) == abi.ERR_INVALID
+    assert b"null" in lib.need_last_error()
+    a.form = abi.FORM_SSD
+    assert lib.need_gated_scan(ctypes.byref(a), None) == abi.ERR_INVALID  # wrong form for the entry point
+    a.form = abi.FORM_GATED
+    a.dtype = abi.BF16
+    a.nb, a.nh, a.T, a.C = 1, 1, 0, 8
+    assert lib.need_gated_scan(ctypes.byref(a), None) == abi.ERR_INVALID  # T == 0
+    a.T, a.C = 16, 12
+    assert lib.need_gated_scan(ctypes.byref(a), None) == abi.ERR_UNSUPPORTED  # C not a multiple of 8
+    assert b"multiple of 8" in lib.need_last_error()
+    v = abi.NeedVerifyArgs()
+    v.form = abi.FORM_AFFINE
+    assert lib.need_ragged_verify(ctypes.byref(v), None) == abi.ERR_INVALID
+    assert lib.need_commit_states(abi.BF16, 4, 12, None, None, None, None, None, None) == abi.ERR_UNSUPPORTED
+    assert lib.need_sp_fixup(None, None, 2, 0, None) == abi.ERR_INVALID

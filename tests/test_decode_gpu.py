@@ -1,0 +1,102 @@
+"""Ragged decode / speculative verify and commit against the oracle's
+sequential one-token steps (need_core.py:6420-6428 arithmetic)."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from need_b200 import need_kernels as nk
+from need_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16"])
+def test_verify_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    spec = cases.CASES[name]
+    bf = lambda k: torch.from_numpy(inp[k]).to(cuda).to(torch.bfloat16)  # noqa: E731
+    states = bf("states")
+    cu = torch.from_numpy(inp["cu_k"].astype(np.int32)).to(cuda)
+    if spec["form"] == "gated":
+        ins = (bf("p0"), bf("p1"), bf("p2"))
+        y, sk = nk.ragged_verify(states, cu, ins, form="gated")
+    else:
+        ins = tuple(bf(f"p{i}") for i in range(5))
+        y, sk = nk.ragged_verify(states, cu, ins, form="ssd", d_skip=torch.from_numpy(inp["dskip"]).to(cuda))
+    assert np.mean(host(y) == g["y"]) >= 0.99 and np.mean(host(sk) == g["states_k"]) >= 0.99
+    assert np.abs(host(y) - g["y"]).max() <= 2e-2 * np.abs(g["y"]).max()
+    assert torch.equal(states, bf("states")), "the state pool must not change"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_verify_and_commit_ragged_batch(cuda, dtype):
+    """256 sequences x 1024 channels, ragged k in {0..4}, gathered pool slots."""
+    w = workloads.verify(cuda, N=256, C=1024, k=4, seed=3, dtype=dtype)
+    rs = np.random.RandomState(4)
+    ks = rs.randint(0, 5, 256).astype(np.int32)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(ks)]).astype(np.int32)).to(cuda)
+    tot = int(ks.sum())
+    pool = torch.randn(300, 1024, device=cuda).to(dtype) * 0.5
+    slot = torch.from_numpy(rs.permutation(300)[:256].astype(np.int32)).to(cuda)
+    z, g, x = w.z[:tot].contiguous(), w.g[:tot].contiguous(), w.x[:tot].contiguous()
+    y, sk = nk.ragged_verify(pool, cu, (z, g, x), slot=slot)
+    mode = "bf16" if dtype == torch.bfloat16 else "fp32"
+    want_y, want_sk = oracle.ragged_verify("gated", host(pool)[slot.cpu().numpy()], cu.cpu().numpy(),
+                                           host(z), host(g), host(x), dtype=mode)
+    if mode == "bf16":
+        assert np.mean(host(sk) == want_sk) >= 0.99
+        assert np.abs(host(sk) - want_sk).max() <= 2e-2 * np.abs(want_sk).max()
+    else:
+        assert np.abs(host(sk) - want_sk).max() <= 1e-5 * np.abs(want_sk).max()
+    np.testing.assert_array_equal(host(y), host(sk))  # the gated step's output is its state
+
+    accept = torch.from_numpy(np.minimum(rs.randint(0, 5, 256), ks).astype(np.int32)).to(cuda)
+    before = pool.clone()
+    nk.commit_states(pool, sk, cu, accept, slot=slot)
+    want_pool = host(before)
+    acc = accept.cpu().numpy()
+    cun = cu.cpu().numpy()
+    sl = slot.cpu().numpy()
+    for i in range(256):
+        if acc[i] > 0:
+            want_pool[sl[i]] = host(sk)[cun[i] + acc[i] - 1]
+    np.testing.assert_array_equal(host(pool), want_pool)
+
+
+def test_commit_clamps_accept_length(cuda):
+    states = torch.zeros(2, 8, device=cuda, dtype=torch.bfloat16)
+    sk = torch.arange(3 * 8, device=cuda, dtype=torch.float32).reshape(3, 8).to(torch.bfloat16)
+    cu = torch.tensor([0, 2, 3], dtype=torch.int32, device=cuda)
+    acc = torch.tensor([9, -1], dtype=torch.int32, device=cuda)  # clamped to [0, k_i]
+    nk.commit_states(states, sk, cu, acc)
+    assert torch.equal(states[0], sk[1]) and torch.equal(states[1], torch.zeros_like(states[1]))
+
+
+def test_verify_graph_capture(cuda):
+    """The decode step is launch-bound: verify + commit replay as one CUDA graph."""
+    w = workloads.verify(cuda, N=64, C=1024, k=4, seed=5)
+    pool = w.states.clone()
+    y = torch.empty_like(w.x)
+    sk = torch.empty_like(w.x)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        nk.ragged_verify(pool, w.cu_k, (w.z, w.g, w.x), out=(y, sk))
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        nk.ragged_verify(pool, w.cu_k, (w.z, w.g, w.x), out=(y, sk))
+        nk.commit_states(pool, sk, w.cu_k, w.accept)
+    ref_pool = pool.clone()
+    y2, sk2 = nk.ragged_verify(ref_pool, w.cu_k, (w.z, w.g, w.x))
+    nk.commit_states(ref_pool, sk2, w.cu_k, w.accept)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(pool, ref_pool) and torch.equal(y, y2)

@@ -1,0 +1,201 @@
+"""CUDA scan kernels (through the C ABI) against the oracle and the reference's
+golden outputs.
+
+Tolerances (max|kernel - ref| / max|ref| per tensor): fp32 1e-5, bf16 2e-2.
+bf16 results are also required to agree element for element with the oracle
+on at least 99% of elements: the kernels round at the reference's rounding
+points, so only rare ties (approximate exp/rcp inside a rounded gate, fp32
+scan order) may differ.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from need_b200 import need_kernels as nk
+from need_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+TD = {"fp32": torch.float32, "bf16": torch.bfloat16}
+
+
+def dev_t(x, dtype, dev):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev).to(TD[dtype])
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def check(got, want, dtype, what=""):
+    r = rel(got, want)
+    if dtype == "bf16":
+        assert r <= BF16_TOL, f"{what}: rel err {r}"
+        frac = float(np.mean(got == want))
+        assert frac >= 0.99, f"{what}: only {frac:.5f} of bf16 elements equal"
+    else:
+        assert r <= FP32_TOL, f"{what}: rel err {r}"
+
+
+def no_device_error():
+    assert nk.workspace_error() == 0, "a device-side wait gave up"
+
+
+# ------------------------------------------------------------------ golden fixtures
+
+@pytest.mark.parametrize("name", ["cfg1_gated_fp32", "gated_bf16_ragged", "gated_fp32_noreset"])
+def test_gated_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    dt = cases.CASES[name]["dtype"]
+    seg = None if inp["seg"] is None else torch.from_numpy(inp["seg"]).to(cuda)
+    h, hf = nk.gated_scan(dev_t(inp["x"], dt, cuda), dev_t(inp["z"], dt, cuda), dev_t(inp["g"], dt, cuda),
+                          seg_start=seg, return_final_state=True)
+    check(host(h), g["h"], dt, name)
+    assert rel(host(hf), g["h_final"]) <= FP32_TOL
+    no_device_error()
+
+
+@pytest.mark.parametrize("name", ["retention_fp32", "retention_bf16"])
+def test_retention_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    dt = cases.CASES[name]["dtype"]
+    q, kv = dev_t(inp["q"], dt, cuda), dev_t(inp["kv"], dt, cuda)
+    decay = torch.from_numpy(inp["decay"]).to(cuda)  # fp32 [B,H,T,1]
+    with torch.no_grad():
+        s = nk.affine_recurrence_scan(decay, kv, dim=2)
+        y = nk.recurrent_retention_scan(q, kv, decay)
+    assert s.dtype == kv.dtype and s.shape == kv.shape
+    check(host(s), g["state_seq"], dt, "state_seq")
+    check(host(y), g["y"], dt, "y")
+
+
+@pytest.mark.parametrize("name", ["ssd_fp32", "ssd_bf16"])
+def test_ssd_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    dt = cases.CASES[name]["dtype"]
+    args = [dev_t(inp[k], dt, cuda) for k in ("u", "bg", "cg", "dt", "og")]
+    y = nk.ssd_scan(*args, torch.from_numpy(inp["dskip"]).to(cuda), inp["dt_min"], inp["dt_max"])
+    assert y.dtype == args[0].dtype
+    check(host(y), g["y"], dt, name)
+
+
+# ------------------------------------------------------------------ oracle, full size
+
+def test_prefill_full_size_vs_oracle(cuda):
+    """The bf16 prefill workload (B=16, T=4096, C=1024, resets) against the oracle."""
+    w = workloads.prefill(cuda)
+    h, hf = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg, return_final_state=True)
+    want, wf = oracle.gated_scan(host(w.x), host(w.z), host(w.g), w.seg.cpu().numpy(), dtype="bf16")
+    check(host(h), want, "bf16", "prefill")
+    assert rel(host(hf), wf) <= 1e-5
+    no_device_error()
+
+
+def test_cpu_case_vs_oracle(cuda):
+    w = workloads.cpu_case(cuda)
+    h = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg)
+    want, _ = oracle.gated_scan(host(w.x), host(w.z), host(w.g), w.seg.cpu().numpy(), dtype="fp32")
+    check(host(h), want, "fp32", "cpu_case")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+@pytest.mark.parametrize("B,T,C", [(1, 1, 8), (2, 63, 16), (1, 64, 256), (3, 65, 264), (2, 129, 520),
+                                   (1, 1000, 24), (4, 300, 1024)])
+def test_gated_shapes(cuda, dtype, B, T, C):
+    if dtype == "fp32" and C % 4:
+        pytest.skip("fp32 needs C % 4 == 0")
+    w = workloads.gated_inputs(B, T, C, z_mean=3.0, dtype=TD[dtype], device=cuda, seed=B * 7 + T + C,
+                               resets="uniform", seg_lo=1, seg_hi=40)
+    seg = w.seg.clone()
+    seg[:, -1] = 1  # reset on the last token
+    h0 = torch.randn(B, C, device=cuda)
+    h, hf = nk.gated_scan(w.x, w.z, w.g, seg_start=seg, h0=h0, return_final_state=True)
+    want, wf = oracle.gated_scan(host(w.x), host(w.z), host(w.g), seg.cpu().numpy(), host(h0), dtype=dtype)
+    check(host(h), want, dtype, f"{B}x{T}x{C}")
+    assert rel(host(hf), wf) <= FP32_TOL
+    no_device_error()
+
+
+def test_h0_without_resets_carries_state(cuda):
+    w = workloads.gated_inputs(2, 200, 64, z_mean=5.0, dtype=torch.float32, device=cuda, seed=3, resets=None)
+    h0 = 10 * torch.randn(2, 64, device=cuda)
+    h = nk.gated_scan(w.x, w.z, w.g, h0=h0)
+    want, _ = oracle.gated_scan(host(w.x), host(w.z), host(w.g), None, host(h0))
+    check(host(h), want, "fp32")
+    h_no = nk.gated_scan(w.x, w.z, w.g)
+    assert not torch.allclose(h, h_no)
+
+
+# ------------------------------------------------------------------ affine drop-in
+
+@pytest.mark.parametrize("ddt,udt", [("fp32", "fp32"), ("bf16", "bf16"), ("fp32", "bf16")])
+@pytest.mark.parametrize("shape,dim", [((2, 300, 64), 1), ((3, 130, 264), -2), ((2, 3, 77, 64), 2)])
+def test_affine_full_decay(cuda, ddt, udt, shape, dim):
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    a = torch.sigmoid(torch.randn(shape, generator=gen, device=cuda) + 3).to(TD[ddt])
+    b = torch.randn(shape, generator=gen, device=cuda).to(TD[udt])
+    with torch.no_grad():
+        h = nk.affine_recurrence_scan(a, b, dim=dim)
+    assert h.dtype == b.dtype and h.shape == b.shape
+    d = dim % len(shape)
+    an = np.moveaxis(host(a), d, -2).reshape(-1, shape[d], np.prod(shape[d + 1:], dtype=int))
+    bn = np.moveaxis(host(b), d, -2).reshape(an.shape)
+    want, _ = oracle.affine_scan(an, bn, out_dtype=udt)
+    got = np.moveaxis(host(h), d, -2).reshape(an.shape)
+    check(got, want, udt, f"{shape} dim={dim}")
+
+
+def test_affine_generic_layouts(cuda):
+    """Layouts outside [B,(H),T,C]: last-dim scans, odd channel counts, rank 5."""
+    gen = torch.Generator(device=cuda).manual_seed(9)
+    for shape, dim in [((5, 37), -1), ((3, 50, 7), 1), ((2, 2, 2, 40, 3), 3)]:
+        a = torch.rand(shape, generator=gen, device=cuda)
+        b = torch.randn(shape, generator=gen, device=cuda)
+        h = nk.affine_recurrence_scan(a, b, dim=dim)
+        d = dim % len(shape)
+        an = np.moveaxis(host(a), d, 0).reshape(1, shape[d], -1)
+        bn = np.moveaxis(host(b), d, 0).reshape(an.shape)
+        want, _ = oracle.affine_scan(an, bn)
+        got = np.moveaxis(host(h), d, 0).reshape(an.shape)
+        check(got, want, "fp32", f"{shape}")
+
+
+def test_affine_contract(cuda):
+    b = torch.randn(2, 0, 8, device=cuda)
+    assert nk.affine_recurrence_scan(torch.rand(2, 0, 8, device=cuda), b) is b
+    with pytest.raises(IndexError):
+        nk.affine_recurrence_scan(torch.rand(2, 3, 8, device=cuda), torch.randn(2, 3, 8, device=cuda), dim=3)
+    with pytest.raises(RuntimeError):
+        nk.affine_recurrence_scan(torch.rand(2, 3, 8), torch.randn(2, 3, 8))
+    x = torch.randn(2, 3, 8, device=cuda, requires_grad=True)
+    with pytest.raises(NotImplementedError):
+        nk.affine_recurrence_scan(torch.rand(2, 3, 8, device=cuda), x)
+    a, u = torch.rand(2, 64, 8, device=cuda), torch.randn(2, 64, 8, device=cuda)
+    a0, u0 = a.clone(), u.clone()
+    nk.affine_recurrence_scan(a, u)
+    assert torch.equal(a, a0) and torch.equal(u, u0)
+
+
+def test_workspace_reuse_is_deterministic(cuda):
+    """The look-back records are epoch-tagged: repeated calls reuse the
+    workspace without clearing and give identical results."""
+    w = workloads.gated_inputs(4, 1000, 512, z_mean=4.0, dtype=torch.bfloat16, device=cuda, seed=1,
+                               resets="lognormal", seg_lo=16, seg_hi=400)
+    first = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg)
+    for _ in range(5):
+        # a different-sized call in between re-tiles the same workspace
+        nk.gated_scan(w.x[:1, :77], w.z[:1, :77], w.g[:1, :77])
+        again = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg)
+        assert torch.equal(first, again)
+    no_device_error()

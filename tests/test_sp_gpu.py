@@ -1,0 +1,68 @@
+"""Sequence-parallel scan: P ranks emulated on one GPU (the slices are
+scanned, their summaries stacked as the all-gather would, then fixed up),
+against the whole-T scan.  The real multi-process run on several GPUs is
+exercised when the box has them."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from need_b200 import need_kernels as nk
+from need_b200 import sp, workloads
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def emulate(w, P):
+    T = w.x.shape[1]
+    bounds = [T * r // P for r in range(P + 1)]
+    locs = []
+    for r in range(P):
+        sl = slice(bounds[r], bounds[r + 1])
+        seg = None if w.seg is None else w.seg[:, sl].contiguous()
+        locs.append(sp.local_scan(w.x[:, sl], w.z[:, sl], w.g[:, sl], seg_start=seg))
+    gathered = torch.stack([loc.summary for loc in locs])
+    for r, loc in enumerate(locs):
+        sp.fixup(loc, gathered, P, r)
+    return torch.cat([loc.out for loc in locs], dim=1), locs[-1].h_final
+
+
+@pytest.mark.parametrize("P", [2, 3, 8])
+@pytest.mark.parametrize("z_mean,resets", [(5.0, None), (2.0, "uniform"), (8.0, None)])
+def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets):
+    w = workloads.gated_inputs(2, 3000, 512, z_mean=z_mean, dtype=torch.bfloat16, device=cuda, seed=P,
+                               resets=resets, seg_lo=100, seg_hi=900)
+    whole, whole_f = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg, return_final_state=True)
+    got, got_f = emulate(w, P)
+    g, wh = host(got), host(whole)
+    assert np.abs(g - wh).max() <= 2e-2 * np.abs(wh).max()
+    assert np.mean(g == wh) >= 0.99
+    assert np.abs(host(got_f) - host(whole_f)).max() <= 1e-5 * np.abs(host(whole_f)).max() + 1e-6
+
+
+def test_emulated_ranks_fp32_exact_carry(cuda):
+    """fp32: the fix-up reproduces the whole-T scan to fp32 accuracy (decays
+    near 1 keep the carry alive across the whole slice)."""
+    w = workloads.gated_inputs(1, 2048, 256, z_mean=8.0, dtype=torch.float32, device=cuda, seed=1, resets=None)
+    got, _ = emulate(w, 4)
+    want, _ = oracle.gated_scan(host(w.x), host(w.z), host(w.g))
+    assert np.abs(host(got) - want).max() <= 1e-5 * np.abs(want).max()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_process_nccl_run():
+    env = dict(os.environ, PYTHONPATH=ROOT)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(ROOT, "tests", "sp_worker.py")]
+    r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "SP-OK" in r.stdout
