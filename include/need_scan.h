@@ -111,6 +111,7 @@ typedef struct {
                               per-slice summary the sequence-parallel combine exchanges */
     float* tile_prod;      /* optional [nb*nh, ceil(T/L), C] fp32: product of a over
                               [0, start of chunk), L = need_scan_chunk_len(form, dtype, ...) */
+    float* tile_carry;     /* optional [nb*nh, ceil(T/L), C] fp32: the state entering each chunk */
     void* workspace;       /* >= need_scan_workspace_size(...) bytes, zero-filled before its
                               first use; reusable by later calls on the same stream without
                               clearing; never used by two launches at once */
@@ -184,15 +185,16 @@ NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* st
 /* Sequence parallelism (T sharded over ranks)                               */
 /* ------------------------------------------------------------------------ */
 
-/* After a rank scanned its T-slice from a zero state (with `summary` and
- * `tile_prod` requested) and gathered every rank's summary into
- * `all_summary` [nranks, nb*nh, C, 2], this adds the carry from ranks < rank:
- *     carry = compose(summary[0..rank-1]);  h[t] += (prod_{s<=t} a[s]) * carry
- * over the leading tiles of the slice, stopping at the first tile where the
- * product has fallen to 2^-24 or below for every channel of the tile (the
- * correction is then below fp32 resolution of the carry).  It also corrects
- * h_final / summary when given.  `args` is the same description the local scan
- * got (form AFFINE or GATED); `args->out` is read and rewritten. */
+/* After a rank scanned its T-slice from a zero state (with `summary`,
+ * `tile_prod` and `tile_carry` requested) and gathered every rank's summary
+ * into `all_summary` [nranks, nb*nh, C, 2], this applies the carry from ranks
+ * < rank: carry = compose(summary[0..rank-1]); every tile whose entering
+ * correction prod(a) * carry exceeds 2^-24 * |carry| on some channel is
+ * re-scanned from the corrected fp32 state tile_carry + tile_prod * carry, with
+ * the scan's own arithmetic, and its outputs rewritten; later tiles are left
+ * as they are (their correction is below fp32 resolution of the carry).  It
+ * also corrects h_final / summary when given.  `args` is the description the
+ * local scan got (form AFFINE or GATED). */
 NEED_API int need_sp_fixup(const need_scan_args* args, const float* all_summary, int32_t nranks,
                   int32_t rank, need_stream_t stream);
 

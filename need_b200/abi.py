@@ -36,7 +36,7 @@ class NeedScanArgs(Structure):
         ("d_skip", c_void_p), ("dt_min", c_double), ("dt_max", c_double),
         ("h0", c_void_p), ("h_final", c_void_p),
         ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
-        ("summary", c_void_p), ("tile_prod", c_void_p),
+        ("summary", c_void_p), ("tile_prod", c_void_p), ("tile_carry", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 

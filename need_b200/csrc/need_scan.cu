@@ -19,8 +19,16 @@ namespace {
 // One instantiation of scan_kernel per (form, stream dtype, decay dtype,
 // row-broadcast decay).  Tile lengths keep each CTA's staged tile near 96 KB
 // so two CTAs fit an SM's 228 KB of shared memory.
+// tile shape of the 16-bit gated scan (tokens per tile, warps per CTA)
+#ifndef NEED_GATED16_L
+#define NEED_GATED16_L 64
+#endif
+#ifndef NEED_GATED16_NW
+#define NEED_GATED16_NW 8
+#endif
 template <typename T>
-using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? 64 : 32, sizeof(T) == 2 ? 8 : 4>;
+using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? NEED_GATED16_L : 32,
+                         sizeof(T) == 2 ? NEED_GATED16_NW : 4>;
 template <typename T>
 using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? 32 : 16, sizeof(T) == 2 ? 8 : 4>;
 
@@ -41,7 +49,7 @@ template <typename TS, typename TD, bool RD>
 using RetCfg = ScanCfg<FORM_RETENTION, TS, TD, RD, RetL<TS, TD, RD>::L, RetL<TS, TD, RD>::NW>;
 
 struct Plan {
-    int L = 0, nin = 0, in0 = 0;
+    int L = 0, R = 0, nin = 0, in0 = 0;
     bool dstream = false, split = false;
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
 };
@@ -61,6 +69,7 @@ template <class K>
 Plan plan_of() {
     Plan p;
     p.L = K::L;
+    p.R = K::R;
     p.nin = K::NIN;
     p.in0 = K::IN0;
     p.dstream = K::HAS_DSTREAM;
@@ -120,8 +129,7 @@ Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) 
 
 size_t ws_bytes(int64_t ntiles) {
     const size_t hdr = WS_HDR_WORDS * 4;
-    const size_t flags = ((size_t(ntiles) * 4 + 255) / 256) * 256;
-    return hdr + flags + size_t(ntiles) * 256 * sizeof(float2) * 2;
+    return hdr + size_t(ntiles) * 256 * sizeof(ulonglong2) * 2;  // tagged AGG and INCL records
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -140,7 +148,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t nh, int64_t T, int64_t C,
-                int L, int which) {
+                int box_rows, int which) {
     if (v.ptr == nullptr) return fail(NEED_ERR_INVALID, "in[%d] is null", which);
     if (!aligned16(v.ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[%d] is not 16-byte aligned", which);
     const int64_t es = dtype_bytes(dt);
@@ -162,7 +170,7 @@ int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t
         prev = static_cast<int64_t>(gs[i]) * sizes[i];
     }
     const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(T), cuuint64_t(nh), cuuint64_t(nb)};
-    const cuuint32_t box[4] = {cuuint32_t(CB), cuuint32_t(L), 1, 1};
+    const cuuint32_t box[4] = {cuuint32_t(CB), cuuint32_t(box_rows), 1, 1};  // one warp's rows
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUtensorMapDataType ty = dt == NEED_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                    : dt == NEED_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -204,7 +212,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     memset(P, 0, sizeof(*P));
     for (int k = 0; k < pl->nin; ++k) {
         const int dt = (pl->dstream && k == 0) ? ddt : a->dtype;
-        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->L, pl->in0 + k))
+        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->R, pl->in0 + k))
             return rc;
     }
     if (rowdec_form && rd) {
@@ -252,11 +260,10 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     P->sgt = a->seg_stride_t;
     P->summary = a->summary;
     P->tile_prod = a->tile_prod;
+    P->tile_carry = a->tile_carry;
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P->hdr = reinterpret_cast<uint32_t*>(ws);
-    P->flags = reinterpret_cast<uint32_t*>(ws + WS_HDR_WORDS * 4);
-    const size_t flag_bytes = ((size_t(g.ntiles) * 4 + 255) / 256) * 256;
-    P->agg = reinterpret_cast<float2*>(ws + WS_HDR_WORDS * 4 + flag_bytes);
+    P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * 256;
     return NEED_OK;
 }

@@ -86,7 +86,26 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
     return v;
 }
 
-// L2-only vector loads for data another CTA published (after an acquire).
-__device__ __forceinline__ float4 ld_cg_f4(const float4* p) { return __ldcg(p); }
+// Self-validating records: each 64-bit word holds a float (low half) and the
+// launch's tag (high half).  Naturally aligned 64-bit elements are accessed
+// single-copy atomically, so a reader that sees the current tag in a word
+// also sees the float written with it -- no fence or flag is needed.
+__device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float untag(unsigned long long w) {
+    return __uint_as_float(static_cast<uint32_t>(w));
+}
+__device__ __forceinline__ bool tag_ok(unsigned long long w, uint32_t tag) {
+    return static_cast<uint32_t>(w >> 32) == tag;
+}
+__device__ __forceinline__ void st_relaxed_v2u64(ulonglong2* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_relaxed_v2u64(const ulonglong2* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
 
 }  // namespace need

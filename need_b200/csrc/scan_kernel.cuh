@@ -3,9 +3,8 @@
 //
 // Work decomposition.  A call scans nseq = nb*nh independent sequences of C
 // channels over T steps.  A tile is (sequence, 256-channel block, L-token
-// chunk).  Tiles are processed in ticket order (an atomic counter), chunk-major,
-// so every tile's predecessor along T was handed out earlier and is resident or
-// finished: waiting on it cannot deadlock.
+// chunk), one CTA per tile, numbered chunk-major by blockIdx.x, so every
+// tile's predecessors along T have lower block indices.
 //
 // Per tile (one CTA, NW warps):
 //   1. TMA (cp.async.bulk.tensor, no multicast) stages the tile's input rows
@@ -18,15 +17,18 @@
 //      affine map (A, B): h_out = A*h_in + B.
 //   3. The warps' maps are composed through shared memory: each warp gets the
 //      map of the rows before it, the last warp the tile's whole map.
-//   4. Decoupled look-back (last warp): publish the tile map (AGG), walk back
-//      over predecessors composing their maps until one that has published its
-//      inclusive state (INCL), publish our own inclusive state.  Every wait is
-//      bounded; on give-up an error bit is set and the tile continues.
+//   4. Look-back (last two warps): publish the tile map (AGG); compose the
+//      maps of the kLookbackDepth tiles before this one and the inclusive
+//      state (INCL) of the tile before those -- a fixed order, so results are
+//      bit-reproducible; publish the inclusive state.  Records carry the
+//      launch's tag in every 64-bit word, so neither side needs a fence or a
+//      flag.  Every wait is bounded; on give-up an error bit is set and the
+//      tile continues.
 //   5. Phase 2: every thread restarts its rows from the exact carry, writes
 //      the outputs straight to global memory (16-byte stores, a warp writes
 //      512 contiguous bytes per row).
 // HBM traffic is the algorithmic minimum (inputs read once, outputs written
-// once) plus a 4 KB workspace record per tile.
+// once) plus an 8 KB workspace record per tile (normally L2-resident).
 #pragma once
 
 #include <cuda.h>
@@ -44,11 +46,17 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 constexpr int CB = 256;  // channels per tile (32 lanes x 8 channels)
 
 // workspace header words (uint32)
-enum { WS_TICKET = 0, WS_DONE = 1, WS_EPOCH = 2, WS_ERROR = 3, WS_HDR_WORDS = 32 };
+// words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
+enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_HDR_WORDS = 32 };
 enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
-enum { ST_AGG = 1u, ST_INCL = 2u };
 
-constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~100 ns sleeps: < 1 s worst case
+constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst case
+#ifndef NEED_LOOKBACK_DEPTH
+#define NEED_LOOKBACK_DEPTH 3
+#endif
+// Tile maps composed before an inclusive state (at most 31: one lane polls each).
+constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
+static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
 
 struct ScanParams {
@@ -67,10 +75,10 @@ struct ScanParams {
     int64_t sgb, sgt;
     float* summary;
     float* tile_prod;
+    float* tile_carry;
     uint32_t* hdr;
-    uint32_t* flags;
-    float2* agg;   // [ntiles][8][32]
-    float2* incl;  // [ntiles][8][32]
+    ulonglong2* agg;   // [ntiles][8][32] tagged (A, B): the tile's map
+    ulonglong2* incl;  // [ntiles][8][32] tagged (prod, h): state after the tile
 };
 
 // ------------------------------------------------------------------ types
@@ -234,6 +242,8 @@ struct ScanCfg {
     static constexpr bool ROWDEC = ROWDEC_;
     static constexpr int L = L_, NW = NW_, NT = NW * 32, R = L / NW;
     static_assert(L % NW == 0, "rows must split evenly over warps");
+    static_assert(NW >= 2, "the look-back uses the last two warps");
+    static_assert(R <= 32, "a warp loads the reset flags of its rows one per lane");
     static constexpr bool HAS_DSTREAM = (FORM == FORM_AFFINE || FORM == FORM_RETENTION) && !ROWDEC;
     static constexpr bool SPLIT = (Ops<TS>::BYTES == 4) || (HAS_DSTREAM && Ops<TD>::BYTES == 4);
     // streamed inputs, in[] order of the C ABI
@@ -254,16 +264,20 @@ struct ScanCfg {
     // GATED frees its input-gate slot after phase 1: the warp maps live there.
     static constexpr int AGG_SLOT = FORM == FORM_GATED ? 1 : -1;
     static constexpr int AGG_BYTES = NW * 8 * 32 * 8;
+    // warp maps: in the freed slot each warp's map sits in that warp's own rows
+    // (no barrier needed before writing it); otherwise packed
+    static constexpr int AGG_W = AGG_SLOT >= 0 ? (L * CB * Ops<TS>::BYTES / NW) / 8 : 8 * 32;
+    static_assert(AGG_SLOT < 0 || AGG_W >= 8 * 32, "a warp's rows must hold its map");
     static constexpr int OFF_AGG = slots_bytes();
     static constexpr int OFF_CARRY = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
-    static constexpr int OFF_ROWDEC = OFF_CARRY + 8 * 32 * 4;
+    static constexpr int OFF_ROWDEC = OFF_CARRY + 8 * 32 * 8;  // (carry, prod) per channel
     static constexpr int OFF_RESET = OFF_ROWDEC + (ROWDEC ? L * 4 : 0);
     static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
-    static constexpr int SMEM = OFF_MISC + 32 + 128;  // + alignment slack
+    static constexpr int SMEM = OFF_MISC + NW * 8 + 16 + 128;  // per-warp mbarriers, misc, alignment slack
     // resident CTAs per SM: bounded by shared memory (228 KB per SM, 1 KB
-    // reserved per CTA) and by 128 registers per thread at 256 threads
+    // reserved per CTA) and by ~112 registers per thread
     static constexpr int MINB_SMEM = (228 * 1024) / (SMEM + 1024);
-    static constexpr int MINB_CAP = NT >= 256 ? 2 : 4;
+    static constexpr int MINB_CAP = 65536 / (NT * 112) < 1 ? 1 : (65536 / (NT * 112) > 8 ? 8 : 65536 / (NT * 112));
     static constexpr int MINB = MINB_SMEM < 1 ? 1 : (MINB_SMEM < MINB_CAP ? MINB_SMEM : MINB_CAP);
 };
 
@@ -294,20 +308,31 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     float* s_carry = reinterpret_cast<float*>(base + K::OFF_CARRY);
     float* s_rowdec = reinterpret_cast<float*>(base + K::OFF_ROWDEC);
     uint8_t* s_reset = base + K::OFF_RESET;
-    uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(base + K::OFF_MISC + 8);
+    uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per warp
+    uint32_t* s_misc = reinterpret_cast<uint32_t*>(base + K::OFF_MISC + NW * 8);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+    // Tile ids follow blockIdx.x (chunk-major).  CTAs are dispatched in
+    // increasing blockIdx order, so every tile a CTA waits on belongs to a CTA
+    // that is already resident or finished -- the property single-pass
+    // decoupled look-back scans rely on; the waits are bounded regardless.
+    const int tile = static_cast<int>(blockIdx.x);
     if (tid == 0) {
-        s_misc[0] = atomicAdd(&p.hdr[WS_TICKET], 1u);
-        s_misc[1] = ld_volatile_u32(&p.hdr[WS_EPOCH]);
-        mbar_init(s_bar, 1);
+        for (int w = 0; w < NW; ++w) mbar_init(&s_bar[w], 1);
         fence_barrier_init();
     }
+    if (tid == 32) {
+        // Every CTA of a launch gets the same epoch: the counter in the low half
+        // counts CTAs in, and the last one to start moves the epoch on for the
+        // next launch.  Used only by the look-back, long after this returns.
+        unsigned long long* lw = reinterpret_cast<unsigned long long*>(p.hdr + WS_LAUNCH);
+        const unsigned long long old = atomicAdd(lw, 1ull);
+        if (static_cast<uint32_t>(old) == static_cast<uint32_t>(p.ntiles) - 1u)
+            atomicAdd(lw, (1ull << 32) - static_cast<unsigned long long>(p.ntiles));
+        s_misc[1] = static_cast<uint32_t>(old >> 32);
+    }
     __syncthreads();
-    const int tile = static_cast<int>(s_misc[0]);
-    const uint32_t epoch = s_misc[1] & 0x3fffffffu;
     const int chunk = tile / p.nchains;
     const int chain = tile - chunk * p.nchains;
     const int seq = chain / p.ncb;
@@ -315,18 +340,25 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     const int bi = seq / p.nh, hi = seq - bi * p.nh;
     const int t0 = chunk * L, c0 = cblk * CB;
 
-    if (tid == 0) {
+    // Each warp loads its own rows (one TMA box of R rows per input) and starts
+    // on them as soon as they land, so compute overlaps the rest of the tile's
+    // load instead of waiting for all of it.
+    const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
+    const int r0 = warp * R;
+    const int rend = max(0, min(R, nvalid - r0));  // this warp's rows inside T
+    if (lane == 0 && rend > 0) {
         uint32_t bytes = 0;
 #pragma unroll
-        for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k);
-        mbar_arrive_expect_tx(s_bar, bytes);
+        for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
+        mbar_arrive_expect_tx(&s_bar[warp], bytes);
 #pragma unroll
         for (int k = 0; k < K::NIN; ++k)
-            tma_load_4d(slot_ptr<K>(base, k), &p.tm[k], c0, t0, hi, bi, s_bar);
+            tma_load_4d(slot_ptr<K>(base, k) + r0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + r0, hi, bi,
+                        &s_bar[warp]);
     }
-    // reset flags and per-row decay while the tile is in flight
-    for (int r = tid; r < L; r += K::NT) {
-        const int t = t0 + r;
+    // this warp's reset flags and per-row decay while its rows are in flight
+    if (lane < R) {
+        const int r = r0 + lane, t = t0 + r;
         uint8_t rs = 0;
         if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
         s_reset[r] = rs;
@@ -336,14 +368,13 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             s_rowdec[r] = d;
         }
     }
-    if (!mbar_wait_bounded(s_bar, 0, kTmaPolls)) {
+    __syncwarp();
+    if (rend > 0 && !mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls)) {
         atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
-        mbar_wait_bounded(s_bar, 0, kTmaPolls);
+        mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls);
     }
-    __syncthreads();
 
     // per-thread constants
-    const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
     float dsk[8];
     if constexpr (K::FORM == FORM_SSD) {
 #pragma unroll
@@ -368,8 +399,12 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float2 f = Ops<TD>::unpack(dp[i]);
-                    a[2 * i] = reset ? 0.0f : f.x;
-                    a[2 * i + 1] = reset ? 0.0f : f.y;
+                    a[2 * i] = f.x;
+                    a[2 * i + 1] = f.y;
+                }
+                if (reset) {  // uniform across the warp: one branch per row
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) a[e] = 0.0f;
                 }
             }
             PS up[4];
@@ -403,10 +438,15 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     dec = OS::pack(expo<TS>(-dx), expo<TS>(-dy));
                 }
                 const PS gs = OS::pack(sigm<TS>(f1.x), sigm<TS>(f1.y));
-                const PS gx = OS::mul(gs, p2[i]);
-                const PS om = OS::sub(OS::one(), dec);
-                bp[i] = OS::mul(om, gx);
-                ap[i] = reset ? OS::zero() : dec;
+                bp[i] = OS::mul(OS::sub(OS::one(), dec), OS::mul(gs, p2[i]));
+                ap[i] = dec;
+            }
+            if (reset) {  // uniform across the warp: one branch per row
+#pragma unroll
+                for (int i = 0; i < 4; ++i) ap[i] = OS::zero();
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
                 const float2 af = OS::unpack(ap[i]);
                 const float2 bf = OS::unpack(bp[i]);
                 a[2 * i] = af.x;
@@ -418,13 +458,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 Row8<TS, SPLIT>::sts(s0, lane, ap);  // a over the decay input
                 if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, lane, bp);  // b over x
                 else Row8<TS, SPLIT>::sts(s1, lane, bp);  // b over b_gate
-            }
-        }
-        if (r >= nvalid) {  // rows past T: identity map
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                a[e] = 1.0f;
-                b[e] = 0.0f;
             }
         }
     };
@@ -455,18 +488,17 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         B[e] = 0.0f;
     }
 #pragma unroll 2
-    for (int j = 0; j < R; ++j) {
+    for (int j = 0; j < rend; ++j) {  // rows past T act as the identity
         float a[8], b[8];
-        gates(warp * R + j, true, a, b);
+        gates(r0 + j, true, a, b);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             B[e] = fmaf(a[e], B[e], b[e]);
             A[e] = a[e] * A[e];
         }
     }
-    if constexpr (K::AGG_SLOT >= 0) __syncthreads();  // the slot's last readers are done
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s_agg[(warp * 8 + e) * 32 + lane] = make_float2(A[e], B[e]);
+    for (int e = 0; e < 8; ++e) s_agg[warp * K::AGG_W + e * 32 + lane] = make_float2(A[e], B[e]);
     __syncthreads();
 
     // ---------------------------------------------------------- compose warps
@@ -479,180 +511,159 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     for (int w = 0; w < warp; ++w) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const float2 m = s_agg[(w * 8 + e) * 32 + lane];
+            const float2 m = s_agg[w * K::AGG_W + e * 32 + lane];
             EB[e] = fmaf(m.x, EB[e], m.y);
             EA[e] = m.x * EA[e];
         }
     }
 
     // ---------------------------------------------------------- look-back
-    if (warp == NW - 1) {
-        float TA[8], TB[8];  // the whole tile's map
+    // Two warps share it.  The last warp publishes this tile's map (AGG) for
+    // its successors; the warp before it reads the predecessors' records and
+    // forms the carry.  The composition order is fixed (the maps of the up to
+    // kLookbackDepth tiles before this one, then the inclusive state of the
+    // tile before those), so results are bit-reproducible.  Records are
+    // tagged with the launch epoch word by word, so publishing needs no fence
+    // and a poll returns the data itself.
+    const uint32_t tag = (s_misc[1] & 0x7fffffffu) | 0x80000000u;
+    float2* s_cc = reinterpret_cast<float2*>(s_carry);  // (carry, prod) per channel
+    if (warp == NW - 1 && chunk > 0) {
+        ulonglong2* my = p.agg + (int64_t)tile * 256;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            TA[e] = A[e] * EA[e];
-            TB[e] = fmaf(A[e], EB[e], B[e]);
-        }
-        const int seqC = seq;  // row of h0 / h_final / summary
+        for (int e = 0; e < 8; ++e)
+            st_relaxed_v2u64(&my[e * 32 + lane], tagged(A[e] * EA[e], tag), tagged(fmaf(A[e], EB[e], B[e]), tag));
+    }
+    if (warp == NW - 2) {
         float carry[8], carryP[8];
         if (chunk == 0) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const int c = c0 + chan<SPLIT>(e, lane);
-                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seqC * p.C + c] : 0.0f;
+                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
                 carryP[e] = 1.0f;
             }
         } else {
-            // publish this tile's map
-            float2* my = p.agg + (int64_t)tile * 256;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) __stcg(&my[e * 32 + lane], make_float2(TA[e], TB[e]));
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release_gpu(&p.flags[tile], (epoch << 2) | ST_AGG);
-            // walk back along the chain
-            float accA[8], accB[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                accA[e] = 1.0f;
-                accB[e] = 0.0f;
-            }
-            int k = tile - p.nchains;
-            for (;;) {
-                uint32_t f = 0;
-                bool ok = false;
-                for (uint32_t it = 0; it < kLookbackPolls; ++it) {
-                    uint32_t v = 0;
-                    if (lane == 0) v = ld_acquire_gpu(&p.flags[k]);
-                    v = __shfl_sync(0xffffffffu, v, 0);
-                    if ((v >> 2) == epoch && (v & 3u) != 0) {
-                        f = v;
-                        ok = true;
-                        break;
-                    }
-                    if (it >= 4) __nanosleep(100);
-                }
-                if (!ok) {
-                    if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        carry[e] = accB[e];
-                        carryP[e] = accA[e];
-                    }
-                    break;
-                }
-                (void)ld_acquire_gpu(&p.flags[k]);  // every lane acquires before reading the record
-                if ((f & 3u) == ST_INCL) {
-                    const float2* src = p.incl + (int64_t)k * 256;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 m = __ldcg(&src[e * 32 + lane]);  // (prod, h)
-                        carry[e] = fmaf(accA[e], m.y, accB[e]);
-                        carryP[e] = accA[e] * m.x;
-                    }
-                    break;
-                }
-                const float2* src = p.agg + (int64_t)k * 256;
+            const int nagg = min(chunk - 1, kLookbackDepth);
+            bool ok = false;
+            for (uint32_t it = 0; it < kLookbackPolls; ++it) {
+                bool valid = true;
+                float accA[8], accB[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const float2 m = __ldcg(&src[e * 32 + lane]);  // (A, B)
-                    accB[e] = fmaf(accA[e], m.y, accB[e]);
-                    accA[e] = accA[e] * m.x;
+                    accA[e] = 1.0f;
+                    accB[e] = 0.0f;
                 }
-                k -= p.nchains;
+                for (int j = 0; j < nagg; ++j) {
+                    const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * 256;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * 32 + lane]);  // (A, B)
+                        valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                        accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                        accA[e] = accA[e] * untag(m.x);
+                    }
+                }
+                const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * 256;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const ulonglong2 m = ld_relaxed_v2u64(&src[e * 32 + lane]);  // (prod, h)
+                    valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                    carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                    carryP[e] = accA[e] * untag(m.x);
+                }
+                if (__all_sync(0xffffffffu, valid)) {
+                    ok = true;
+                    break;
+                }
+                if (it >= 2) __nanosleep(64);
+                if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
             }
+            if (!ok && lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
         }
-        // publish the inclusive state
-        float inclP[8], inclH[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s_cc[e * 32 + lane] = make_float2(carry[e], carryP[e]);
+    }
+    __syncthreads();
+    if (warp == NW - 1) {
+        // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
+        // the final state, the slice summary and the per-tile products
+        float inclP[8], inclH[8], carryP[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            inclP[e] = TA[e] * carryP[e];
-            inclH[e] = fmaf(TA[e], carry[e], TB[e]);
+            const float2 cc = s_cc[e * 32 + lane];
+            const float TA = A[e] * EA[e], TB = fmaf(A[e], EB[e], B[e]);
+            carryP[e] = cc.y;
+            inclP[e] = TA * cc.y;
+            inclH[e] = fmaf(TA, cc.x, TB);
         }
         if (chunk + 1 < p.nchunks) {
-            float2* mi = p.incl + (int64_t)tile * 256;
+            ulonglong2* mi = p.incl + (int64_t)tile * 256;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) __stcg(&mi[e * 32 + lane], make_float2(inclP[e], inclH[e]));
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) st_release_gpu(&p.flags[tile], (epoch << 2) | ST_INCL);
+            for (int e = 0; e < 8; ++e) st_relaxed_v2u64(&mi[e * 32 + lane], tagged(inclP[e], tag), tagged(inclH[e], tag));
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            s_carry[e * 32 + lane] = carry[e];
             const int c = c0 + chan<SPLIT>(e, lane);
             if (c < p.C) {
                 if (p.tile_prod != nullptr)
-                    p.tile_prod[((int64_t)seqC * p.nchunks + chunk) * p.C + c] = carryP[e];
+                    p.tile_prod[((int64_t)seq * p.nchunks + chunk) * p.C + c] = carryP[e];
+                if (p.tile_carry != nullptr)
+                    p.tile_carry[((int64_t)seq * p.nchunks + chunk) * p.C + c] = s_cc[e * 32 + lane].x;
                 if (chunk + 1 == p.nchunks) {
-                    if (p.h_final != nullptr) p.h_final[(int64_t)seqC * p.C + c] = inclH[e];
+                    if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
                     if (p.summary != nullptr)
-                        reinterpret_cast<float2*>(p.summary)[(int64_t)seqC * p.C + c] = make_float2(inclP[e], inclH[e]);
+                        reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
+                            make_float2(inclP[e], inclH[e]);
                 }
             }
         }
     }
-    __syncthreads();
 
     // ---------------------------------------------------------- phase 2
     float h[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = fmaf(EA[e], s_carry[e * 32 + lane], EB[e]);
+    for (int e = 0; e < 8; ++e) h[e] = fmaf(EA[e], s_cc[e * 32 + lane].x, EB[e]);
     const bool ok0 = c0 + chan<SPLIT>(0, lane) < p.C;
     const bool ok1 = c0 + chan<SPLIT>(4, lane) < p.C;
-    TS* orow0 = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + c0;
+    TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
     PS dsp[4];
     if constexpr (K::FORM == FORM_SSD) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) dsp[i] = OS::pack(dsk[2 * i], dsk[2 * i + 1]);
     }
 #pragma unroll 2
-    for (int j = 0; j < R; ++j) {
-        const int r = warp * R + j;
+    for (int j = 0; j < rend; ++j, orow += p.ost) {
+        const int r = r0 + j;
         float a[8], b[8];
         reload(r, a, b);
 #pragma unroll
         for (int e = 0; e < 8; ++e) h[e] = fmaf(a[e], h[e], b[e]);
-        if (r < nvalid) {
-            PS o[4];
+        PS o[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = OS::pack(h[2 * i], h[2 * i + 1]);  // state in the input dtype
-            if constexpr (K::FORM == FORM_SSD) {
-                PS up[4], cp[4], gp[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CB, lane, up);
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CB, lane, cp);
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CB, lane, gp);
+        for (int i = 0; i < 4; ++i) o[i] = OS::pack(h[2 * i], h[2 * i + 1]);  // state in the input dtype
+        if constexpr (K::FORM == FORM_SSD) {
+            PS up[4], cp[4], gp[4];
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CB, lane, up);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CB, lane, cp);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CB, lane, gp);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 cf = OS::unpack(cp[i]);
-                    const float2 gf = OS::unpack(gp[i]);
-                    const PS cgs = OS::pack(sigm<TS>(cf.x), sigm<TS>(cf.y));
-                    const PS ogs = OS::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
-                    // (cg * state + D * u) * og, each op in the input dtype
-                    o[i] = OS::mul(OS::add(OS::mul(cgs, o[i]), OS::mul(dsp[i], up[i])), ogs);
-                }
-            } else if constexpr (K::FORM == FORM_RETENTION) {
-                PS qp[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CB, lane, qp);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
+            for (int i = 0; i < 4; ++i) {
+                const float2 cf = OS::unpack(cp[i]);
+                const float2 gf = OS::unpack(gp[i]);
+                const PS cgs = OS::pack(sigm<TS>(cf.x), sigm<TS>(cf.y));
+                const PS ogs = OS::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
+                // (cg * state + D * u) * og, each op in the input dtype
+                o[i] = OS::mul(OS::add(OS::mul(cgs, o[i]), OS::mul(dsp[i], up[i])), ogs);
             }
-            Row8<TS, SPLIT>::stg(orow0 + (int64_t)(t0 + r) * p.ost, lane, o, ok0, ok1);
+        } else if constexpr (K::FORM == FORM_RETENTION) {
+            PS qp[4];
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CB, lane, qp);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
         }
+        Row8<TS, SPLIT>::stg(orow, lane, o, ok0, ok1);
     }
 
-    // ---------------------------------------------------------- retire
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const uint32_t d = atomicAdd(&p.hdr[WS_DONE], 1u);
-        if (d == static_cast<uint32_t>(p.ntiles) - 1u) {
-            atomicExch(&p.hdr[WS_TICKET], 0u);
-            atomicExch(&p.hdr[WS_DONE], 0u);
-            __threadfence();
-            atomicAdd(&p.hdr[WS_EPOCH], 1u);
-        }
-    }
 }
 
 }  // namespace need

@@ -1,17 +1,20 @@
 // sp.cu -- carry fix-up of the sequence-parallel (T-sharded) scan.
 //
 // Rank r scanned its slice [r*T/P, (r+1)*T/P) from a zero state and produced,
-// per channel, the slice map (A_r = prod a, B_r = h at the slice end).  With
-// every rank's map gathered, the true state entering slice r is
+// per channel, the slice map (A_r = prod a, B_r = h at the slice end), plus for
+// every tile the product of a before it (tile_prod) and the state entering it
+// (tile_carry).  With every rank's map gathered, the true state entering
+// slice r is
 //     carry_r = B_{r-1} + A_{r-1} * (B_{r-2} + A_{r-2} * ( ... ))
-// and the slice's outputs need h[t] += (prod_{s<=t} a[s]) * carry_r.  The
-// product at each tile start was recorded by the local scan (tile_prod), so
-// tiles are independent: one warp per tile recomputes a (the same rounded
-// gate the scan used), walks its rows and rewrites the outputs.  A tile whose
-// starting correction is at most 2^-24 * |carry| on every channel is skipped
-// (gated decays lie in [0, 1], so the correction only shrinks from there);
-// with decays in (0, 1) only the leading ~log(2^-24)/log(mean a) tokens of a
-// slice are touched.
+// and the state entering tile k of the slice is tile_carry[k] +
+// tile_prod[k] * carry_r.  Tiles are independent: one warp per tile rebuilds
+// a and b with the scan's own (rounded) gate arithmetic, runs the recurrence
+// from that corrected fp32 state and rewrites the tile's outputs -- so the
+// result is the whole-sequence scan up to fp32 association, with no second
+// rounding of already-rounded outputs.  A tile whose entering correction is at
+// most 2^-24 * |carry| on every channel is skipped (gated decays lie in
+// [0, 1], so the correction only shrinks from there); with decays in (0, 1)
+// only the leading ~log(2^-24)/log(mean a) tokens of a slice are touched.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -27,58 +30,56 @@ struct FixParams {
     int32_t form, rowdec;
     int32_t nb, nh, T, C, L, ncb, nchains, nchunks, ntiles;
     int32_t nranks, rank;
-    const void* dec;  // GATED: z; AFFINE: decay (full or per row)
-    int64_t dsb, dsh, dst;
+    const void* in[3];  // GATED: z, g, x; AFFINE: decay (full or per row), update
+    int64_t isb[3], ish[3], ist[3];
     void* out;
     int64_t osb, osh, ost;
     const uint8_t* seg;
     int64_t sgb, sgt;
     const float* tile_prod;
+    const float* tile_carry;
     const float* all_summary;
     float* h_final;
     float* summary;
 };
 
+// 8 consecutive elements as 4 packed pairs
 template <typename T>
-__device__ __forceinline__ void ld8f(const T* p, float (&f)[8]) {
-    using O = Ops<T>;
-    if constexpr (O::BYTES == 4) {
+__device__ __forceinline__ void ld8(const T* p, typename Ops<T>::P (&v)[4]) {
+    using P = typename Ops<T>::P;
+    if constexpr (Ops<T>::BYTES == 4) {
         const float4 a = *reinterpret_cast<const float4*>(p);
         const float4 b = *reinterpret_cast<const float4*>(p + 4);
-        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        v[0] = make_float2(a.x, a.y);
+        v[1] = make_float2(a.z, a.w);
+        v[2] = make_float2(b.x, b.y);
+        v[3] = make_float2(b.z, b.w);
     } else {
         const uint4 a = *reinterpret_cast<const uint4*>(p);
         const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 v = O::unpack(*reinterpret_cast<const typename O::P*>(&w[i]));
-            f[2 * i] = v.x;
-            f[2 * i + 1] = v.y;
-        }
+        for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const P*>(&w[i]);
     }
 }
 
 template <typename T>
-__device__ __forceinline__ void st8f(T* p, const float (&f)[8]) {
-    using O = Ops<T>;
-    if constexpr (O::BYTES == 4) {
-        *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
-        *reinterpret_cast<float4*>(p + 4) = make_float4(f[4], f[5], f[6], f[7]);
+__device__ __forceinline__ void st8(T* p, const typename Ops<T>::P (&v)[4]) {
+    if constexpr (Ops<T>::BYTES == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+        *reinterpret_cast<float4*>(p + 4) = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
     } else {
         uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const typename O::P v = O::pack(f[2 * i], f[2 * i + 1]);
-            w[i] = *reinterpret_cast<const uint32_t*>(&v);
-        }
+        for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(&v[i]);
         *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
-// TS: dtype of out (and of z for GATED); TD: dtype of an AFFINE decay.
+// TS: dtype of the streams and out; TD: dtype of an AFFINE decay.
 template <typename TS, typename TD>
 __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
+    using O = Ops<TS>;
+    using PS = typename O::P;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x * 4 + warp;
     if (tile >= p.ntiles) return;
@@ -90,14 +91,13 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     const int c = cblk * CB + lane * 8;
     const bool active = c < p.C;
 
-    float carry[8], At[8], corr[8];
+    float carry[8], h[8];
+    bool need = false;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         carry[e] = 0.0f;
-        At[e] = 1.0f;
-        corr[e] = 0.0f;
+        h[e] = 0.0f;
     }
-    bool need = false;
     if (active) {
         const size_t nsc = size_t(p.nb) * p.nh * p.C;
         for (int j = 0; j < p.rank; ++j) {
@@ -108,13 +108,12 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
                 carry[e] = fmaf(m.x, carry[e], m.y);
             }
         }
-        const float* tp = p.tile_prod + (size_t(seq) * p.nchunks + chunk) * p.C + c;
+        const size_t ti = (size_t(seq) * p.nchunks + chunk) * p.C + c;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            corr[e] = tp[e] * carry[e];
-            const bool tiny = p.form == FORM_GATED ? fabsf(corr[e]) <= 5.9604645e-8f * fabsf(carry[e])
-                                                   : corr[e] == 0.0f;
-            need |= !tiny;
+            const float corr = p.tile_prod[ti + e] * carry[e];
+            h[e] = p.tile_carry[ti + e] + corr;
+            need |= p.form == FORM_GATED ? fabsf(corr) > 5.9604645e-8f * fabsf(carry[e]) : corr != 0.0f;
         }
     }
     // slice summary / final state: the chunk-0 warp of each chain
@@ -138,31 +137,61 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     for (int r = 0; r < nrows; ++r) {
         const int64_t t = t0 + r;
         const bool reset = p.seg != nullptr && p.seg[bi * p.sgb + t * p.sgt] != 0;
-        float a[8];
+        float a[8], b[8];
         if (p.form == FORM_GATED) {
-            float z[8];
-            ld8f<TS>(reinterpret_cast<const TS*>(p.dec) + bi * p.dsb + hi * p.dsh + t * p.dst + c, z);
+            // the scan's gate arithmetic (scan_kernel.cuh, phase 1)
+            PS zp[4], gp[4], xp[4];
+            ld8<TS>(reinterpret_cast<const TS*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, zp);
+            ld8<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, gp);
+            ld8<TS>(reinterpret_cast<const TS*>(p.in[2]) + bi * p.isb[2] + hi * p.ish[2] + t * p.ist[2] + c, xp);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                const float2 d = Ops<TS>::unpack(Ops<TS>::pack(sigm<TS>(z[e]), sigm<TS>(z[e + 1])));
-                a[e] = d.x;
-                a[e + 1] = d.y;
+            for (int i = 0; i < 4; ++i) {
+                const float2 zf = O::unpack(zp[i]);
+                const float2 gf = O::unpack(gp[i]);
+                PS ap = O::pack(sigm<TS>(zf.x), sigm<TS>(zf.y));
+                const PS gs = O::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
+                const PS bp = O::mul(O::sub(O::one(), ap), O::mul(gs, xp[i]));
+                if (reset) ap = O::zero();
+                const float2 af = O::unpack(ap), bf = O::unpack(bp);
+                a[2 * i] = af.x;
+                a[2 * i + 1] = af.y;
+                b[2 * i] = bf.x;
+                b[2 * i + 1] = bf.y;
             }
-        } else if (p.rowdec) {
-            const float d = to_f(reinterpret_cast<const TD*>(p.dec)[bi * p.dsb + hi * p.dsh + t * p.dst]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) a[e] = d;
         } else {
-            ld8f<TD>(reinterpret_cast<const TD*>(p.dec) + bi * p.dsb + hi * p.dsh + t * p.dst + c, a);
-        }
-        float h[8];
-        ld8f<TS>(orow + t * p.ost, h);
+            if (p.rowdec) {
+                const float d = to_f(reinterpret_cast<const TD*>(p.in[0])[bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0]]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            corr[e] = (reset ? 0.0f : a[e]) * corr[e];
-            h[e] += corr[e];
+                for (int e = 0; e < 8; ++e) a[e] = d;
+            } else {
+                typename Ops<TD>::P dp[4];
+                ld8<TD>(reinterpret_cast<const TD*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, dp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = Ops<TD>::unpack(dp[i]);
+                    a[2 * i] = f.x;
+                    a[2 * i + 1] = f.y;
+                }
+            }
+            if (reset) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) a[e] = 0.0f;
+            }
+            PS up[4];
+            ld8<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, up);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = O::unpack(up[i]);
+                b[2 * i] = f.x;
+                b[2 * i + 1] = f.y;
+            }
         }
-        st8f<TS>(orow + t * p.ost, h);
+        PS o[4];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = fmaf(a[e], h[e], b[e]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = O::pack(h[2 * i], h[2 * i + 1]);
+        st8<TS>(orow + t * p.ost, o);
     }
 }
 
@@ -176,16 +205,19 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     if (nranks < 1 || rank < 0 || rank >= nranks) return fail(NEED_ERR_INVALID, "rank %d of %d", rank, nranks);
     if (a->nb < 1 || a->nh < 1 || a->T < 1 || a->C < 1) return fail(NEED_ERR_INVALID, "bad sizes");
     if (a->C % 8 != 0) return fail(NEED_ERR_UNSUPPORTED, "C must be a multiple of 8");
-    if (a->tile_prod == nullptr) return fail(NEED_ERR_INVALID, "tile_prod is null (request it from the local scan)");
+    if (a->tile_prod == nullptr || a->tile_carry == nullptr)
+        return fail(NEED_ERR_INVALID, "tile_prod / tile_carry are null (request them from the local scan)");
     if (!aligned16(a->out)) return fail(NEED_ERR_UNSUPPORTED, "out is not 16-byte aligned");
     const bool gated = a->form == NEED_FORM_GATED;
     const int rd = gated ? 0 : (a->decay_per_row ? 1 : 0);
     const int ddt = gated ? a->dtype : a->decay_dtype;
     const int64_t L = need_scan_chunk_len(a->form, a->dtype, ddt, rd);
     if (L <= 0) return fail(NEED_ERR_UNSUPPORTED, "no kernel for this dtype combination");
-    const need_view& dv = a->in[0];
-    if (dv.ptr == nullptr) return fail(NEED_ERR_INVALID, "in[0] is null");
-    if (!rd && !aligned16(dv.ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[0] is not 16-byte aligned");
+    const int nin = gated ? 3 : 2;
+    for (int k = 0; k < nin; ++k) {
+        if (a->in[k].ptr == nullptr) return fail(NEED_ERR_INVALID, "in[%d] is null", k);
+        if (!(k == 0 && rd) && !aligned16(a->in[k].ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[%d] is not 16-byte aligned", k);
+    }
     if (rank == 0) return ok();  // no carry enters the first slice
 
     FixParams p{};
@@ -202,10 +234,12 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     p.ntiles = p.nchains * p.nchunks;
     p.nranks = nranks;
     p.rank = rank;
-    p.dec = dv.ptr;
-    p.dsb = dv.stride_b;
-    p.dsh = dv.stride_h;
-    p.dst = dv.stride_t;
+    for (int k = 0; k < nin; ++k) {
+        p.in[k] = a->in[k].ptr;
+        p.isb[k] = a->in[k].stride_b;
+        p.ish[k] = a->in[k].stride_h;
+        p.ist[k] = a->in[k].stride_t;
+    }
     p.out = a->out;
     p.osb = a->out_stride_b;
     p.osh = a->out_stride_h;
@@ -214,6 +248,7 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     p.sgb = a->seg_stride_b;
     p.sgt = a->seg_stride_t;
     p.tile_prod = a->tile_prod;
+    p.tile_carry = a->tile_carry;
     p.all_summary = all_summary;
     p.h_final = a->h_final;
     p.summary = a->summary;

@@ -9,8 +9,9 @@ step:
 2. the slice maps (``[B, C, 2]`` fp32 per rank, 2*B*C*4 bytes) are
    all-gathered with NCCL into local memory;
 3. ``need_sp_fixup`` composes the maps of ranks < r into the carry entering
-   slice r and adds ``prod(a) * carry`` to the leading tiles of the slice
-   until that correction is below 2^-24 of the carry on every channel.
+   slice r and re-scans the leading tiles of the slice from their corrected
+   fp32 entering state, until the correction is below 2^-24 of the carry on
+   every channel.
 
 Batch/channel sharding needs no exchange at all; only the T split does.  The
 oracle for this path is the whole-T scan on one device.
@@ -34,7 +35,8 @@ class LocalScan:
     args: abi.NeedScanArgs
     out: torch.Tensor
     summary: torch.Tensor    # [B, C, 2] fp32 (prod a, h_end) of this slice
-    tile_prod: torch.Tensor  # [B, nchunks, C] fp32
+    tile_prod: torch.Tensor  # [B, nchunks, C] fp32: product of a before each tile
+    tile_carry: torch.Tensor  # [B, nchunks, C] fp32: local state entering each tile
     h_final: torch.Tensor    # [B, C] fp32
     keep: List[torch.Tensor] = field(default_factory=list)
 
@@ -57,6 +59,7 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
     out = torch.empty((B, T, C), dtype=ts, device=dev)
     summary = torch.empty((B, C, 2), dtype=torch.float32, device=dev)
     tile_prod = torch.empty((B, nchunks, C), dtype=torch.float32, device=dev)
+    tile_carry = torch.empty((B, nchunks, C), dtype=torch.float32, device=dev)
     hf = torch.empty((B, C), dtype=torch.float32, device=dev)
     a = abi.NeedScanArgs()
     nk._fill_common(a, abi.FORM_GATED, ts, B, 1, T, C, out)
@@ -65,8 +68,9 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
     keep = [xs, zs, gs] + nk._fill_state(a, dev, B, 1, C, seg_start, None, hf)
     a.summary = summary.data_ptr()
     a.tile_prod = tile_prod.data_ptr()
+    a.tile_carry = tile_carry.data_ptr()
     nk._launch("need_gated_scan", a, dev)
-    return LocalScan(a, out, summary, tile_prod, hf, keep)
+    return LocalScan(a, out, summary, tile_prod, tile_carry, hf, keep)
 
 
 def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> None:
