@@ -151,6 +151,30 @@ NEED_API int need_recurrent_retention_scan(const need_scan_args* args, need_stre
  * args->form == NEED_FORM_GATED. */
 NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
 
+/* Bytes of the static scratch array behind need_gated_scan_noalloc: a 128-byte
+ * header plus 8 KB of look-back records for each of at most 1024 tiles. */
+#define NEED_GATED_SCAN_NOALLOC_SCRATCH_BYTES (128 + 1024 * 8192)
+
+/* need_gated_scan for callers that cannot allocate device memory where they run
+ * the scan -- e.g. an inference-engine plugin whose enqueue step may not
+ * allocate, a serving loop that cannot afford cudaMalloc's implicit
+ * device-wide synchronisation, or a runtime that owns a fixed memory budget.
+ * No counterpart in the reference.
+ *
+ * It takes args->workspace / workspace_bytes as unused and instead uses a
+ * static device array of NEED_GATED_SCAN_NOALLOC_SCRATCH_BYTES bytes, which
+ * every GPU that loads this library holds until the process exits.  A call
+ * whose scan needs more scratch than that (more than 1024 tiles of 256
+ * channels x need_scan_chunk_len tokens) fails with NEED_ERR_WORKSPACE and
+ * launches nothing.  The first call on each device looks up the array's device
+ * address and zero-fills it (a synchronous cudaMemset), so make that first call
+ * before any stream capture.  Each call then clears the array's error word on
+ * `stream` and launches the same kernel as need_gated_scan.  All calls share
+ * the one array: calls that overlap on the GPU (different streams or host
+ * threads at once) race on it; calls that run one after another, on any
+ * stream, are fine.  It allocates nothing (no cudaMalloc or cudaFree). */
+NEED_API int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Ragged decode / speculative verify                                        */
 /* ------------------------------------------------------------------------ */

@@ -61,6 +61,7 @@ SIGNATURES = {
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ragged_verify": (c_int32, [POINTER(NeedVerifyArgs), c_void_p]),
     "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
