@@ -26,9 +26,12 @@ namespace {
 #ifndef NEED_GATED16_NW
 #define NEED_GATED16_NW 8
 #endif
+#ifndef NEED_GATED16_CB
+#define NEED_GATED16_CB 256
+#endif
 template <typename T>
 using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? NEED_GATED16_L : 32,
-                         sizeof(T) == 2 ? NEED_GATED16_NW : 4>;
+                         sizeof(T) == 2 ? NEED_GATED16_NW : 4, sizeof(T) == 2 ? NEED_GATED16_CB : 256>;
 template <typename T>
 using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? 32 : 16, sizeof(T) == 2 ? 8 : 4>;
 
@@ -49,7 +52,7 @@ template <typename TS, typename TD, bool RD>
 using RetCfg = ScanCfg<FORM_RETENTION, TS, TD, RD, RetL<TS, TD, RD>::L, RetL<TS, TD, RD>::NW>;
 
 struct Plan {
-    int L = 0, R = 0, nin = 0, in0 = 0;
+    int L = 0, R = 0, CB = 0, nin = 0, in0 = 0;  // tokens, rows per warp, channels per tile
     bool dstream = false, split = false;
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
 };
@@ -70,6 +73,7 @@ Plan plan_of() {
     Plan p;
     p.L = K::L;
     p.R = K::R;
+    p.CB = K::CBW;
     p.nin = K::NIN;
     p.in0 = K::IN0;
     p.dstream = K::HAS_DSTREAM;
@@ -120,16 +124,16 @@ struct Geometry {
 
 Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) {
     Geometry g;
-    g.ncb = cdiv(C, CB);
+    g.ncb = cdiv(C, pl.CB);
     g.nchains = nb * nh * g.ncb;
     g.nchunks = cdiv(T, pl.L);
     g.ntiles = g.nchains * g.nchunks;
     return g;
 }
 
-size_t ws_bytes(int64_t ntiles) {
+size_t ws_bytes(int64_t ntiles, int cb) {
     const size_t hdr = WS_HDR_WORDS * 4;
-    return hdr + size_t(ntiles) * 256 * sizeof(ulonglong2) * 2;  // tagged AGG and INCL records
+    return hdr + size_t(ntiles) * size_t(cb) * sizeof(ulonglong2) * 2;  // tagged AGG and INCL records
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -148,7 +152,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t nh, int64_t T, int64_t C,
-                int box_rows, int which) {
+                int box_c, int box_rows, int which) {
     if (v.ptr == nullptr) return fail(NEED_ERR_INVALID, "in[%d] is null", which);
     if (!aligned16(v.ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[%d] is not 16-byte aligned", which);
     const int64_t es = dtype_bytes(dt);
@@ -170,7 +174,7 @@ int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t
         prev = static_cast<int64_t>(gs[i]) * sizes[i];
     }
     const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(T), cuuint64_t(nh), cuuint64_t(nb)};
-    const cuuint32_t box[4] = {cuuint32_t(CB), cuuint32_t(box_rows), 1, 1};  // one warp's rows
+    const cuuint32_t box[4] = {cuuint32_t(box_c), cuuint32_t(box_rows), 1, 1};  // one warp's rows
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUtensorMapDataType ty = dt == NEED_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                    : dt == NEED_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -212,7 +216,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     memset(P, 0, sizeof(*P));
     for (int k = 0; k < pl->nin; ++k) {
         const int dt = (pl->dstream && k == 0) ? ddt : a->dtype;
-        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->R, pl->in0 + k))
+        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->CB, pl->R, pl->in0 + k))
             return rc;
     }
     if (rowdec_form && rd) {
@@ -233,7 +237,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     if (a->form == NEED_FORM_SSD && a->d_skip == nullptr) return fail(NEED_ERR_INVALID, "d_skip is null");
     if (a->workspace == nullptr) return fail(NEED_ERR_WORKSPACE, "workspace is null");
     if (!aligned16(a->workspace)) return fail(NEED_ERR_WORKSPACE, "workspace is not 16-byte aligned");
-    const size_t need = ws_bytes(g.ntiles);
+    const size_t need = ws_bytes(g.ntiles, pl->CB);
     if (a->workspace_bytes < need)
         return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, need);
 
@@ -264,7 +268,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P->hdr = reinterpret_cast<uint32_t*>(ws);
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
-    P->incl = P->agg + size_t(g.ntiles) * 256;
+    P->incl = P->agg + size_t(g.ntiles) * pl->CB;
     return NEED_OK;
 }
 
@@ -297,8 +301,8 @@ size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t decay_dtype
     Plan pl;
     const bool rf = form == NEED_FORM_AFFINE || form == NEED_FORM_RETENTION;
     if (!select_plan(form, dtype, rf ? decay_dtype : dtype, rf ? decay_per_row : 0, &pl)) return 0;
-    if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(0);
-    return ws_bytes(geometry(pl, nb, nh, T, C).ntiles);
+    if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(0, pl.CB);
+    return ws_bytes(geometry(pl, nb, nh, T, C).ntiles, pl.CB);
 }
 
 int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream) {

@@ -43,7 +43,7 @@ namespace need {
 
 enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 
-constexpr int CB = 256;  // channels per tile (32 lanes x 8 channels)
+constexpr int CB = 256;  // channel block of the sequence-parallel fix-up tiles
 
 // workspace header words (uint32)
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
@@ -77,8 +77,8 @@ struct ScanParams {
     float* tile_prod;
     float* tile_carry;
     uint32_t* hdr;
-    ulonglong2* agg;   // [ntiles][8][32] tagged (A, B): the tile's map
-    ulonglong2* incl;  // [ntiles][8][32] tagged (prod, h): state after the tile
+    ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
+    ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
 };
 
 // ------------------------------------------------------------------ types
@@ -163,6 +163,52 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 
+// ------------------------------------------------------------------ packed fp32 pairs
+// sm_100 executes these as single f32x2 instructions (FFMA2 / FMUL2 / FADD2);
+// each lane is an ordinary IEEE round-to-nearest fp32 op.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+
+// a packed 16-bit pair (or an fp32 pair) as two fp32 values
+__device__ __forceinline__ float2 widen(__nv_bfloat162 p) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&p);
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+__device__ __forceinline__ float2 widen(__half2 p) { return __half22float2(p); }
+__device__ __forceinline__ float2 widen(float2 p) { return p; }
+
+// sigmoid / exp of a pair: 16-bit paths use the hardware approximations (the
+// result is rounded to 16 bits next), fp32 paths the library exp and IEEE division
+template <typename T>
+__device__ __forceinline__ float2 sig2(float2 x) {
+    if constexpr (Ops<T>::BYTES == 4) {
+        return make_float2(sigmoid_exact(x.x), sigmoid_exact(x.y));
+    } else {
+        const float2 t = fmul2(x, splat2(-1.4426950408889634f));
+        float e0, e1, r0, r1;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t.x));
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t.y));
+        const float2 d = fadd2(make_float2(e0, e1), splat2(1.0f));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d.x));
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d.y));
+        return make_float2(r0, r1);
+    }
+}
+template <typename T>
+__device__ __forceinline__ float2 exp2_pair(float2 x) {  // exp(x) of a pair
+    if constexpr (Ops<T>::BYTES == 4) {
+        return make_float2(expf(x.x), expf(x.y));
+    } else {
+        const float2 t = fmul2(x, splat2(1.4426950408889634f));
+        float e0, e1;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t.x));
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t.y));
+        return make_float2(e0, e1);
+    }
+}
+
 // ------------------------------------------------------------------ 8-channel rows
 // A thread's 8 channels: with SPLIT (any 4-byte stream) they are two groups of
 // four, channels [lane*4, +4) and [128 + lane*4, +4); otherwise one group of
@@ -234,18 +280,26 @@ struct Row8 {
 };
 
 // ------------------------------------------------------------------ config
-template <int FORM_, typename TS_, typename TD_, bool ROWDEC_, int L_, int NW_>
+// FORM, stream dtype TS, decay dtype TD (AFFINE / RETENTION), decay broadcast
+// over channels (ROWDEC), tokens per tile L, row warps NW, channels per tile CBW.
+// A lane owns 8 channels; a row of a tile takes LPR = CBW/8 lanes, so a warp
+// works on SS = 32/LPR rows side by side.
+template <int FORM_, typename TS_, typename TD_, bool ROWDEC_, int L_, int NW_, int CBW_ = 256>
 struct ScanCfg {
     static constexpr int FORM = FORM_;
     using TS = TS_;  // streamed dtype (inputs other than a separate decay, and the output)
     using TD = TD_;  // decay dtype (AFFINE / RETENTION)
     static constexpr bool ROWDEC = ROWDEC_;
-    static constexpr int L = L_, NW = NW_, NT = NW * 32, R = L / NW;
-    static_assert(L % NW == 0, "rows must split evenly over warps");
-    static_assert(NW >= 2, "the look-back uses the last two warps");
-    static_assert(R <= 32, "a warp loads the reset flags of its rows one per lane");
+    static constexpr int L = L_, NW = NW_, CBW = CBW_, R = L / NW;
+    static constexpr int LB = NW;  // the look-back warp (after the NW row warps)
+    static constexpr int NT = (NW + 1) * 32;
     static constexpr bool HAS_DSTREAM = (FORM == FORM_AFFINE || FORM == FORM_RETENTION) && !ROWDEC;
     static constexpr bool SPLIT = (Ops<TS>::BYTES == 4) || (HAS_DSTREAM && Ops<TD>::BYTES == 4);
+    static constexpr int LPR = CBW / 8, SS = 32 / LPR, RS = R / SS;  // lanes per row, rows side by side, rows per thread
+    static_assert(L % NW == 0 && R % SS == 0, "rows must split evenly over warps and lanes");
+    static_assert(!SPLIT || CBW == 256, "4-byte streams use 256-channel tiles");
+    static_assert(CBW == 64 || CBW == 128 || CBW == 256, "64, 128 or 256 channels per tile");
+    static_assert(R <= 32, "a warp loads the reset flags of its rows one per lane");
     // streamed inputs, in[] order of the C ABI
     static constexpr int NIN = FORM == FORM_AFFINE      ? (ROWDEC ? 1 : 2)
                                : FORM == FORM_GATED     ? 3
@@ -254,7 +308,7 @@ struct ScanCfg {
     // in[] index of the first streamed tensor (AFFINE/RETENTION with a row decay skip in[0])
     static constexpr int IN0 = ((FORM == FORM_AFFINE || FORM == FORM_RETENTION) && ROWDEC) ? 1 : 0;
     __host__ __device__ static constexpr int slot_bytes(int k) {
-        return L * CB * ((HAS_DSTREAM && k == 0) ? Ops<TD>::BYTES : Ops<TS>::BYTES);
+        return L * CBW * ((HAS_DSTREAM && k == 0) ? Ops<TD>::BYTES : Ops<TS>::BYTES);
     }
     __host__ __device__ static constexpr int slots_bytes() {
         int s = 0;
@@ -263,17 +317,17 @@ struct ScanCfg {
     }
     // GATED frees its input-gate slot after phase 1: the warp maps live there.
     static constexpr int AGG_SLOT = FORM == FORM_GATED ? 1 : -1;
-    static constexpr int AGG_BYTES = NW * 8 * 32 * 8;
+    static constexpr int AGG_BYTES = NW * 4 * 32 * 16;  // per warp: 4 pairs x 32 lanes x (A2, B2)
     // warp maps: in the freed slot each warp's map sits in that warp's own rows
     // (no barrier needed before writing it); otherwise packed
-    static constexpr int AGG_W = AGG_SLOT >= 0 ? (L * CB * Ops<TS>::BYTES / NW) / 8 : 8 * 32;
-    static_assert(AGG_SLOT < 0 || AGG_W >= 8 * 32, "a warp's rows must hold its map");
+    static constexpr int AGG_STRIDE = AGG_SLOT >= 0 ? (L * CBW * Ops<TS>::BYTES / NW) : 4 * 32 * 16;
+    static_assert(AGG_SLOT < 0 || AGG_STRIDE >= 4 * 32 * 16, "a warp's rows must hold its map");
     static constexpr int OFF_AGG = slots_bytes();
     static constexpr int OFF_CARRY = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
     static constexpr int OFF_ROWDEC = OFF_CARRY + 8 * 32 * 8;  // (carry, prod) per channel
     static constexpr int OFF_RESET = OFF_ROWDEC + (ROWDEC ? L * 4 : 0);
     static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
-    static constexpr int SMEM = OFF_MISC + NW * 8 + 16 + 128;  // per-warp mbarriers, misc, alignment slack
+    static constexpr int SMEM = OFF_MISC + (NW + 1) * 8 + 16 + 128;  // mbarriers, misc, alignment slack
     // resident CTAs per SM: bounded by shared memory (228 KB per SM, 1 KB
     // reserved per CTA) and by ~112 registers per thread
     static constexpr int MINB_SMEM = (228 * 1024) / (SMEM + 1024);
@@ -298,20 +352,23 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     using OS = Ops<TS>;
     using PS = typename OS::P;
     constexpr bool SPLIT = K::SPLIT;
-    constexpr int L = K::L, NW = K::NW, R = K::R;
+    constexpr int L = K::L, NW = K::NW, R = K::R, CBW = K::CBW, LPR = K::LPR, SS = K::SS, RS = K::RS;
 
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    float2* s_agg = reinterpret_cast<float2*>(K::AGG_SLOT >= 0 ? slot_ptr<K>(base, K::AGG_SLOT)
-                                                                 : base + K::OFF_AGG);
-    float* s_carry = reinterpret_cast<float*>(base + K::OFF_CARRY);
+    unsigned char* s_agg = K::AGG_SLOT >= 0 ? slot_ptr<K>(base, K::AGG_SLOT) : base + K::OFF_AGG;
+    float2* s_cc = reinterpret_cast<float2*>(base + K::OFF_CARRY);  // (carry, prod) per channel
     float* s_rowdec = reinterpret_cast<float*>(base + K::OFF_ROWDEC);
     uint8_t* s_reset = base + K::OFF_RESET;
-    uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per warp
-    uint32_t* s_misc = reinterpret_cast<uint32_t*>(base + K::OFF_MISC + NW * 8);
+    uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
+    uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
+    // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
+    auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int v = lane % LPR;  // channel vector (8 channels) of this lane
+    const int q = lane / LPR;  // row group of this lane within its warp
 
     // Tile ids follow blockIdx.x (chunk-major).  CTAs are dispatched in
     // increasing blockIdx order, so every tile a CTA waits on belongs to a CTA
@@ -320,17 +377,8 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     const int tile = static_cast<int>(blockIdx.x);
     if (tid == 0) {
         for (int w = 0; w < NW; ++w) mbar_init(&s_bar[w], 1);
+        mbar_init(s_p1, NW * 32);
         fence_barrier_init();
-    }
-    if (tid == 32) {
-        // Every CTA of a launch gets the same epoch: the counter in the low half
-        // counts CTAs in, and the last one to start moves the epoch on for the
-        // next launch.  Used only by the look-back, long after this returns.
-        unsigned long long* lw = reinterpret_cast<unsigned long long*>(p.hdr + WS_LAUNCH);
-        const unsigned long long old = atomicAdd(lw, 1ull);
-        if (static_cast<uint32_t>(old) == static_cast<uint32_t>(p.ntiles) - 1u)
-            atomicAdd(lw, (1ull << 32) - static_cast<unsigned long long>(p.ntiles));
-        s_misc[1] = static_cast<uint32_t>(old >> 32);
     }
     __syncthreads();
     const int chunk = tile / p.nchains;
@@ -338,27 +386,198 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     const int seq = chain / p.ncb;
     const int cblk = chain - seq * p.ncb;
     const int bi = seq / p.nh, hi = seq - bi * p.nh;
-    const int t0 = chunk * L, c0 = cblk * CB;
-
-    // Each warp loads its own rows (one TMA box of R rows per input) and starts
-    // on them as soon as they land, so compute overlaps the rest of the tile's
-    // load instead of waiting for all of it.
+    const int t0 = chunk * L, c0 = cblk * CBW;
     const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
-    const int r0 = warp * R;
-    const int rend = max(0, min(R, nvalid - r0));  // this warp's rows inside T
-    if (lane == 0 && rend > 0) {
+
+    if (warp == K::LB) {
+        // ------------------------------------------------------ look-back warp
+        // It owns no rows.  From the start of the CTA it polls the predecessors'
+        // records -- the maps of the up to kLookbackDepth tiles before this one
+        // and the inclusive state of the tile before those, composed in that
+        // fixed order, so results are bit-reproducible -- while the row warps
+        // load and run phase 1.  It releases the carry to the row warps (named
+        // barrier) as soon as the records are in, publishes this tile's map (AGG)
+        // the moment the row warps' maps are in -- never held back by a
+        // predecessor -- and then the inclusive state.  Records carry the launch
+        // epoch in every 64-bit word, so publishing needs no fence and a poll
+        // returns the data itself.  Lanes >= LPR duplicate lane % LPR and store nothing.
+        const bool act = lane < LPR;
+        uint32_t ep = 0;
+        if (lane == 0) {
+            // Every CTA of a launch gets the same epoch: the low half counts CTAs
+            // in, and the last one to start moves the epoch on for the next launch.
+            unsigned long long* lw = reinterpret_cast<unsigned long long*>(p.hdr + WS_LAUNCH);
+            const unsigned long long old = atomicAdd(lw, 1ull);
+            if (static_cast<uint32_t>(old) == static_cast<uint32_t>(p.ntiles) - 1u)
+                atomicAdd(lw, (1ull << 32) - static_cast<unsigned long long>(p.ntiles));
+            ep = static_cast<uint32_t>(old >> 32);
+        }
+        const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
+        auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
+        float carry[8], carryP[8];
+        float2 TA[4], TB[4];  // this tile's map
+        const int nagg = chunk == 0 ? 0 : min(chunk - 1, kLookbackDepth);
+        bool pread = chunk == 0, mapped = false, agg_pub = chunk == 0;  // chunk 0 publishes no bare map
+        bool released = false;
+        if (chunk == 0) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int c = c0 + chan<SPLIT>(e, v);
+                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
+                carryP[e] = 1.0f;
+            }
+        }
+        auto release = [&]() {
+            if (act) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s_cc[e * LPR + v] = make_float2(carry[e], carryP[e]);
+            }
+            __syncwarp();
+            named_arrive(1, K::NT);  // the row warps may run phase 2
+            released = true;
+        };
+        auto compose_map = [&]() {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                TA[i] = splat2(1.0f);
+                TB[i] = splat2(0.0f);
+            }
+            for (int w = 0; w < NW; ++w)
+                for (int qq = 0; qq < SS; ++qq) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 m = agg4(w)[i * 32 + qq * LPR + v];
+                        TB[i] = ffma2(make_float2(m.x, m.y), TB[i], make_float2(m.z, m.w));
+                        TA[i] = fmul2(make_float2(m.x, m.y), TA[i]);
+                    }
+                }
+        };
+        if (pread) release();
+        bool ok = false;
+        for (uint32_t it = 0; it < kLookbackPolls; ++it) {
+            bool progressed = false;
+            if (!pread) {
+                bool valid = true;
+                float accA[8], accB[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    accA[e] = 1.0f;
+                    accB[e] = 0.0f;
+                }
+                for (int j = 0; j < nagg; ++j) {
+                    const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * CBW;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (A, B)
+                        valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                        accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                        accA[e] = accA[e] * untag(m.x);
+                    }
+                }
+                const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * CBW;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (prod, h)
+                    valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                    carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                    carryP[e] = accA[e] * untag(m.x);
+                }
+                if (__all_sync(0xffffffffu, valid)) {
+                    pread = progressed = true;
+                    release();
+                }
+            }
+            if (!mapped && __all_sync(0xffffffffu, mbar_test_wait(s_p1, 0))) {
+                compose_map();
+                mapped = progressed = true;
+            }
+            if (mapped && pread) {
+                ok = true;
+                break;
+            }
+            if (mapped && !agg_pub) {
+                ulonglong2* my = p.agg + (int64_t)tile * CBW;
+                if (act) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        st_relaxed_v2u64(&my[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
+                }
+                agg_pub = progressed = true;
+            }
+            if (!progressed && it >= 2) __nanosleep(64);
+            if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
+            if (!pread) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    carry[e] = 0.0f;
+                    carryP[e] = 0.0f;
+                }
+            }
+            if (!released) release();
+            if (!mapped) {
+                mbar_wait_bounded(s_p1, 0, kTmaPolls);
+                compose_map();
+            }
+        }
+        // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
+        // the final state, the slice summary and the per-tile products
+        float inclP[8], inclH[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            inclP[e] = el(TA, e) * carryP[e];
+            inclH[e] = fmaf(el(TA, e), carry[e], el(TB, e));
+        }
+        if (act) {
+            if (chunk + 1 < p.nchunks) {
+                ulonglong2* ma = p.agg + (int64_t)tile * CBW;
+                ulonglong2* mi = p.incl + (int64_t)tile * CBW;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    if (!agg_pub) st_relaxed_v2u64(&ma[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
+                    st_relaxed_v2u64(&mi[e * LPR + v], tagged(inclP[e], tag), tagged(inclH[e], tag));
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int c = c0 + chan<SPLIT>(e, v);
+                if (c < p.C) {
+                    const int64_t ti = ((int64_t)seq * p.nchunks + chunk) * p.C + c;
+                    if (p.tile_prod != nullptr) p.tile_prod[ti] = carryP[e];
+                    if (p.tile_carry != nullptr) p.tile_carry[ti] = carry[e];
+                    if (chunk + 1 == p.nchunks) {
+                        if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
+                        if (p.summary != nullptr)
+                            reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
+                                make_float2(inclP[e], inclH[e]);
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- row warps
+    // Each warp loads its own R rows (one TMA box per input) and starts on them
+    // as soon as they land, so compute overlaps the rest of the tile's load.
+    const int wr0 = warp * R;                              // this warp's first row
+    const int r0 = wr0 + q * RS;                           // this thread's first row
+    const int rend = max(0, min(RS, nvalid - r0));         // this thread's rows inside T
+    if (lane == 0 && nvalid > wr0) {
         uint32_t bytes = 0;
 #pragma unroll
         for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
         mbar_arrive_expect_tx(&s_bar[warp], bytes);
 #pragma unroll
         for (int k = 0; k < K::NIN; ++k)
-            tma_load_4d(slot_ptr<K>(base, k) + r0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + r0, hi, bi,
+            tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + wr0, hi, bi,
                         &s_bar[warp]);
     }
     // this warp's reset flags and per-row decay while its rows are in flight
     if (lane < R) {
-        const int r = r0 + lane, t = t0 + r;
+        const int r = wr0 + lane, t = t0 + r;
         uint8_t rs = 0;
         if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
         s_reset[r] = rs;
@@ -369,301 +588,179 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         }
     }
     __syncwarp();
-    if (rend > 0 && !mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls)) {
+    if (nvalid > wr0 && !mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls)) {
         atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
         mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls);
     }
 
-    // per-thread constants
-    float dsk[8];
-    if constexpr (K::FORM == FORM_SSD) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int c = c0 + chan<SPLIT>(e, lane);
-            dsk[e] = c < p.C ? p.dskip[c] : 0.0f;
-        }
-    }
-
     // ---------------------------------------------------------- phase 1
-    // a, b for row r of this thread; `write` stores the rounded a, b back for phase 2.
-    auto gates = [&](int r, bool write, float (&a)[8], float (&b)[8]) {
+    // a, b of row r as 4 fp32 pairs (channels 2i, 2i+1 of this lane's vector);
+    // `write` stores the rounded a, b back for phase 2.
+    auto gates = [&](int r, bool write, float2 (&a)[4], float2 (&b)[4]) {
         const bool reset = s_reset[r] != 0;
         if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
             if constexpr (K::ROWDEC) {
                 const float d = reset ? 0.0f : s_rowdec[r];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) a[e] = d;
+                for (int i = 0; i < 4; ++i) a[i] = splat2(d);
             } else {
                 typename Ops<TD>::P dp[4];
-                Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CB, lane, dp);
+                Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CBW, v, dp);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = Ops<TD>::unpack(dp[i]);
-                    a[2 * i] = f.x;
-                    a[2 * i + 1] = f.y;
-                }
-                if (reset) {  // uniform across the warp: one branch per row
+                for (int i = 0; i < 4; ++i) a[i] = widen(dp[i]);
+                if (reset) {  // uniform across the row group
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) a[e] = 0.0f;
+                    for (int i = 0; i < 4; ++i) a[i] = splat2(0.0f);
                 }
             }
             PS up[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CB, lane, up);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CBW, v, up);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 f = OS::unpack(up[i]);
-                b[2 * i] = f.x;
-                b[2 * i + 1] = f.y;
-            }
+            for (int i = 0; i < 4; ++i) b[i] = widen(up[i]);
         } else {
             // GATED: slots z, g, x.  SSD: slots dt, bg, u (cg, og used in phase 2)
-            TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CB;
-            TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CB;
-            TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CB;
+            TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CBW;
+            TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CBW;
+            TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CBW;
             PS p0[4], p1[4], p2[4], ap[4], bp[4];
-            Row8<TS, SPLIT>::lds(s0, lane, p0);
-            Row8<TS, SPLIT>::lds(s1, lane, p1);
-            Row8<TS, SPLIT>::lds(s2, lane, p2);
+            Row8<TS, SPLIT>::lds(s0, v, p0);
+            Row8<TS, SPLIT>::lds(s1, v, p1);
+            Row8<TS, SPLIT>::lds(s2, v, p2);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 f0 = OS::unpack(p0[i]);
-                const float2 f1 = OS::unpack(p1[i]);
-                PS dec;
+                float2 dec;
                 if constexpr (K::FORM == FORM_GATED) {
-                    dec = OS::pack(sigm<TS>(f0.x), sigm<TS>(f0.y));
+                    dec = sig2<TS>(widen(p0[i]));
                 } else {
-                    // need_kernels.py:330-332: fp32 dt, decay rounded to the input dtype
-                    const float dx = __fadd_rn(__fmul_rn(sigm<TS>(f0.x), p.dt_scale), p.dt_min);
-                    const float dy = __fadd_rn(__fmul_rn(sigm<TS>(f0.y), p.dt_scale), p.dt_min);
-                    dec = OS::pack(expo<TS>(-dx), expo<TS>(-dy));
+                    // need_kernels.py:330-332: fp32 dt = dt_min + scale * sigmoid(dt_raw)
+                    // (separately rounded), decay = exp(-dt) rounded to the input dtype
+                    const float2 dt = fadd2(fmul2(sig2<TS>(widen(p0[i])), splat2(p.dt_scale)), splat2(p.dt_min));
+                    dec = exp2_pair<TS>(make_float2(-dt.x, -dt.y));
                 }
-                const PS gs = OS::pack(sigm<TS>(f1.x), sigm<TS>(f1.y));
-                bp[i] = OS::mul(OS::sub(OS::one(), dec), OS::mul(gs, p2[i]));
-                ap[i] = dec;
+                ap[i] = OS::pack(dec.x, dec.y);
+                const float2 g = sig2<TS>(widen(p1[i]));
+                bp[i] = OS::mul(OS::sub(OS::one(), ap[i]), OS::mul(OS::pack(g.x, g.y), p2[i]));
             }
-            if (reset) {  // uniform across the warp: one branch per row
+            if (reset) {  // uniform across the row group: one branch per row
 #pragma unroll
                 for (int i = 0; i < 4; ++i) ap[i] = OS::zero();
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 af = OS::unpack(ap[i]);
-                const float2 bf = OS::unpack(bp[i]);
-                a[2 * i] = af.x;
-                a[2 * i + 1] = af.y;
-                b[2 * i] = bf.x;
-                b[2 * i + 1] = bf.y;
+                a[i] = widen(ap[i]);
+                b[i] = widen(bp[i]);
             }
             if (write) {
-                Row8<TS, SPLIT>::sts(s0, lane, ap);  // a over the decay input
-                if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, lane, bp);  // b over x
-                else Row8<TS, SPLIT>::sts(s1, lane, bp);  // b over b_gate
+                Row8<TS, SPLIT>::sts(s0, v, ap);  // a over the decay input
+                if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, v, bp);  // b over x
+                else Row8<TS, SPLIT>::sts(s1, v, bp);  // b over b_gate
             }
         }
     };
     // a, b written back by phase 1
-    auto reload = [&](int r, float (&a)[8], float (&b)[8]) {
+    auto reload = [&](int r, float2 (&a)[4], float2 (&b)[4]) {
         if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
             gates(r, false, a, b);
         } else {
             PS ap[4], bp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CB, lane, ap);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CB, lane, bp);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CBW, v, ap);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CBW, v, bp);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 af = OS::unpack(ap[i]);
-                const float2 bf = OS::unpack(bp[i]);
-                a[2 * i] = af.x;
-                a[2 * i + 1] = af.y;
-                b[2 * i] = bf.x;
-                b[2 * i + 1] = bf.y;
+                a[i] = widen(ap[i]);
+                b[i] = widen(bp[i]);
             }
         }
     };
 
-    float A[8], B[8];
+    float2 A[4], B[4];  // this thread's map, channel pairs
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        A[e] = 1.0f;
-        B[e] = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+        A[i] = splat2(1.0f);
+        B[i] = splat2(0.0f);
     }
 #pragma unroll 2
     for (int j = 0; j < rend; ++j) {  // rows past T act as the identity
-        float a[8], b[8];
+        float2 a[4], b[4];
         gates(r0 + j, true, a, b);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            B[e] = fmaf(a[e], B[e], b[e]);
-            A[e] = a[e] * A[e];
+        for (int i = 0; i < 4; ++i) {
+            B[i] = ffma2(a[i], B[i], b[i]);
+            A[i] = fmul2(a[i], A[i]);
         }
     }
+    if constexpr (K::AGG_SLOT >= 0) __syncwarp();  // every lane is done with the slot rows the map overwrites
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s_agg[warp * K::AGG_W + e * 32 + lane] = make_float2(A[e], B[e]);
-    __syncthreads();
+    for (int i = 0; i < 4; ++i) agg4(warp)[i * 32 + lane] = make_float4(A[i].x, A[i].y, B[i].x, B[i].y);
+    mbar_arrive(s_p1);
+    if (!mbar_wait_bounded(s_p1, 0, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
 
-    // ---------------------------------------------------------- compose warps
-    float EA[8], EB[8];  // map of the rows before this warp
+    // ---------------------------------------------------------- compose
+    float2 EA[4], EB[4];  // map of the rows before this thread's rows
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        EA[e] = 1.0f;
-        EB[e] = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+        EA[i] = splat2(1.0f);
+        EB[i] = splat2(0.0f);
     }
-    for (int w = 0; w < warp; ++w) {
+    for (int w = 0; w <= warp; ++w)
+        for (int qq = 0; qq < (w < warp ? SS : q); ++qq) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float2 m = s_agg[w * K::AGG_W + e * 32 + lane];
-            EB[e] = fmaf(m.x, EB[e], m.y);
-            EA[e] = m.x * EA[e];
-        }
-    }
-
-    // ---------------------------------------------------------- look-back
-    // Two warps share it.  The last warp publishes this tile's map (AGG) for
-    // its successors; the warp before it reads the predecessors' records and
-    // forms the carry.  The composition order is fixed (the maps of the up to
-    // kLookbackDepth tiles before this one, then the inclusive state of the
-    // tile before those), so results are bit-reproducible.  Records are
-    // tagged with the launch epoch word by word, so publishing needs no fence
-    // and a poll returns the data itself.
-    const uint32_t tag = (s_misc[1] & 0x7fffffffu) | 0x80000000u;
-    float2* s_cc = reinterpret_cast<float2*>(s_carry);  // (carry, prod) per channel
-    if (warp == NW - 1 && chunk > 0) {
-        ulonglong2* my = p.agg + (int64_t)tile * 256;
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-            st_relaxed_v2u64(&my[e * 32 + lane], tagged(A[e] * EA[e], tag), tagged(fmaf(A[e], EB[e], B[e]), tag));
-    }
-    if (warp == NW - 2) {
-        float carry[8], carryP[8];
-        if (chunk == 0) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int c = c0 + chan<SPLIT>(e, lane);
-                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
-                carryP[e] = 1.0f;
-            }
-        } else {
-            const int nagg = min(chunk - 1, kLookbackDepth);
-            bool ok = false;
-            for (uint32_t it = 0; it < kLookbackPolls; ++it) {
-                bool valid = true;
-                float accA[8], accB[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    accA[e] = 1.0f;
-                    accB[e] = 0.0f;
-                }
-                for (int j = 0; j < nagg; ++j) {
-                    const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * 256;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * 32 + lane]);  // (A, B)
-                        valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                        accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                        accA[e] = accA[e] * untag(m.x);
-                    }
-                }
-                const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * 256;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const ulonglong2 m = ld_relaxed_v2u64(&src[e * 32 + lane]);  // (prod, h)
-                    valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                    carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                    carryP[e] = accA[e] * untag(m.x);
-                }
-                if (__all_sync(0xffffffffu, valid)) {
-                    ok = true;
-                    break;
-                }
-                if (it >= 2) __nanosleep(64);
-                if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
-            }
-            if (!ok && lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) s_cc[e * 32 + lane] = make_float2(carry[e], carryP[e]);
-    }
-    __syncthreads();
-    if (warp == NW - 1) {
-        // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
-        // the final state, the slice summary and the per-tile products
-        float inclP[8], inclH[8], carryP[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float2 cc = s_cc[e * 32 + lane];
-            const float TA = A[e] * EA[e], TB = fmaf(A[e], EB[e], B[e]);
-            carryP[e] = cc.y;
-            inclP[e] = TA * cc.y;
-            inclH[e] = fmaf(TA, cc.x, TB);
-        }
-        if (chunk + 1 < p.nchunks) {
-            ulonglong2* mi = p.incl + (int64_t)tile * 256;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) st_relaxed_v2u64(&mi[e * 32 + lane], tagged(inclP[e], tag), tagged(inclH[e], tag));
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int c = c0 + chan<SPLIT>(e, lane);
-            if (c < p.C) {
-                if (p.tile_prod != nullptr)
-                    p.tile_prod[((int64_t)seq * p.nchunks + chunk) * p.C + c] = carryP[e];
-                if (p.tile_carry != nullptr)
-                    p.tile_carry[((int64_t)seq * p.nchunks + chunk) * p.C + c] = s_cc[e * 32 + lane].x;
-                if (chunk + 1 == p.nchunks) {
-                    if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
-                    if (p.summary != nullptr)
-                        reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
-                            make_float2(inclP[e], inclH[e]);
-                }
+            for (int i = 0; i < 4; ++i) {
+                const float4 m = agg4(w)[i * 32 + qq * LPR + v];
+                EB[i] = ffma2(make_float2(m.x, m.y), EB[i], make_float2(m.z, m.w));
+                EA[i] = fmul2(make_float2(m.x, m.y), EA[i]);
             }
         }
-    }
+    named_sync(1, K::NT);  // the look-back warp has put the carry in s_cc
 
     // ---------------------------------------------------------- phase 2
-    float h[8];
+    float2 h[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = fmaf(EA[e], s_cc[e * 32 + lane].x, EB[e]);
-    const bool ok0 = c0 + chan<SPLIT>(0, lane) < p.C;
-    const bool ok1 = c0 + chan<SPLIT>(4, lane) < p.C;
+    for (int i = 0; i < 4; ++i)
+        h[i] = ffma2(EA[i], make_float2(s_cc[(2 * i) * LPR + v].x, s_cc[(2 * i + 1) * LPR + v].x), EB[i]);
+    const bool ok0 = c0 + chan<SPLIT>(0, v) < p.C;
+    const bool ok1 = c0 + chan<SPLIT>(4, v) < p.C;
     TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
     PS dsp[4];
     if constexpr (K::FORM == FORM_SSD) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dsp[i] = OS::pack(dsk[2 * i], dsk[2 * i + 1]);
+        for (int i = 0; i < 4; ++i) {
+            const int ca = c0 + chan<SPLIT>(2 * i, v), cb = c0 + chan<SPLIT>(2 * i + 1, v);
+            dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
+        }
     }
 #pragma unroll 2
     for (int j = 0; j < rend; ++j, orow += p.ost) {
         const int r = r0 + j;
-        float a[8], b[8];
+        float2 a[4], b[4];
         reload(r, a, b);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = fmaf(a[e], h[e], b[e]);
         PS o[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = OS::pack(h[2 * i], h[2 * i + 1]);  // state in the input dtype
+        for (int i = 0; i < 4; ++i) {
+            h[i] = ffma2(a[i], h[i], b[i]);
+            o[i] = OS::pack(h[i].x, h[i].y);  // state in the input dtype
+        }
         if constexpr (K::FORM == FORM_SSD) {
             PS up[4], cp[4], gp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CB, lane, up);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CB, lane, cp);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CB, lane, gp);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CBW, v, up);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CBW, v, cp);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CBW, v, gp);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 cf = OS::unpack(cp[i]);
-                const float2 gf = OS::unpack(gp[i]);
-                const PS cgs = OS::pack(sigm<TS>(cf.x), sigm<TS>(cf.y));
-                const PS ogs = OS::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
+                const float2 cgs = sig2<TS>(widen(cp[i]));
+                const float2 ogs = sig2<TS>(widen(gp[i]));
                 // (cg * state + D * u) * og, each op in the input dtype
-                o[i] = OS::mul(OS::add(OS::mul(cgs, o[i]), OS::mul(dsp[i], up[i])), ogs);
+                o[i] = OS::mul(OS::add(OS::mul(OS::pack(cgs.x, cgs.y), o[i]), OS::mul(dsp[i], up[i])),
+                               OS::pack(ogs.x, ogs.y));
             }
         } else if constexpr (K::FORM == FORM_RETENTION) {
             PS qp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CB, lane, qp);
+            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CBW, v, qp);
 #pragma unroll
             for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
         }
-        Row8<TS, SPLIT>::stg(orow, lane, o, ok0, ok1);
+        Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
     }
-
 }
 
 }  // namespace need
