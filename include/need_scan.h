@@ -152,7 +152,8 @@ NEED_API int need_recurrent_retention_scan(const need_scan_args* args, need_stre
 NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
 
 /* Bytes of the static scratch array behind need_gated_scan_noalloc: a 128-byte
- * header plus 8 KB of look-back records for each of at most 1024 tiles. */
+ * header plus 8 MiB of look-back records, 32 bytes per channel of each tile
+ * (2048 tiles of 128 channels, or 1024 of 256). */
 #define NEED_GATED_SCAN_NOALLOC_SCRATCH_BYTES (128 + 1024 * 8192)
 
 /* need_gated_scan for callers that cannot allocate device memory where they run
@@ -164,9 +165,9 @@ NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
  * It takes args->workspace / workspace_bytes as unused and instead uses a
  * static device array of NEED_GATED_SCAN_NOALLOC_SCRATCH_BYTES bytes, which
  * every GPU that loads this library holds until the process exits.  A call
- * whose scan needs more scratch than that (more than 1024 tiles of 256
- * channels x need_scan_chunk_len tokens) fails with NEED_ERR_WORKSPACE and
- * launches nothing.  The first call on each device looks up the array's device
+ * whose scan needs more scratch than that (more tiles than the array has
+ * records for; need_scan_workspace_size gives the bytes a scan needs) fails
+ * with NEED_ERR_WORKSPACE and launches nothing.  The first call on each device looks up the array's device
  * address and zero-fills it (a synchronous cudaMemset), so make that first call
  * before any stream capture.  Each call then clears the array's error word on
  * `stream` and launches the same kernel as need_gated_scan.  All calls share

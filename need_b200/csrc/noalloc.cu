@@ -49,12 +49,15 @@ extern "C" int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t
     const size_t need = need_scan_workspace_size(args->form, args->dtype, args->dtype, 0, args->nb, args->nh,
                                                  args->T, args->C);
     if (need == 0) return need::fail(NEED_ERR_UNSUPPORTED, "no kernel for dtype %d", args->dtype);
-    if (need > kScratchBytes)
+    if (need > kScratchBytes) {
+        // one tile of this plan: its records are the workspace of a 1 x 1 x 1 scan past the header
+        const size_t tile_bytes = need_scan_workspace_size(args->form, args->dtype, args->dtype, 0, 1, 1, 1, 1) - 128;
         return need::fail(NEED_ERR_WORKSPACE,
-                          "this scan needs %zu bytes of scratch; the static array holds %zu (at most 1024 tiles "
-                          "of 256 channels x %lld tokens); use need_gated_scan with a workspace",
-                          need, kScratchBytes,
+                          "this scan needs %zu bytes of scratch; the static array holds %zu (at most %zu tiles "
+                          "of %zu channels x %lld tokens); use need_gated_scan with a workspace",
+                          need, kScratchBytes, (kScratchBytes - 128) / tile_bytes, tile_bytes / 32,
                           static_cast<long long>(need_scan_chunk_len(args->form, args->dtype, args->dtype, 0)));
+    }
     void* scratch = nullptr;
     if (int rc = scratch_address(&scratch)) return rc;
     // a bounded wait that gave up in an earlier call must not shorten this call's waits

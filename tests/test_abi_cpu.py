@@ -68,10 +68,10 @@ def test_struct_layout_matches_header(tmp_path):
 
 def test_sizes_and_chunk_lengths(lib):
     L = lib.need_scan_chunk_len(abi.FORM_GATED, abi.BF16, abi.BF16, 0)
-    assert L == 64
+    assert L == 128
     ws = lib.need_scan_workspace_size(abi.FORM_GATED, abi.BF16, abi.BF16, 0, 16, 1, 4096, 1024)
-    ntiles = 16 * 4 * 64
-    assert ws >= ntiles * 4096
+    ntiles = 16 * (1024 // 128) * (4096 // L)  # 128-channel tiles
+    assert ws == 128 + ntiles * 128 * 32  # header + tagged (A, B) and (prod, h) records per channel
     assert lib.need_scan_workspace_size(abi.FORM_GATED, 7, 7, 0, 1, 1, 1, 8) == 0  # unknown dtype
     assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
 
