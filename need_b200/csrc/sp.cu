@@ -7,16 +7,17 @@
 // slice r is
 //     carry_r = B_{r-1} + A_{r-1} * (B_{r-2} + A_{r-2} * ( ... ))
 // and the state entering tile k of the slice is tile_carry[k] +
-// tile_prod[k] * carry_r.  Tiles are independent: one warp per tile rebuilds
-// a and b with the scan's own (rounded) gate arithmetic, runs the recurrence
-// from that corrected fp32 state and rewrites the tile's outputs -- so the
-// result is the whole-sequence scan up to fp32 association, with no second
-// rounding of already-rounded outputs.  A tile whose entering correction is at
-// most 2^-24 * |carry| on every channel is skipped (gated decays lie in
-// [0, 1], so the correction only shrinks from there); with decays in (0, 1)
-// only the leading ~log(2^-24)/log(mean a) tokens of a slice are touched.
+// tile_prod[k] * carry_r.  Tiles are independent: one warp per tile and
+// 32 x kFixLane channels rebuilds a and b with the scan's own (rounded) gate arithmetic,
+// runs the recurrence from that corrected fp32 state and rewrites the tile's
+// outputs -- so the result is the whole-sequence scan up to fp32 association,
+// with no second rounding of already-rounded outputs.  Tiles stop being
+// rewritten once the correction entering them falls below fp32 resolution
+// (kFixTau); with decays in (0, 1) only the leading
+// ~log(2^-24)/log(mean a) tokens of a slice are touched.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
 
 #include "host_common.h"
 #include "need_scan.h"
@@ -43,40 +44,42 @@ struct FixParams {
     float* summary;
 };
 
-// 8 consecutive elements as 4 packed pairs
-template <typename T>
-__device__ __forceinline__ void ld8(const T* p, typename Ops<T>::P (&v)[4]) {
-    using P = typename Ops<T>::P;
-    if constexpr (Ops<T>::BYTES == 4) {
-        const float4 a = *reinterpret_cast<const float4*>(p);
-        const float4 b = *reinterpret_cast<const float4*>(p + 4);
-        v[0] = make_float2(a.x, a.y);
-        v[1] = make_float2(a.z, a.w);
-        v[2] = make_float2(b.x, b.y);
-        v[3] = make_float2(b.z, b.w);
-    } else {
-        const uint4 a = *reinterpret_cast<const uint4*>(p);
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const P*>(&w[i]);
-    }
-}
+// Channels per lane of a fix-up warp (a warp covers 32 x kFixLane channels).
+#ifndef NEED_FIX_LANE
+#define NEED_FIX_LANE 4
+#endif
+constexpr int kFixLane = NEED_FIX_LANE;
+constexpr int kFixChannels = 32 * kFixLane;
+constexpr int kFixPairs = kFixLane / 2;
 
-template <typename T>
-__device__ __forceinline__ void st8(T* p, const typename Ops<T>::P (&v)[4]) {
-    if constexpr (Ops<T>::BYTES == 4) {
-        *reinterpret_cast<float4*>(p) = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
-        *reinterpret_cast<float4*>(p + 4) = make_float4(v[2].x, v[2].y, v[3].x, v[3].y);
-    } else {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(&v[i]);
-        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-}
+// A tile is left alone when the correction entering it is at most 2^-24 *
+// |carry| on every one of its channels (fp32 resolution); gated decays lie in
+// [0, 1], so the correction only shrinks further along the slice.  (Stopping
+// at the 16-bit output's own resolution instead saved only 7% of the fix-up's
+// time on the T=65536 workload, for 20x more outputs that differ by one unit
+// from the whole-sequence scan, so the rule is the same for every dtype.)
+constexpr float kFixTau = 0x1p-24f;
 
-// TS: dtype of the streams and out; TD: dtype of an AFFINE decay.
+// One row's inputs for one lane (kFixLane channels), loaded ahead of their use.
 template <typename TS, typename TD>
+struct RowIn {
+    typename Ops<TS>::P u[3][kFixPairs];  // GATED: z, g, x; AFFINE: u[1] = update
+    typename Ops<TD>::P d[kFixPairs];     // AFFINE decay per channel
+    float dr;                             // AFFINE decay per row
+    bool reset;
+};
+
+// kFixLane consecutive elements as packed pairs
+template <typename T>
+__device__ __forceinline__ void ldp(const T* p, typename Ops<T>::P (&v)[kFixPairs]) {
+    using P = typename Ops<T>::P;
+#pragma unroll
+    for (int i = 0; i < kFixPairs; ++i) v[i] = reinterpret_cast<const P*>(p)[i];
+}
+
+// TS: dtype of the streams and out; TD: dtype of an AFFINE decay; GATED: the
+// form (GATED or AFFINE).
+template <typename TS, typename TD, bool GATED>
 __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     using O = Ops<TS>;
     using PS = typename O::P;
@@ -88,13 +91,13 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     const int seq = chain / p.ncb;
     const int cblk = chain - seq * p.ncb;
     const int bi = seq / p.nh, hi = seq - bi * p.nh;
-    const int c = cblk * CB + lane * 8;
+    const int c = cblk * kFixChannels + lane * kFixLane;
     const bool active = c < p.C;
 
-    float carry[8], h[8];
+    float carry[kFixLane], h[kFixLane];
     bool need = false;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < kFixLane; ++e) {
         carry[e] = 0.0f;
         h[e] = 0.0f;
     }
@@ -103,17 +106,17 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
         for (int j = 0; j < p.rank; ++j) {
             const float2* sj = reinterpret_cast<const float2*>(p.all_summary) + j * nsc + size_t(seq) * p.C + c;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
+            for (int e = 0; e < kFixLane; ++e) {
                 const float2 m = sj[e];
                 carry[e] = fmaf(m.x, carry[e], m.y);
             }
         }
         const size_t ti = (size_t(seq) * p.nchunks + chunk) * p.C + c;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < kFixLane; ++e) {
             const float corr = p.tile_prod[ti + e] * carry[e];
             h[e] = p.tile_carry[ti + e] + corr;
-            need |= p.form == FORM_GATED ? fabsf(corr) > 5.9604645e-8f * fabsf(carry[e]) : corr != 0.0f;
+            need |= GATED ? fabsf(corr) > kFixTau * fabsf(carry[e]) : corr != 0.0f;
         }
     }
     // slice summary / final state: the chunk-0 warp of each chain
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
         const float2* mine = reinterpret_cast<const float2*>(p.all_summary) +
                              size_t(p.rank) * p.nb * p.nh * p.C + size_t(seq) * p.C + c;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < kFixLane; ++e) {
             const float2 m = mine[e];
             const float hl = fmaf(m.x, carry[e], m.y);
             if (p.h_final) p.h_final[size_t(seq) * p.C + c + e] = hl;
@@ -134,64 +137,66 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     const int t0 = chunk * p.L;
     const int nrows = min(p.L, p.T - t0);
     TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + c;
-    for (int r = 0; r < nrows; ++r) {
+    // A warp walks its tile's rows in order; the loads of the next D rows are
+    // in flight while a row is computed (the rows' inputs do not depend on h).
+#ifndef NEED_FIX_DEPTH
+#define NEED_FIX_DEPTH 8
+#endif
+    constexpr int D = Ops<TS>::BYTES == 2 ? NEED_FIX_DEPTH : (NEED_FIX_DEPTH + 1) / 2;
+    RowIn<TS, TD> buf[D];
+    auto load_row = [&](int r, RowIn<TS, TD>& in) {
         const int64_t t = t0 + r;
-        const bool reset = p.seg != nullptr && p.seg[bi * p.sgb + t * p.sgt] != 0;
-        float a[8], b[8];
-        if (p.form == FORM_GATED) {
-            // the scan's gate arithmetic (scan_kernel.cuh, phase 1)
-            PS zp[4], gp[4], xp[4];
-            ld8<TS>(reinterpret_cast<const TS*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, zp);
-            ld8<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, gp);
-            ld8<TS>(reinterpret_cast<const TS*>(p.in[2]) + bi * p.isb[2] + hi * p.ish[2] + t * p.ist[2] + c, xp);
+        in.reset = p.seg != nullptr && p.seg[bi * p.sgb + t * p.sgt] != 0;
+        if constexpr (GATED) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 zf = O::unpack(zp[i]);
-                const float2 gf = O::unpack(gp[i]);
+            for (int k = 0; k < 3; ++k)
+                ldp<TS>(reinterpret_cast<const TS*>(p.in[k]) + bi * p.isb[k] + hi * p.ish[k] + t * p.ist[k] + c, in.u[k]);
+        } else {
+            if (p.rowdec) in.dr = to_f(reinterpret_cast<const TD*>(p.in[0])[bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0]]);
+            else ldp<TD>(reinterpret_cast<const TD*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, in.d);
+            ldp<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, in.u[1]);
+        }
+    };
+    auto compute_row = [&](int r, const RowIn<TS, TD>& in) {
+        PS o[kFixPairs];
+#pragma unroll
+        for (int i = 0; i < kFixPairs; ++i) {
+            float2 a, b;
+            if constexpr (GATED) {
+                // the scan's gate arithmetic (scan_kernel.cuh, phase 1)
+                const float2 zf = O::unpack(in.u[0][i]);
+                const float2 gf = O::unpack(in.u[1][i]);
                 PS ap = O::pack(sigm<TS>(zf.x), sigm<TS>(zf.y));
                 const PS gs = O::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
-                const PS bp = O::mul(O::sub(O::one(), ap), O::mul(gs, xp[i]));
-                if (reset) ap = O::zero();
-                const float2 af = O::unpack(ap), bf = O::unpack(bp);
-                a[2 * i] = af.x;
-                a[2 * i + 1] = af.y;
-                b[2 * i] = bf.x;
-                b[2 * i + 1] = bf.y;
-            }
-        } else {
-            if (p.rowdec) {
-                const float d = to_f(reinterpret_cast<const TD*>(p.in[0])[bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0]]);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) a[e] = d;
+                const PS bp = O::mul(O::sub(O::one(), ap), O::mul(gs, in.u[2][i]));
+                if (in.reset) ap = O::zero();
+                a = O::unpack(ap);
+                b = O::unpack(bp);
             } else {
-                typename Ops<TD>::P dp[4];
-                ld8<TD>(reinterpret_cast<const TD*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, dp);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = Ops<TD>::unpack(dp[i]);
-                    a[2 * i] = f.x;
-                    a[2 * i + 1] = f.y;
-                }
+                a = p.rowdec ? make_float2(in.dr, in.dr) : Ops<TD>::unpack(in.d[i]);
+                if (in.reset) a = make_float2(0.0f, 0.0f);
+                b = O::unpack(in.u[1][i]);
             }
-            if (reset) {
+            h[2 * i] = fmaf(a.x, h[2 * i], b.x);
+            h[2 * i + 1] = fmaf(a.y, h[2 * i + 1], b.y);
+            o[i] = O::pack(h[2 * i], h[2 * i + 1]);
+        }
+        PS* dst = reinterpret_cast<PS*>(orow + (int64_t)(t0 + r) * p.ost);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) a[e] = 0.0f;
-            }
-            PS up[4];
-            ld8<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, up);
+        for (int i = 0; i < kFixPairs; ++i) dst[i] = o[i];
+    };
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 f = O::unpack(up[i]);
-                b[2 * i] = f.x;
-                b[2 * i + 1] = f.y;
+    for (int j = 0; j < D; ++j)
+        if (j < nrows) load_row(j, buf[j]);
+    for (int r0 = 0; r0 < nrows; r0 += D) {
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+            const int r = r0 + j;
+            if (r < nrows) {
+                compute_row(r, buf[j]);
+                if (r + D < nrows) load_row(r + D, buf[j]);
             }
         }
-        PS o[4];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = fmaf(a[e], h[e], b[e]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = O::pack(h[2 * i], h[2 * i + 1]);
-        st8<TS>(orow + t * p.ost, o);
     }
 }
 
@@ -228,7 +233,7 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     p.T = int32_t(a->T);
     p.C = int32_t(a->C);
     p.L = int32_t(L);
-    p.ncb = int32_t((a->C + CB - 1) / CB);
+    p.ncb = int32_t((a->C + kFixChannels - 1) / kFixChannels);
     p.nchains = p.nb * p.nh * p.ncb;
     p.nchunks = int32_t((a->T + L - 1) / L);
     p.ntiles = p.nchains * p.nchunks;
@@ -254,11 +259,15 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     p.summary = a->summary;
     const unsigned blocks = static_cast<unsigned>((p.ntiles + 3) / 4);
     const int dt = a->dtype;
-    if (dt == NEED_BF16 && ddt == NEED_BF16) fixup_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 128, 0, stream>>>(p);
-    else if (dt == NEED_BF16 && ddt == NEED_F32) fixup_kernel<__nv_bfloat16, float><<<blocks, 128, 0, stream>>>(p);
-    else if (dt == NEED_F16 && ddt == NEED_F16) fixup_kernel<__half, __half><<<blocks, 128, 0, stream>>>(p);
-    else if (dt == NEED_F16 && ddt == NEED_F32) fixup_kernel<__half, float><<<blocks, 128, 0, stream>>>(p);
-    else if (dt == NEED_F32 && ddt == NEED_F32) fixup_kernel<float, float><<<blocks, 128, 0, stream>>>(p);
+    auto launch = [&](auto kern) { kern<<<blocks, 128, 0, stream>>>(p); };
+    if (dt == NEED_BF16 && ddt == NEED_BF16)
+        gated ? launch(fixup_kernel<__nv_bfloat16, __nv_bfloat16, true>) : launch(fixup_kernel<__nv_bfloat16, __nv_bfloat16, false>);
+    else if (dt == NEED_BF16 && ddt == NEED_F32 && !gated) launch(fixup_kernel<__nv_bfloat16, float, false>);
+    else if (dt == NEED_F16 && ddt == NEED_F16)
+        gated ? launch(fixup_kernel<__half, __half, true>) : launch(fixup_kernel<__half, __half, false>);
+    else if (dt == NEED_F16 && ddt == NEED_F32 && !gated) launch(fixup_kernel<__half, float, false>);
+    else if (dt == NEED_F32 && ddt == NEED_F32)
+        gated ? launch(fixup_kernel<float, float, true>) : launch(fixup_kernel<float, float, false>);
     else return fail(NEED_ERR_UNSUPPORTED, "dtype %d / decay dtype %d", dt, ddt);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? ok() : cuda_fail(e, "fixup_kernel launch");
