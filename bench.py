@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--no-side", action="store_true", help="skip the sequence-parallel and decode side runs")
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup"], default="prefill",
+                    help="with --profile: which kernel's workload to run (one GPU)")
     return ap.parse_args()
 
 
@@ -225,6 +227,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.profile and args.profile_case != "prefill":
+        profile_side_case(args, dev, nk, sp, workloads)
+        return
+
     w = workloads.prefill(dev, seed=1000 + rank)
     stream = torch.cuda.current_stream(dev)
 
@@ -362,6 +368,33 @@ def run_sp(dev, world, rank, barrier, max_over_ranks, sp, workloads):
     return {"workload": "B=4, T=65536, H=32, D=128 bf16, decay logits~N(5,1), no resets; T split over ranks",
             "tokens_per_s": Bs * Ts / (ms / 1e3), "ms_per_step": ms, "steps": KS,
             "hbm_gbs_per_gpu": byts / world / (ms / 1e3) / 1e9, "scaling": "strong"}
+
+
+def profile_side_case(args, dev, nk, sp, workloads):
+    """One-GPU workloads of the other kernels, for ncu: ``decode`` replays the
+    verify + commit graph of 256 sequences x 4 drafted tokens; ``sp-fixup``
+    scans the 8 slices of a B=1, T=65536, C=4096 sequence, stacks their
+    summaries as the all-gather would and fixes up the last slice."""
+    import torch
+    if args.profile_case == "decode":
+        w = workloads.verify(dev, N=256, C=1024, k=4, seed=11)
+        pool = w.states.clone()
+        y, sk = torch.empty_like(w.x), torch.empty_like(w.x)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk.ragged_verify(pool, w.cu_k, (w.z, w.g, w.x), out=(y, sk))
+            nk.commit_states(pool, sk, w.cu_k, w.accept)
+    else:
+        P, T = 8, 65536
+        locs = []
+        for r in range(P):
+            w = workloads.long_sp(dev, B=1, T=T, H=32, D=128, seed=7, t_begin=r * T // P, t_end=(r + 1) * T // P)
+            locs.append((w, sp.local_scan(w.x, w.z, w.g)))
+        gathered = torch.stack([loc.summary for _, loc in locs])
+        last = locs[-1][1]
+        for _ in range(max(args.warmup, 3) + args.steps):
+            sp.fixup(last, gathered, P, P - 1)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_run": True, "case": args.profile_case}), flush=True)
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):

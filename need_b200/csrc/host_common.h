@@ -39,6 +39,9 @@ inline int cuda_fail(cudaError_t e, const char* what) {
     return fail(NEED_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+// Per-device caches (shared-memory opt-in masks, grid sizes) cover ordinals below this.
+constexpr int kMaxDevices = 64;
+
 // Raises a kernel's dynamic shared-memory limit once per device.
 template <typename Kern>
 inline cudaError_t ensure_smem(Kern kern, int bytes, std::atomic<uint64_t>& done_mask) {

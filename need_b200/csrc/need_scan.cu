@@ -2,6 +2,8 @@
 // validation, TMA descriptor encoding, tile planning and launch.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <atomic>
 #include <climits>
 #include <mutex>
 
@@ -57,6 +59,7 @@ struct Plan {
     int L = 0, R = 0, CB = 0, nin = 0, in0 = 0;  // tokens, rows per warp, channels per tile
     bool dstream = false, split = false;
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
+    int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;  // gated form only
 };
 
 template <class K>
@@ -67,6 +70,34 @@ int launch_cfg(const ScanParams& prm, cudaStream_t s) {
     scan_kernel<K><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch");
+    return NEED_OK;
+}
+
+// The sequence-parallel fix-up: as many CTAs as fit on the device at once
+// (occupancy x SMs, found once per device), striding over the tiles to rewrite.
+template <class K>
+int launch_fix_cfg(const ScanParams& prm, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_done{0};
+    static std::atomic<int> resident[kMaxDevices];
+    cudaError_t e = ensure_smem(scan_kernel<K, true>, K::SMEM, smem_done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel, fix-up)");
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(NEED_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    int ctas = resident[dev].load(std::memory_order_relaxed);
+    if (ctas == 0) {
+        int per_sm = 0, sms = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_kernel<K, true>, K::NT, K::SMEM)) !=
+            cudaSuccess)
+            return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+        ctas = std::max(1, per_sm) * std::max(1, sms);
+        resident[dev].store(ctas, std::memory_order_relaxed);
+    }
+    scan_kernel<K, true><<<std::min(ctas, prm.ntiles), K::NT, K::SMEM, s>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch (fix-up)");
     return NEED_OK;
 }
 
@@ -81,6 +112,7 @@ Plan plan_of() {
     p.dstream = K::HAS_DSTREAM;
     p.split = K::SPLIT;
     p.launch = &launch_cfg<K>;
+    if constexpr (K::FORM == FORM_GATED) p.launch_fix = &launch_fix_cfg<K>;
     return p;
 }
 
@@ -283,6 +315,29 @@ int run(const need_scan_args* a, int form, cudaStream_t s) {
 }
 
 }  // namespace
+
+namespace need {
+// The gated scan kernel in fix-up mode over the slice described by `a`, whose
+// tile_prod / tile_carry the local scan filled (sp.cu prepares fix_carry and
+// fix_chunks).  Writes only the rewritten tiles' outputs.
+int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_chunks,
+                       cudaStream_t stream) {
+    Plan pl;
+    ScanParams P;
+    if (int rc = prepare(a, NEED_FORM_GATED, &pl, &P)) return rc;
+    if (pl.launch_fix == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no fix-up kernel for dtype %d", a->dtype);
+    P.fix_tile_prod = a->tile_prod;
+    P.fix_tile_carry = a->tile_carry;
+    P.fix_carry = fix_carry;
+    P.fix_chunks = fix_chunks;
+    P.tile_prod = nullptr;
+    P.tile_carry = nullptr;
+    P.h_final = nullptr;
+    P.summary = nullptr;
+    P.h0 = nullptr;
+    return pl.launch_fix(P, stream);
+}
+}  // namespace need
 
 // ------------------------------------------------------------------ exported
 extern "C" {

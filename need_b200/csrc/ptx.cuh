@@ -24,6 +24,12 @@ __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's earlier shared-memory accesses (generic proxy) before
+// later TMA writes (async proxy) to the same bytes, when a stage is refilled.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
                      smem_addr(bar)),

@@ -47,7 +47,8 @@ constexpr int CB = 256;  // channel block of the sequence-parallel fix-up tiles
 
 // workspace header words (uint32)
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
-enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_HDR_WORDS = 32 };
+// word 8: leading chunks a sequence-parallel fix-up rewrites
+enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_CHUNKS = 8, WS_HDR_WORDS = 32 };
 enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
 
 constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst case
@@ -77,6 +78,13 @@ struct ScanParams {
     float* tile_prod;
     float* tile_carry;
     uint32_t* hdr;
+    // sequence-parallel fix-up (scan_kernel<K, true>): the local scan's
+    // per-tile entering product and state, the carry entering the slice per
+    // (sequence, channel) in .x, and the number of leading chunks to rewrite
+    const float* fix_tile_prod;
+    const float* fix_tile_carry;
+    const float2* fix_carry;
+    const uint32_t* fix_chunks;
     ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
 };
@@ -345,7 +353,11 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
 }
 
 // ------------------------------------------------------------------ the kernel
-template <class K>
+// FIX = false: the scan, one tile per CTA.  FIX = true: the sequence-parallel
+// fix-up -- the same tile pipeline over the leading fix_chunks chunks of a
+// slice, each tile entered from its known corrected state (no look-back),
+// CTAs striding over those tiles.
+template <class K, bool FIX = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
     using TS = typename K::TS;
     using TD = typename K::TD;
@@ -374,393 +386,416 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     // increasing blockIdx order, so every tile a CTA waits on belongs to a CTA
     // that is already resident or finished -- the property single-pass
     // decoupled look-back scans rely on; the waits are bounded regardless.
-    const int tile = static_cast<int>(blockIdx.x);
     if (tid == 0) {
         for (int w = 0; w < NW; ++w) mbar_init(&s_bar[w], 1);
         mbar_init(s_p1, NW * 32);
         fence_barrier_init();
     }
     __syncthreads();
-    const int chunk = tile / p.nchains;
-    const int chain = tile - chunk * p.nchains;
-    const int seq = chain / p.ncb;
-    const int cblk = chain - seq * p.ncb;
-    const int bi = seq / p.nh, hi = seq - bi * p.nh;
-    const int t0 = chunk * L, c0 = cblk * CBW;
-    const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
+    const int ntl = FIX ? min(p.ntiles, static_cast<int>(*p.fix_chunks) * p.nchains) : p.ntiles;
+    const int stride = FIX ? static_cast<int>(gridDim.x) : p.ntiles;
+    uint32_t par = 0;  // mbarrier phase of this CTA's current tile
+    for (int tile = static_cast<int>(blockIdx.x); tile < ntl; tile += stride, par ^= 1u) {
+        const int chunk = tile / p.nchains;
+        const int chain = tile - chunk * p.nchains;
+        const int seq = chain / p.ncb;
+        const int cblk = chain - seq * p.ncb;
+        const int bi = seq / p.nh, hi = seq - bi * p.nh;
+        const int t0 = chunk * L, c0 = cblk * CBW;
+        const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
 
-    if (warp == K::LB) {
-        // ------------------------------------------------------ look-back warp
-        // It owns no rows.  From the start of the CTA it polls the predecessors'
-        // records -- the maps of the up to kLookbackDepth tiles before this one
-        // and the inclusive state of the tile before those, composed in that
-        // fixed order, so results are bit-reproducible -- while the row warps
-        // load and run phase 1.  It releases the carry to the row warps (named
-        // barrier) as soon as the records are in, publishes this tile's map (AGG)
-        // the moment the row warps' maps are in -- never held back by a
-        // predecessor -- and then the inclusive state.  Records carry the launch
-        // epoch in every 64-bit word, so publishing needs no fence and a poll
-        // returns the data itself.  Lanes >= LPR duplicate lane % LPR and store nothing.
-        const bool act = lane < LPR;
-        uint32_t ep = 0;
-        if (lane == 0) {
-            // Every CTA of a launch gets the same epoch: the low half counts CTAs
-            // in, and the last one to start moves the epoch on for the next launch.
-            unsigned long long* lw = reinterpret_cast<unsigned long long*>(p.hdr + WS_LAUNCH);
-            const unsigned long long old = atomicAdd(lw, 1ull);
-            if (static_cast<uint32_t>(old) == static_cast<uint32_t>(p.ntiles) - 1u)
-                atomicAdd(lw, (1ull << 32) - static_cast<unsigned long long>(p.ntiles));
-            ep = static_cast<uint32_t>(old >> 32);
-        }
-        const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
-        auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
-        float carry[8], carryP[8];
-        float2 TA[4], TB[4];  // this tile's map
-        const int nagg = chunk == 0 ? 0 : min(chunk - 1, kLookbackDepth);
-        bool pread = chunk == 0, mapped = false, agg_pub = chunk == 0;  // chunk 0 publishes no bare map
-        bool released = false;
-        if (chunk == 0) {
+        if (FIX && warp == K::LB) {
+            // ------------------------------------------------------ fix-up carry
+            // The state entering this tile of the slice: the local scan's state plus
+            // the carry entering the slice times the product of a before the tile.
+            const int64_t ti0 = ((int64_t)seq * p.nchunks + chunk) * p.C;
+            if (lane < LPR) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int c = c0 + chan<SPLIT>(e, v);
-                carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
-                carryP[e] = 1.0f;
-            }
-        }
-        auto release = [&]() {
-            if (act) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) s_cc[e * LPR + v] = make_float2(carry[e], carryP[e]);
+                for (int e = 0; e < 8; ++e) {
+                    const int c = c0 + chan<SPLIT>(e, v);
+                    float h = 0.0f;
+                    if (c < p.C) h = fmaf(p.fix_tile_prod[ti0 + c], p.fix_carry[(int64_t)seq * p.C + c].x, p.fix_tile_carry[ti0 + c]);
+                    s_cc[e * LPR + v] = make_float2(h, 0.0f);
+                }
             }
             __syncwarp();
             named_arrive(1, K::NT);  // the row warps may run phase 2
-            released = true;
-        };
-        auto compose_map = [&]() {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                TA[i] = splat2(1.0f);
-                TB[i] = splat2(0.0f);
+        } else if (warp == K::LB) {
+            // ------------------------------------------------------ look-back warp
+            // It owns no rows.  From the start of the CTA it polls the predecessors'
+            // records -- the maps of the up to kLookbackDepth tiles before this one
+            // and the inclusive state of the tile before those, composed in that
+            // fixed order, so results are bit-reproducible -- while the row warps
+            // load and run phase 1.  It releases the carry to the row warps (named
+            // barrier) as soon as the records are in, publishes this tile's map (AGG)
+            // the moment the row warps' maps are in -- never held back by a
+            // predecessor -- and then the inclusive state.  Records carry the launch
+            // epoch in every 64-bit word, so publishing needs no fence and a poll
+            // returns the data itself.  Lanes >= LPR duplicate lane % LPR and store nothing.
+            const bool act = lane < LPR;
+            uint32_t ep = 0;
+            if (lane == 0) {
+                // Every CTA of a launch gets the same epoch: the low half counts CTAs
+                // in, and the last one to start moves the epoch on for the next launch.
+                unsigned long long* lw = reinterpret_cast<unsigned long long*>(p.hdr + WS_LAUNCH);
+                const unsigned long long old = atomicAdd(lw, 1ull);
+                if (static_cast<uint32_t>(old) == static_cast<uint32_t>(p.ntiles) - 1u)
+                    atomicAdd(lw, (1ull << 32) - static_cast<unsigned long long>(p.ntiles));
+                ep = static_cast<uint32_t>(old >> 32);
             }
-            for (int w = 0; w < NW; ++w)
-                for (int qq = 0; qq < SS; ++qq) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float4 m = agg4(w)[i * 32 + qq * LPR + v];
-                        TB[i] = ffma2(make_float2(m.x, m.y), TB[i], make_float2(m.z, m.w));
-                        TA[i] = fmul2(make_float2(m.x, m.y), TA[i]);
-                    }
-                }
-        };
-        if (pread) release();
-        bool ok = false;
-        for (uint32_t it = 0; it < kLookbackPolls; ++it) {
-            bool progressed = false;
-            if (!pread) {
-                bool valid = true;
-                float accA[8], accB[8];
+            const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
+            auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
+            float carry[8], carryP[8];
+            float2 TA[4], TB[4];  // this tile's map
+            const int nagg = chunk == 0 ? 0 : min(chunk - 1, kLookbackDepth);
+            bool pread = chunk == 0, mapped = false, agg_pub = chunk == 0;  // chunk 0 publishes no bare map
+            bool released = false;
+            if (chunk == 0) {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    accA[e] = 1.0f;
-                    accB[e] = 0.0f;
-                }
-                for (int j = 0; j < nagg; ++j) {
-                    const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * CBW;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (A, B)
-                        valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                        accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                        accA[e] = accA[e] * untag(m.x);
-                    }
-                }
-                const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * CBW;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (prod, h)
-                    valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                    carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                    carryP[e] = accA[e] * untag(m.x);
-                }
-                if (__all_sync(0xffffffffu, valid)) {
-                    pread = progressed = true;
-                    release();
+                    const int c = c0 + chan<SPLIT>(e, v);
+                    carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
+                    carryP[e] = 1.0f;
                 }
             }
-            if (!mapped && __all_sync(0xffffffffu, mbar_test_wait(s_p1, 0))) {
-                compose_map();
-                mapped = progressed = true;
-            }
-            if (mapped && pread) {
-                ok = true;
-                break;
-            }
-            if (mapped && !agg_pub) {
-                ulonglong2* my = p.agg + (int64_t)tile * CBW;
+            auto release = [&]() {
                 if (act) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        st_relaxed_v2u64(&my[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
+                    for (int e = 0; e < 8; ++e) s_cc[e * LPR + v] = make_float2(carry[e], carryP[e]);
                 }
-                agg_pub = progressed = true;
-            }
-            if (!progressed && it >= 2) __nanosleep(64);
-            if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
-        }
-        if (!ok) {
-            if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
-            if (!pread) {
+                __syncwarp();
+                named_arrive(1, K::NT);  // the row warps may run phase 2
+                released = true;
+            };
+            auto compose_map = [&]() {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    carry[e] = 0.0f;
-                    carryP[e] = 0.0f;
+                for (int i = 0; i < 4; ++i) {
+                    TA[i] = splat2(1.0f);
+                    TB[i] = splat2(0.0f);
+                }
+                for (int w = 0; w < NW; ++w)
+                    for (int qq = 0; qq < SS; ++qq) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 m = agg4(w)[i * 32 + qq * LPR + v];
+                            TB[i] = ffma2(make_float2(m.x, m.y), TB[i], make_float2(m.z, m.w));
+                            TA[i] = fmul2(make_float2(m.x, m.y), TA[i]);
+                        }
+                    }
+            };
+            if (pread) release();
+            bool ok = false;
+            for (uint32_t it = 0; it < kLookbackPolls; ++it) {
+                bool progressed = false;
+                if (!pread) {
+                    bool valid = true;
+                    float accA[8], accB[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        accA[e] = 1.0f;
+                        accB[e] = 0.0f;
+                    }
+                    for (int j = 0; j < nagg; ++j) {
+                        const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * CBW;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (A, B)
+                            valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                            accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                            accA[e] = accA[e] * untag(m.x);
+                        }
+                    }
+                    const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * CBW;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (prod, h)
+                        valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
+                        carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
+                        carryP[e] = accA[e] * untag(m.x);
+                    }
+                    if (__all_sync(0xffffffffu, valid)) {
+                        pread = progressed = true;
+                        release();
+                    }
+                }
+                if (!mapped && __all_sync(0xffffffffu, mbar_test_wait(s_p1, par))) {
+                    compose_map();
+                    mapped = progressed = true;
+                }
+                if (mapped && pread) {
+                    ok = true;
+                    break;
+                }
+                if (mapped && !agg_pub) {
+                    ulonglong2* my = p.agg + (int64_t)tile * CBW;
+                    if (act) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            st_relaxed_v2u64(&my[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
+                    }
+                    agg_pub = progressed = true;
+                }
+                if (!progressed && it >= 2) __nanosleep(64);
+                if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
+            }
+            if (!ok) {
+                if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
+                if (!pread) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        carry[e] = 0.0f;
+                        carryP[e] = 0.0f;
+                    }
+                }
+                if (!released) release();
+                if (!mapped) {
+                    mbar_wait_bounded(s_p1, par, kTmaPolls);
+                    compose_map();
                 }
             }
-            if (!released) release();
-            if (!mapped) {
-                mbar_wait_bounded(s_p1, 0, kTmaPolls);
-                compose_map();
-            }
-        }
-        // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
-        // the final state, the slice summary and the per-tile products
-        float inclP[8], inclH[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            inclP[e] = el(TA, e) * carryP[e];
-            inclH[e] = fmaf(el(TA, e), carry[e], el(TB, e));
-        }
-        if (act) {
-            if (chunk + 1 < p.nchunks) {
-                ulonglong2* ma = p.agg + (int64_t)tile * CBW;
-                ulonglong2* mi = p.incl + (int64_t)tile * CBW;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    if (!agg_pub) st_relaxed_v2u64(&ma[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
-                    st_relaxed_v2u64(&mi[e * LPR + v], tagged(inclP[e], tag), tagged(inclH[e], tag));
-                }
-            }
+            // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
+            // the final state, the slice summary and the per-tile products
+            float inclP[8], inclH[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                const int c = c0 + chan<SPLIT>(e, v);
-                if (c < p.C) {
-                    const int64_t ti = ((int64_t)seq * p.nchunks + chunk) * p.C + c;
-                    if (p.tile_prod != nullptr) p.tile_prod[ti] = carryP[e];
-                    if (p.tile_carry != nullptr) p.tile_carry[ti] = carry[e];
-                    if (chunk + 1 == p.nchunks) {
-                        if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
-                        if (p.summary != nullptr)
-                            reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
-                                make_float2(inclP[e], inclH[e]);
+                inclP[e] = el(TA, e) * carryP[e];
+                inclH[e] = fmaf(el(TA, e), carry[e], el(TB, e));
+            }
+            if (act) {
+                if (chunk + 1 < p.nchunks) {
+                    ulonglong2* ma = p.agg + (int64_t)tile * CBW;
+                    ulonglong2* mi = p.incl + (int64_t)tile * CBW;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        if (!agg_pub) st_relaxed_v2u64(&ma[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
+                        st_relaxed_v2u64(&mi[e * LPR + v], tagged(inclP[e], tag), tagged(inclH[e], tag));
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int c = c0 + chan<SPLIT>(e, v);
+                    if (c < p.C) {
+                        const int64_t ti = ((int64_t)seq * p.nchunks + chunk) * p.C + c;
+                        if (p.tile_prod != nullptr) p.tile_prod[ti] = carryP[e];
+                        if (p.tile_carry != nullptr) p.tile_carry[ti] = carry[e];
+                        if (chunk + 1 == p.nchunks) {
+                            if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
+                            if (p.summary != nullptr)
+                                reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
+                                    make_float2(inclP[e], inclH[e]);
+                        }
                     }
                 }
             }
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------- row warps
-    // Each warp loads its own R rows (one TMA box per input) and starts on them
-    // as soon as they land, so compute overlaps the rest of the tile's load.
-    const int wr0 = warp * R;                              // this warp's first row
-    const int r0 = wr0 + q * RS;                           // this thread's first row
-    const int rend = max(0, min(RS, nvalid - r0));         // this thread's rows inside T
-    if (lane == 0 && nvalid > wr0) {
-        uint32_t bytes = 0;
+        } else {
+        // ---------------------------------------------------------- row warps
+        // Each warp loads its own R rows (one TMA box per input) and starts on them
+        // as soon as they land, so compute overlaps the rest of the tile's load.
+        const int wr0 = warp * R;                              // this warp's first row
+        const int r0 = wr0 + q * RS;                           // this thread's first row
+        const int rend = max(0, min(RS, nvalid - r0));         // this thread's rows inside T
+        if (lane == 0 && nvalid > wr0) {
+            uint32_t bytes = 0;
 #pragma unroll
-        for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
-        mbar_arrive_expect_tx(&s_bar[warp], bytes);
+            for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
+            mbar_arrive_expect_tx(&s_bar[warp], bytes);
 #pragma unroll
-        for (int k = 0; k < K::NIN; ++k)
-            tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + wr0, hi, bi,
-                        &s_bar[warp]);
-    }
-    // this warp's reset flags and per-row decay while its rows are in flight
-    if (lane < R) {
-        const int r = wr0 + lane, t = t0 + r;
-        uint8_t rs = 0;
-        if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
-        s_reset[r] = rs;
-        if constexpr (K::ROWDEC) {
-            float d = 1.0f;
-            if (t < p.T) d = to_f(reinterpret_cast<const TD*>(p.rowdec)[bi * p.dsb + hi * p.dsh + (int64_t)t * p.dst]);
-            s_rowdec[r] = d;
+            for (int k = 0; k < K::NIN; ++k)
+                tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + wr0, hi, bi,
+                            &s_bar[warp]);
         }
-    }
-    __syncwarp();
-    if (nvalid > wr0 && !mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls)) {
-        atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
-        mbar_wait_bounded(&s_bar[warp], 0, kTmaPolls);
-    }
-
-    // ---------------------------------------------------------- phase 1
-    // a, b of row r as 4 fp32 pairs (channels 2i, 2i+1 of this lane's vector);
-    // `write` stores the rounded a, b back for phase 2.
-    auto gates = [&](int r, bool write, float2 (&a)[4], float2 (&b)[4]) {
-        const bool reset = s_reset[r] != 0;
-        if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
+        // this warp's reset flags and per-row decay while its rows are in flight
+        if (lane < R) {
+            const int r = wr0 + lane, t = t0 + r;
+            uint8_t rs = 0;
+            if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
+            s_reset[r] = rs;
             if constexpr (K::ROWDEC) {
-                const float d = reset ? 0.0f : s_rowdec[r];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) a[i] = splat2(d);
-            } else {
-                typename Ops<TD>::P dp[4];
-                Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CBW, v, dp);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) a[i] = widen(dp[i]);
-                if (reset) {  // uniform across the row group
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) a[i] = splat2(0.0f);
-                }
+                float d = 1.0f;
+                if (t < p.T) d = to_f(reinterpret_cast<const TD*>(p.rowdec)[bi * p.dsb + hi * p.dsh + (int64_t)t * p.dst]);
+                s_rowdec[r] = d;
             }
-            PS up[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CBW, v, up);
+        }
+        __syncwarp();
+        if (nvalid > wr0 && !mbar_wait_bounded(&s_bar[warp], par, kTmaPolls)) {
+            atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+            mbar_wait_bounded(&s_bar[warp], par, kTmaPolls);
+        }
+
+        // ---------------------------------------------------------- phase 1
+        // a, b of row r as 4 fp32 pairs (channels 2i, 2i+1 of this lane's vector);
+        // `write` stores the rounded a, b back for phase 2.
+        auto gates = [&](int r, bool write, float2 (&a)[4], float2 (&b)[4]) {
+            const bool reset = s_reset[r] != 0;
+            if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
+                if constexpr (K::ROWDEC) {
+                    const float d = reset ? 0.0f : s_rowdec[r];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) b[i] = widen(up[i]);
-        } else {
-            // GATED: slots z, g, x.  SSD: slots dt, bg, u (cg, og used in phase 2)
-            TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CBW;
-            TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CBW;
-            TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CBW;
-            PS p0[4], p1[4], p2[4], ap[4], bp[4];
-            Row8<TS, SPLIT>::lds(s0, v, p0);
-            Row8<TS, SPLIT>::lds(s1, v, p1);
-            Row8<TS, SPLIT>::lds(s2, v, p2);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float2 dec;
-                if constexpr (K::FORM == FORM_GATED) {
-                    dec = sig2<TS>(widen(p0[i]));
+                    for (int i = 0; i < 4; ++i) a[i] = splat2(d);
                 } else {
-                    // need_kernels.py:330-332: fp32 dt = dt_min + scale * sigmoid(dt_raw)
-                    // (separately rounded), decay = exp(-dt) rounded to the input dtype
-                    const float2 dt = fadd2(fmul2(sig2<TS>(widen(p0[i])), splat2(p.dt_scale)), splat2(p.dt_min));
-                    dec = exp2_pair<TS>(make_float2(-dt.x, -dt.y));
+                    typename Ops<TD>::P dp[4];
+                    Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CBW, v, dp);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) a[i] = widen(dp[i]);
+                    if (reset) {  // uniform across the row group
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) a[i] = splat2(0.0f);
+                    }
                 }
-                ap[i] = OS::pack(dec.x, dec.y);
-                const float2 g = sig2<TS>(widen(p1[i]));
-                bp[i] = OS::mul(OS::sub(OS::one(), ap[i]), OS::mul(OS::pack(g.x, g.y), p2[i]));
-            }
-            if (reset) {  // uniform across the row group: one branch per row
+                PS up[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CBW, v, up);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) ap[i] = OS::zero();
-            }
+                for (int i = 0; i < 4; ++i) b[i] = widen(up[i]);
+            } else {
+                // GATED: slots z, g, x.  SSD: slots dt, bg, u (cg, og used in phase 2)
+                TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CBW;
+                TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CBW;
+                TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CBW;
+                PS p0[4], p1[4], p2[4], ap[4], bp[4];
+                Row8<TS, SPLIT>::lds(s0, v, p0);
+                Row8<TS, SPLIT>::lds(s1, v, p1);
+                Row8<TS, SPLIT>::lds(s2, v, p2);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i] = widen(ap[i]);
-                b[i] = widen(bp[i]);
-            }
-            if (write) {
-                Row8<TS, SPLIT>::sts(s0, v, ap);  // a over the decay input
-                if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, v, bp);  // b over x
-                else Row8<TS, SPLIT>::sts(s1, v, bp);  // b over b_gate
-            }
-        }
-    };
-    // a, b written back by phase 1
-    auto reload = [&](int r, float2 (&a)[4], float2 (&b)[4]) {
-        if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
-            gates(r, false, a, b);
-        } else {
-            PS ap[4], bp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CBW, v, ap);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CBW, v, bp);
+                for (int i = 0; i < 4; ++i) {
+                    float2 dec;
+                    if constexpr (K::FORM == FORM_GATED) {
+                        dec = sig2<TS>(widen(p0[i]));
+                    } else {
+                        // need_kernels.py:330-332: fp32 dt = dt_min + scale * sigmoid(dt_raw)
+                        // (separately rounded), decay = exp(-dt) rounded to the input dtype
+                        const float2 dt = fadd2(fmul2(sig2<TS>(widen(p0[i])), splat2(p.dt_scale)), splat2(p.dt_min));
+                        dec = exp2_pair<TS>(make_float2(-dt.x, -dt.y));
+                    }
+                    ap[i] = OS::pack(dec.x, dec.y);
+                    const float2 g = sig2<TS>(widen(p1[i]));
+                    bp[i] = OS::mul(OS::sub(OS::one(), ap[i]), OS::mul(OS::pack(g.x, g.y), p2[i]));
+                }
+                if (reset) {  // uniform across the row group: one branch per row
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i] = widen(ap[i]);
-                b[i] = widen(bp[i]);
+                    for (int i = 0; i < 4; ++i) ap[i] = OS::zero();
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    a[i] = widen(ap[i]);
+                    b[i] = widen(bp[i]);
+                }
+                if (write) {
+                    Row8<TS, SPLIT>::sts(s0, v, ap);  // a over the decay input
+                    if constexpr (K::FORM == FORM_GATED) Row8<TS, SPLIT>::sts(s2, v, bp);  // b over x
+                    else Row8<TS, SPLIT>::sts(s1, v, bp);  // b over b_gate
+                }
             }
-        }
-    };
+        };
+        // a, b written back by phase 1
+        auto reload = [&](int r, float2 (&a)[4], float2 (&b)[4]) {
+            if constexpr (K::FORM == FORM_AFFINE || K::FORM == FORM_RETENTION) {
+                gates(r, false, a, b);
+            } else {
+                PS ap[4], bp[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CBW, v, ap);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CBW, v, bp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    a[i] = widen(ap[i]);
+                    b[i] = widen(bp[i]);
+                }
+            }
+        };
 
-    float2 A[4], B[4];  // this thread's map, channel pairs
+        float2 A[4], B[4];  // this thread's map, channel pairs
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        A[i] = splat2(1.0f);
-        B[i] = splat2(0.0f);
-    }
+        for (int i = 0; i < 4; ++i) {
+            A[i] = splat2(1.0f);
+            B[i] = splat2(0.0f);
+        }
 #pragma unroll 2
-    for (int j = 0; j < rend; ++j) {  // rows past T act as the identity
-        float2 a[4], b[4];
-        gates(r0 + j, true, a, b);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            B[i] = ffma2(a[i], B[i], b[i]);
-            A[i] = fmul2(a[i], A[i]);
-        }
-    }
-    if constexpr (K::AGG_SLOT >= 0) __syncwarp();  // every lane is done with the slot rows the map overwrites
-#pragma unroll
-    for (int i = 0; i < 4; ++i) agg4(warp)[i * 32 + lane] = make_float4(A[i].x, A[i].y, B[i].x, B[i].y);
-    mbar_arrive(s_p1);
-    if (!mbar_wait_bounded(s_p1, 0, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
-
-    // ---------------------------------------------------------- compose
-    float2 EA[4], EB[4];  // map of the rows before this thread's rows
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        EA[i] = splat2(1.0f);
-        EB[i] = splat2(0.0f);
-    }
-    for (int w = 0; w <= warp; ++w)
-        for (int qq = 0; qq < (w < warp ? SS : q); ++qq) {
+        for (int j = 0; j < rend; ++j) {  // rows past T act as the identity
+            float2 a[4], b[4];
+            gates(r0 + j, true, a, b);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float4 m = agg4(w)[i * 32 + qq * LPR + v];
-                EB[i] = ffma2(make_float2(m.x, m.y), EB[i], make_float2(m.z, m.w));
-                EA[i] = fmul2(make_float2(m.x, m.y), EA[i]);
+                B[i] = ffma2(a[i], B[i], b[i]);
+                A[i] = fmul2(a[i], A[i]);
             }
         }
-    named_sync(1, K::NT);  // the look-back warp has put the carry in s_cc
+        if constexpr (K::AGG_SLOT >= 0) __syncwarp();  // every lane is done with the slot rows the map overwrites
+#pragma unroll
+        for (int i = 0; i < 4; ++i) agg4(warp)[i * 32 + lane] = make_float4(A[i].x, A[i].y, B[i].x, B[i].y);
+        mbar_arrive(s_p1);
+        if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
 
-    // ---------------------------------------------------------- phase 2
-    float2 h[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        h[i] = ffma2(EA[i], make_float2(s_cc[(2 * i) * LPR + v].x, s_cc[(2 * i + 1) * LPR + v].x), EB[i]);
-    const bool ok0 = c0 + chan<SPLIT>(0, v) < p.C;
-    const bool ok1 = c0 + chan<SPLIT>(4, v) < p.C;
-    TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
-    PS dsp[4];
-    if constexpr (K::FORM == FORM_SSD) {
+        // ---------------------------------------------------------- compose
+        float2 EA[4], EB[4];  // map of the rows before this thread's rows
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int ca = c0 + chan<SPLIT>(2 * i, v), cb = c0 + chan<SPLIT>(2 * i + 1, v);
-            dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
+            EA[i] = splat2(1.0f);
+            EB[i] = splat2(0.0f);
         }
-    }
-#pragma unroll 2
-    for (int j = 0; j < rend; ++j, orow += p.ost) {
-        const int r = r0 + j;
-        float2 a[4], b[4];
-        reload(r, a, b);
-        PS o[4];
+        for (int w = 0; w <= warp; ++w)
+            for (int qq = 0; qq < (w < warp ? SS : q); ++qq) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            h[i] = ffma2(a[i], h[i], b[i]);
-            o[i] = OS::pack(h[i].x, h[i].y);  // state in the input dtype
-        }
+                for (int i = 0; i < 4; ++i) {
+                    const float4 m = agg4(w)[i * 32 + qq * LPR + v];
+                    EB[i] = ffma2(make_float2(m.x, m.y), EB[i], make_float2(m.z, m.w));
+                    EA[i] = fmul2(make_float2(m.x, m.y), EA[i]);
+                }
+            }
+        named_sync(1, K::NT);  // the look-back warp has put the carry in s_cc
+
+        // ---------------------------------------------------------- phase 2
+        float2 h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            h[i] = ffma2(EA[i], make_float2(s_cc[(2 * i) * LPR + v].x, s_cc[(2 * i + 1) * LPR + v].x), EB[i]);
+        const bool ok0 = c0 + chan<SPLIT>(0, v) < p.C;
+        const bool ok1 = c0 + chan<SPLIT>(4, v) < p.C;
+        TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
+        PS dsp[4];
         if constexpr (K::FORM == FORM_SSD) {
-            PS up[4], cp[4], gp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CBW, v, up);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CBW, v, cp);
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CBW, v, gp);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float2 cgs = sig2<TS>(widen(cp[i]));
-                const float2 ogs = sig2<TS>(widen(gp[i]));
-                // (cg * state + D * u) * og, each op in the input dtype
-                o[i] = OS::mul(OS::add(OS::mul(OS::pack(cgs.x, cgs.y), o[i]), OS::mul(dsp[i], up[i])),
-                               OS::pack(ogs.x, ogs.y));
+                const int ca = c0 + chan<SPLIT>(2 * i, v), cb = c0 + chan<SPLIT>(2 * i + 1, v);
+                dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
             }
-        } else if constexpr (K::FORM == FORM_RETENTION) {
-            PS qp[4];
-            Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CBW, v, qp);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
         }
-        Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
-    }
+#pragma unroll 2
+        for (int j = 0; j < rend; ++j, orow += p.ost) {
+            const int r = r0 + j;
+            float2 a[4], b[4];
+            reload(r, a, b);
+            PS o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                h[i] = ffma2(a[i], h[i], b[i]);
+                o[i] = OS::pack(h[i].x, h[i].y);  // state in the input dtype
+            }
+            if constexpr (K::FORM == FORM_SSD) {
+                PS up[4], cp[4], gp[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CBW, v, up);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CBW, v, cp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CBW, v, gp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 cgs = sig2<TS>(widen(cp[i]));
+                    const float2 ogs = sig2<TS>(widen(gp[i]));
+                    // (cg * state + D * u) * og, each op in the input dtype
+                    o[i] = OS::mul(OS::add(OS::mul(OS::pack(cgs.x, cgs.y), o[i]), OS::mul(dsp[i], up[i])),
+                                   OS::pack(ogs.x, ogs.y));
+                }
+            } else if constexpr (K::FORM == FORM_RETENTION) {
+                PS qp[4];
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CBW, v, qp);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
+            }
+            Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
+        }
+        }  // row warps
+        if constexpr (FIX) {  // the stage is refilled by the next tile's TMA
+            fence_proxy_async_shared();
+            __syncthreads();
+        }
+    }  // tiles
 }
 
 }  // namespace need

@@ -7,14 +7,19 @@
 // slice r is
 //     carry_r = B_{r-1} + A_{r-1} * (B_{r-2} + A_{r-2} * ( ... ))
 // and the state entering tile k of the slice is tile_carry[k] +
-// tile_prod[k] * carry_r.  Tiles are independent: one warp per tile and
-// 32 x kFixLane channels rebuilds a and b with the scan's own (rounded) gate arithmetic,
-// runs the recurrence from that corrected fp32 state and rewrites the tile's
-// outputs -- so the result is the whole-sequence scan up to fp32 association,
-// with no second rounding of already-rounded outputs.  Tiles stop being
-// rewritten once the correction entering them falls below fp32 resolution
-// (kFixTau); with decays in (0, 1) only the leading
-// ~log(2^-24)/log(mean a) tokens of a slice are touched.
+// tile_prod[k] * carry_r.  The fix-up rebuilds a and b of the leading tiles
+// with the scan's own (rounded) arithmetic, runs the recurrence from that
+// corrected fp32 state and rewrites those tiles' outputs -- so the result is
+// the whole-sequence scan up to fp32 association, with no second rounding of
+// already-rounded outputs.  Tiles stop being rewritten once the correction
+// entering them is at most 2^-24 * |carry| (kFixTau) on every channel; with
+// decays in (0, 1) only the leading ~log(2^-24)/log(mean a) tokens of a slice
+// are touched.
+//
+// The gated form runs the scan kernel itself in fix-up mode (TMA tiles, the
+// row warps' two-phase scan) over those leading chunks, after
+// fix_prepare_kernel has composed the carries and counted the chunks.  The
+// affine form uses fixup_kernel: one warp per tile walks the rows in order.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -31,7 +36,7 @@ struct FixParams {
     int32_t form, rowdec;
     int32_t nb, nh, T, C, L, ncb, nchains, nchunks, ntiles;
     int32_t nranks, rank;
-    const void* in[3];  // GATED: z, g, x; AFFINE: decay (full or per row), update
+    const void* in[2];  // decay (full or per row), update
     int64_t isb[3], ish[3], ist[3];
     void* out;
     int64_t osb, osh, ost;
@@ -63,9 +68,9 @@ constexpr float kFixTau = 0x1p-24f;
 // One row's inputs for one lane (kFixLane channels), loaded ahead of their use.
 template <typename TS, typename TD>
 struct RowIn {
-    typename Ops<TS>::P u[3][kFixPairs];  // GATED: z, g, x; AFFINE: u[1] = update
-    typename Ops<TD>::P d[kFixPairs];     // AFFINE decay per channel
-    float dr;                             // AFFINE decay per row
+    typename Ops<TS>::P u[kFixPairs];  // update
+    typename Ops<TD>::P d[kFixPairs];  // decay per channel
+    float dr;                          // decay per row
     bool reset;
 };
 
@@ -77,9 +82,9 @@ __device__ __forceinline__ void ldp(const T* p, typename Ops<T>::P (&v)[kFixPair
     for (int i = 0; i < kFixPairs; ++i) v[i] = reinterpret_cast<const P*>(p)[i];
 }
 
-// TS: dtype of the streams and out; TD: dtype of an AFFINE decay; GATED: the
-// form (GATED or AFFINE).
-template <typename TS, typename TD, bool GATED>
+// The affine form's fix-up.  TS: dtype of the update stream and out; TD:
+// dtype of the decay.
+template <typename TS, typename TD>
 __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     using O = Ops<TS>;
     using PS = typename O::P;
@@ -116,7 +121,7 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
         for (int e = 0; e < kFixLane; ++e) {
             const float corr = p.tile_prod[ti + e] * carry[e];
             h[e] = p.tile_carry[ti + e] + corr;
-            need |= GATED ? fabsf(corr) > kFixTau * fabsf(carry[e]) : corr != 0.0f;
+            need |= corr != 0.0f;  // affine decays may exceed 1: any correction counts
         }
     }
     // slice summary / final state: the chunk-0 warp of each chain
@@ -147,36 +152,17 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     auto load_row = [&](int r, RowIn<TS, TD>& in) {
         const int64_t t = t0 + r;
         in.reset = p.seg != nullptr && p.seg[bi * p.sgb + t * p.sgt] != 0;
-        if constexpr (GATED) {
-#pragma unroll
-            for (int k = 0; k < 3; ++k)
-                ldp<TS>(reinterpret_cast<const TS*>(p.in[k]) + bi * p.isb[k] + hi * p.ish[k] + t * p.ist[k] + c, in.u[k]);
-        } else {
-            if (p.rowdec) in.dr = to_f(reinterpret_cast<const TD*>(p.in[0])[bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0]]);
-            else ldp<TD>(reinterpret_cast<const TD*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, in.d);
-            ldp<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, in.u[1]);
-        }
+        if (p.rowdec) in.dr = to_f(reinterpret_cast<const TD*>(p.in[0])[bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0]]);
+        else ldp<TD>(reinterpret_cast<const TD*>(p.in[0]) + bi * p.isb[0] + hi * p.ish[0] + t * p.ist[0] + c, in.d);
+        ldp<TS>(reinterpret_cast<const TS*>(p.in[1]) + bi * p.isb[1] + hi * p.ish[1] + t * p.ist[1] + c, in.u);
     };
     auto compute_row = [&](int r, const RowIn<TS, TD>& in) {
         PS o[kFixPairs];
 #pragma unroll
         for (int i = 0; i < kFixPairs; ++i) {
-            float2 a, b;
-            if constexpr (GATED) {
-                // the scan's gate arithmetic (scan_kernel.cuh, phase 1)
-                const float2 zf = O::unpack(in.u[0][i]);
-                const float2 gf = O::unpack(in.u[1][i]);
-                PS ap = O::pack(sigm<TS>(zf.x), sigm<TS>(zf.y));
-                const PS gs = O::pack(sigm<TS>(gf.x), sigm<TS>(gf.y));
-                const PS bp = O::mul(O::sub(O::one(), ap), O::mul(gs, in.u[2][i]));
-                if (in.reset) ap = O::zero();
-                a = O::unpack(ap);
-                b = O::unpack(bp);
-            } else {
-                a = p.rowdec ? make_float2(in.dr, in.dr) : Ops<TD>::unpack(in.d[i]);
-                if (in.reset) a = make_float2(0.0f, 0.0f);
-                b = O::unpack(in.u[1][i]);
-            }
+            float2 a = p.rowdec ? make_float2(in.dr, in.dr) : Ops<TD>::unpack(in.d[i]);
+            if (in.reset) a = make_float2(0.0f, 0.0f);
+            const float2 b = O::unpack(in.u[i]);
             h[2 * i] = fmaf(a.x, h[2 * i], b.x);
             h[2 * i + 1] = fmaf(a.y, h[2 * i + 1], b.y);
             o[i] = O::pack(h[2 * i], h[2 * i + 1]);
@@ -200,7 +186,38 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     }
 }
 
+// Per (sequence, channel): the carry entering this slice, composed from the
+// gathered maps of the ranks before it; the slice's final state and summary;
+// and how many leading chunks still see a correction above fp32 resolution
+// (the maximum over channels goes to fix_chunks).
+__global__ void __launch_bounds__(256) fix_prepare_kernel(int64_t nsc, int32_t C, int32_t nchunks, int32_t rank,
+                                                          const float2* all_summary, const float* tile_prod,
+                                                          float* h_final, float2* summary, float2* fix_carry,
+                                                          uint32_t* fix_chunks) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= nsc) return;
+    const int64_t seq = i / C, c = i - seq * C;
+    float carry = 0.0f;
+    for (int j = 0; j < rank; ++j) {
+        const float2 m = all_summary[j * nsc + i];
+        carry = fmaf(m.x, carry, m.y);
+    }
+    fix_carry[i] = make_float2(carry, 0.0f);
+    const float2 mine = all_summary[rank * nsc + i];
+    const float hl = fmaf(mine.x, carry, mine.y);
+    if (h_final != nullptr) h_final[i] = hl;
+    if (summary != nullptr) summary[i] = make_float2(mine.x, hl);
+    int k = 0;
+    while (k < nchunks && fabsf(tile_prod[(seq * nchunks + k) * C + c] * carry) > kFixTau * fabsf(carry)) ++k;
+    if (k > 0) atomicMax(fix_chunks, static_cast<uint32_t>(k));
+}
+
 }  // namespace
+
+namespace need {
+int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_chunks,
+                       cudaStream_t stream);
+}
 
 extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, int32_t nranks, int32_t rank,
                              need_stream_t stream) {
@@ -224,6 +241,26 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
         if (!(k == 0 && rd) && !aligned16(a->in[k].ptr)) return fail(NEED_ERR_UNSUPPORTED, "in[%d] is not 16-byte aligned", k);
     }
     if (rank == 0) return ok();  // no carry enters the first slice
+
+    if (gated) {
+        // The gated form re-scans the leading tiles with the scan kernel itself
+        // (fix-up mode); its scratch is the caller's scan workspace.
+        const int64_t nsc = a->nb * a->nh * a->C;
+        const size_t need = size_t(WS_HDR_WORDS) * 4 + size_t(nsc) * sizeof(float2);
+        if (a->workspace == nullptr || !aligned16(a->workspace) || a->workspace_bytes < need)
+            return fail(NEED_ERR_WORKSPACE, "the fix-up needs a scan workspace of at least %zu bytes", need);
+        uint32_t* hdr = static_cast<uint32_t*>(a->workspace);
+        float2* fix_carry = reinterpret_cast<float2*>(static_cast<unsigned char*>(a->workspace) + WS_HDR_WORDS * 4);
+        cudaError_t e = cudaMemsetAsync(hdr + WS_FIX_CHUNKS, 0, sizeof(uint32_t), stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(fix-up chunk count)");
+        const int32_t nchunks = int32_t((a->T + L - 1) / L);
+        fix_prepare_kernel<<<static_cast<unsigned>((nsc + 255) / 256), 256, 0, stream>>>(
+            nsc, int32_t(a->C), nchunks, rank, reinterpret_cast<const float2*>(all_summary), a->tile_prod,
+            a->h_final, reinterpret_cast<float2*>(a->summary), fix_carry, hdr + WS_FIX_CHUNKS);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "fix_prepare_kernel launch");
+        if (int rc = gated_fixup_launch(a, fix_carry, hdr + WS_FIX_CHUNKS, stream)) return rc;
+        return ok();
+    }
 
     FixParams p{};
     p.form = a->form;
@@ -259,15 +296,11 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     p.summary = a->summary;
     const unsigned blocks = static_cast<unsigned>((p.ntiles + 3) / 4);
     const int dt = a->dtype;
-    auto launch = [&](auto kern) { kern<<<blocks, 128, 0, stream>>>(p); };
-    if (dt == NEED_BF16 && ddt == NEED_BF16)
-        gated ? launch(fixup_kernel<__nv_bfloat16, __nv_bfloat16, true>) : launch(fixup_kernel<__nv_bfloat16, __nv_bfloat16, false>);
-    else if (dt == NEED_BF16 && ddt == NEED_F32 && !gated) launch(fixup_kernel<__nv_bfloat16, float, false>);
-    else if (dt == NEED_F16 && ddt == NEED_F16)
-        gated ? launch(fixup_kernel<__half, __half, true>) : launch(fixup_kernel<__half, __half, false>);
-    else if (dt == NEED_F16 && ddt == NEED_F32 && !gated) launch(fixup_kernel<__half, float, false>);
-    else if (dt == NEED_F32 && ddt == NEED_F32)
-        gated ? launch(fixup_kernel<float, float, true>) : launch(fixup_kernel<float, float, false>);
+    if (dt == NEED_BF16 && ddt == NEED_BF16) fixup_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 128, 0, stream>>>(p);
+    else if (dt == NEED_BF16 && ddt == NEED_F32) fixup_kernel<__nv_bfloat16, float><<<blocks, 128, 0, stream>>>(p);
+    else if (dt == NEED_F16 && ddt == NEED_F16) fixup_kernel<__half, __half><<<blocks, 128, 0, stream>>>(p);
+    else if (dt == NEED_F16 && ddt == NEED_F32) fixup_kernel<__half, float><<<blocks, 128, 0, stream>>>(p);
+    else if (dt == NEED_F32 && ddt == NEED_F32) fixup_kernel<float, float><<<blocks, 128, 0, stream>>>(p);
     else return fail(NEED_ERR_UNSUPPORTED, "dtype %d / decay dtype %d", dt, ddt);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? ok() : cuda_fail(e, "fixup_kernel launch");

@@ -78,8 +78,15 @@ def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> 
     ``loc.summary``.  ``all_summary`` is [nranks, B, C, 2] fp32 on this device."""
     all_summary = all_summary.contiguous()
     dev = loc.out.device
-    abi.check("need_sp_fixup", nk._lib().need_sp_fixup(
-        ctypes.byref(loc.args), all_summary.data_ptr(), int(nranks), int(rank), nk._stream(dev)))
+    a = loc.args
+    lib = nk._lib()
+    # scratch for the fix-up: this stream's scan workspace, which may have been
+    # replaced since the local scan ran
+    nbytes = lib.need_scan_workspace_size(a.form, a.dtype, a.decay_dtype, 0, a.nb, a.nh, a.T, a.C)
+    ws = nk.workspace(dev, nbytes)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    abi.check("need_sp_fixup", lib.need_sp_fixup(
+        ctypes.byref(a), all_summary.data_ptr(), int(nranks), int(rank), nk._stream(dev)))
 
 
 def sp_gated_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Tensor, *,
