@@ -207,8 +207,20 @@ __global__ void __launch_bounds__(256) fix_prepare_kernel(int64_t nsc, int32_t C
     const float hl = fmaf(mine.x, carry, mine.y);
     if (h_final != nullptr) h_final[i] = hl;
     if (summary != nullptr) summary[i] = make_float2(mine.x, hl);
+    // tile_prod only shrinks along the slice: the count is the first chunk
+    // whose correction is negligible, found 8 chunks (8 independent loads) at a time
+    const float lim = kFixTau * fabsf(carry);
     int k = 0;
-    while (k < nchunks && fabsf(tile_prod[(seq * nchunks + k) * C + c] * carry) > kFixTau * fabsf(carry)) ++k;
+    for (int k0 = 0; k0 < nchunks; k0 += 8) {
+        float pr[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pr[j] = k0 + j < nchunks ? tile_prod[(seq * nchunks + k0 + j) * C + c] : 0.0f;
+        int j = 0;
+        while (j < 8 && fabsf(pr[j] * carry) > lim) ++j;
+        k = k0 + j;
+        if (j < 8) break;
+    }
+    k = min(k, nchunks);
     if (k > 0) atomicMax(fix_chunks, static_cast<uint32_t>(k));
 }
 
