@@ -59,6 +59,10 @@ constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst 
 constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
 static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
+// registers per thread the occupancy bound plans for
+#ifndef NEED_REG_BUDGET
+#define NEED_REG_BUDGET 112
+#endif
 
 struct ScanParams {
     CUtensorMap tm[5];  // streamed inputs (64-byte aligned members)
@@ -337,9 +341,10 @@ struct ScanCfg {
     static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
     static constexpr int SMEM = OFF_MISC + (NW + 1) * 8 + 16 + 128;  // mbarriers, misc, alignment slack
     // resident CTAs per SM: bounded by shared memory (228 KB per SM, 1 KB
-    // reserved per CTA) and by ~112 registers per thread
+    // reserved per CTA) and by a register budget per thread
     static constexpr int MINB_SMEM = (228 * 1024) / (SMEM + 1024);
-    static constexpr int MINB_CAP = 65536 / (NT * 112) < 1 ? 1 : (65536 / (NT * 112) > 8 ? 8 : 65536 / (NT * 112));
+    static constexpr int MINB_REGS = 65536 / (NT * NEED_REG_BUDGET);
+    static constexpr int MINB_CAP = MINB_REGS < 1 ? 1 : (MINB_REGS > 8 ? 8 : MINB_REGS);
     static constexpr int MINB = MINB_SMEM < 1 ? 1 : (MINB_SMEM < MINB_CAP ? MINB_SMEM : MINB_CAP);
 };
 
