@@ -310,6 +310,7 @@ def main():
     if not args.no_side:
         side["sequence_parallel"] = run_sp(dev, world, rank, barrier, max_over_ranks, sp, workloads)
         side["decode_verify"] = run_decode(dev, nk, workloads, barrier, max_over_ranks)
+        side["affine_backward"] = run_backward(dev, nk, barrier, max_over_ranks)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -395,6 +396,44 @@ def profile_side_case(args, dev, nk, sp, workloads):
             sp.fixup(last, gathered, P, P - 1)
     torch.cuda.synchronize()
     print(json.dumps({"profile_run": True, "case": args.profile_case}), flush=True)
+
+
+def run_backward(dev, nk, barrier, max_over_ranks):
+    """Backward of affine_recurrence_scan at the prefill shape (B=16, T=4096,
+    C=1024, bf16): the reversed-time adjoint scan alone (reads decay and the
+    output gradient, writes the update gradient: 6 B per token-channel), and a
+    whole scan training step (forward + backward through autograd)."""
+    import torch
+    g0 = torch.Generator(device=dev).manual_seed(21)
+    shape = (B, T, C)
+    decay = torch.sigmoid(torch.randn(shape, device=dev, generator=g0) + 4.0).to(torch.bfloat16)
+    update = torch.randn(shape, device=dev, generator=g0).to(torch.bfloat16)
+    g = torch.randn(shape, device=dev, generator=g0).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, k):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / k
+
+    adj_ms = timed(lambda: nk._affine_adjoint(decay, g, 1), 20)
+    d_req, u_req = decay.clone().requires_grad_(True), update.clone().requires_grad_(True)
+
+    def train_step():
+        d_req.grad = u_req.grad = None
+        nk.affine_recurrence_scan(d_req, u_req).backward(g)
+
+    step_ms = timed(train_step, 10)
+    return {"workload": "affine scan backward, B=16, T=4096, C=1024 bf16, decay=sigmoid(N(4,1))",
+            "adjoint_ms": adj_ms, "adjoint_hbm_gbs": B * T * C * 6 / (adj_ms / 1e3) / 1e9,
+            "fwd_bwd_ms": step_ms, "fwd_bwd_tokens_per_s": B * T / (step_ms / 1e3)}
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):

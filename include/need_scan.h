@@ -23,6 +23,8 @@
  *   need_commit_states           <- keeping the state at the accepted prefix
  *                                   (generate.py:1078-1083 appends the accepted tokens)
  *   need_sp_fixup                <- no counterpart (sequence-parallel extension)
+ *   need_affine_recurrence_scan_backward <- no counterpart (the reference differentiates
+ *                                   its scan with torch autograd, need_kernels.py:177-226)
  *
  * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
  * message for the calling thread's last failure.  All entry points are
@@ -139,6 +141,20 @@ NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_str
 /* need_kernels.affine_recurrence_scan (need_kernels.py:229-264): args->form must be
  * NEED_FORM_AFFINE. */
 NEED_API int need_affine_recurrence_scan(const need_scan_args* args, need_stream_t stream);
+
+/* The backward of need_affine_recurrence_scan: no counterpart in the reference,
+ * whose gradient is torch autograd through the chunked CPU scan
+ * (need_kernels.py:177-226) or through torch's associative_scan on CUDA
+ * (need_kernels.py:245-262).  For h_t = a_t h_{t-1} + b_t and the output
+ * gradient g it writes the adjoint
+ *     lam_t = g_t + a_{t+1} lam_{t+1}   (lam_{T-1} = g_{T-1}),
+ * which is the gradient of b; the gradient of a is lam_t * h_{t-1}.
+ * args->form = NEED_FORM_AFFINE; in[0] is the forward's decay (per channel or
+ * per row, as for the forward), in[1] is g, out receives lam (dtype `dtype`),
+ * h_final optionally receives lam_0 in fp32 (the gradient of an initial state
+ * is a_0 lam_0).  seg_start, h0, summary and the tile records must be null;
+ * T >= 2.  Workspace as for the forward. */
+NEED_API int need_affine_recurrence_scan_backward(const need_scan_args* args, need_stream_t stream);
 
 /* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
 NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);

@@ -58,6 +58,7 @@ SIGNATURES = {
     "need_scan_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int64, c_int64, c_int64, c_int64]),
     "need_workspace_error": (c_int32, [c_void_p, POINTER(c_uint32), c_void_p]),
     "need_affine_recurrence_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

@@ -60,6 +60,7 @@ struct Plan {
     bool dstream = false, split = false;
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
     int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;  // gated form only
+    int (*launch_rev)(const ScanParams&, cudaStream_t) = nullptr;  // affine form only
 };
 
 template <class K>
@@ -101,6 +102,18 @@ int launch_fix_cfg(const ScanParams& prm, cudaStream_t s) {
     return NEED_OK;
 }
 
+// The reversed-time scan (the backward's adjoint recurrence), one tile per CTA.
+template <class K>
+int launch_rev_cfg(const ScanParams& prm, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_done{0};
+    cudaError_t e = ensure_smem(scan_kernel<K, false, true>, K::SMEM, smem_done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel, reversed)");
+    scan_kernel<K, false, true><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch (reversed)");
+    return NEED_OK;
+}
+
 template <class K>
 Plan plan_of() {
     Plan p;
@@ -113,6 +126,7 @@ Plan plan_of() {
     p.split = K::SPLIT;
     p.launch = &launch_cfg<K>;
     if constexpr (K::FORM == FORM_GATED) p.launch_fix = &launch_fix_cfg<K>;
+    if constexpr (K::FORM == FORM_AFFINE) p.launch_rev = &launch_rev_cfg<K>;
     return p;
 }
 
@@ -232,7 +246,9 @@ int check_sizes(const need_scan_args* a) {
 }
 
 // Validates `a` and fills the kernel parameters.
-int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
+// rev: the backward's reversed scan -- a streamed decay (in[0]) is viewed from
+// row 1 with T-1 rows, so row t reads a_{t+1} and row T-1 reads the zero fill.
+int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, bool rev = false) {
     if (a == nullptr) return fail(NEED_ERR_INVALID, "args is null");
     if (a->form != expect_form) return fail(NEED_ERR_INVALID, "args->form %d does not match the entry point", a->form);
     if (int rc = check_sizes(a)) return rc;
@@ -250,7 +266,13 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P) {
     memset(P, 0, sizeof(*P));
     for (int k = 0; k < pl->nin; ++k) {
         const int dt = (pl->dstream && k == 0) ? ddt : a->dtype;
-        if (int rc = encode_view(&P->tm[k], a->in[pl->in0 + k], dt, a->nb, a->nh, a->T, a->C, pl->CB, pl->R, pl->in0 + k))
+        need_view view = a->in[pl->in0 + k];
+        int64_t rows = a->T;
+        if (rev && pl->dstream && k == 0) {
+            view.ptr = static_cast<const unsigned char*>(view.ptr) + view.stride_t * dtype_bytes(dt);
+            rows = a->T - 1;
+        }
+        if (int rc = encode_view(&P->tm[k], view, dt, a->nb, a->nh, rows, a->C, pl->CB, pl->R, pl->in0 + k))
             return rc;
     }
     if (rowdec_form && rd) {
@@ -374,6 +396,20 @@ int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t str
 
 int need_affine_recurrence_scan(const need_scan_args* args, need_stream_t stream) {
     return run(args, NEED_FORM_AFFINE, stream);
+}
+
+int need_affine_recurrence_scan_backward(const need_scan_args* args, need_stream_t stream) {
+    if (args == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (args->seg_start != nullptr || args->h0 != nullptr || args->summary != nullptr ||
+        args->tile_prod != nullptr || args->tile_carry != nullptr)
+        return fail(NEED_ERR_INVALID, "the backward scan takes no seg_start, h0, summary or tile records");
+    if (args->T < 2) return fail(NEED_ERR_INVALID, "the backward scan needs T >= 2 (for T = 1 the gradient is g)");
+    Plan pl;
+    ScanParams P;
+    if (int rc = prepare(args, NEED_FORM_AFFINE, &pl, &P, true)) return rc;
+    if (pl.launch_rev == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no reversed scan for this dtype combination");
+    if (int rc = pl.launch_rev(P, stream)) return rc;
+    return ok();
 }
 
 int need_ssd_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_SSD, stream); }

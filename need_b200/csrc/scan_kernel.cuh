@@ -362,7 +362,14 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
 // fix-up -- the same tile pipeline over the leading fix_chunks chunks of a
 // slice, each tile entered from its known corrected state (no look-back),
 // CTAs striding over those tiles.
-template <class K, bool FIX = false>
+// REV = true (AFFINE only, no resets): the scan runs from t = T-1 down to 0,
+// h_t = a'_t h_{t+1} + b_t -- the adjoint recurrence of the backward pass.
+// Tiles, rows and the look-back work in reversed ("virtual") time tau =
+// T-1-t; only the tile loads, the row order inside a warp's rows and the
+// output rows are mirrored.  The caller passes the decay already shifted by
+// one row (a'_t = a_{t+1}, a'_{T-1} = 0): a tensor map based at row 1 with
+// T-1 rows, or, for a decay per row, a guarded load of row t+1.
+template <class K, bool FIX = false, bool REV = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
     using TS = typename K::TS;
     using TD = typename K::TD;
@@ -606,18 +613,24 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             mbar_arrive_expect_tx(&s_bar[warp], bytes);
 #pragma unroll
             for (int k = 0; k < K::NIN; ++k)
-                tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0, t0 + wr0, hi, bi,
+                tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0,
+                            REV ? p.T - t0 - wr0 - R : t0 + wr0, hi, bi,
                             &s_bar[warp]);
         }
         // this warp's reset flags and per-row decay while its rows are in flight
         if (lane < R) {
             const int r = wr0 + lane, t = t0 + r;
             uint8_t rs = 0;
-            if (p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
+            if (!REV && p.seg != nullptr && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
             s_reset[r] = rs;
             if constexpr (K::ROWDEC) {
                 float d = 1.0f;
-                if (t < p.T) d = to_f(reinterpret_cast<const TD*>(p.rowdec)[bi * p.dsb + hi * p.dsh + (int64_t)t * p.dst]);
+                if (t < p.T) {
+                    // REV: the decay of the row after this one in time (0 past the end)
+                    const int tt = REV ? p.T - t : t;
+                    d = tt < p.T ? to_f(reinterpret_cast<const TD*>(p.rowdec)[bi * p.dsb + hi * p.dsh + (int64_t)tt * p.dst])
+                                 : 0.0f;
+                }
                 s_rowdec[r] = d;
             }
         }
@@ -626,6 +639,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
             mbar_wait_bounded(&s_bar[warp], par, kTmaPolls);
         }
+
+        // shared-memory row of virtual row r (REV: mirrored inside this warp's rows)
+        auto srow = [&](int r) { return REV ? 2 * wr0 + R - 1 - r : r; };
 
         // ---------------------------------------------------------- phase 1
         // a, b of row r as 4 fp32 pairs (channels 2i, 2i+1 of this lane's vector);
@@ -639,7 +655,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     for (int i = 0; i < 4; ++i) a[i] = splat2(d);
                 } else {
                     typename Ops<TD>::P dp[4];
-                    Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + r * CBW, v, dp);
+                    Row8<TD, SPLIT>::lds(reinterpret_cast<const TD*>(slot_ptr<K>(base, 0)) + srow(r) * CBW, v, dp);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) a[i] = widen(dp[i]);
                     if (reset) {  // uniform across the row group
@@ -648,14 +664,14 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     }
                 }
                 PS up[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + r * CBW, v, up);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 1 : 0)) + srow(r) * CBW, v, up);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) b[i] = widen(up[i]);
             } else {
                 // GATED: slots z, g, x.  SSD: slots dt, bg, u (cg, og used in phase 2)
-                TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + r * CBW;
-                TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + r * CBW;
-                TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + r * CBW;
+                TS* s0 = reinterpret_cast<TS*>(slot_ptr<K>(base, 0)) + srow(r) * CBW;
+                TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + srow(r) * CBW;
+                TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + srow(r) * CBW;
                 PS p0[4], p1[4], p2[4], ap[4], bp[4];
                 Row8<TS, SPLIT>::lds(s0, v, p0);
                 Row8<TS, SPLIT>::lds(s1, v, p1);
@@ -697,8 +713,8 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 gates(r, false, a, b);
             } else {
                 PS ap[4], bp[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + r * CBW, v, ap);
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + r * CBW, v, bp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 0)) + srow(r) * CBW, v, ap);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::FORM == FORM_GATED ? 2 : 1)) + srow(r) * CBW, v, bp);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     a[i] = widen(ap[i]);
@@ -754,7 +770,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             h[i] = ffma2(EA[i], make_float2(s_cc[(2 * i) * LPR + v].x, s_cc[(2 * i + 1) * LPR + v].x), EB[i]);
         const bool ok0 = c0 + chan<SPLIT>(0, v) < p.C;
         const bool ok1 = c0 + chan<SPLIT>(4, v) < p.C;
-        TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
+        const int64_t ostep = REV ? -p.ost : p.ost;  // REV: rows are written in decreasing t
+        TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh +
+                   (int64_t)(REV ? p.T - 1 - t0 - r0 : t0 + r0) * p.ost + c0;
         PS dsp[4];
         if constexpr (K::FORM == FORM_SSD) {
 #pragma unroll
@@ -764,7 +782,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             }
         }
 #pragma unroll 2
-        for (int j = 0; j < rend; ++j, orow += p.ost) {
+        for (int j = 0; j < rend; ++j, orow += ostep) {
             const int r = r0 + j;
             float2 a[4], b[4];
             reload(r, a, b);
@@ -776,9 +794,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             }
             if constexpr (K::FORM == FORM_SSD) {
                 PS up[4], cp[4], gp[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + r * CBW, v, up);
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + r * CBW, v, cp);
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + r * CBW, v, gp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + srow(r) * CBW, v, up);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 3)) + srow(r) * CBW, v, cp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 4)) + srow(r) * CBW, v, gp);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float2 cgs = sig2<TS>(widen(cp[i]));
@@ -789,7 +807,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 }
             } else if constexpr (K::FORM == FORM_RETENTION) {
                 PS qp[4];
-                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + r * CBW, v, qp);
+                Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, K::HAS_DSTREAM ? 2 : 1)) + srow(r) * CBW, v, qp);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
             }

@@ -178,7 +178,7 @@ def affine_recurrence_scan(decay: torch.Tensor, update: torch.Tensor, *, dim: in
     """``state_t = decay_t * state_{t-1} + update_t`` along ``dim`` (need_kernels.py:229-264).
 
     The scan is carried in fp32 and returned in ``update.dtype``; ``backend`` is
-    ignored.
+    ignored.  Differentiable: the backward runs the reversed-time scan kernel.
     """
     del backend
     if update.numel() == 0:
@@ -186,11 +186,89 @@ def affine_recurrence_scan(decay: torch.Tensor, update: torch.Tensor, *, dim: in
     dim = dim if dim >= 0 else update.ndim + dim
     if dim < 0 or dim >= update.ndim:
         raise IndexError(f"scan dim {dim} out of range for rank {update.ndim}")
+    _require_cuda(decay, update)
+    if torch.is_grad_enabled() and (decay.requires_grad or update.requires_grad):
+        return _AffineScanFn.apply(decay, update, dim)
     if decay.shape != update.shape:
         decay = torch.broadcast_to(decay, update.shape)
-    _require_cuda(decay, update)
-    _no_grad(decay, update)
     return _affine(decay, update, dim)
+
+
+class _AffineScanFn(torch.autograd.Function):
+    """The scan with its gradient.  For h_t = a_t h_{t-1} + b_t and the output
+    gradient g, the adjoint lam_t = g_t + a_{t+1} lam_{t+1} (a reversed-time
+    scan, need_affine_recurrence_scan_backward) is the gradient of b, and
+    lam_t * h_{t-1} (h_{-1} = 0) the gradient of a, summed back over the
+    dims the decay was broadcast along."""
+
+    @staticmethod
+    def forward(ctx, decay, update, dim):
+        d = decay if decay.shape == update.shape else torch.broadcast_to(decay, update.shape)
+        out = _affine(d, update, dim)
+        ctx.save_for_backward(d, out)
+        ctx.dim = dim
+        ctx.decay_shape, ctx.decay_dtype, ctx.update_dtype = decay.shape, decay.dtype, update.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        d, out = ctx.saved_tensors
+        dim = ctx.dim
+        lam = _affine_adjoint(d, g, dim)
+        grad_decay = grad_update = None
+        if ctx.needs_input_grad[0]:
+            T = out.shape[dim]
+            gd = torch.zeros(out.shape, dtype=torch.float32, device=out.device)
+            if T > 1:
+                gd.narrow(dim, 1, T - 1).copy_(lam.narrow(dim, 1, T - 1).float() * out.narrow(dim, 0, T - 1).float())
+            grad_decay = gd.sum_to_size(ctx.decay_shape).to(ctx.decay_dtype)
+        if ctx.needs_input_grad[1]:
+            grad_update = lam.to(ctx.update_dtype)
+        return grad_decay, grad_update, None
+
+
+def _affine_adjoint(decay: torch.Tensor, g: torch.Tensor, dim: int) -> torch.Tensor:
+    """``lam_t = g_t + decay_{t+1} * lam_{t+1}`` along ``dim`` (lam_{T-1} = g_{T-1}),
+    carried in fp32 and returned in ``g.dtype``: the reversed-time scan kernel
+    (need_affine_recurrence_scan_backward), laid out as ``_affine`` lays out the
+    forward."""
+    T = g.shape[dim]
+    if T == 1:
+        return g.clone()
+    dev = g.device
+    ts = g.dtype if g.dtype in _DT else torch.float32
+    gg = g if g.dtype == ts else g.to(ts)
+    td = decay.dtype if decay.dtype in (ts, torch.float32) else torch.float32
+    d = decay if decay.dtype == td else decay.to(td)
+    C = math.prod(gg.shape[dim + 1:]) if dim + 1 < gg.ndim else 1
+    rowdec = all(s == 0 or n == 1 for n, s in zip(d.shape[dim + 1:], d.stride()[dim + 1:]))
+    split = ts == torch.float32 or (not rowdec and td == torch.float32)
+    if dim > 2 or dim == gg.ndim - 1 or not _channel_ok(C, split):
+        # any other layout: scanned dim first, the rest flattened into padded channels
+        g2 = gg.movedim(dim, 0).reshape(T, -1)
+        d2 = torch.broadcast_to(d, gg.shape).movedim(dim, 0).reshape(T, -1)
+        M = g2.shape[1]
+        pad = (-M) % 8
+        lam = _affine_adjoint(F.pad(d2, (0, pad)).contiguous().unsqueeze(0),
+                              F.pad(g2, (0, pad)).contiguous().unsqueeze(0), 1)[0, :, :M]
+        return lam.reshape(list(gg.movedim(dim, 0).shape)).movedim(0, dim).to(g.dtype)
+    gg = _bhtc(gg, dim)
+    nb, nh, sb, sh = _lead(gg, dim)
+    out = torch.empty(gg.shape, dtype=ts, device=dev)
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_AFFINE, ts, nb, nh, T, C, out)
+    _, _, osb, osh = _lead(out, dim)
+    a.out_stride_b, a.out_stride_h, a.out_stride_t = osb, osh, out.stride(dim)
+    a.decay_dtype = _DT[td]
+    a.decay_per_row = 1 if rowdec else 0
+    if not rowdec:
+        d = _bhtc(d, dim)
+    _, _, dsb, dsh = _lead(d, dim)
+    a.in_[0] = abi.NeedView(d.data_ptr(), dsb, dsh, d.stride(dim))
+    a.in_[1] = abi.NeedView(gg.data_ptr(), sb, sh, gg.stride(dim))
+    keep = [d, gg, out]  # noqa: F841 (alive until the launch is queued)
+    _launch("need_affine_recurrence_scan_backward", a, dev, rowdec=a.decay_per_row)
+    return out if ts == g.dtype else out.to(g.dtype)
 
 
 def _affine(decay: torch.Tensor, update: torch.Tensor, dim: int, *, q: Optional[torch.Tensor] = None,
@@ -276,10 +354,11 @@ def recurrent_retention_scan(q: torch.Tensor, kv: torch.Tensor, decay: torch.Ten
     del backend
     if kv.numel() == 0:
         return q * kv
+    _require_cuda(q, kv, decay)
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, kv, decay)):
+        return q * _AffineScanFn.apply(decay, kv, 2)  # unfused, differentiable
     if decay.shape != kv.shape:
         decay = torch.broadcast_to(decay, kv.shape)
-    _require_cuda(q, kv, decay)
-    _no_grad(q, kv, decay)
     if q.shape != kv.shape or q.dtype != kv.dtype or kv.dtype not in _DT:
         return q * _affine(decay, kv, 2)
     return _affine(decay, kv, 2, q=q)

@@ -179,8 +179,9 @@ def test_affine_contract(cuda):
     with pytest.raises(RuntimeError):
         nk.affine_recurrence_scan(torch.rand(2, 3, 8), torch.randn(2, 3, 8))
     x = torch.randn(2, 3, 8, device=cuda, requires_grad=True)
-    with pytest.raises(NotImplementedError):
-        nk.affine_recurrence_scan(torch.rand(2, 3, 8, device=cuda), x)
+    assert nk.affine_recurrence_scan(torch.rand(2, 3, 8, device=cuda), x).grad_fn is not None
+    with pytest.raises(NotImplementedError):  # the gated form has no backward
+        nk.gated_scan(x, torch.randn(2, 3, 8, device=cuda), torch.randn(2, 3, 8, device=cuda))
     a, u = torch.rand(2, 64, 8, device=cuda), torch.randn(2, 64, 8, device=cuda)
     a0, u0 = a.clone(), u.clone()
     nk.affine_recurrence_scan(a, u)
