@@ -218,10 +218,19 @@ class _AffineScanFn(torch.autograd.Function):
         grad_decay = grad_update = None
         if ctx.needs_input_grad[0]:
             T = out.shape[dim]
-            gd = torch.zeros(out.shape, dtype=torch.float32, device=out.device)
-            if T > 1:
-                gd.narrow(dim, 1, T - 1).copy_(lam.narrow(dim, 1, T - 1).float() * out.narrow(dim, 0, T - 1).float())
-            grad_decay = gd.sum_to_size(ctx.decay_shape).to(ctx.decay_dtype)
+            if tuple(ctx.decay_shape) == tuple(out.shape):
+                # one product per element, rounded once to the decay's dtype
+                gd = torch.empty(out.shape, dtype=ctx.decay_dtype, device=out.device)
+                gd.narrow(dim, 0, 1).zero_()
+                if T > 1:
+                    torch.mul(lam.narrow(dim, 1, T - 1), out.narrow(dim, 0, T - 1), out=gd.narrow(dim, 1, T - 1))
+                grad_decay = gd
+            else:
+                # a broadcast decay: the products are summed in fp32 over the broadcast dims
+                gd = torch.zeros(out.shape, dtype=torch.float32, device=out.device)
+                if T > 1:
+                    gd.narrow(dim, 1, T - 1).copy_(lam.narrow(dim, 1, T - 1).float() * out.narrow(dim, 0, T - 1).float())
+                grad_decay = gd.sum_to_size(ctx.decay_shape).to(ctx.decay_dtype)
         if ctx.needs_input_grad[1]:
             grad_update = lam.to(ctx.update_dtype)
         return grad_decay, grad_update, None

@@ -95,3 +95,27 @@ def test_retention_backward(cuda):
     nk.recurrent_retention_scan(tc[0], tc[1], tc[2]).backward(g.to(cuda))
     for want, got in zip(ts, tc):
         assert rel(got.grad, want.grad) <= 1e-5
+
+
+def test_backward_on_a_fresh_thread(cuda):
+    """The autograd engine runs the backward on its own thread; the library must
+    work from a thread that has made no CUDA call yet."""
+    import threading
+    decay = torch.sigmoid(torch.randn(2, 256, 64, device=cuda) + 2.0)
+    g = torch.randn(2, 256, 64, device=cuda)
+    want = nk._affine_adjoint(decay, g, 1)
+    torch.cuda.synchronize()
+    box = {}
+
+    def run():
+        try:
+            box["lam"] = nk._affine_adjoint(decay, g, 1)
+            torch.cuda.synchronize()
+        except Exception as e:  # surfaced by the assert below
+            box["err"] = e
+
+    th = threading.Thread(target=run)
+    th.start()
+    th.join()
+    assert "err" not in box, box.get("err")
+    assert torch.equal(box["lam"], want)
