@@ -218,7 +218,7 @@ class _AffineScanFn(torch.autograd.Function):
         grad_decay = grad_update = None
         if ctx.needs_input_grad[0]:
             T = out.shape[dim]
-            if tuple(ctx.decay_shape) == tuple(out.shape):
+            if tuple(ctx.decay_shape) == tuple(out.shape) and ctx.decay_dtype == lam.dtype == out.dtype:
                 # one product per element, rounded once to the decay's dtype
                 gd = torch.empty(out.shape, dtype=ctx.decay_dtype, device=out.device)
                 gd.narrow(dim, 0, 1).zero_()

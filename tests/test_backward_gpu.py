@@ -119,3 +119,18 @@ def test_backward_on_a_fresh_thread(cuda):
     th.join()
     assert "err" not in box, box.get("err")
     assert torch.equal(box["lam"], want)
+
+
+def test_backward_mixed_dtypes(cuda):
+    """fp32 decay with a bf16 update, and a bf16 decay with an fp32 update."""
+    for dd, du, tol in ((torch.float32, torch.bfloat16, 2e-2), (torch.bfloat16, torch.float32, 1e-5)):
+        gen = torch.Generator().manual_seed(3)
+        decay = torch.sigmoid(torch.randn(2, 200, 64, generator=gen) + 2.0).to(dd)
+        update = torch.randn(2, 200, 64, generator=gen).to(du)
+        g = torch.randn(2, 200, 64, generator=gen).to(du)
+        _, want_d, want_u = grads(lambda d, u: seq_scan(d, u, 1), decay.double(), update.double(), g.double())
+        _, got_d, got_u = grads(lambda d, u: nk.affine_recurrence_scan(d, u), decay.to(cuda), update.to(cuda),
+                                g.to(cuda))
+        assert got_d.dtype == dd and got_u.dtype == du
+        assert rel(got_u, want_u) <= tol
+        assert rel(got_d, want_d) <= max(tol, 2e-2 if dd == torch.bfloat16 else tol)
