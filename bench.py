@@ -311,6 +311,7 @@ def main():
         side["sequence_parallel"] = run_sp(dev, world, rank, barrier, max_over_ranks, sp, workloads)
         side["decode_verify"] = run_decode(dev, nk, workloads, barrier, max_over_ranks)
         side["affine_backward"] = run_backward(dev, nk, barrier, max_over_ranks)
+        side["segment_starts"] = run_segments(dev, nk, barrier, max_over_ranks)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -434,6 +435,28 @@ def run_backward(dev, nk, barrier, max_over_ranks):
     return {"workload": "affine scan backward, B=16, T=4096, C=1024 bf16, decay=sigmoid(N(4,1))",
             "adjoint_ms": adj_ms, "adjoint_hbm_gbs": B * T * C * 6 / (adj_ms / 1e3) / 1e9,
             "fwd_bwd_ms": step_ms, "fwd_bwd_tokens_per_s": B * T / (step_ms / 1e3)}
+
+
+def run_segments(dev, nk, barrier, max_over_ranks):
+    """Reset masks of the prefill's packed windows from int64 token ids
+    (B=16, T=4096): reads 8 B and writes 1 B per token."""
+    import torch
+    g0 = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(3, 5000, (B, T), device=dev, generator=g0, dtype=torch.int64)
+    ids[torch.rand((B, T), device=dev, generator=g0) < 1.0 / 512] = 2  # EOS, ~512-token documents
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(5):
+        nk.segment_starts(ids)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(100):
+        nk.segment_starts(ids)
+    e1.record(stream)
+    barrier()
+    us = 1e3 * max_over_ranks(e0.elapsed_time(e1)) / 100
+    return {"workload": "segment starts of B=16 x T=4096 int64 windows", "us_per_call": us,
+            "hbm_gbs": B * T * 9 / (us / 1e6) / 1e9}
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):

@@ -25,6 +25,8 @@
  *   need_sp_fixup                <- no counterpart (sequence-parallel extension)
  *   need_affine_recurrence_scan_backward <- no counterpart (the reference differentiates
  *                                   its scan with torch autograd, need_kernels.py:177-226)
+ *   need_segment_starts          <- no counterpart (resets from the packed stream format
+ *                                   of train.py:320-352)
  *
  * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
  * message for the calling thread's last failure.  All entry points are
@@ -120,6 +122,21 @@ typedef struct {
     size_t workspace_bytes;
 } need_scan_args;
 
+/* Token dtypes of a packed stream (the packer writes uint16 or uint32,
+ * train.py:320-335; the dataloader hands int64 windows to the model). */
+typedef enum { NEED_TOK_U16 = 0, NEED_TOK_U32 = 1, NEED_TOK_I32 = 2, NEED_TOK_I64 = 3 } need_token_dtype;
+
+/* need_segment_starts: tokens [nb, T] (element strides), reset mask out. */
+typedef struct {
+    const void* tokens;
+    int32_t token_dtype;   /* need_token_dtype */
+    int64_t nb, T;
+    int64_t tok_stride_b, tok_stride_t;
+    int64_t eos_id, bos_id; /* NEED's Special.eos = 2, Special.bos = 1 (need_core.py:50-53) */
+    uint8_t* seg_start;    /* out [nb, T]: 1 where a document starts */
+    int64_t seg_stride_b, seg_stride_t;
+} need_segment_args;
+
 /* Version of this header the library was built from. */
 NEED_API int need_abi_version(void);
 
@@ -155,6 +172,13 @@ NEED_API int need_affine_recurrence_scan(const need_scan_args* args, need_stream
  * is a_0 lam_0).  seg_start, h0, summary and the tile records must be null;
  * T >= 2.  Workspace as for the forward. */
 NEED_API int need_affine_recurrence_scan_backward(const need_scan_args* args, need_stream_t stream);
+
+/* The reset mask of packed windows, derived on the GPU: no counterpart in the
+ * reference (its scan has no resets; its packer, train.py:320-352, separates
+ * documents with EOS after each and one BOS at the start of the stream).
+ * seg_start[b, t] = 1 at t = 0, after an EOS (tokens[b, t-1] == eos_id) and at
+ * a BOS (tokens[b, t] == bos_id); 0 elsewhere. */
+NEED_API int need_segment_starts(const need_segment_args* args, need_stream_t stream);
 
 /* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
 NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);

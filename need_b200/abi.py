@@ -50,6 +50,17 @@ class NeedVerifyArgs(Structure):
     ]
 
 
+TOK_U16, TOK_U32, TOK_I32, TOK_I64 = 0, 1, 2, 3
+
+
+class NeedSegmentArgs(Structure):
+    _fields_ = [
+        ("tokens", c_void_p), ("token_dtype", c_int32), ("nb", c_int64), ("T", c_int64),
+        ("tok_stride_b", c_int64), ("tok_stride_t", c_int64), ("eos_id", c_int64), ("bos_id", c_int64),
+        ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
+    ]
+
+
 # every symbol the header declares, with (restype, argtypes)
 SIGNATURES = {
     "need_abi_version": (c_int32, []),
@@ -64,6 +75,7 @@ SIGNATURES = {
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ragged_verify": (c_int32, [POINTER(NeedVerifyArgs), c_void_p]),
+    "need_segment_starts": (c_int32, [POINTER(NeedSegmentArgs), c_void_p]),
     "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
     "need_sp_fixup": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_int32, c_void_p]),

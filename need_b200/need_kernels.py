@@ -352,6 +352,41 @@ def _affine_generic(decay, update, dim, out_dtype, q=None):
     return out.reshape(moved).movedim(0, dim).to(out_dtype)
 
 
+
+# --------------------------------------------------------------------------
+# segment starts from the packed token stream (train.py:320-352, :406-418)
+# --------------------------------------------------------------------------
+
+_TOK = {torch.uint16: abi.TOK_U16, torch.uint32: abi.TOK_U32, torch.int32: abi.TOK_I32,
+        torch.int64: abi.TOK_I64}
+
+
+def segment_starts(input_ids: torch.Tensor, *, eos_id: int = 2, bos_id: int = 1) -> torch.Tensor:
+    """The reset mask of packed windows, computed on the GPU: ``seg[b, t]`` is 1
+    at t = 0, right after an EOS and at a BOS (NEED packs BOS once, then each
+    document followed by EOS; Special.eos = 2, Special.bos = 1).  ``input_ids``
+    is [B, T] (or [T]) of int64 / int32 / uint32 / uint16; returns uint8 [B, T],
+    ready for ``gated_scan(..., seg_start=)``."""
+    _require_cuda(input_ids)
+    ids = input_ids if input_ids.dim() == 2 else input_ids.reshape(1, -1)
+    if ids.dim() != 2:
+        raise ValueError(f"input_ids must be [B, T] or [T]; got {tuple(input_ids.shape)}")
+    code = _TOK.get(ids.dtype)
+    if code is None:
+        raise TypeError(f"token dtype {ids.dtype} (expected int64, int32, uint32 or uint16)")
+    B, T = ids.shape
+    seg = torch.empty((B, T), dtype=torch.uint8, device=ids.device)
+    if seg.numel() == 0:
+        return seg
+    a = abi.NeedSegmentArgs()
+    a.tokens, a.token_dtype, a.nb, a.T = ids.data_ptr(), code, B, T
+    a.tok_stride_b, a.tok_stride_t = ids.stride()
+    a.eos_id, a.bos_id = int(eos_id), int(bos_id)
+    a.seg_start = seg.data_ptr()
+    a.seg_stride_b, a.seg_stride_t = seg.stride()
+    abi.check("need_segment_starts", _lib().need_segment_starts(ctypes.byref(a), _stream(ids.device)))
+    return seg if input_ids.dim() == 2 else seg.reshape(-1)
+
 # --------------------------------------------------------------------------
 # recurrent_retention_scan  (need_kernels.py:342-345)
 # --------------------------------------------------------------------------
