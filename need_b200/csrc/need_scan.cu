@@ -37,14 +37,36 @@ template <typename T>
 using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? NEED_GATED16_L : 32,
                          sizeof(T) == 2 ? NEED_GATED16_NW : 4, sizeof(T) == 2 ? NEED_GATED16_CB : 256>;
 template <typename T>
-using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? 32 : 16, sizeof(T) == 2 ? 8 : 4>;
+#ifndef NEED_SSD16_L
+#define NEED_SSD16_L 64
+#endif
+#ifndef NEED_SSD16_NW
+#define NEED_SSD16_NW 8
+#endif
+#ifndef NEED_SSD16_CB
+#define NEED_SSD16_CB 128
+#endif
+using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? NEED_SSD16_L : 16, sizeof(T) == 2 ? NEED_SSD16_NW : 4,
+                       sizeof(T) == 2 ? NEED_SSD16_CB : 256>;
 
+#ifndef NEED_AFF16_L
+#define NEED_AFF16_L 128
+#endif
+#ifndef NEED_AFF16_NW
+#define NEED_AFF16_NW 4
+#endif
+#ifndef NEED_AFF16_CB
+#define NEED_AFF16_CB 128
+#endif
 template <typename TS, typename TD, bool RD>
 struct AffL {
-    static constexpr int L = RD ? (sizeof(TS) == 2 ? 64 : 32) : ((sizeof(TS) == 2 && sizeof(TD) == 2) ? 64 : 32);
+    static constexpr bool B16 = !RD && sizeof(TS) == 2 && sizeof(TD) == 2;  // 16-bit decay and update streams
+    static constexpr int L = RD ? (sizeof(TS) == 2 ? 64 : 32) : (B16 ? NEED_AFF16_L : 32);
+    static constexpr int NW = B16 ? NEED_AFF16_NW : 8;
+    static constexpr int CB = B16 ? NEED_AFF16_CB : 256;
 };
 template <typename TS, typename TD, bool RD>
-using AffCfg = ScanCfg<FORM_AFFINE, TS, TD, RD, AffL<TS, TD, RD>::L, 8>;
+using AffCfg = ScanCfg<FORM_AFFINE, TS, TD, RD, AffL<TS, TD, RD>::L, AffL<TS, TD, RD>::NW, AffL<TS, TD, RD>::CB>;
 
 template <typename TS, typename TD, bool RD>
 struct RetL {
