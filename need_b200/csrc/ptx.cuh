@@ -1,5 +1,5 @@
 // ptx.cuh -- small inline-PTX helpers for sm_100a: mbarriers, TMA tensor
-// loads (no multicast), acquire/release flags, bounded waits.
+// loads (no multicast), tagged look-back records, bounded waits.
 #pragma once
 
 #include <cuda.h>
@@ -86,10 +86,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------- TMA
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(tm) : "memory");
-}
-
 // 4-D tiled tensor load global -> shared, completion counted on `bar`.
 // Coordinates are in elements, innermost first; out-of-range elements are
 // zero-filled.  c0 * element size must be a multiple of 16 bytes.
@@ -102,17 +98,8 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
-// ---------------------------------------------------------------- flags
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
+// ---------------------------------------------------------------- global words
+// A plain re-read of a word another CTA may update (the error word).
 __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

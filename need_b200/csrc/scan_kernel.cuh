@@ -2,33 +2,35 @@
 // sm_100a (B200).
 //
 // Work decomposition.  A call scans nseq = nb*nh independent sequences of C
-// channels over T steps.  A tile is (sequence, 256-channel block, L-token
+// channels over T steps.  A tile is (sequence, CBW-channel block, L-token
 // chunk), one CTA per tile, numbered chunk-major by blockIdx.x, so every
 // tile's predecessors along T have lower block indices.
 //
-// Per tile (one CTA, NW warps):
-//   1. TMA (cp.async.bulk.tensor, no multicast) stages the tile's input rows
-//      [L x 256] of every streamed tensor into shared memory (zero fill past
-//      T and C), completion on one mbarrier.
-//   2. Phase 1: warp w owns rows [w*R, (w+1)*R), lane owns 8 channels.  Each
-//      thread computes a, b for its rows (gate math per form; 16-bit inputs
-//      are rounded where the reference's torch path rounds), writes them back
-//      in place where later phases need them, and reduces its rows to one
-//      affine map (A, B): h_out = A*h_in + B.
-//   3. The warps' maps are composed through shared memory: each warp gets the
-//      map of the rows before it, the last warp the tile's whole map.
-//   4. Look-back (last two warps): publish the tile map (AGG); compose the
-//      maps of the kLookbackDepth tiles before this one and the inclusive
-//      state (INCL) of the tile before those -- a fixed order, so results are
-//      bit-reproducible; publish the inclusive state.  Records carry the
-//      launch's tag in every 64-bit word, so neither side needs a fence or a
-//      flag.  Every wait is bounded; on give-up an error bit is set and the
-//      tile continues.
-//   5. Phase 2: every thread restarts its rows from the exact carry, writes
-//      the outputs straight to global memory (16-byte stores, a warp writes
-//      512 contiguous bytes per row).
+// Per tile (one CTA: NW row warps and one look-back warp):
+//   1. TMA (cp.async.bulk.tensor, no multicast): each row warp loads its own
+//      R = L/NW rows of every streamed tensor into shared memory (zero fill
+//      past T and C), completing on its own mbarrier.
+//   2. Phase 1: a lane owns 8 channels of one or more rows.  Each thread
+//      computes a, b for its rows (gate math per form; 16-bit inputs are
+//      rounded where the reference's torch path rounds), writes them back in
+//      place for phase 2, and reduces its rows to one affine map (A, B):
+//      h_out = A*h_in + B, written to shared memory.
+//   3. The look-back warp, from the CTA's start, polls the records of the
+//      kLookbackDepth tiles before this one along T (their maps, AGG) and the
+//      inclusive state (INCL) of the tile before those, composing them in that
+//      fixed order, so results are bit-reproducible; it composes and
+//      publishes this tile's map the moment the row maps are in, hands the
+//      carry to the row warps and publishes the inclusive state.  Records
+//      carry the launch's tag in every 64-bit word, so neither side needs a
+//      fence or a flag.  Every wait is bounded; on give-up an error bit is set
+//      and the tile continues.
+//   4. Phase 2: every thread composes the maps of the rows before its own,
+//      restarts its rows from the exact carry and writes the outputs straight
+//      to global memory (16-byte stores).
 // HBM traffic is the algorithmic minimum (inputs read once, outputs written
-// once) plus an 8 KB workspace record per tile (normally L2-resident).
+// once) plus 32 bytes of look-back records per channel and tile (normally
+// L2-resident).  The same kernel also runs the sequence-parallel fix-up
+// (FIX) and the backward's reversed-time scan (REV); see scan_kernel below.
 #pragma once
 
 #include <cuda.h>
@@ -42,8 +44,6 @@
 namespace need {
 
 enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
-
-constexpr int CB = 256;  // channel block of the sequence-parallel fix-up tiles
 
 // workspace header words (uint32)
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
