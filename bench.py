@@ -312,6 +312,7 @@ def main():
         side["decode_verify"] = run_decode(dev, nk, workloads, barrier, max_over_ranks)
         side["affine_backward"] = run_backward(dev, nk, barrier, max_over_ranks)
         side["segment_starts"] = run_segments(dev, nk, barrier, max_over_ranks)
+        side["ssd_prologue"] = run_prologue(dev, nk, barrier, max_over_ranks)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -439,24 +440,79 @@ def run_backward(dev, nk, barrier, max_over_ranks):
 
 def run_segments(dev, nk, barrier, max_over_ranks):
     """Reset masks of the prefill's packed windows from int64 token ids
-    (B=16, T=4096): reads 8 B and writes 1 B per token."""
+    (B=16, T=4096): reads 8 B and writes 1 B per token; replayed from a CUDA
+    graph so that the host's per-call cost is not timed."""
     import torch
     g0 = torch.Generator(device=dev).manual_seed(5)
     ids = torch.randint(3, 5000, (B, T), device=dev, generator=g0, dtype=torch.int64)
     ids[torch.rand((B, T), device=dev, generator=g0) < 1.0 / 512] = 2  # EOS, ~512-token documents
     stream = torch.cuda.current_stream(dev)
-    for _ in range(5):
+    side = torch.cuda.Stream(dev)  # warm up off the capture, then replay a graph (device time only)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
         nk.segment_starts(ids)
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        nk.segment_starts(ids)
+    for _ in range(5):
+        graph.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record(stream)
     for _ in range(100):
-        nk.segment_starts(ids)
+        graph.replay()
     e1.record(stream)
     barrier()
     us = 1e3 * max_over_ranks(e0.elapsed_time(e1)) / 100
     return {"workload": "segment starts of B=16 x T=4096 int64 windows", "us_per_call": us,
             "hbm_gbs": B * T * 9 / (us / 1e6) / 1e9}
+
+
+def run_prologue(dev, nk, barrier, max_over_ranks):
+    """The SSD block's conv + SiLU prologue at NEED's model shape (B=8, T=2048,
+    C=832, K=3, bf16): the fused kernel (reads 2 B, writes 2 B per element)
+    against the same computation as torch ops on the GPU, both replayed from
+    CUDA graphs so that the host's per-call cost is not timed."""
+    import torch
+    import torch.nn.functional as F
+    g0 = torch.Generator(device=dev).manual_seed(8)
+    Bm, Tm, Cm, K = 8, 2048, 832, 3
+    u = torch.randn(Bm, Tm, Cm, device=dev, generator=g0).to(torch.bfloat16)
+    w = (torch.randn(Cm, 1, K, device=dev, generator=g0) * 0.5).to(torch.bfloat16)
+    b = (torch.randn(Cm, device=dev, generator=g0) * 0.1).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, k=50):
+        for _ in range(5):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        barrier()
+        return 1e3 * max_over_ranks(e0.elapsed_time(e1)) / k
+
+    def graphed(fn):  # device time only: the call replayed from a CUDA graph
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
+
+    g_fused = graphed(lambda: nk.ssd_conv_silu(u, w, b))
+    g_torch = graphed(lambda: F.silu(F.conv1d(u.transpose(1, 2), w, b, padding=K - 1, groups=Cm)[..., :Tm]
+                                     .transpose(1, 2)).contiguous())
+    fused_us = timed(g_fused.replay)
+    torch_us = timed(g_torch.replay)
+    return {"workload": "silu(causal depthwise conv K=3), B=8, T=2048, C=832 bf16", "fused_us": fused_us,
+            "fused_hbm_gbs": Bm * Tm * Cm * 4 / (fused_us / 1e6) / 1e9, "torch_ops_us": torch_us}
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):

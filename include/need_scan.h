@@ -27,6 +27,8 @@
  *                                   its scan with torch autograd, need_kernels.py:177-226)
  *   need_segment_starts          <- no counterpart (resets from the packed stream format
  *                                   of train.py:320-352)
+ *   need_ssd_conv_silu           <- the conv + SiLU prologue of StructuredDualRetention
+ *                                   (need_core.py:1620-1622), as one kernel
  *
  * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
  * message for the calling thread's last failure.  All entry points are
@@ -137,6 +139,22 @@ typedef struct {
     int64_t seg_stride_b, seg_stride_t;
 } need_segment_args;
 
+/* need_ssd_conv_silu: the SSD block's input prologue. */
+typedef struct {
+    int32_t dtype;          /* NEED_BF16 or NEED_F16: u, out, weight and bias */
+    int32_t K;              /* taps, 1..4 (NEED's ssd_conv_kernel) */
+    int64_t nb, T, C;       /* C a multiple of 8 */
+    const void* u;          /* [nb, T, C], channel stride 1, 16-byte aligned rows */
+    int64_t u_stride_b, u_stride_t;
+    void* out;              /* [nb, T, C], same layout rules */
+    int64_t out_stride_b, out_stride_t;
+    const void* weight;     /* [C, K] taps, oldest first: nn.Conv1d(C, C, K, groups=C).weight[:, 0, :] */
+    int64_t w_stride_c, w_stride_k;
+    const void* bias;       /* [C] or null */
+    const uint8_t* seg_start; /* optional reset mask [nb, T]: the window stops at a segment start */
+    int64_t seg_stride_b, seg_stride_t;
+} need_conv_args;
+
 /* Version of this header the library was built from. */
 NEED_API int need_abi_version(void);
 
@@ -179,6 +197,14 @@ NEED_API int need_affine_recurrence_scan_backward(const need_scan_args* args, ne
  * seg_start[b, t] = 1 at t = 0, after an EOS (tokens[b, t-1] == eos_id) and at
  * a BOS (tokens[b, t] == bos_id); 0 elsewhere. */
 NEED_API int need_segment_starts(const need_segment_args* args, need_stream_t stream);
+
+/* u = silu(causal depthwise conv_K(u_raw)), the SSD block's prologue
+ * (need_core.py:1620-1622: nn.Conv1d with padding K-1 trimmed to T, then
+ * F.silu), fused into one pass; no counterpart as a single call in the
+ * reference.  The conv is accumulated in fp32 and rounded to `dtype`, SiLU is
+ * computed in fp32 and rounded again (the reference's rounding points).  With
+ * seg_start, inputs before a token's segment start count as 0. */
+NEED_API int need_ssd_conv_silu(const need_conv_args* args, need_stream_t stream);
 
 /* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
 NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);

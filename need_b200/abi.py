@@ -61,6 +61,16 @@ class NeedSegmentArgs(Structure):
     ]
 
 
+class NeedConvArgs(Structure):
+    _fields_ = [
+        ("dtype", c_int32), ("K", c_int32), ("nb", c_int64), ("T", c_int64), ("C", c_int64),
+        ("u", c_void_p), ("u_stride_b", c_int64), ("u_stride_t", c_int64),
+        ("out", c_void_p), ("out_stride_b", c_int64), ("out_stride_t", c_int64),
+        ("weight", c_void_p), ("w_stride_c", c_int64), ("w_stride_k", c_int64), ("bias", c_void_p),
+        ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
+    ]
+
+
 # every symbol the header declares, with (restype, argtypes)
 SIGNATURES = {
     "need_abi_version": (c_int32, []),
@@ -76,6 +86,7 @@ SIGNATURES = {
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ragged_verify": (c_int32, [POINTER(NeedVerifyArgs), c_void_p]),
     "need_segment_starts": (c_int32, [POINTER(NeedSegmentArgs), c_void_p]),
+    "need_ssd_conv_silu": (c_int32, [POINTER(NeedConvArgs), c_void_p]),
     "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
     "need_sp_fixup": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_int32, c_void_p]),

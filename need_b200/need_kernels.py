@@ -387,6 +387,49 @@ def segment_starts(input_ids: torch.Tensor, *, eos_id: int = 2, bos_id: int = 1)
     abi.check("need_segment_starts", _lib().need_segment_starts(ctypes.byref(a), _stream(ids.device)))
     return seg if input_ids.dim() == 2 else seg.reshape(-1)
 
+
+# --------------------------------------------------------------------------
+# the SSD block's input prologue (need_core.py:1620-1622), fused
+# --------------------------------------------------------------------------
+
+def ssd_conv_silu(u: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
+                  seg_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``silu(conv1d(u, weight, bias, padding=K-1, groups=C)[..., :T])`` over
+    ``u`` [B, T, C] (channels last) in one kernel: the causal depthwise conv
+    ``StructuredDualRetention`` applies before its scan.  ``weight`` is the
+    Conv1d weight [C, 1, K] (or [C, K]), K <= 4; ``bias`` [C] or None.  With
+    ``seg_start`` [B, T], tokens before a segment start do not feed the conv.
+    Returns a new [B, T, C] tensor in ``u.dtype`` (bf16 or f16)."""
+    _require_cuda(u, weight, bias, seg_start)
+    if u.dim() != 3:
+        raise ValueError(f"u must be [B, T, C]; got {tuple(u.shape)}")
+    if u.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"ssd_conv_silu takes bf16 or f16 data; got {u.dtype}")
+    _no_grad(u, weight, bias)
+    B, T, C = u.shape
+    w = weight.reshape(C, -1).to(u.dtype)
+    K = w.shape[1]
+    uu = u if (u.stride(-1) == 1 and u.data_ptr() % 16 == 0 and all((s * 2) % 16 == 0 for s in u.stride()[:2])) \
+        else u.contiguous()
+    out = torch.empty((B, T, C), dtype=u.dtype, device=u.device)
+    a = abi.NeedConvArgs()
+    a.dtype, a.K, a.nb, a.T, a.C = _DT[u.dtype], K, B, T, C
+    a.u, a.u_stride_b, a.u_stride_t = uu.data_ptr(), uu.stride(0), uu.stride(1)
+    a.out, a.out_stride_b, a.out_stride_t = out.data_ptr(), out.stride(0), out.stride(1)
+    a.weight, a.w_stride_c, a.w_stride_k = w.data_ptr(), w.stride(0), w.stride(1)
+    keep = [uu, w]
+    if bias is not None:
+        bb = bias.to(u.dtype).contiguous()
+        a.bias = bb.data_ptr()
+        keep.append(bb)
+    if seg_start is not None:
+        seg = seg_start.to(device=u.device, dtype=torch.uint8)
+        a.seg_start = seg.data_ptr()
+        a.seg_stride_b, a.seg_stride_t = seg.stride()
+        keep.append(seg)
+    abi.check("need_ssd_conv_silu", _lib().need_ssd_conv_silu(ctypes.byref(a), _stream(u.device)))
+    return out
+
 # --------------------------------------------------------------------------
 # recurrent_retention_scan  (need_kernels.py:342-345)
 # --------------------------------------------------------------------------

@@ -47,6 +47,7 @@ def test_struct_layout_matches_header(tmp_path):
         "need_verify_args": (abi.NeedVerifyArgs, [f[0] for f in abi.NeedVerifyArgs._fields_]),
         "need_view": (abi.NeedView, [f[0] for f in abi.NeedView._fields_]),
         "need_segment_args": (abi.NeedSegmentArgs, [f[0] for f in abi.NeedSegmentArgs._fields_]),
+        "need_conv_args": (abi.NeedConvArgs, [f[0] for f in abi.NeedConvArgs._fields_]),
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
     for cname, (_, names) in fields.items():
