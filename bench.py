@@ -331,6 +331,7 @@ def main():
         side["affine_backward"] = run_backward(dev, nk, barrier, max_over_ranks)
         side["segment_starts"] = run_segments(dev, nk, barrier, max_over_ranks)
         side["ssd_prologue"] = run_prologue(dev, nk, barrier, max_over_ranks)
+        side["ssd_block"] = run_ssd_block(dev, nk, barrier, max_over_ranks)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -532,6 +533,68 @@ def run_prologue(dev, nk, barrier, max_over_ranks):
     torch_us = timed(g_torch.replay)
     return {"workload": "silu(causal depthwise conv K=3), B=8, T=2048, C=832 bf16", "fused_us": fused_us,
             "fused_hbm_gbs": Bm * Tm * Cm * 4 / (fused_us / 1e6) / 1e9, "torch_ops_us": torch_us}
+
+
+def run_ssd_block(dev, nk, barrier, max_over_ranks):
+    """One StructuredDualRetention forward at NEED's 350M shape (B=8, T=2048,
+    d_model=832, conv K=3, dt in [0.001, 0.2], bf16, random weights):
+    in-projection, the conv + SiLU prologue, the SSD scan reading the
+    projection's chunks in place, RMSNorm and the out-projection
+    (need_core.py:1617-1643).  Reports the block's time and the share of the
+    two kernels of this repository, both replayed from CUDA graphs."""
+    import torch
+    import torch.nn.functional as F
+    g0 = torch.Generator(device=dev).manual_seed(13)
+    Bm, Tm, d = 8, 2048, 832
+    bf = torch.bfloat16
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, device=dev, generator=g0) * scale).to(bf)
+
+    x = rnd(Bm, Tm, d)
+    w_in, w_out = rnd(5 * d, d, scale=d ** -0.5), rnd(d, d, scale=d ** -0.5)
+    conv_w, conv_b = rnd(d, 1, 3, scale=0.5), rnd(d, scale=0.1)
+    d_skip = torch.full((d,), 0.1, device=dev)
+    norm_w = torch.ones(d, device=dev, dtype=bf)
+    proj = F.linear(x, w_in)
+
+    def kernels(p):
+        u, bg, cg, dt, og = p.chunk(5, dim=-1)
+        return nk.ssd_scan(nk.ssd_conv_silu(u, conv_w, conv_b), bg, cg, dt, og, d_skip, 0.001, 0.2)
+
+    def block():
+        return F.linear(F.rms_norm(kernels(F.linear(x, w_in)), (d,), norm_w, 1e-6), w_out)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def graphed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
+
+    def timed(graph, k=30):
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(k):
+            graph.replay()
+        e1.record(stream)
+        barrier()
+        return 1e3 * max_over_ranks(e0.elapsed_time(e1)) / k
+
+    block_us = timed(graphed(block))
+    kernels_us = timed(graphed(lambda: kernels(proj)))
+    return {"workload": "StructuredDualRetention forward, B=8, T=2048, d_model=832, bf16, random weights",
+            "block_us": block_us, "prologue_and_scan_us": kernels_us, "scan_share": kernels_us / block_us,
+            "block_tokens_per_s": Bm * Tm / (block_us / 1e6)}
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):
