@@ -29,6 +29,9 @@
  *                                   of train.py:320-352)
  *   need_ssd_conv_silu           <- the conv + SiLU prologue of StructuredDualRetention
  *                                   (need_core.py:1620-1622), as one kernel
+ *   need_ssd_scan_rms_norm       <- need_kernels.ssd_scan followed by the block's
+ *                                   out_norm (need_core.py:1624-1643 with
+ *                                   need_kernels.rms_norm, need_kernels.py:266-276), fused
  *
  * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
  * message for the calling thread's last failure.  All entry points are
@@ -170,7 +173,8 @@ NEED_API size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t de
                                 int64_t C);
 
 /* Reads (and clears) the workspace's device-side error word: bit 0 = a look-back
- * wait gave up, bit 1 = a tile load wait gave up.  Synchronises `stream`. */
+ * wait gave up, bit 1 = a tile load wait gave up, bit 2 = an RMSNorm epilogue
+ * wait for another channel block's sums gave up.  Synchronises `stream`. */
 NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream);
 
 /* need_kernels.affine_recurrence_scan (need_kernels.py:229-264): args->form must be
@@ -208,6 +212,20 @@ NEED_API int need_ssd_conv_silu(const need_conv_args* args, need_stream_t stream
 
 /* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
 NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);
+
+/* need_ssd_scan with StructuredDualRetention's out_norm fused after it
+ * (need_core.py:1624-1643: out_norm(ssd_scan(...)), an RMSNorm over the C
+ * channels of each token).  `out` receives, per token,
+ *     y * rsqrt(sum_c(y^2) / C + eps) * weight
+ * where y is need_ssd_scan's output in `dtype`; the sum, the scale and the
+ * products are fp32 and the result is rounded once to `dtype`, as the
+ * reference's GPU rms_norm computes (need_kernels.py:99-107).  weight is [C],
+ * NEED_F32 or `dtype` (weight_dtype).  C is at most 64 tiles of channels
+ * (8192 for 16-bit streams); the tiles of one token chunk run at the same time
+ * and exchange their sums through the workspace.  Workspace as for
+ * need_ssd_scan. */
+NEED_API int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, int32_t weight_dtype,
+                                    double eps, need_stream_t stream);
 
 /* need_kernels.recurrent_retention_scan (need_kernels.py:342-345):
  * args->form == NEED_FORM_RETENTION. */

@@ -81,6 +81,7 @@ SIGNATURES = {
     "need_affine_recurrence_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_ssd_scan_rms_norm": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_double, c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

@@ -80,9 +80,11 @@ using RetCfg = ScanCfg<FORM_RETENTION, TS, TD, RD, RetL<TS, TD, RD>::L, RetL<TS,
 struct Plan {
     int L = 0, R = 0, CB = 0, nin = 0, in0 = 0;  // tokens, rows per warp, channels per tile
     bool dstream = false, split = false;
+    int norm_rows = 0;  // SSD: rows of RMSNorm sum records per tile in the workspace (L)
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
-    int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;  // gated form only
-    int (*launch_rev)(const ScanParams&, cudaStream_t) = nullptr;  // affine form only
+    int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;   // gated form only
+    int (*launch_rev)(const ScanParams&, cudaStream_t) = nullptr;   // affine form only
+    int (*launch_norm)(const ScanParams&, cudaStream_t) = nullptr;  // SSD form only
 };
 
 template <class K>
@@ -136,6 +138,18 @@ int launch_rev_cfg(const ScanParams& prm, cudaStream_t s) {
     return NEED_OK;
 }
 
+// The SSD scan with the RMSNorm epilogue, one tile per CTA.
+template <class K>
+int launch_norm_cfg(const ScanParams& prm, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_done{0};
+    cudaError_t e = ensure_smem(scan_kernel<K, false, false, true>, K::SMEM, smem_done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel, rms norm)");
+    scan_kernel<K, false, false, true><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch (rms norm)");
+    return NEED_OK;
+}
+
 template <class K>
 Plan plan_of() {
     Plan p;
@@ -149,6 +163,10 @@ Plan plan_of() {
     p.launch = &launch_cfg<K>;
     if constexpr (K::FORM == FORM_GATED) p.launch_fix = &launch_fix_cfg<K>;
     if constexpr (K::FORM == FORM_AFFINE) p.launch_rev = &launch_rev_cfg<K>;
+    if constexpr (K::FORM == FORM_SSD) {
+        p.norm_rows = K::L;
+        p.launch_norm = &launch_norm_cfg<K>;
+    }
     return p;
 }
 
@@ -188,6 +206,10 @@ bool select_plan(int form, int dt, int ddt, int rd, Plan* out) {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// channel blocks (tiles per token chunk) the RMSNorm epilogue takes: 8192
+// channels in 16-bit tiles of 128, as many as the reference's fused norm
+constexpr int kMaxNormBlocks = 64;
+
 struct Geometry {
     int64_t ncb, nchains, nchunks, ntiles;
 };
@@ -201,9 +223,10 @@ Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) 
     return g;
 }
 
-size_t ws_bytes(int64_t ntiles, int cb) {
+// header, tagged AGG and INCL records, and (SSD) the RMSNorm sums per tile row
+size_t ws_bytes(const Plan& pl, int64_t ntiles) {
     const size_t hdr = WS_HDR_WORDS * 4;
-    return hdr + size_t(ntiles) * size_t(cb) * sizeof(ulonglong2) * 2;  // tagged AGG and INCL records
+    return hdr + size_t(ntiles) * (size_t(pl.CB) * sizeof(ulonglong2) * 2 + size_t(pl.norm_rows) * 8);
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -338,7 +361,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     if (a->form == NEED_FORM_SSD && a->d_skip == nullptr) return fail(NEED_ERR_INVALID, "d_skip is null");
     if (a->workspace == nullptr) return fail(NEED_ERR_WORKSPACE, "workspace is null");
     if (!aligned16(a->workspace)) return fail(NEED_ERR_WORKSPACE, "workspace is not 16-byte aligned");
-    const size_t need = ws_bytes(g.ntiles, pl->CB);
+    const size_t need = ws_bytes(*pl, g.ntiles);
     if (a->workspace_bytes < need)
         return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, need);
 
@@ -370,6 +393,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     P->hdr = reinterpret_cast<uint32_t*>(ws);
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * pl->CB;
+    P->norm_part = reinterpret_cast<unsigned long long*>(P->incl + size_t(g.ntiles) * pl->CB);
     return NEED_OK;
 }
 
@@ -425,8 +449,8 @@ size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t decay_dtype
     Plan pl;
     const bool rf = form == NEED_FORM_AFFINE || form == NEED_FORM_RETENTION;
     if (!select_plan(form, dtype, rf ? decay_dtype : dtype, rf ? decay_per_row : 0, &pl)) return 0;
-    if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(0, pl.CB);
-    return ws_bytes(geometry(pl, nb, nh, T, C).ntiles, pl.CB);
+    if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(pl, 0);
+    return ws_bytes(pl, geometry(pl, nb, nh, T, C).ntiles);
 }
 
 int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream) {
@@ -458,6 +482,31 @@ int need_affine_recurrence_scan_backward(const need_scan_args* args, need_stream
 }
 
 int need_ssd_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_SSD, stream); }
+
+int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, int32_t weight_dtype, double eps,
+                           need_stream_t stream) {
+    if (args == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (norm_weight == nullptr) return fail(NEED_ERR_INVALID, "norm_weight is null");
+    if (weight_dtype != NEED_F32 && weight_dtype != args->dtype)
+        return fail(NEED_ERR_UNSUPPORTED, "norm weight dtype %d must be fp32 or the stream dtype %d", weight_dtype,
+                    args->dtype);
+    if (!(eps >= 0.0)) return fail(NEED_ERR_INVALID, "eps must be >= 0");
+    Plan pl;
+    if (args->form == NEED_FORM_SSD && select_plan(NEED_FORM_SSD, args->dtype, args->dtype, 0, &pl) &&
+        args->C > int64_t(kMaxNormBlocks) * pl.CB)
+        // The tiles of one token chunk wait for one another's sums: all of them
+        // must be resident on the GPU at once.
+        return fail(NEED_ERR_UNSUPPORTED, "C=%lld: the RMSNorm epilogue takes at most %d channels",
+                    (long long)args->C, kMaxNormBlocks * pl.CB);
+    ScanParams P;
+    if (int rc = prepare(args, NEED_FORM_SSD, &pl, &P)) return rc;
+    if (pl.launch_norm == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no RMSNorm epilogue for dtype %d", args->dtype);
+    P.norm_w = norm_weight;
+    P.norm_w32 = weight_dtype == NEED_F32 ? 1 : 0;
+    P.norm_eps = static_cast<float>(eps);
+    if (int rc = pl.launch_norm(P, stream)) return rc;
+    return ok();
+}
 
 int need_recurrent_retention_scan(const need_scan_args* args, need_stream_t stream) {
     return run(args, NEED_FORM_RETENTION, stream);

@@ -30,7 +30,8 @@
 // HBM traffic is the algorithmic minimum (inputs read once, outputs written
 // once) plus 32 bytes of look-back records per channel and tile (normally
 // L2-resident).  The same kernel also runs the sequence-parallel fix-up
-// (FIX) and the backward's reversed-time scan (REV); see scan_kernel below.
+// (FIX), the backward's reversed-time scan (REV) and the SSD scan with an
+// RMSNorm over each token's channels after it (NORM); see scan_kernel below.
 #pragma once
 
 #include <cuda.h>
@@ -49,7 +50,7 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
 // word 8: leading chunks a sequence-parallel fix-up rewrites
 enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_CHUNKS = 8, WS_HDR_WORDS = 32 };
-enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
+enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u, ERR_NORM = 4u };
 
 constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst case
 #ifndef NEED_LOOKBACK_DEPTH
@@ -59,6 +60,8 @@ constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst 
 constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
 static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
+// RMSNorm epilogue: polls of the sibling tiles' sums (~0.5 us each: ~0.1 s worst case)
+constexpr uint32_t kNormPolls = 1u << 18;
 // registers per thread the occupancy bound plans for
 #ifndef NEED_REG_BUDGET
 #define NEED_REG_BUDGET 112
@@ -91,6 +94,13 @@ struct ScanParams {
     const uint32_t* fix_chunks;
     ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
+    // RMSNorm over the C channels of each output token (scan_kernel<K, false,
+    // false, true>): weight [C] (fp32 when norm_w32, else the stream dtype),
+    // eps, and per tile and row the tagged sum of squares of the tile's outputs
+    const void* norm_w;
+    int32_t norm_w32;
+    float norm_eps;
+    unsigned long long* norm_part;  // [ntiles][L]
 };
 
 // ------------------------------------------------------------------ types
@@ -369,8 +379,13 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
 // output rows are mirrored.  The caller passes the decay already shifted by
 // one row (a'_t = a_{t+1}, a'_{T-1} = 0): a tensor map based at row 1 with
 // T-1 rows, or, for a decay per row, a guarded load of row t+1.
-template <class K, bool FIX = false, bool REV = false>
+// NORM = true (SSD only): the outputs of each token are RMS-normalised over all
+// C channels before they are stored (RMSNorm after the scan).  The ncb tiles
+// of one token chunk, adjacent in blockIdx, exchange per-row sums of squares
+// through tagged records and each waits (bounded) for its siblings' sums.
+template <class K, bool FIX = false, bool REV = false, bool NORM = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
+    static_assert(!NORM || (K::FORM == FORM_SSD && !FIX && !REV), "RMSNorm epilogue: SSD forward only");
     using TS = typename K::TS;
     using TD = typename K::TD;
     using OS = Ops<TS>;
@@ -387,6 +402,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
+    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // the launch's record tag
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -456,6 +472,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 ep = static_cast<uint32_t>(old >> 32);
             }
             const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
+            if (NORM && lane == 0) *s_tag = tag;  // read by the row warps after the carry barrier
             auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
             float carry[8], carryP[8];
             float2 TA[4], TB[4];  // this tile's map
@@ -781,12 +798,10 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
             }
         }
-#pragma unroll 2
-        for (int j = 0; j < rend; ++j, orow += ostep) {
-            const int r = r0 + j;
+        // output row r: advances the state and forms the epilogue in o
+        auto step = [&](int r, PS (&o)[4]) {
             float2 a[4], b[4];
             reload(r, a, b);
-            PS o[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 h[i] = ffma2(a[i], h[i], b[i]);
@@ -811,7 +826,94 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
             }
-            Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
+        };
+        if constexpr (!NORM) {
+#pragma unroll 2
+            for (int j = 0; j < rend; ++j, orow += ostep) {
+                PS o[4];
+                step(r0 + j, o);
+                Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
+            }
+        } else {
+            // RMSNorm epilogue (need_kernels.py:99-107, the reference's GPU
+            // rms_norm): y is the scan's output in the stream dtype; per token
+            // ss = sum(y^2) / C in fp32, inv = rsqrt(ss + eps), out = y * inv * w
+            // in fp32, rounded once.  The rows stay in registers while the
+            // channel blocks of the token chunk exchange their sums.
+            PS ys[RS][4];
+            float ss[RS];
+#pragma unroll
+            for (int j = 0; j < RS; ++j) {
+                ss[j] = 0.0f;
+                if (j < rend) {
+                    step(r0 + j, ys[j]);
+                    float2 acc = splat2(0.0f);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 y = widen(ys[j][i]);
+                        if (i < 2 ? ok0 : ok1) acc = ffma2(y, y, acc);
+                    }
+                    ss[j] = acc.x + acc.y;
+                }
+            }
+#pragma unroll
+            for (int m = 1; m < LPR; m <<= 1)
+#pragma unroll
+                for (int j = 0; j < RS; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], m);
+            const uint32_t tag = *s_tag;
+            unsigned long long* part = p.norm_part + (int64_t)(tile - cblk) * L + r0;  // channel block 0's rows
+            if (v == 0) {
+#pragma unroll
+                for (int j = 0; j < RS; ++j)
+                    if (j < rend) st_relaxed_u64(part + (int64_t)cblk * L + j, tagged(ss[j], tag));
+            }
+            float wv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int c = c0 + chan<SPLIT>(e, v);
+                wv[e] = c >= p.C ? 0.0f
+                        : p.norm_w32 ? static_cast<const float*>(p.norm_w)[c]
+                                     : to_f(static_cast<const TS*>(p.norm_w)[c]);
+            }
+            // the sums of all channel blocks, added in block order (bounded wait)
+            float tot[RS];
+            bool got = false;
+            for (uint32_t it = 0; it < kNormPolls; ++it) {
+                bool valid = true;
+#pragma unroll
+                for (int j = 0; j < RS; ++j) {
+                    tot[j] = 0.0f;
+                    if (j < rend) {
+                        for (int s = 0; s < p.ncb; ++s) {
+                            const unsigned long long w = ld_relaxed_u64(part + (int64_t)s * L + j);
+                            valid &= tag_ok(w, tag);
+                            tot[j] += untag(w);
+                        }
+                    }
+                }
+                if (__all_sync(0xffffffffu, valid)) {
+                    got = true;
+                    break;
+                }
+                __nanosleep(64);
+                if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
+            }
+            if (!got && lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_NORM);
+            const float rc = static_cast<float>(p.C);
+#pragma unroll
+            for (int j = 0; j < RS; ++j) {
+                if (j < rend) {
+                    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(tot[j], rc), p.norm_eps));
+                    PS o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 y = widen(ys[j][i]);
+                        o[i] = OS::pack(__fmul_rn(__fmul_rn(y.x, inv), wv[2 * i]),
+                                        __fmul_rn(__fmul_rn(y.y, inv), wv[2 * i + 1]));
+                    }
+                    Row8<TS, SPLIT>::stg(orow + j * ostep, v, o, ok0, ok1);
+                }
+            }
         }
         }  // row warps
         if constexpr (FIX) {  // the stage is refilled by the next tile's TMA

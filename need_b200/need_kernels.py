@@ -129,7 +129,8 @@ def _fill_state(a: abi.NeedScanArgs, dev, nb: int, nh: int, C: int, seg_start, h
     return keep
 
 
-def _launch(fn_name: str, a: abi.NeedScanArgs, dev: torch.device, rowdec: int = 0) -> None:
+def _launch(fn_name: str, a: abi.NeedScanArgs, dev: torch.device, rowdec: int = 0, extra: tuple = ()) -> None:
+    """Runs ``fn_name(&a, *extra, stream)`` with this stream's workspace."""
     lib = _lib()
     nbytes = lib.need_scan_workspace_size(a.form, a.dtype, a.decay_dtype, rowdec, a.nb, a.nh, a.T, a.C)
     if nbytes == 0:
@@ -137,7 +138,7 @@ def _launch(fn_name: str, a: abi.NeedScanArgs, dev: torch.device, rowdec: int = 
     ws = workspace(dev, nbytes)
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
-    abi.check(fn_name, getattr(lib, fn_name)(ctypes.byref(a), _stream(dev)))
+    abi.check(fn_name, getattr(lib, fn_name)(ctypes.byref(a), *extra, _stream(dev)))
 
 
 def _channel_ok(C: int, split: bool) -> bool:
@@ -550,6 +551,70 @@ def ssd_scan(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tensor, dt_raw
     a.dt_min, a.dt_max = float(dt_min), float(dt_max)
     keep = _fill_state(a, u.device, b, 1, d, seg_start, h0, h_final)
     _launch("need_ssd_scan", a, u.device)
+    del keep
+    return out if out.dtype == u.dtype else out.to(u.dtype)
+
+
+# Channels the fused RMSNorm epilogue takes (64 channel tiles of 128 or 256).
+_NORM_MAX_C = {torch.bfloat16: 8192, torch.float16: 8192, torch.float32: 16384}
+
+
+def _rms_norm_gpu(y: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """The reference's GPU rms_norm arithmetic (need_kernels.py:99-107) as torch
+    ops: fp32 mean of squares, rsqrt, y * inv * w in fp32, one rounding."""
+    yf = y.float()
+    inv = torch.rsqrt(yf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return (yf * inv * weight.float()).to(y.dtype)
+
+
+def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tensor, dt_raw: torch.Tensor,
+                      out_gate: torch.Tensor, d_skip: torch.Tensor, dt_min: float, dt_max: float,
+                      norm_weight: torch.Tensor, eps: float = 1e-6, backend: str = "auto", *,
+                      seg_start: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+                      h_final: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``rms_norm(ssd_scan(...), norm_weight, eps)`` in one kernel: the SSD block's
+    scan and its ``out_norm`` (need_core.py:1624-1643).
+
+    The scan is :func:`ssd_scan`'s (same arguments and extensions); each output
+    token is then normalised over its D channels as the reference's GPU
+    ``rms_norm`` computes (need_kernels.py:99-107): ``y * rsqrt(mean(y^2) + eps)
+    * weight`` in fp32 from the scan's output in ``u.dtype``, rounded once.  The
+    normalised tensor is written straight from the scan's registers, so the
+    scan's output never makes a round trip through HBM.  Shapes the fused
+    kernel does not take (D not a multiple of 8, or above 8192 channels for
+    16-bit inputs) run :func:`ssd_scan` and the same normalisation as torch ops.
+    """
+    del backend
+    b, t, d = u.shape
+    tensors = (u, b_gate, c_gate, dt_raw, out_gate)
+    _require_cuda(*tensors, d_skip, norm_weight)
+    _no_grad(*tensors, d_skip, norm_weight)
+    if norm_weight.numel() != d:
+        raise ValueError(f"norm_weight must have D={d} elements; got {tuple(norm_weight.shape)}")
+    ts = u.dtype if u.dtype in _DT else torch.float32
+    if u.numel() == 0:
+        return torch.empty_like(u)
+    if not _channel_ok(d, ts == torch.float32) or d > _NORM_MAX_C[ts]:
+        y = ssd_scan(u, b_gate, c_gate, dt_raw, out_gate, d_skip, dt_min, dt_max,
+                     seg_start=seg_start, h0=h0, h_final=h_final)
+        return _rms_norm_gpu(y, norm_weight.reshape(-1), eps)
+    xs = [_bt_c_tensor(x if x.dtype == ts else x.to(ts), n)
+          for x, n in zip(tensors, ("u", "b_gate", "c_gate", "dt_raw", "out_gate"))]
+    out = torch.empty((b, t, d), dtype=ts, device=u.device)
+    ds = d_skip.to(device=u.device, dtype=torch.float32).reshape(-1).contiguous()
+    w = norm_weight.reshape(-1)
+    if w.dtype not in (torch.float32, ts):
+        w = w.float()
+    w = w.contiguous()
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_SSD, ts, b, 1, t, d, out)
+    xu, xbg, xcg, xdt, xog = xs
+    for k, x in enumerate((xdt, xbg, xu, xcg, xog)):
+        a.in_[k] = abi.NeedView(x.data_ptr(), x.stride(0), 0, x.stride(1))
+    a.d_skip = ds.data_ptr()
+    a.dt_min, a.dt_max = float(dt_min), float(dt_max)
+    keep = _fill_state(a, u.device, b, 1, d, seg_start, h0, h_final)
+    _launch("need_ssd_scan_rms_norm", a, u.device, extra=(w.data_ptr(), _DT[w.dtype], float(eps)))
     del keep
     return out if out.dtype == u.dtype else out.to(u.dtype)
 

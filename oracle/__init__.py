@@ -48,8 +48,9 @@ def _lib():
         lib.ora_ssd_prep.argtypes = [p, p, p, p, p, p, i64, i64, i64, d, d, i32, i32]
         lib.ora_ssd_epilogue.argtypes = [p, p, p, p, p, p, i64, i64, i64, i32, i32]
         lib.ora_stream_step.argtypes = [i32, p, p, p, p, p, p, p, p, i64, i64, d, d, i32]
+        lib.ora_rms_norm.argtypes = [p, p, p, i64, i64, d, i32]
         for fn in ("ora_round", "ora_affine_scan", "ora_affine_scan_seq", "ora_gated_prep",
-                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step"):
+                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm"):
             getattr(lib, fn).restype = None
         del f
         _LIB = lib
@@ -162,6 +163,19 @@ def ssd_scan(u, bg, cg, dt, og, dskip, dt_min: float, dt_max: float, seg=None, h
     y = np.empty_like(u)
     _lib().ora_ssd_epilogue(_ptr(h), _ptr(u), _ptr(cg), _ptr(og), _ptr(dskip), _ptr(y), n, t, c, MODE[dtype], nt)
     return y, hf
+
+
+def rms_norm(x, w, eps: float = 1e-6, *, dtype: str = "fp32") -> np.ndarray:
+    """The reference's GPU rms_norm (need_kernels.py:99-107) over the last axis:
+    fp32 arithmetic, the result rounded once to ``dtype``."""
+    x = _f32(x)
+    w = _f32(w).reshape(-1)
+    n = x.shape[-1]
+    if w.size != n:
+        raise ValueError(f"weight has {w.size} elements, x has {n} channels")
+    out = np.empty_like(x)
+    _lib().ora_rms_norm(_ptr(x), _ptr(w), _ptr(out), x.size // max(n, 1), n, float(eps), MODE[dtype])
+    return out
 
 
 def stream_step(form: str, state, p0, p1, p2, p3=None, p4=None, dskip=None,

@@ -26,6 +26,8 @@
  *                        bf16 op in fp32 and rounds the result).
  *   ora_ssd_prep /       need_kernels.py:330-339 (ssd_scan, torch path).
  *   ora_ssd_epilogue
+ *   ora_rms_norm         need_kernels.py:99-107 (rms_norm's GPU kernel), the SSD
+ *                        block's out_norm after ssd_scan (need_core.py:1643).
  *   ora_stream_step      need_core.py:6420-6428 (_stream_retention_step) and
  *                        :1674-1685 (StructuredDualRetention.stream_step): one
  *                        token, state kept in the model dtype.
@@ -335,6 +337,32 @@ ORA_API void ora_ssd_epilogue(const float* h, const float* u, const float* cg, c
                               int mode, int nthreads) {
     ssde_ctx s = {h, u, cg, og, dskip, y, T, C, mode};
     run_rows(ssd_epi_row, &s, N, nthreads);
+}
+
+/* ------------------------------------------------------------------ */
+/* RMSNorm after the scan (the SSD block's out_norm)                   */
+/* ------------------------------------------------------------------ */
+
+/* out[r, :] = x[r, :] * rsqrt(sum_c(x[r, c]^2) / n + eps) * w, the reference's
+ * GPU rms_norm (need_kernels.py:99-107, the kernel need_core.py:1396 reaches on
+ * CUDA): x widened to fp32, the sum of squares and the scale in fp32, the two
+ * products separately rounded fp32 ops, the result rounded once to `mode` (the
+ * store into a tensor of x's dtype).  The sum is accumulated in double and
+ * rounded to fp32, so the checker is independent of the kernel's order of
+ * summation; rsqrt is 1/sqrt in double, rounded to fp32. */
+ORA_API void ora_rms_norm(const float* x, const float* w, float* out, int64_t rows, int64_t n, double eps,
+                          int mode) {
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * n;
+        double acc = 0.0;
+        for (int64_t c = 0; c < n; ++c) acc += (double)xr[c] * (double)xr[c];
+        const float ss = (float)acc / (float)n;
+        const float inv = (float)(1.0 / sqrt((double)(ss + (float)eps)));
+        for (int64_t c = 0; c < n; ++c) {
+            const float p = xr[c] * inv;
+            out[r * n + c] = rnd(p * w[c], mode);
+        }
+    }
 }
 
 /* ------------------------------------------------------------------ */

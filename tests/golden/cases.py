@@ -76,6 +76,9 @@ CASES = {
     # ssd_scan's torch path
     "ssd_fp32": dict(kind="ssd", seed=5, n=2, t=200, c=96, dtype="fp32"),
     "ssd_bf16": dict(kind="ssd", seed=6, n=2, t=200, c=96, dtype="bf16"),
+    # ssd_scan followed by the block's out_norm (need_kernels.rms_norm)
+    "ssd_norm_fp32": dict(kind="ssd_norm", seed=9, n=2, t=70, c=200, dtype="fp32"),
+    "ssd_norm_bf16": dict(kind="ssd_norm", seed=10, n=2, t=70, c=200, dtype="bf16"),
     # streaming one-token steps (ragged verify oracle)
     "stream_gated_bf16": dict(kind="stream", form="gated", seed=7, s=5, c=64, kmax=4, dtype="bf16"),
     "stream_ssd_bf16": dict(kind="stream", form="ssd", seed=8, s=5, c=64, kmax=4, dtype="bf16"),
@@ -102,6 +105,14 @@ def ssd_case(seed: int, n: int, t: int, c: int, dtype: str):
     dskip = (0.1 + 0.05 * rs.standard_normal(c)).astype(F32)   # nn.Parameter, fp32
     return {"u": u, "bg": bg, "cg": cg, "dt": dt, "og": og, "dskip": dskip,
             "dt_min": 0.001, "dt_max": 0.2}
+
+
+def ssd_norm_case(seed: int, n: int, t: int, c: int, dtype: str):
+    out = ssd_case(seed, n, t, c, dtype)
+    rs = np.random.RandomState(seed + 1000)
+    out["norm_w"] = (1.0 + 0.1 * rs.standard_normal(c)).astype(F32)  # RMSNorm.weight, fp32
+    out["eps"] = 1e-6
+    return out
 
 
 def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
@@ -133,6 +144,8 @@ def make_inputs(name: str):
         return retention_case(**spec)
     if kind == "ssd":
         return ssd_case(**spec)
+    if kind == "ssd_norm":
+        return ssd_norm_case(**spec)
     if kind == "stream":
         return stream_case(**spec)
     raise KeyError(kind)

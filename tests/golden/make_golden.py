@@ -14,6 +14,7 @@ guards against drift).  Reference entry points used (file:line in NEED):
   need_core.affine_recurrence_scan_torch    need_core.py:1419-1461
   need_kernels.recurrent_retention_scan     need_kernels.py:342-345
   need_kernels.ssd_scan (torch path)        need_kernels.py:302-339
+  need_kernels.rms_norm (torch path)        need_kernels.py:266-276 (with need_core.RMSNorm)
   StructuredDualRetention.stream_step       need_core.py:1653-1686
   the one-token formula of                  need_core.py:6420-6428
 
@@ -78,6 +79,20 @@ def ref_ssd(inp, dtype):
     dskip = torch.from_numpy(inp["dskip"])
     y = need_kernels.ssd_scan(*args, dskip, inp["dt_min"], inp["dt_max"], backend="auto")
     return {"y": npf(y)}
+
+
+def ref_ssd_norm(inp, dtype):
+    """ssd_scan, then the block's out_norm: need_kernels.rms_norm (CPU: the torch
+    expression of need_kernels.py:276), checked against the RMSNorm module."""
+    y = ref_ssd(inp, dtype)["y"]
+    yt = T(y, dtype)
+    w = torch.from_numpy(inp["norm_w"])
+    out = need_kernels.rms_norm(yt, w, inp["eps"])
+    mod = need_core.RMSNorm(w.numel(), eps=inp["eps"])
+    with torch.no_grad():
+        mod.weight.copy_(w)
+        assert torch.equal(mod(yt), out), "RMSNorm module and need_kernels.rms_norm disagree"
+    return {"y": y, "norm": npf(out)}
 
 
 def ref_stream(inp, form, dtype):
@@ -152,6 +167,8 @@ def main():
             out = ref_retention(inp, dtype)
         elif kind == "ssd":
             out = ref_ssd(inp, dtype)
+        elif kind == "ssd_norm":
+            out = ref_ssd_norm(inp, dtype)
         else:
             out = ref_stream(inp, spec["form"], dtype)
         if inp.get("x") is not None and inp["x"].size > 250_000:

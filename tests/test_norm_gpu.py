@@ -1,0 +1,143 @@
+"""The SSD scan with the block's out_norm fused after it (need_core.py:1624-1643:
+out_norm(ssd_scan(...))), against the oracle: the reference's ssd_scan followed
+by the reference's GPU rms_norm arithmetic (need_kernels.py:99-107).
+
+Tolerances as for the scan: fp32 1e-5 relative; 16-bit 2e-2 relative with at
+least 99% of outputs bit-identical.  Against the same normalisation applied by
+torch ops to this library's own ssd_scan output, the fused kernel differs only
+by the order of the fp32 sum of squares: 99.9% of outputs bit-identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle
+from need_b200 import need_kernels as nk
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 5e-3}
+NAME = {torch.float32: "fp32", torch.bfloat16: "bf16", torch.float16: "fp16"}
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def check(got, want, dtype, what=""):
+    r = float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+    assert r <= TOL[dtype], f"{what}: rel err {r}"
+    if dtype != torch.float32:
+        frac = float(np.mean(got == want))
+        assert frac >= 0.99, f"{what}: only {frac:.5f} of outputs equal"
+
+
+def inputs(B, T, C, dtype, seed, resets=False):
+    gen = torch.Generator().manual_seed(seed)
+    xs = [torch.randn(B, T, C, generator=gen).to(dtype) for _ in range(5)]  # u, bg, cg, dt, og
+    dskip = 0.1 + 0.05 * torch.randn(C, generator=gen)
+    w = 1.0 + 0.1 * torch.randn(C, generator=gen)
+    seg = None
+    if resets:
+        seg = (torch.rand(B, T, generator=gen) < 0.02).to(torch.uint8)
+        seg[:, 0] = 1
+        seg[0, T - 1] = 1
+    return xs, dskip, w, seg
+
+
+def oracle_norm(xs, dskip, w, seg, dtype, eps, h0=None):
+    u, bg, cg, dt, og = (x.float().numpy() for x in xs)
+    y, hf = oracle.ssd_scan(u, bg, cg, dt, og, dskip.numpy(), 0.001, 0.2,
+                            None if seg is None else seg.numpy(),
+                            None if h0 is None else h0.numpy(), dtype=NAME[dtype])
+    return oracle.rms_norm(y, w.float().numpy(), eps, dtype=NAME[dtype]), hf
+
+
+def no_device_error():
+    assert nk.workspace_error() == 0, "a device-side wait gave up"
+
+
+@pytest.mark.parametrize("name", ["ssd_norm_fp32", "ssd_norm_bf16"])
+def test_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    dtype = {"fp32": torch.float32, "bf16": torch.bfloat16}[cases.CASES[name]["dtype"]]
+    args = [torch.from_numpy(inp[k]).to(cuda).to(dtype) for k in ("u", "bg", "cg", "dt", "og")]
+    w = torch.from_numpy(inp["norm_w"]).to(cuda)
+    got = nk.ssd_scan_rms_norm(*args, torch.from_numpy(inp["dskip"]).to(cuda), inp["dt_min"], inp["dt_max"],
+                               w, inp["eps"])
+    assert got.dtype == dtype and got.shape == args[0].shape
+    if dtype == torch.float32:
+        check(host(got), g["norm"], dtype, name)  # the reference's own output
+    else:
+        # the reference's GPU arithmetic on the reference's own scan output
+        check(host(got), oracle.rms_norm(g["y"], inp["norm_w"], inp["eps"], dtype="bf16"), dtype, name)
+    no_device_error()
+
+
+@pytest.mark.parametrize("B,T,C,dtype,resets", [
+    (2, 333, 832, torch.bfloat16, True),     # NEED's d_model: 7 channel tiles, the last half full
+    (1, 64, 128, torch.bfloat16, False),     # one tile
+    (3, 200, 96, torch.float16, True),       # one partial tile
+    (2, 130, 520, torch.float32, True),      # fp32: 256-channel tiles
+    (1, 70, 8192, torch.bfloat16, False),    # the largest fused width: 64 channel tiles
+])
+def test_matches_oracle(cuda, B, T, C, dtype, resets):
+    xs, dskip, w, seg = inputs(B, T, C, dtype, seed=C + T, resets=resets)
+    h0 = torch.randn(B, C, generator=torch.Generator().manual_seed(1)) * 0.5
+    hf = torch.empty(B, C, device=cuda)
+    got = nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs], dskip.to(cuda), 0.001, 0.2, w.to(cuda), 1e-6,
+                               seg_start=None if seg is None else seg.to(cuda), h0=h0.to(cuda), h_final=hf)
+    want, want_hf = oracle_norm(xs, dskip, w, seg, dtype, 1e-6, h0=h0)
+    check(host(got), want, dtype, f"{B}x{T}x{C}")
+    assert float(np.abs(host(hf) - want_hf).max() / max(np.abs(want_hf).max(), 1e-30)) <= 1e-4
+    no_device_error()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_same_as_unfused_on_gpu(cuda, dtype):
+    """Fused against ssd_scan followed by the same normalisation as torch ops."""
+    xs, dskip, w, seg = inputs(4, 1000, 832, dtype, seed=5, resets=True)
+    xs = [x.to(cuda) for x in xs]
+    args = (*xs, dskip.to(cuda), 0.001, 0.2)
+    seg = seg.to(cuda)
+    y = nk.ssd_scan(*args, seg_start=seg)
+    want = nk._rms_norm_gpu(y, w.to(cuda), 1e-6)
+    got = nk.ssd_scan_rms_norm(*args, w.to(cuda), 1e-6, seg_start=seg)
+    g, wv = host(got), host(want)
+    assert float(np.mean(g == wv)) >= 0.999
+    assert float(np.abs(g - wv).max() / np.abs(wv).max()) <= TOL[dtype]
+    no_device_error()
+
+
+def test_weight_in_model_dtype_and_projection_chunks(cuda):
+    """A bf16 model: bf16 norm weight, and the five gates as chunks of one
+    in-projection output (stride 5*D along T), as need_core.py:1619 makes them."""
+    gen = torch.Generator().manual_seed(4)
+    B, T, D = 2, 257, 832
+    proj = torch.randn(B, T, 5 * D, generator=gen).to(torch.bfloat16)
+    dskip = torch.full((D,), 0.1)
+    w = (1.0 + 0.1 * torch.randn(D, generator=gen)).to(torch.bfloat16)
+    u, bg, cg, dt, og = proj.to(cuda).chunk(5, dim=-1)
+    assert u.stride(1) == 5 * D
+    got = nk.ssd_scan_rms_norm(u, bg, cg, dt, og, dskip.to(cuda), 0.001, 0.2, w.to(cuda), 1e-6)
+    xs = [c.contiguous() for c in proj.chunk(5, dim=-1)]
+    want, _ = oracle_norm(xs, dskip, w, None, torch.bfloat16, 1e-6)
+    check(host(got), want, torch.bfloat16, "projection chunks")
+    no_device_error()
+
+
+@pytest.mark.parametrize("C", [100, 8200])
+def test_widths_outside_the_fused_kernel(cuda, C):
+    """D not a multiple of 8, or wider than the fused kernel takes: the scan
+    kernel and the normalisation as torch ops, same arithmetic."""
+    xs, dskip, w, _ = inputs(1, 40, C, torch.bfloat16, seed=C)
+    got = nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs], dskip.to(cuda), 0.001, 0.2, w.to(cuda), 1e-5)
+    want, _ = oracle_norm(xs, dskip, w, None, torch.bfloat16, 1e-5)
+    check(host(got), want, torch.bfloat16, f"C={C}")
+
+
+def test_bad_weight_size(cuda):
+    xs, dskip, w, _ = inputs(1, 8, 64, torch.bfloat16, seed=0)
+    with pytest.raises(ValueError):
+        nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs], dskip.to(cuda), 0.001, 0.2, w[:32].to(cuda))

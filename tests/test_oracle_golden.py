@@ -76,6 +76,35 @@ def test_ssd(name):
         assert rel(y, g["y"]) < FP32_TOL
 
 
+@pytest.mark.parametrize("name", ["ssd_norm_fp32", "ssd_norm_bf16"])
+def test_ssd_rms_norm(name):
+    """The out_norm after ssd_scan.  The oracle restates the reference's GPU
+    rms_norm (fp32 throughout, one rounding); the fixture comes from its CPU
+    path (need_kernels.py:276), which in fp32 is the same function and in bf16
+    rounds the scale and y * scale to bf16 before the fp32 weight.  Restating
+    those two roundings on the oracle's scale reproduces the fixture exactly."""
+    inp, g = load(name)
+    dtype = cases.CASES[name]["dtype"]
+    y, _ = oracle.ssd_scan(inp["u"], inp["bg"], inp["cg"], inp["dt"], inp["og"], inp["dskip"],
+                           inp["dt_min"], inp["dt_max"], dtype=dtype)
+    if dtype == "bf16":
+        assert np.array_equal(y, g["y"])
+    else:
+        assert rel(y, g["y"]) < FP32_TOL
+    w, eps = inp["norm_w"], inp["eps"]
+    out = oracle.rms_norm(g["y"], w, eps, dtype=dtype)
+    if dtype == "fp32":
+        assert rel(out, g["norm"]) < FP32_TOL
+    else:
+        # within the two extra bf16 roundings of the CPU path
+        assert rel(out, g["norm"]) < 2.0 ** -7
+        yy = g["y"]
+        ss = (yy.astype(np.float64) ** 2).sum(-1, keepdims=True).astype(np.float32) / np.float32(yy.shape[-1])
+        inv = (1.0 / np.sqrt((ss + np.float32(eps)).astype(np.float64))).astype(np.float32)  # the oracle's scale
+        cpu_path = oracle.round_to(yy * oracle.round_to(inv, "bf16"), "bf16") * w
+        assert np.array_equal(cpu_path.astype(np.float32), g["norm"])
+
+
 @pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16"])
 def test_stream_steps(name):
     inp, g = load(name)
