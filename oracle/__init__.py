@@ -49,8 +49,9 @@ def _lib():
         lib.ora_ssd_epilogue.argtypes = [p, p, p, p, p, p, i64, i64, i64, i32, i32]
         lib.ora_stream_step.argtypes = [i32, p, p, p, p, p, p, p, p, i64, i64, d, d, i32]
         lib.ora_rms_norm.argtypes = [p, p, p, i64, i64, d, i32]
+        lib.ora_assoc_memory.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i32, i32]
         for fn in ("ora_round", "ora_affine_scan", "ora_affine_scan_seq", "ora_gated_prep",
-                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm"):
+                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory"):
             getattr(lib, fn).restype = None
         del f
         _LIB = lib
@@ -175,6 +176,21 @@ def rms_norm(x, w, eps: float = 1e-6, *, dtype: str = "fp32") -> np.ndarray:
         raise ValueError(f"weight has {w.size} elements, x has {n} channels")
     out = np.empty_like(x)
     _lib().ora_rms_norm(_ptr(x), _ptr(w), _ptr(out), x.size // max(n, 1), n, float(eps), MODE[dtype])
+    return out
+
+
+def assoc_memory(q_raw, k_raw, v, write_mask=None, *, chunk: int = 32, dtype: str = "bf16",
+                 nthreads: Optional[int] = None) -> np.ndarray:
+    """HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001) with
+    its model-dtype roundings: q_raw, k_raw [B, T, r] fp32, v [B, T, d] (values
+    in ``dtype``), write_mask [B, T] (or [B, T, 1]) or None; returns [B, T, d]."""
+    q, k, v = _f32(q_raw), _f32(k_raw), _f32(v)
+    b, t, r = q.shape
+    d = v.shape[-1]
+    wm = None if write_mask is None else _f32(write_mask).reshape(b, t)
+    out = np.empty((b, t, d), np.float32)
+    _lib().ora_assoc_memory(_ptr(q), _ptr(k), _ptr(v), _ptr(wm), _ptr(out), b, t, r, d, int(chunk),
+                            MODE[dtype], _threads(nthreads))
     return out
 
 

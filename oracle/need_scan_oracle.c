@@ -26,6 +26,8 @@
  *                        bf16 op in fp32 and rounds the result).
  *   ora_ssd_prep /       need_kernels.py:330-339 (ssd_scan, torch path).
  *   ora_ssd_epilogue
+ *   ora_assoc_memory     need_core.py:1960-2001 (HierarchicalMemory's linear
+ *                        associative memory, the matrix-state recurrence).
  *   ora_rms_norm         need_kernels.py:99-107 (rms_norm's GPU kernel), the SSD
  *                        block's out_norm after ssd_scan (need_core.py:1643).
  *   ora_stream_step      need_core.py:6420-6428 (_stream_retention_step) and
@@ -363,6 +365,89 @@ ORA_API void ora_rms_norm(const float* x, const float* w, float* out, int64_t ro
             out[r * n + c] = rnd(p * w[c], mode);
         }
     }
+}
+
+/* ------------------------------------------------------------------ */
+/* matrix-state associative memory                                     */
+/* ------------------------------------------------------------------ */
+
+/* HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001):
+ *   qf = rnd(elu(q_raw) + 1), kf = rnd(elu(k_raw) + 1)   (fp32 in, model dtype out;
+ *        torch's CPU elu is expm1 below 0)
+ *   with a write mask: kf = rnd(kf * wm), v = rnd(v * wm)
+ *   per chunk of `chunk` tokens, with state [r, d] and denom_state [r] in the model dtype:
+ *     kv[s]      = rnd(kf[s] (x) v[s])                     (outer product)
+ *     state_c[s] = rnd(state + rnd(cumsum_s kv))            (fp32 running sum, rounded per s)
+ *     denom_c[s] = rnd(denom_state + rnd(cumsum_s kf))
+ *     numer[s]   = rnd(sum_i qf[s,i] * state_c[s,i,:])     (fp32 accumulation)
+ *     den[s]     = max(rnd(sum_i rnd(qf[s,i] * denom_c[s,i])), rnd(1e-6))
+ *     out[s]     = rnd(numer[s] / den[s])
+ *   and state, denom_state := state_c, denom_c of the chunk's last token.
+ * q_raw, k_raw [B, T, r] fp32; v [B, T, d] (values in the model dtype); wm [B, T]
+ * or NULL; out [B, T, d]. */
+typedef struct {
+    const float *q, *k, *v, *wm;
+    float* out;
+    int64_t T, r, d, chunk;
+    int mode;
+} assoc_ctx;
+
+static void assoc_row(void* ctx_, int64_t b) {
+    const assoc_ctx* s = (const assoc_ctx*)ctx_;
+    const int m = s->mode;
+    const int64_t T = s->T, r = s->r, d = s->d;
+    float* state = calloc((size_t)(r * d), sizeof(float));
+    float* denom_state = calloc((size_t)r, sizeof(float));
+    float* acc = malloc(sizeof(float) * (size_t)(r * d));    /* fp32 cumsum of kv */
+    float* acck = malloc(sizeof(float) * (size_t)r);         /* fp32 cumsum of kf */
+    float* sc = malloc(sizeof(float) * (size_t)(r * d));     /* state_c[s] */
+    float* dc = malloc(sizeof(float) * (size_t)r);           /* denom_c[s] */
+    float* qf = malloc(sizeof(float) * (size_t)r);
+    float* kf = malloc(sizeof(float) * (size_t)r);
+    float* vv = malloc(sizeof(float) * (size_t)d);
+    const float eps = rnd(1e-6f, m);
+    for (int64_t t0 = 0; t0 < T; t0 += s->chunk) {
+        const int64_t t1 = t0 + s->chunk < T ? t0 + s->chunk : T;
+        memset(acc, 0, sizeof(float) * (size_t)(r * d));
+        memset(acck, 0, sizeof(float) * (size_t)r);
+        for (int64_t t = t0; t < t1; ++t) {
+            const int64_t row = b * T + t;
+            const float w = s->wm ? rnd(fminf(fmaxf(s->wm[row], 0.0f), 1.0f), m) : 1.0f;
+            for (int64_t i = 0; i < r; ++i) {
+                const float qv = s->q[row * r + i], kv = s->k[row * r + i];
+                qf[i] = rnd((qv > 0.0f ? qv : expm1f(qv)) + 1.0f, m);
+                kf[i] = rnd((kv > 0.0f ? kv : expm1f(kv)) + 1.0f, m);
+                if (s->wm) kf[i] = rnd(kf[i] * w, m);
+            }
+            for (int64_t j = 0; j < d; ++j) vv[j] = s->wm ? rnd(s->v[row * d + j] * w, m) : s->v[row * d + j];
+            for (int64_t i = 0; i < r; ++i) {
+                acck[i] += kf[i];
+                dc[i] = rnd(denom_state[i] + rnd(acck[i], m), m);
+                for (int64_t j = 0; j < d; ++j) {
+                    acc[i * d + j] += rnd(kf[i] * vv[j], m);
+                    sc[i * d + j] = rnd(state[i * d + j] + rnd(acc[i * d + j], m), m);
+                }
+            }
+            float den = 0.0f;
+            for (int64_t i = 0; i < r; ++i) den += rnd(qf[i] * dc[i], m);
+            den = rnd(den, m);
+            if (den < eps) den = eps;
+            for (int64_t j = 0; j < d; ++j) {
+                float num = 0.0f;
+                for (int64_t i = 0; i < r; ++i) num += qf[i] * sc[i * d + j];
+                s->out[row * d + j] = rnd(rnd(num, m) / den, m);
+            }
+        }
+        memcpy(state, sc, sizeof(float) * (size_t)(r * d));
+        memcpy(denom_state, dc, sizeof(float) * (size_t)r);
+    }
+    free(state); free(denom_state); free(acc); free(acck); free(sc); free(dc); free(qf); free(kf); free(vv);
+}
+
+ORA_API void ora_assoc_memory(const float* q_raw, const float* k_raw, const float* v, const float* wm, float* out,
+                              int64_t B, int64_t T, int64_t r, int64_t d, int64_t chunk, int mode, int nthreads) {
+    assoc_ctx s = {q_raw, k_raw, v, wm, out, T, r, d, chunk, mode};
+    run_rows(assoc_row, &s, B, nthreads);
 }
 
 /* ------------------------------------------------------------------ */

@@ -79,6 +79,10 @@ CASES = {
     # ssd_scan followed by the block's out_norm (need_kernels.rms_norm)
     "ssd_norm_fp32": dict(kind="ssd_norm", seed=9, n=2, t=70, c=200, dtype="fp32"),
     "ssd_norm_bf16": dict(kind="ssd_norm", seed=10, n=2, t=70, c=200, dtype="bf16"),
+    # HierarchicalMemory's linear associative memory (matrix state, chunks of 32)
+    "assoc_bf16": dict(kind="assoc", seed=11, b=2, t=100, r=16, d=48, dtype="bf16", mask=False),
+    "assoc_bf16_mask": dict(kind="assoc", seed=12, b=2, t=70, r=8, d=24, dtype="bf16", mask=True),
+    "assoc_fp32": dict(kind="assoc", seed=13, b=1, t=80, r=16, d=32, dtype="fp32", mask=False),
     # streaming one-token steps (ragged verify oracle)
     "stream_gated_bf16": dict(kind="stream", form="gated", seed=7, s=5, c=64, kmax=4, dtype="bf16"),
     "stream_ssd_bf16": dict(kind="stream", form="ssd", seed=8, s=5, c=64, kmax=4, dtype="bf16"),
@@ -115,6 +119,17 @@ def ssd_norm_case(seed: int, n: int, t: int, c: int, dtype: str):
     return out
 
 
+def assoc_case(seed: int, b: int, t: int, r: int, d: int, dtype: str, mask: bool):
+    rs = np.random.RandomState(seed)
+    q = rs.standard_normal((b, t, r)).astype(F32)   # q_raw, k_raw: fp32 projections
+    k = rs.standard_normal((b, t, r)).astype(F32)
+    v = cast(rs.standard_normal((b, t, d)), dtype)
+    out = {"q": q, "k": k, "v": v}
+    if mask:  # adaptive-depth hard skip: zeros, ones and fractions
+        out["wm"] = np.clip(rs.uniform(-0.3, 1.3, (b, t)), 0.0, 1.0).astype(F32)
+    return out
+
+
 def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
     rs = np.random.RandomState(seed)
     k = rs.randint(0, kmax + 1, size=s)
@@ -146,6 +161,8 @@ def make_inputs(name: str):
         return ssd_case(**spec)
     if kind == "ssd_norm":
         return ssd_norm_case(**spec)
+    if kind == "assoc":
+        return assoc_case(**spec)
     if kind == "stream":
         return stream_case(**spec)
     raise KeyError(kind)

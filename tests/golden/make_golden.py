@@ -15,6 +15,7 @@ guards against drift).  Reference entry points used (file:line in NEED):
   need_kernels.recurrent_retention_scan     need_kernels.py:342-345
   need_kernels.ssd_scan (torch path)        need_kernels.py:302-339
   need_kernels.rms_norm (torch path)        need_kernels.py:266-276 (with need_core.RMSNorm)
+  HierarchicalMemory._linear_associative_memory  need_core.py:1960-2001
   StructuredDualRetention.stream_step       need_core.py:1653-1686
   the one-token formula of                  need_core.py:6420-6428
 
@@ -26,6 +27,7 @@ from __future__ import annotations
 
 import os
 import sys
+import types
 
 import numpy as np
 import torch
@@ -93,6 +95,18 @@ def ref_ssd_norm(inp, dtype):
         mod.weight.copy_(w)
         assert torch.equal(mod(yt), out), "RMSNorm module and need_kernels.rms_norm disagree"
     return {"y": y, "norm": npf(out)}
+
+
+def ref_assoc(inp, dtype):
+    """HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001) with
+    memory_chunk_size 32, in the no-grad branch the forward runs in eval."""
+    holder = types.SimpleNamespace(cfg=types.SimpleNamespace(memory_chunk_size=32))
+    q, k = torch.from_numpy(inp["q"]), torch.from_numpy(inp["k"])
+    v = T(inp["v"], dtype)
+    wm = None if "wm" not in inp else torch.from_numpy(inp["wm"])[..., None]
+    with torch.no_grad():
+        y = need_core.HierarchicalMemory._linear_associative_memory(holder, q, k, v, write_mask=wm)
+    return {"y": npf(y)}
 
 
 def ref_stream(inp, form, dtype):
@@ -169,6 +183,8 @@ def main():
             out = ref_ssd(inp, dtype)
         elif kind == "ssd_norm":
             out = ref_ssd_norm(inp, dtype)
+        elif kind == "assoc":
+            out = ref_assoc(inp, dtype)
         else:
             out = ref_stream(inp, spec["form"], dtype)
         if inp.get("x") is not None and inp["x"].size > 250_000:

@@ -90,7 +90,9 @@ def test_matches_oracle(cuda, B, T, C, dtype, resets):
                                seg_start=None if seg is None else seg.to(cuda), h0=h0.to(cuda), h_final=hf)
     want, want_hf = oracle_norm(xs, dskip, w, seg, dtype, 1e-6, h0=h0)
     check(host(got), want, dtype, f"{B}x{T}x{C}")
-    assert float(np.abs(host(hf) - want_hf).max() / max(np.abs(want_hf).max(), 1e-30)) <= 1e-4
+    # the fp32 final state: a one-ulp difference in a 16-bit gate moves it by ~2^-11 (fp16)
+    hf_tol = {torch.float32: 1e-5, torch.bfloat16: 1e-3, torch.float16: 5e-3}[dtype]
+    assert float(np.abs(host(hf) - want_hf).max() / max(np.abs(want_hf).max(), 1e-30)) <= hf_tol
     no_device_error()
 
 

@@ -105,6 +105,19 @@ def test_ssd_rms_norm(name):
         assert np.array_equal(cpu_path.astype(np.float32), g["norm"])
 
 
+@pytest.mark.parametrize("name", ["assoc_bf16", "assoc_bf16_mask", "assoc_fp32"])
+def test_assoc_memory(name):
+    """HierarchicalMemory's linear associative memory: bit for bit in bf16 (every
+    model-dtype rounding of the chunked torch computation restated)."""
+    inp, g = load(name)
+    dtype = cases.CASES[name]["dtype"]
+    y = oracle.assoc_memory(inp["q"], inp["k"], inp["v"], inp.get("wm"), dtype=dtype)
+    if dtype == "bf16":
+        assert np.array_equal(y, g["y"])
+    else:
+        assert rel(y, g["y"]) < FP32_TOL
+
+
 @pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16"])
 def test_stream_steps(name):
     inp, g = load(name)
