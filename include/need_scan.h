@@ -29,6 +29,8 @@
  *                                   of train.py:320-352)
  *   need_ssd_conv_silu           <- the conv + SiLU prologue of StructuredDualRetention
  *                                   (need_core.py:1620-1622), as one kernel
+ *   need_assoc_memory            <- HierarchicalMemory._linear_associative_memory
+ *                                   (need_core.py:1960-2001), the matrix-state memory
  *   need_ssd_scan_rms_norm       <- need_kernels.ssd_scan followed by the block's
  *                                   out_norm (need_core.py:1624-1643 with
  *                                   need_kernels.rms_norm, need_kernels.py:266-276), fused
@@ -158,6 +160,28 @@ typedef struct {
     int64_t seg_stride_b, seg_stride_t;
 } need_conv_args;
 
+/* need_assoc_memory: the matrix-state associative memory of HierarchicalMemory. */
+typedef struct {
+    int32_t dtype;          /* v and out: NEED_BF16 */
+    int32_t qk_dtype;       /* q_raw and k_raw: NEED_F32 (the model's fp32 projections) or NEED_BF16 */
+    int64_t nb, T, r, d;    /* r <= 64 features; d a multiple of 8 */
+    const void* q_raw;      /* [nb, T, r], feature stride 1 */
+    int64_t q_stride_b, q_stride_t;
+    const void* k_raw;      /* [nb, T, r], feature stride 1 */
+    int64_t k_stride_b, k_stride_t;
+    const void* v;          /* [nb, T, d], column stride 1, 16-byte aligned rows */
+    int64_t v_stride_b, v_stride_t;
+    const void* write_mask; /* optional [nb, T]: write weights, rounded to bf16 and clamped to [0, 1] */
+    int32_t mask_dtype;     /* NEED_F32 or NEED_BF16 */
+    int64_t mask_stride_b, mask_stride_t;
+    void* out;              /* [nb, T, d], column stride 1, 16-byte aligned rows */
+    int64_t out_stride_b, out_stride_t;
+    double eps;             /* denominator floor (the reference's 1e-6) */
+    void* workspace;        /* >= need_assoc_memory_workspace_size(...) bytes, 16-byte aligned; the
+                               first 128 bytes zero-filled before first use (the error word) */
+    size_t workspace_bytes;
+} need_assoc_args;
+
 /* Version of this header the library was built from. */
 NEED_API int need_abi_version(void);
 
@@ -259,6 +283,23 @@ NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
  * threads at once) race on it; calls that run one after another, on any
  * stream, are fine.  It allocates nothing (no cudaMalloc or cudaFree). */
 NEED_API int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t stream);
+
+/* Workspace bytes need_assoc_memory needs: a 128-byte header, the bf16
+ * feature-mapped q and k ([nb, T, 64] each) and, with a write mask, the masked
+ * values [nb, T, d]. */
+NEED_API size_t need_assoc_memory_workspace_size(int64_t nb, int64_t T, int64_t d, int32_t has_mask);
+
+/* HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001):
+ * with q = elu(q_raw) + 1 and k = elu(k_raw) + 1 rounded to bf16 (and k, v
+ * scaled by the write mask, each product rounded to bf16, need_core.py:1977-1984),
+ *     out[b, t] = (sum_{s<=t} (q_t . k_s) v_s) / max(sum_{s<=t} q_t . k_s, eps),
+ * rounded once to bf16.  The reference evaluates the same sums in chunks of
+ * memory_chunk_size tokens with its running state and every partial product
+ * rounded to the model dtype; here the products are bf16 tensor-core operands
+ * (the intra-tile scores q_t . k_s and the state rounded to bf16 for the
+ * second product) with fp32 accumulation, and the denominator is fp32.  The
+ * chunk length therefore does not enter. */
+NEED_API int need_assoc_memory(const need_assoc_args* args, need_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Ragged decode / speculative verify                                        */

@@ -71,6 +71,19 @@ class NeedConvArgs(Structure):
     ]
 
 
+class NeedAssocArgs(Structure):
+    _fields_ = [
+        ("dtype", c_int32), ("qk_dtype", c_int32),
+        ("nb", c_int64), ("T", c_int64), ("r", c_int64), ("d", c_int64),
+        ("q_raw", c_void_p), ("q_stride_b", c_int64), ("q_stride_t", c_int64),
+        ("k_raw", c_void_p), ("k_stride_b", c_int64), ("k_stride_t", c_int64),
+        ("v", c_void_p), ("v_stride_b", c_int64), ("v_stride_t", c_int64),
+        ("write_mask", c_void_p), ("mask_dtype", c_int32), ("mask_stride_b", c_int64), ("mask_stride_t", c_int64),
+        ("out", c_void_p), ("out_stride_b", c_int64), ("out_stride_t", c_int64),
+        ("eps", c_double), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
 # every symbol the header declares, with (restype, argtypes)
 SIGNATURES = {
     "need_abi_version": (c_int32, []),
@@ -82,6 +95,8 @@ SIGNATURES = {
     "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan_rms_norm": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_double, c_void_p]),
+    "need_assoc_memory_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int32]),
+    "need_assoc_memory": (c_int32, [POINTER(NeedAssocArgs), c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

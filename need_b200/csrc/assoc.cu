@@ -1,0 +1,453 @@
+// assoc.cu -- NEED's matrix-state associative memory on sm_100a tensor cores.
+//
+// HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001) keeps,
+// per sequence, a state S_t = sum_{s<=t} k_s (x) v_s [r, d] and z_t = sum k_s
+// [r] over feature-mapped keys k = elu(k_raw) + 1, and reads
+//     out_t = (q_t . S_t) / max(q_t . z_t, eps)      q = elu(q_raw) + 1.
+// The reference materialises S_t for every token of a 32-token chunk.  Here a
+// CTA owns one sequence and 128 columns of d and walks the sequence in tiles
+// of 128 tokens with the chunked (linear-attention) form, every product on
+// tcgen05 tensor cores with fp32 accumulators in tensor memory:
+//     P   = Q K^T                 (128 x 128, masked to s <= t)    TMEM cols   0..127
+//     O   = P V + Q S             (128 tokens x 128 columns)       TMEM cols 128..255
+//     S^T += V^T K                (128 columns x 64 features)      TMEM cols 256..319
+// with the denominator q_t . z + sum_{s<=t} P[t, s] in fp32 on the CUDA cores.
+// The state stays in tensor memory in fp32 for the whole sequence; its bf16
+// copy in shared memory is the B operand of the next tile's Q S.
+//
+// Operands arrive by TMA with the 128-byte swizzle (no multicast); every tile
+// is a canonical UMMA layout (umma.cuh), so the same shared-memory tile of V
+// serves as the MN-major B of P V and the MN-major A of V^T K, and the tile of
+// K as the K-major B of Q K^T and the MN-major B of V^T K.  Loads of the next
+// tile overlap the current one (two stages); outputs leave through a TMA store.
+//
+// A prologue kernel applies the feature map (and the optional write mask) and
+// writes q, k as bf16 [B, T, 64] (features past r zero) into the workspace.
+#include <algorithm>
+#include <atomic>
+#include <climits>
+
+#include "host_common.h"
+#include "need_scan.h"
+#include "ptx.cuh"
+#include "scan_kernel.cuh"
+#include "umma.cuh"
+
+using namespace need;
+
+namespace {
+
+constexpr int kTok = 128;    // tokens per tile
+constexpr int kCols = 128;   // columns of d per CTA
+constexpr int kRank = 64;    // feature rank, zero padded
+constexpr int kThreads = 128;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAssocPolls = 1u << 20;  // try_wait polls per wait before giving up
+
+// shared memory map (offsets from a 1024-byte aligned base)
+constexpr int OFF_Q = 0;                       // 2 stages x [128 tokens][64 features] bf16
+constexpr int OFF_K = OFF_Q + 2 * 16384;       // 2 stages x [128 tokens][64 features]
+constexpr int OFF_V = OFF_K + 2 * 16384;       // 2 stages x 2 boxes x [128 tokens][64 columns]
+constexpr int OFF_P = OFF_V + 2 * 32768;       // 2 K-atoms x [128 tokens][64 tokens]
+constexpr int OFF_S = OFF_P + 32768;           // [128 columns][64 features] (K-major B of Q S)
+constexpr int OFF_O = OFF_S + 16384;           // 2 boxes x [128 tokens][64 columns], TMA store source
+constexpr int OFF_Z = OFF_O + 32768;           // z: 64 fp32
+constexpr int OFF_BAR = OFF_Z + kRank * 4;     // full[2], mma, tmem base
+constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
+
+struct AssocParams {
+    CUtensorMap tm_q, tm_k, tm_v, tm_out;  // 3-D maps (column, token, sequence), 64 x 128 boxes, 128-byte swizzle
+    int32_t T, d;
+    float eps;
+    uint32_t* hdr;  // workspace header: error word
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// ------------------------------------------------------------------ main kernel
+__global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constant__ AssocParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* z = reinterpret_cast<float*>(base + OFF_Z);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + OFF_BAR);  // [2]
+    uint64_t* mmab = full + 2;
+    uint32_t* tbase = reinterpret_cast<uint32_t*>(full + 3);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int c0 = blockIdx.x * kCols, b = blockIdx.y;
+    const int ntile = (p.T + kTok - 1) / kTok;
+    const uint32_t sbase = smem_addr(base);
+
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_init(mmab, 1);
+        fence_barrier_init();
+    }
+    if (tid < kRank) z[tid] = 0.0f;
+    if (warp == 0) {
+        umma::tmem_alloc(tbase, kTmemCols);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tbase;
+    const uint32_t tP = tmem, tO = tmem + 128, tS = tmem + 256;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;  // this warp's TMEM lanes
+
+    constexpr uint32_t ID_QK = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
+    constexpr uint32_t ID_PV = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::MN_MAJOR);
+    constexpr uint32_t ID_QS = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
+    constexpr uint32_t ID_VK = umma::idesc_bf16(128, 64, umma::MN_MAJOR, umma::MN_MAJOR);
+
+    auto issue_load = [&](int tile, int st) {
+        const int t0 = tile * kTok;
+        unsigned char* q = base + OFF_Q + st * 16384;
+        unsigned char* k = base + OFF_K + st * 16384;
+        unsigned char* v = base + OFF_V + st * 32768;
+        mbar_arrive_expect_tx(&full[st], 16384u * 2u + 32768u);
+        umma::tma_load_3d(q, &p.tm_q, 0, t0, b, &full[st]);
+        umma::tma_load_3d(k, &p.tm_k, 0, t0, b, &full[st]);
+        umma::tma_load_3d(v, &p.tm_v, c0, t0, b, &full[st]);
+        umma::tma_load_3d(v + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);  // may lie past d: zero fill
+    };
+    if (tid == 0) {
+        issue_load(0, 0);
+        if (ntile > 1) issue_load(1, 1);
+    }
+
+    bool ok = true;
+    uint32_t mph = 0;
+    for (int it = 0; it < ntile; ++it) {
+        const int st = it & 1;
+        const int t0 = it * kTok;
+        const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
+        const uint32_t sV = sbase + OFF_V + st * 32768;
+        const uint32_t sP = sbase + OFF_P, sS = sbase + OFF_S;
+        const unsigned char* qrow = base + OFF_Q + st * 16384;
+        const unsigned char* krow = base + OFF_K + st * 16384;
+
+        ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
+        // ---- P = Q K^T
+        if (tid == 0) {
+            umma::fence_after_sync();
+#pragma unroll
+            for (int k = 0; k < kRank / 16; ++k)
+                umma::mma_bf16(tP, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sK + 32 * k, 16, 1024),
+                               ID_QK, k > 0);
+            umma::mma_commit(mmab);
+        }
+        // q_t . z over the tiles before this one (this thread's token t = tid)
+        float qz = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(tid, j));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                qz = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz);
+                qz = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz);
+            }
+        }
+        ok &= mbar_wait_bounded(mmab, mph, kAssocPolls);
+        mph ^= 1u;
+        umma::fence_after_sync();
+
+        // ---- P epilogue: causal mask, row sum (fp32), bf16 P as the K-major A of P V
+        float rs = 0.0f;
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+            float v[32];
+            umma::tmem_ld32(tP + lane_off + 32 * cb, v);
+            umma::tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                const float a0 = (32 * cb + e <= tid) ? v[e] : 0.0f;
+                const float a1 = (32 * cb + e + 1 <= tid) ? v[e + 1] : 0.0f;
+                rs += a0 + a1;
+                pk[e / 2] = pack_bf16(a0, a1);
+            }
+            unsigned char* prow = base + OFF_P + (cb >> 1) * 16384;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<uint4*>(prow + umma::sw128(tid, (cb & 1) * 4 + q4)) =
+                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+        fence_proxy_async_shared();  // P and last tile's S copy visible to the tensor cores
+        if (tid == 0) umma::tma_store_wait_read();  // last tile's output store has left shared memory
+        umma::fence_before_sync();
+        __syncthreads();
+
+        // ---- O = P V + Q S; S^T += V^T K
+        if (tid == 0) {
+            umma::fence_after_sync();
+#pragma unroll
+            for (int k = 0; k < kTok / 16; ++k)
+                umma::mma_bf16(tO, umma::smem_desc(sP + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
+                               umma::smem_desc(sV + 2048 * k, 16384, 1024), ID_PV, k > 0);
+            if (it > 0) {
+#pragma unroll
+                for (int k = 0; k < kRank / 16; ++k)
+                    umma::mma_bf16(tO, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sS + 32 * k, 16, 1024),
+                                   ID_QS, true);
+            }
+#pragma unroll
+            for (int k = 0; k < kTok / 16; ++k)
+                umma::mma_bf16(tS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
+                               umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
+            umma::mma_commit(mmab);
+        }
+        // z += column sums of this tile's k (every thread has read z for q_t . z)
+        if (tid < kRank) {
+            float s = 0.0f;
+            const int j = tid >> 3, e = tid & 7;
+            for (int r = 0; r < kTok; ++r) {
+                const uint16_t h = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r, j) + 2 * e);
+                s += __uint_as_float(static_cast<uint32_t>(h) << 16);
+            }
+            z[tid] += s;
+        }
+        ok &= mbar_wait_bounded(mmab, mph, kAssocPolls);
+        mph ^= 1u;
+        umma::fence_after_sync();
+
+        // ---- outputs: O / max(q.z + rowsum, eps) in bf16, staged for the TMA store
+        const float inv = 1.0f / fmaxf(qz + rs, p.eps);
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+            float v[32];
+            umma::tmem_ld32(tO + lane_off + 32 * cb, v);
+            umma::tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e] * inv, v[e + 1] * inv);
+            unsigned char* orow = base + OFF_O + (cb >> 1) * 16384;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<uint4*>(orow + umma::sw128(tid, (cb & 1) * 4 + q4)) =
+                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+        // ---- the state after this tile, bf16, as the K-major B of the next Q S (row = column of d)
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+            float v[32];
+            umma::tmem_ld32(tS + lane_off + 32 * cb, v);
+            umma::tmem_wait_ld();
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e], v[e + 1]);
+            unsigned char* srow = base + OFF_S;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<uint4*>(srow + umma::sw128(tid, cb * 4 + q4)) =
+                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+        fence_proxy_async_shared();  // staged outputs (TMA store) and S (next MMA) visible to the async proxy
+        umma::fence_before_sync();
+        if (!__syncthreads_and(ok)) break;  // a wait gave up: stop (uniformly) and report
+        if (tid == 0) {
+            umma::tma_store_3d(&p.tm_out, base + OFF_O, c0, t0, b);
+            if (c0 + 64 < p.d) umma::tma_store_3d(&p.tm_out, base + OFF_O + 16384, c0 + 64, t0, b);
+            umma::tma_store_commit();
+            if (it + 2 < ntile) issue_load(it + 2, st);  // this stage's MMAs and readers are done
+        }
+    }
+    if (tid == 0) umma::tma_store_wait_all();
+    if (!ok) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        umma::fence_after_sync();
+        umma::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ feature map
+// One warp per token: q, k -> bf16(elu(x) + 1) (need_core.py:1977-1978), zero past
+// r; with a write mask w = bf16(clamp(mask, 0, 1)): k := bf16(k * w) and
+// v := bf16(v * w) (need_core.py:1979-1984).
+struct FeatArgs {
+    const void* q;
+    const void* k;
+    int64_t qsb, qst, ksb, kst;
+    int32_t qk32;  // q, k are fp32 (else bf16)
+    const void* mask;
+    int32_t mask32;
+    int64_t msb, mst;
+    const __nv_bfloat16* v;
+    int64_t vsb, vst;
+    __nv_bfloat16* qf;
+    __nv_bfloat16* kf;
+    __nv_bfloat16* vm;  // [nb, T, d] masked values, when mask
+    int64_t nb, T, r, d;
+};
+
+__device__ __forceinline__ float ld_any(const void* base, int64_t i, bool f32) {
+    return f32 ? static_cast<const float*>(base)[i] : __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+}
+__device__ __forceinline__ float feature(float x) { return __bfloat162float(__float2bfloat16_rn((x > 0.0f ? x : expm1f(x)) + 1.0f)); }
+
+__global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= a.nb * a.T) return;
+    const int64_t bi = row / a.T, t = row - bi * a.T;
+    float w = 1.0f;
+    if (a.mask != nullptr)
+        w = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(ld_any(a.mask, bi * a.msb + t * a.mst, a.mask32))),
+                        0.0f),
+                  1.0f);
+    float qv[2], kv[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const int c = 2 * lane + e;
+        qv[e] = c < a.r ? feature(ld_any(a.q, bi * a.qsb + t * a.qst + c, a.qk32)) : 0.0f;
+        kv[e] = c < a.r ? feature(ld_any(a.k, bi * a.ksb + t * a.kst + c, a.qk32)) : 0.0f;
+        if (a.mask != nullptr) kv[e] = __bfloat162float(__float2bfloat16_rn(kv[e] * w));
+    }
+    reinterpret_cast<uint32_t*>(a.qf + row * kRank)[lane] = pack_bf16(qv[0], qv[1]);
+    reinterpret_cast<uint32_t*>(a.kf + row * kRank)[lane] = pack_bf16(kv[0], kv[1]);
+    if (a.mask != nullptr) {
+        const __nv_bfloat16* src = a.v + bi * a.vsb + t * a.vst;
+        __nv_bfloat16* dst = a.vm + row * a.d;
+        for (int64_t c = 8 * lane; c < a.d; c += 256) {
+            const uint4 x = *reinterpret_cast<const uint4*>(src + c);
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                o[i] = pack_bf16(__uint_as_float(xs[i] << 16) * w, __uint_as_float(xs[i] & 0xffff0000u) * w);
+            *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host
+size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
+
+// A bf16 [nb, T, width] view (column stride 1) as a 3-D map with 64 x 128 boxes.
+int encode_bf16(CUtensorMap* tm, const void* ptr, int64_t width, int64_t T, int64_t nb, int64_t st, int64_t sb,
+                const char* what) {
+    if (!aligned16(ptr)) return fail(NEED_ERR_UNSUPPORTED, "%s is not 16-byte aligned", what);
+    if ((st * 2) % 16 != 0 || (nb > 1 && (sb * 2) % 16 != 0) || st < width || (nb > 1 && sb < st * T))
+        return fail(NEED_ERR_UNSUPPORTED, "%s: strides (%lld, %lld) must be 16-byte multiples covering the rows", what,
+                    (long long)sb, (long long)st);
+    const cuuint64_t dims[3] = {cuuint64_t(width), cuuint64_t(T), cuuint64_t(nb)};
+    const cuuint64_t gs[2] = {cuuint64_t(st * 2), cuuint64_t(nb > 1 ? sb * 2 : st * 2 * T)};
+    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    auto fn = encode_fn();
+    if (fn == nullptr) return fail(NEED_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, gs, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NEED_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled(%s) failed: %d", what, int(r));
+    return NEED_OK;
+}
+
+size_t assoc_ws(int64_t nb, int64_t T, int64_t d, bool mask) {
+    const size_t feat = align128(size_t(nb) * size_t(T) * kRank * 2);
+    return WS_HDR_WORDS * 4 + 2 * feat + (mask ? align128(size_t(nb) * size_t(T) * size_t(d) * 2) : 0);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t need_assoc_memory_workspace_size(int64_t nb, int64_t T, int64_t d, int32_t has_mask) {
+    if (nb < 1 || T < 1 || d < 1) return WS_HDR_WORDS * 4;
+    return assoc_ws(nb, T, d, has_mask != 0);
+}
+
+int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
+    if (a == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (a->nb < 1 || a->T < 1 || a->r < 1 || a->d < 1)
+        return fail(NEED_ERR_INVALID, "sizes must be >= 1 (nb=%lld T=%lld r=%lld d=%lld)", (long long)a->nb,
+                    (long long)a->T, (long long)a->r, (long long)a->d);
+    if (a->dtype != NEED_BF16) return fail(NEED_ERR_UNSUPPORTED, "v / out must be bf16 (dtype %d)", a->dtype);
+    if (a->qk_dtype != NEED_F32 && a->qk_dtype != NEED_BF16)
+        return fail(NEED_ERR_UNSUPPORTED, "q_raw / k_raw must be fp32 or bf16 (dtype %d)", a->qk_dtype);
+    if (a->r > kRank) return fail(NEED_ERR_UNSUPPORTED, "r=%lld: at most %d features", (long long)a->r, kRank);
+    if (a->d % 8 != 0) return fail(NEED_ERR_UNSUPPORTED, "d=%lld must be a multiple of 8", (long long)a->d);
+    if (a->T > INT32_MAX / 2 || a->d > INT32_MAX / 2 || a->nb > 65535)
+        return fail(NEED_ERR_UNSUPPORTED, "sizes out of range");
+    if (a->q_raw == nullptr || a->k_raw == nullptr || a->v == nullptr || a->out == nullptr)
+        return fail(NEED_ERR_INVALID, "q_raw, k_raw, v and out must be non-null");
+    const bool mask = a->write_mask != nullptr;
+    if (mask && a->mask_dtype != NEED_F32 && a->mask_dtype != NEED_BF16)
+        return fail(NEED_ERR_UNSUPPORTED, "write_mask must be fp32 or bf16 (dtype %d)", a->mask_dtype);
+    if (a->eps < 0.0) return fail(NEED_ERR_INVALID, "eps must be >= 0");
+    if (a->workspace == nullptr || !aligned16(a->workspace))
+        return fail(NEED_ERR_WORKSPACE, "workspace is null or not 16-byte aligned");
+    const size_t need = assoc_ws(a->nb, a->T, a->d, mask);
+    if (a->workspace_bytes < need)
+        return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, need);
+    if (!aligned16(a->v)) return fail(NEED_ERR_UNSUPPORTED, "v is not 16-byte aligned");
+    if ((a->v_stride_t % 8) != 0 || (a->nb > 1 && (a->v_stride_b % 8) != 0))
+        return fail(NEED_ERR_UNSUPPORTED, "v strides must be multiples of 8 elements");
+
+    unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+    const size_t feat = align128(size_t(a->nb) * size_t(a->T) * kRank * 2);
+    __nv_bfloat16* qf = reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4);
+    __nv_bfloat16* kf = reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4 + feat);
+    __nv_bfloat16* vm = mask ? reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4 + 2 * feat) : nullptr;
+
+    FeatArgs f{};
+    f.q = a->q_raw;
+    f.k = a->k_raw;
+    f.qsb = a->q_stride_b;
+    f.qst = a->q_stride_t;
+    f.ksb = a->k_stride_b;
+    f.kst = a->k_stride_t;
+    f.qk32 = a->qk_dtype == NEED_F32;
+    f.mask = a->write_mask;
+    f.mask32 = a->mask_dtype == NEED_F32;
+    f.msb = a->mask_stride_b;
+    f.mst = a->mask_stride_t;
+    f.v = static_cast<const __nv_bfloat16*>(a->v);
+    f.vsb = a->v_stride_b;
+    f.vst = a->v_stride_t;
+    f.qf = qf;
+    f.kf = kf;
+    f.vm = vm;
+    f.nb = a->nb;
+    f.T = a->T;
+    f.r = a->r;
+    f.d = a->d;
+
+    if (int rc = ensure_context()) return rc;
+    AssocParams P{};
+    if (int rc = encode_bf16(&P.tm_q, qf, kRank, a->T, a->nb, kRank, kRank * a->T, "q features")) return rc;
+    if (int rc = encode_bf16(&P.tm_k, kf, kRank, a->T, a->nb, kRank, kRank * a->T, "k features")) return rc;
+    if (mask) {
+        if (int rc = encode_bf16(&P.tm_v, vm, a->d, a->T, a->nb, a->d, a->d * a->T, "masked v")) return rc;
+    } else if (int rc = encode_bf16(&P.tm_v, a->v, a->d, a->T, a->nb, a->v_stride_t, a->v_stride_b, "v")) {
+        return rc;
+    }
+    if (int rc = encode_bf16(&P.tm_out, a->out, a->d, a->T, a->nb, a->out_stride_t, a->out_stride_b, "out"))
+        return rc;
+    P.T = int32_t(a->T);
+    P.d = int32_t(a->d);
+    P.eps = static_cast<float>(a->eps);
+    P.hdr = reinterpret_cast<uint32_t*>(ws);
+
+    const int64_t rows = a->nb * a->T;
+    assoc_features_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, stream>>>(f);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "assoc_features_kernel launch");
+    static std::atomic<uint64_t> smem_done{0};
+    if ((e = ensure_smem(assoc_kernel, SMEM_BYTES, smem_done)) != cudaSuccess)
+        return cuda_fail(e, "cudaFuncSetAttribute(assoc_kernel)");
+    const dim3 grid(static_cast<unsigned>((a->d + kCols - 1) / kCols), static_cast<unsigned>(a->nb));
+    assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");
+    return ok();
+}
+
+}  // extern "C"

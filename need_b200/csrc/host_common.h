@@ -1,13 +1,16 @@
 // host_common.h -- shared host-side helpers of the C ABI: error reporting,
-// per-device one-time kernel attributes.
+// per-device one-time kernel attributes, the driver entry points the TMA
+// descriptors need.
 #pragma once
 
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
 
 #include <atomic>
+#include <mutex>
 #include <string>
 
 #include "need_scan.h"
@@ -53,6 +56,43 @@ inline cudaError_t ensure_smem(Kern kern, int bytes, std::atomic<uint64_t>& done
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e == cudaSuccess && bit) done_mask.fetch_or(bit, std::memory_order_acq_rel);
     return e;
+}
+
+// The driver's tensor-map encoder (null when the driver lacks it).
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Binds the current device's primary context to the calling thread when no
+// context is current there.  The tensor-map encoder is a driver call and needs
+// one; a thread that has made no runtime call yet (e.g. the autograd engine's
+// worker running a backward) has none until the runtime binds it lazily.
+inline int ensure_context() {
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    });
+    CUcontext ctx = nullptr;
+    if (get_current != nullptr && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr) return NEED_OK;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);  // initialises and binds the primary context
+    return e == cudaSuccess ? NEED_OK : cuda_fail(e, "binding the device context");
 }
 
 inline int dtype_bytes(int dt) { return dt == NEED_F32 ? 4 : 2; }

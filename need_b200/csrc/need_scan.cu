@@ -230,42 +230,6 @@ size_t ws_bytes(const Plan& pl, int64_t ntiles) {
 }
 
 // ------------------------------------------------------------------ TMA descriptors
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// Binds the current device's primary context to the calling thread when no
-// context is current there.  The tensor-map encoder is a driver call and needs
-// one; a thread that has made no runtime call yet (e.g. the autograd engine's
-// worker running a backward) has none until the runtime binds it lazily.
-int ensure_context() {
-    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
-    });
-    CUcontext ctx = nullptr;
-    if (get_current != nullptr && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr) return NEED_OK;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaSetDevice(dev);  // initialises and binds the primary context
-    return e == cudaSuccess ? NEED_OK : cuda_fail(e, "binding the device context");
-}
-
 int encode_view(CUtensorMap* tm, const need_view& v, int dt, int64_t nb, int64_t nh, int64_t T, int64_t C,
                 int box_c, int box_rows, int which) {
     if (v.ptr == nullptr) return fail(NEED_ERR_INVALID, "in[%d] is null", which);

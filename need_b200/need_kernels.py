@@ -72,13 +72,15 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-initialised scratch for the look-back records, one per (device, stream).
+def workspace(dev: torch.device, nbytes: int, kind: str = "scan") -> torch.Tensor:
+    """Zero-initialised scratch, one per (device, stream, kind).
 
-    The kernels leave it ready for the next launch on the same stream, so it is
-    allocated (and zeroed) only when a larger one is needed.
+    ``"scan"`` holds the look-back records: the kernels leave it ready for the
+    next launch on the same stream, so it is allocated (and zeroed) only when a
+    larger one is needed, and nothing else writes into it.  ``"assoc"`` holds the
+    associative memory's feature-mapped q, k.
     """
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream, kind)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -90,13 +92,15 @@ def workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
 def workspace_error(dev: Optional[torch.device] = None) -> int:
     """Reads and clears the device error word of this stream's workspace (synchronises)."""
     dev = dev or torch.device("cuda", torch.cuda.current_device())
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
-    ws = _workspaces.get(key)
-    if ws is None:
-        return 0
-    out = ctypes.c_uint32(0)
-    abi.check("need_workspace_error", _lib().need_workspace_error(ws.data_ptr(), ctypes.byref(out), _stream(dev)))
-    return int(out.value)
+    err = 0
+    for kind in ("scan", "assoc"):
+        ws = _workspaces.get((dev.index, torch.cuda.current_stream(dev).cuda_stream, kind))
+        if ws is not None:
+            out = ctypes.c_uint32(0)
+            abi.check("need_workspace_error",
+                      _lib().need_workspace_error(ws.data_ptr(), ctypes.byref(out), _stream(dev)))
+            err |= int(out.value)
+    return err
 
 
 def _fill_common(a: abi.NeedScanArgs, form: int, dtype: torch.dtype, nb: int, nh: int, T: int, C: int,
@@ -617,6 +621,73 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
     _launch("need_ssd_scan_rms_norm", a, u.device, extra=(w.data_ptr(), _DT[w.dtype], float(eps)))
     del keep
     return out if out.dtype == u.dtype else out.to(u.dtype)
+
+
+# --------------------------------------------------------------------------
+# matrix-state associative memory  (need_core.py:1960-2001)
+# --------------------------------------------------------------------------
+
+_ASSOC_MAX_RANK = 64
+
+
+def linear_associative_memory(q_raw: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor,
+                              write_mask: Optional[torch.Tensor] = None, *, eps: float = 1e-6) -> torch.Tensor:
+    """HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001) on the
+    tensor cores: ``q = elu(q_raw) + 1``, ``k = elu(k_raw) + 1`` (bf16), and
+
+        out[b, t] = sum_{s<=t} (q_t . k_s) v_s / max(sum_{s<=t} q_t . k_s, eps)
+
+    for q_raw, k_raw [B, T, r] (r <= 64, fp32 or bf16) and v [B, T, d] bf16 (d a
+    multiple of 8).  ``write_mask`` [B, T] or [B, T, 1] scales k and v as the
+    reference does.  Returns a new [B, T, d] bf16 tensor.  The reference's chunk
+    length (memory_chunk_size) only sets where it rounds its running state, so it
+    is not an argument here.
+    """
+    _require_cuda(q_raw, k_raw, v, write_mask)
+    _no_grad(q_raw, k_raw, v)
+    if q_raw.dim() != 3 or k_raw.shape != q_raw.shape or v.dim() != 3 or v.shape[:2] != q_raw.shape[:2]:
+        raise ValueError(f"q_raw, k_raw must be [B, T, r] and v [B, T, d]; got {tuple(q_raw.shape)}, "
+                         f"{tuple(k_raw.shape)}, {tuple(v.shape)}")
+    b, t, r = q_raw.shape
+    d = v.shape[-1]
+    if v.dtype != torch.bfloat16:
+        raise NotImplementedError(f"linear_associative_memory: v must be bf16 (got {v.dtype})")
+    if r > _ASSOC_MAX_RANK:
+        raise NotImplementedError(f"linear_associative_memory: at most {_ASSOC_MAX_RANK} features (got {r})")
+    if d % 8 != 0:
+        raise NotImplementedError(f"linear_associative_memory: d must be a multiple of 8 (got {d})")
+    out = torch.empty((b, t, d), dtype=torch.bfloat16, device=v.device)
+    if v.numel() == 0:
+        return out
+    qk = torch.float32 if q_raw.dtype == torch.float32 else torch.bfloat16
+    q = q_raw if q_raw.dtype == qk and q_raw.stride(-1) == 1 else q_raw.to(qk).contiguous()
+    k = k_raw if k_raw.dtype == qk and k_raw.stride(-1) == 1 else k_raw.to(qk).contiguous()
+    vv = _bt_c_tensor(v, "v")
+    a = abi.NeedAssocArgs()
+    a.dtype, a.qk_dtype = abi.BF16, _DT[qk]
+    a.nb, a.T, a.r, a.d = b, t, r, d
+    a.q_raw, a.q_stride_b, a.q_stride_t = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k_raw, a.k_stride_b, a.k_stride_t = k.data_ptr(), k.stride(0), k.stride(1)
+    a.v, a.v_stride_b, a.v_stride_t = vv.data_ptr(), vv.stride(0), vv.stride(1)
+    m = None
+    if write_mask is not None:
+        m = write_mask
+        if m.dim() == 3:
+            m = m[..., 0]
+        if m.shape != (b, t):
+            raise ValueError(f"write_mask must be [B, T] or [B, T, 1]; got {tuple(write_mask.shape)}")
+        if m.dtype not in (torch.float32, torch.bfloat16):
+            m = m.float()
+        a.write_mask, a.mask_dtype = m.data_ptr(), _DT[m.dtype]
+        a.mask_stride_b, a.mask_stride_t = m.stride(0), m.stride(1)
+    a.out, a.out_stride_b, a.out_stride_t = out.data_ptr(), out.stride(0), out.stride(1)
+    a.eps = float(eps)
+    lib = _lib()
+    ws = workspace(v.device, lib.need_assoc_memory_workspace_size(b, t, d, int(m is not None)), "assoc")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    abi.check("need_assoc_memory", lib.need_assoc_memory(ctypes.byref(a), _stream(v.device)))
+    del q, k, vv, m
+    return out
 
 
 # --------------------------------------------------------------------------

@@ -48,6 +48,7 @@ def test_struct_layout_matches_header(tmp_path):
         "need_view": (abi.NeedView, [f[0] for f in abi.NeedView._fields_]),
         "need_segment_args": (abi.NeedSegmentArgs, [f[0] for f in abi.NeedSegmentArgs._fields_]),
         "need_conv_args": (abi.NeedConvArgs, [f[0] for f in abi.NeedConvArgs._fields_]),
+        "need_assoc_args": (abi.NeedAssocArgs, [f[0] for f in abi.NeedAssocArgs._fields_]),
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
     for cname, (_, names) in fields.items():
@@ -113,3 +114,12 @@ def test_argument_errors_return_status(lib):
     assert b"at most 8192 channels" in lib.need_last_error()
     s.C, s.T = 832, 0
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F32, 1e-6, None) == abi.ERR_INVALID
+    m = abi.NeedAssocArgs()
+    assert lib.need_assoc_memory(None, None) == abi.ERR_INVALID
+    m.dtype, m.qk_dtype, m.nb, m.T, m.r, m.d = abi.BF16, abi.F32, 1, 16, 64, 64
+    assert lib.need_assoc_memory(ctypes.byref(m), None) == abi.ERR_INVALID  # null tensors
+    m.r = 65
+    assert lib.need_assoc_memory(ctypes.byref(m), None) == abi.ERR_UNSUPPORTED  # rank above 64
+    m.r, m.dtype = 64, abi.F32
+    assert lib.need_assoc_memory(ctypes.byref(m), None) == abi.ERR_UNSUPPORTED  # fp32 values
+    assert lib.need_assoc_memory_workspace_size(2, 100, 64, 0) == 128 + 2 * ((2 * 100 * 64 * 2 + 127) // 128 * 128)

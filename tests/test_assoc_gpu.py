@@ -1,0 +1,125 @@
+"""HierarchicalMemory's matrix-state associative memory (need_core.py:1960-2001)
+on the tcgen05 kernel, against
+  * the oracle: the reference's chunked computation with every model-dtype
+    rounding restated (pinned bit-exact to the reference's fixtures), and
+  * the exact sums in float64 from the same bf16 features and values.
+The kernel rounds the intra-tile scores and the running state to bf16 as
+tensor-core operands and accumulates in fp32; the reference rounds its running
+state and every partial product to bf16.  Tolerance (bf16): max|diff| <=
+2e-2 * max|ref| against the oracle and the fixtures; against float64, 1e-2 and
+a relative L2 error below 5e-3.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cases
+import oracle
+from need_b200 import need_kernels as nk
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def rel_l2(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def exact(q_raw, k_raw, v, wm=None, eps=1e-6):
+    """sum_{s<=t} (q_t.k_s) v_s / max(sum_{s<=t} q_t.k_s, eps) in float64 from the
+    reference's bf16 features and (masked) values."""
+    bf = torch.bfloat16
+    qf = (F.elu(q_raw.float()) + 1.0).to(bf)
+    kf = (F.elu(k_raw.float()) + 1.0).to(bf)
+    vv = v
+    if wm is not None:
+        w = wm.to(bf).clamp(0.0, 1.0).reshape(v.shape[0], v.shape[1], 1)
+        kf, vv = kf * w, v * w
+    a = torch.einsum("btr,bsr->bts", qf.double(), kf.double()).tril()
+    return (a @ vv.double()) / a.sum(-1, keepdim=True).clamp_min(eps)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def no_device_error():
+    assert nk.workspace_error() == 0, "a device-side wait gave up"
+
+
+@pytest.mark.parametrize("name", ["assoc_bf16", "assoc_bf16_mask"])
+def test_matches_reference_fixture(cuda, name):
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    q, k = torch.from_numpy(inp["q"]).to(cuda), torch.from_numpy(inp["k"]).to(cuda)
+    v = torch.from_numpy(inp["v"]).to(cuda).to(torch.bfloat16)
+    wm = None if "wm" not in inp else torch.from_numpy(inp["wm"]).to(cuda)
+    y = nk.linear_associative_memory(q, k, v, wm)
+    assert y.dtype == torch.bfloat16 and y.shape == v.shape
+    assert rel(host(y), g["y"]) <= TOL
+    assert rel(host(y), host(exact(q, k, v, wm))) <= 1e-2
+    no_device_error()
+
+
+@pytest.mark.parametrize("B,T,r,d,mask", [
+    (1, 128, 64, 128, False),    # one tile, one column block
+    (2, 300, 64, 832, False),    # NEED's d_model: a partial token tile and a half-full column block
+    (3, 1000, 16, 96, True),     # rank below 64, one partial column block, a write mask
+    (1, 2048, 64, 256, False),   # 16 tiles: the state carried across the whole sequence
+])
+def test_matches_oracle(cuda, B, T, r, d, mask):
+    gen = torch.Generator().manual_seed(B * 1000 + T + r + d)
+    q = torch.randn(B, T, r, generator=gen)
+    k = torch.randn(B, T, r, generator=gen)
+    v = torch.randn(B, T, d, generator=gen).to(torch.bfloat16)
+    wm = torch.rand(B, T, generator=gen) * 1.4 - 0.2 if mask else None  # zeros, ones and fractions
+    y = nk.linear_associative_memory(q.to(cuda), k.to(cuda), v.to(cuda), None if wm is None else wm.to(cuda))
+    want = oracle.assoc_memory(q.numpy(), k.numpy(), v.float().numpy(), None if wm is None else wm.numpy(),
+                               dtype="bf16")
+    got = host(y)
+    assert rel(got, want) <= TOL, rel(got, want)
+    ex = host(exact(q.to(cuda), k.to(cuda), v.to(cuda), None if wm is None else wm.to(cuda)))
+    assert rel(got, ex) <= 1e-2 and rel_l2(got, ex) <= 5e-3, (rel(got, ex), rel_l2(got, ex))
+    no_device_error()
+
+
+def test_strided_inputs_and_bf16_projections(cuda):
+    """q_raw / k_raw as bf16 column slices of one projection, v as a chunk of a
+    wider tensor (row stride above d)."""
+    gen = torch.Generator().manual_seed(21)
+    B, T, r, d = 2, 517, 64, 200
+    qk = torch.randn(B, T, 2 * r, generator=gen).to(torch.bfloat16).to(cuda)
+    wide = torch.randn(B, T, 3 * d, generator=gen).to(torch.bfloat16).to(cuda)
+    q, k, v = qk[..., :r], qk[..., r:], wide[..., d:2 * d]
+    assert v.stride(1) == 3 * d
+    y = nk.linear_associative_memory(q, k, v)
+    ex = host(exact(q, k, v))
+    assert rel(host(y), ex) <= 1e-2 and rel_l2(host(y), ex) <= 5e-3
+    no_device_error()
+
+
+def test_repeat_calls_are_identical(cuda):
+    gen = torch.Generator().manual_seed(5)
+    q, k = torch.randn(2, 700, 64, generator=gen).to(cuda), torch.randn(2, 700, 64, generator=gen).to(cuda)
+    v = torch.randn(2, 700, 512, generator=gen).to(torch.bfloat16).to(cuda)
+    a = nk.linear_associative_memory(q, k, v)
+    b = nk.linear_associative_memory(q, k, v)
+    assert torch.equal(a, b)
+
+
+def test_rejects_what_it_does_not_take(cuda):
+    q = torch.randn(1, 8, 80, device=cuda)
+    v = torch.randn(1, 8, 64, device=cuda).to(torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        nk.linear_associative_memory(q, q, v)  # rank above 64
+    with pytest.raises(NotImplementedError):
+        nk.linear_associative_memory(q[..., :64], q[..., :64], v.float())  # fp32 values
+    with pytest.raises(ValueError):
+        nk.linear_associative_memory(q[..., :64], q[..., :64], v[:, :4])
