@@ -332,6 +332,7 @@ def main():
         side["segment_starts"] = run_segments(dev, nk, barrier, max_over_ranks)
         side["ssd_prologue"] = run_prologue(dev, nk, barrier, max_over_ranks)
         side["ssd_block"] = run_ssd_block(dev, nk, barrier, max_over_ranks)
+        side["assoc_memory"] = run_assoc(dev, nk, barrier, max_over_ranks)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -533,6 +534,69 @@ def run_prologue(dev, nk, barrier, max_over_ranks):
     torch_us = timed(g_torch.replay)
     return {"workload": "silu(causal depthwise conv K=3), B=8, T=2048, C=832 bf16", "fused_us": fused_us,
             "fused_hbm_gbs": Bm * Tm * Cm * 4 / (fused_us / 1e6) / 1e9, "torch_ops_us": torch_us}
+
+
+def run_assoc(dev, nk, barrier, max_over_ranks):
+    """HierarchicalMemory's associative memory at NEED's 350M shape (B=8, T=2048,
+    d_model=832, memory_rank=64; fp32 q/k projections, bf16 values): the two
+    kernels of linear_associative_memory against the reference's chunked
+    computation (need_core.py:1960-2001, chunks of 32) as torch ops on the GPU,
+    both replayed from CUDA graphs."""
+    import torch
+    import torch.nn.functional as F
+    g0 = torch.Generator(device=dev).manual_seed(17)
+    Bm, Tm, d, r = 8, 2048, 832, 64
+    q = torch.randn(Bm, Tm, r, device=dev, generator=g0)
+    k = torch.randn(Bm, Tm, r, device=dev, generator=g0)
+    v = torch.randn(Bm, Tm, d, device=dev, generator=g0).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def chunked(chunk=32):  # the reference's algorithm, torch ops in the model dtype
+        qf = (F.elu(q.float()) + 1.0).to(v.dtype)
+        kf = (F.elu(k.float()) + 1.0).to(v.dtype)
+        state = v.new_zeros(Bm, r, d)
+        den_state = v.new_zeros(Bm, r)
+        outs = []
+        for s0 in range(0, Tm, chunk):
+            qc, kc, vc = qf[:, s0:s0 + chunk], kf[:, s0:s0 + chunk], v[:, s0:s0 + chunk]
+            st = state.unsqueeze(1) + (kc.unsqueeze(-1) * vc.unsqueeze(-2)).cumsum(dim=1)
+            dn = den_state.unsqueeze(1) + kc.cumsum(dim=1)
+            num = torch.einsum("bqr,bqrd->bqd", qc, st)
+            outs.append(num / (qc * dn).sum(dim=-1, keepdim=True).clamp_min(1e-6))
+            state, den_state = st[:, -1], dn[:, -1]
+        return torch.cat(outs, dim=1)
+
+    def graphed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
+
+    def timed(graph, k):
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(k):
+            graph.replay()
+        e1.record(stream)
+        barrier()
+        return 1e3 * max_over_ranks(e0.elapsed_time(e1)) / k
+
+    kern_us = timed(graphed(lambda: nk.linear_associative_memory(q, k, v)), 30)
+    torch_us = timed(graphed(chunked), 3)
+    nbytes = 2 * Bm * Tm * r * 4 + 2 * Bm * Tm * d * 2  # q, k (fp32) and v in, out
+    tiles = Bm * -(-Tm // 128) * -(-d // 128)
+    flops = tiles * 2 * 128 * (128 * 64 + 128 * 128 + 64 * 128 + 128 * 64)  # QK^T, PV, QS, V^T K per tile
+    return {"workload": "linear associative memory, B=8, T=2048, d=832, r=64, bf16 values",
+            "kernels_us": kern_us, "hbm_gbs": nbytes / (kern_us / 1e6) / 1e9,
+            "tensor_tflops": flops / (kern_us / 1e6) / 1e12, "torch_ops_us": torch_us}
 
 
 def run_ssd_block(dev, nk, barrier, max_over_ranks):

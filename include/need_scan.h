@@ -197,8 +197,8 @@ NEED_API size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t de
                                 int64_t C);
 
 /* Reads (and clears) the workspace's device-side error word: bit 0 = a look-back
- * wait gave up, bit 1 = a tile load wait gave up, bit 2 = an RMSNorm epilogue
- * wait for another channel block's sums gave up.  Synchronises `stream`. */
+ * wait gave up, bit 1 = a tile load (or tensor-core) wait gave up.
+ * Synchronises `stream`. */
 NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream);
 
 /* need_kernels.affine_recurrence_scan (need_kernels.py:229-264): args->form must be
@@ -244,10 +244,10 @@ NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);
  * where y is need_ssd_scan's output in `dtype`; the sum, the scale and the
  * products are fp32 and the result is rounded once to `dtype`, as the
  * reference's GPU rms_norm computes (need_kernels.py:99-107).  weight is [C],
- * NEED_F32 or `dtype` (weight_dtype).  C is at most 64 tiles of channels
- * (8192 for 16-bit streams); the tiles of one token chunk run at the same time
- * and exchange their sums through the workspace.  Workspace as for
- * need_ssd_scan. */
+ * NEED_F32 or `dtype` (weight_dtype).  Each scan tile stores its outputs and
+ * its rows' sums of squares; the last tile of each token chunk to finish
+ * normalises the chunk's rows in place.  Workspace as for need_ssd_scan (it
+ * holds the sums and a self-resetting counter per chunk). */
 NEED_API int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, int32_t weight_dtype,
                                     double eps, need_stream_t stream);
 

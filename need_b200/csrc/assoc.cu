@@ -51,8 +51,8 @@ constexpr int OFF_V = OFF_K + 2 * 16384;       // 2 stages x 2 boxes x [128 toke
 constexpr int OFF_P = OFF_V + 2 * 32768;       // 2 K-atoms x [128 tokens][64 tokens]
 constexpr int OFF_S = OFF_P + 32768;           // [128 columns][64 features] (K-major B of Q S)
 constexpr int OFF_O = OFF_S + 16384;           // 2 boxes x [128 tokens][64 columns], TMA store source
-constexpr int OFF_Z = OFF_O + 32768;           // z: 64 fp32
-constexpr int OFF_BAR = OFF_Z + kRank * 4;     // full[2], mma, tmem base
+constexpr int OFF_Z = OFF_O + 32768;           // z: 64 fp32, and 64 fp32 of partial column sums
+constexpr int OFF_BAR = OFF_Z + 2 * kRank * 4; // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
 struct AssocParams {
@@ -73,9 +73,11 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* z = reinterpret_cast<float*>(base + OFF_Z);
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + OFF_BAR);  // [2]
-    uint64_t* mmab = full + 2;
-    uint32_t* tbase = reinterpret_cast<uint32_t*>(full + 3);
+    float* zhalf = z + kRank;  // the upper rows' column sums
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + OFF_BAR);  // [2] tile loads
+    uint64_t* pbar = full + 2;  // P = Q K^T done
+    uint64_t* obar = full + 3;  // O and the state update done
+    uint32_t* tbase = reinterpret_cast<uint32_t*>(full + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int c0 = blockIdx.x * kCols, b = blockIdx.y;
@@ -85,7 +87,8 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     if (tid == 0) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
-        mbar_init(mmab, 1);
+        mbar_init(pbar, 1);
+        mbar_init(obar, 1);
         fence_barrier_init();
     }
     if (tid < kRank) z[tid] = 0.0f;
@@ -122,7 +125,20 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     }
 
     bool ok = true;
-    uint32_t mph = 0;
+    uint32_t pph = 0, oph = 0;  // phases of the P barrier and the O / state barrier
+    auto issue_qk = [&](int tile) {  // P = Q K^T of `tile` (its loads waited for here)
+        const int st = tile & 1;
+        const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
+        ok &= mbar_wait_bounded(&full[st], (tile >> 1) & 1, kAssocPolls);
+        umma::fence_after_sync();
+#pragma unroll
+        for (int k = 0; k < kRank / 16; ++k)
+            umma::mma_bf16(tP, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sK + 32 * k, 16, 1024), ID_QK,
+                           k > 0);
+        umma::mma_commit(pbar);
+    };
+    if (tid == 0) issue_qk(0);
+    int aborted_at = -1;
     for (int it = 0; it < ntile; ++it) {
         const int st = it & 1;
         const int t0 = it * kTok;
@@ -132,59 +148,57 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         const unsigned char* qrow = base + OFF_Q + st * 16384;
         const unsigned char* krow = base + OFF_K + st * 16384;
 
+        // q_t . z over the tiles before this one (this thread's token t = tid); the
+        // tile's loads have landed: thread 0 waited on them before issuing its P
         ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
-        // ---- P = Q K^T
-        if (tid == 0) {
-            umma::fence_after_sync();
-#pragma unroll
-            for (int k = 0; k < kRank / 16; ++k)
-                umma::mma_bf16(tP, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sK + 32 * k, 16, 1024),
-                               ID_QK, k > 0);
-            umma::mma_commit(mmab);
-        }
-        // q_t . z over the tiles before this one (this thread's token t = tid)
-        float qz = 0.0f;
+        float qz0 = 0.0f, qz1 = 0.0f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(tid, j));
             const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                qz = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz);
-                qz = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz);
+                qz0 = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz0);
+                qz1 = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz1);
             }
         }
-        ok &= mbar_wait_bounded(mmab, mph, kAssocPolls);
-        mph ^= 1u;
+        const float qz = qz0 + qz1;
+        ok &= mbar_wait_bounded(pbar, pph, kAssocPolls);
+        pph ^= 1u;
         umma::fence_after_sync();
 
         // ---- P epilogue: causal mask, row sum (fp32), bf16 P as the K-major A of P V
         float rs = 0.0f;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-            float v[32];
-            umma::tmem_ld32(tP + lane_off + 32 * cb, v);
+        for (int half = 0; half < 2; ++half) {
+            float v[2][32];
+            umma::tmem_ld32(tP + lane_off + 64 * half, v[0]);
+            umma::tmem_ld32(tP + lane_off + 64 * half + 32, v[1]);
             umma::tmem_wait_ld();
-            uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-                const float a0 = (32 * cb + e <= tid) ? v[e] : 0.0f;
-                const float a1 = (32 * cb + e + 1 <= tid) ? v[e + 1] : 0.0f;
-                rs += a0 + a1;
-                pk[e / 2] = pack_bf16(a0, a1);
+            for (int h = 0; h < 2; ++h) {
+                const int cb = 2 * half + h;
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float a0 = (32 * cb + e <= tid) ? v[h][e] : 0.0f;
+                    const float a1 = (32 * cb + e + 1 <= tid) ? v[h][e + 1] : 0.0f;
+                    rs += a0 + a1;
+                    pk[e / 2] = pack_bf16(a0, a1);
+                }
+                unsigned char* prow = base + OFF_P + half * 16384;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<uint4*>(prow + umma::sw128(tid, h * 4 + q4)) =
+                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
             }
-            unsigned char* prow = base + OFF_P + (cb >> 1) * 16384;
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-                *reinterpret_cast<uint4*>(prow + umma::sw128(tid, (cb & 1) * 4 + q4)) =
-                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
         }
-        fence_proxy_async_shared();  // P and last tile's S copy visible to the tensor cores
+        fence_proxy_async_shared();  // P and last tile's state copy visible to the tensor cores
         if (tid == 0) umma::tma_store_wait_read();  // last tile's output store has left shared memory
         umma::fence_before_sync();
         __syncthreads();
 
-        // ---- O = P V + Q S; S^T += V^T K
+        // ---- O = P V + Q S; S^T += V^T K; then the next tile's P
         if (tid == 0) {
             umma::fence_after_sync();
 #pragma unroll
@@ -201,56 +215,75 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             for (int k = 0; k < kTok / 16; ++k)
                 umma::mma_bf16(tS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
                                umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
-            umma::mma_commit(mmab);
+            umma::mma_commit(obar);
+            // P of the next tile overlaps this tile's output epilogue (its TMEM
+            // columns were read out above)
+            if (it + 1 < ntile) issue_qk(it + 1);
         }
-        // z += column sums of this tile's k (every thread has read z for q_t . z)
-        if (tid < kRank) {
-            float s = 0.0f;
-            const int j = tid >> 3, e = tid & 7;
-            for (int r = 0; r < kTok; ++r) {
-                const uint16_t h = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r, j) + 2 * e);
-                s += __uint_as_float(static_cast<uint32_t>(h) << 16);
+        // z += column sums of this tile's k, after every thread has read z above:
+        // thread c (and c + 64) sums half the rows of feature c
+        {
+            const int c = tid & 63, r0 = (tid >> 6) * 64;
+            const int j = c >> 3, e = c & 7;
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+            for (int r = 0; r < 64; ++r) {
+                const uint16_t h = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
+                a[r & 3] += __uint_as_float(static_cast<uint32_t>(h) << 16);
             }
-            z[tid] += s;
+            const float part = (a[0] + a[1]) + (a[2] + a[3]);
+            if (tid >= 64) zhalf[c] = part;
+            named_sync(1, kThreads);
+            if (tid < 64) z[c] += part + zhalf[c];
         }
-        ok &= mbar_wait_bounded(mmab, mph, kAssocPolls);
-        mph ^= 1u;
+        ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
+        oph ^= 1u;
         umma::fence_after_sync();
 
         // ---- outputs: O / max(q.z + rowsum, eps) in bf16, staged for the TMA store
         const float inv = 1.0f / fmaxf(qz + rs, p.eps);
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-            float v[32];
-            umma::tmem_ld32(tO + lane_off + 32 * cb, v);
+        for (int half = 0; half < 2; ++half) {
+            float v[2][32];
+            umma::tmem_ld32(tO + lane_off + 64 * half, v[0]);
+            umma::tmem_ld32(tO + lane_off + 64 * half + 32, v[1]);
             umma::tmem_wait_ld();
-            uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e] * inv, v[e + 1] * inv);
-            unsigned char* orow = base + OFF_O + (cb >> 1) * 16384;
+            for (int h = 0; h < 2; ++h) {
+                uint32_t pk[16];
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-                *reinterpret_cast<uint4*>(orow + umma::sw128(tid, (cb & 1) * 4 + q4)) =
-                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[h][e] * inv, v[h][e + 1] * inv);
+                unsigned char* orow = base + OFF_O + half * 16384;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<uint4*>(orow + umma::sw128(tid, h * 4 + q4)) =
+                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
         }
         // ---- the state after this tile, bf16, as the K-major B of the next Q S (row = column of d)
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            float v[32];
-            umma::tmem_ld32(tS + lane_off + 32 * cb, v);
+        {
+            float v[2][32];
+            umma::tmem_ld32(tS + lane_off, v[0]);
+            umma::tmem_ld32(tS + lane_off + 32, v[1]);
             umma::tmem_wait_ld();
-            uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e], v[e + 1]);
-            unsigned char* srow = base + OFF_S;
+            for (int cb = 0; cb < 2; ++cb) {
+                uint32_t pk[16];
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-                *reinterpret_cast<uint4*>(srow + umma::sw128(tid, cb * 4 + q4)) =
-                    make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[cb][e], v[cb][e + 1]);
+                unsigned char* srow = base + OFF_S;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<uint4*>(srow + umma::sw128(tid, cb * 4 + q4)) =
+                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+            }
         }
         fence_proxy_async_shared();  // staged outputs (TMA store) and S (next MMA) visible to the async proxy
         umma::fence_before_sync();
-        if (!__syncthreads_and(ok)) break;  // a wait gave up: stop (uniformly) and report
+        if (!__syncthreads_and(ok)) {  // a wait gave up: stop (uniformly) and report
+            aborted_at = it;
+            break;
+        }
         if (tid == 0) {
             umma::tma_store_3d(&p.tm_out, base + OFF_O, c0, t0, b);
             if (c0 + 64 < p.d) umma::tma_store_3d(&p.tm_out, base + OFF_O + 16384, c0 + 64, t0, b);
@@ -258,6 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             if (it + 2 < ntile) issue_load(it + 2, st);  // this stage's MMAs and readers are done
         }
     }
+    // after a give-up, the next tile's P may still be in flight: its commit
+    // covers every MMA issued, so wait (bounded) before freeing tensor memory
+    if (tid == 0 && aborted_at >= 0 && aborted_at + 1 < ntile) mbar_wait_bounded(pbar, pph, kAssocPolls);
     if (tid == 0) umma::tma_store_wait_all();
     if (!ok) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
     umma::fence_before_sync();

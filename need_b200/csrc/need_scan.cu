@@ -206,9 +206,6 @@ bool select_plan(int form, int dt, int ddt, int rd, Plan* out) {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-// channel blocks (tiles per token chunk) the RMSNorm epilogue takes: 8192
-// channels in 16-bit tiles of 128, as many as the reference's fused norm
-constexpr int kMaxNormBlocks = 64;
 
 struct Geometry {
     int64_t ncb, nchains, nchunks, ntiles;
@@ -224,9 +221,11 @@ Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) 
 }
 
 // header, tagged AGG and INCL records, and (SSD) the RMSNorm sums per tile row
+// and a chunk counter per tile
 size_t ws_bytes(const Plan& pl, int64_t ntiles) {
     const size_t hdr = WS_HDR_WORDS * 4;
-    return hdr + size_t(ntiles) * (size_t(pl.CB) * sizeof(ulonglong2) * 2 + size_t(pl.norm_rows) * 8);
+    return hdr + size_t(ntiles) * (size_t(pl.CB) * sizeof(ulonglong2) * 2 +
+                                   (pl.norm_rows ? size_t(pl.norm_rows) * 4 + 4 : 0));
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -357,7 +356,8 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     P->hdr = reinterpret_cast<uint32_t*>(ws);
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * pl->CB;
-    P->norm_part = reinterpret_cast<unsigned long long*>(P->incl + size_t(g.ntiles) * pl->CB);
+    P->norm_part = reinterpret_cast<float*>(P->incl + size_t(g.ntiles) * pl->CB);
+    P->norm_count = reinterpret_cast<uint32_t*>(P->norm_part + size_t(g.ntiles) * pl->norm_rows);
     return NEED_OK;
 }
 
@@ -456,12 +456,6 @@ int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, 
                     args->dtype);
     if (!(eps >= 0.0)) return fail(NEED_ERR_INVALID, "eps must be >= 0");
     Plan pl;
-    if (args->form == NEED_FORM_SSD && select_plan(NEED_FORM_SSD, args->dtype, args->dtype, 0, &pl) &&
-        args->C > int64_t(kMaxNormBlocks) * pl.CB)
-        // The tiles of one token chunk wait for one another's sums: all of them
-        // must be resident on the GPU at once.
-        return fail(NEED_ERR_UNSUPPORTED, "C=%lld: the RMSNorm epilogue takes at most %d channels",
-                    (long long)args->C, kMaxNormBlocks * pl.CB);
     ScanParams P;
     if (int rc = prepare(args, NEED_FORM_SSD, &pl, &P)) return rc;
     if (pl.launch_norm == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no RMSNorm epilogue for dtype %d", args->dtype);

@@ -50,7 +50,7 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
 // word 8: leading chunks a sequence-parallel fix-up rewrites
 enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_CHUNKS = 8, WS_HDR_WORDS = 32 };
-enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u, ERR_NORM = 4u };
+enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
 
 constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst case
 #ifndef NEED_LOOKBACK_DEPTH
@@ -60,8 +60,6 @@ constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst 
 constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
 static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
-// RMSNorm epilogue: polls of the sibling tiles' sums (~0.5 us each: ~0.1 s worst case)
-constexpr uint32_t kNormPolls = 1u << 18;
 // registers per thread the occupancy bound plans for
 #ifndef NEED_REG_BUDGET
 #define NEED_REG_BUDGET 112
@@ -100,7 +98,8 @@ struct ScanParams {
     const void* norm_w;
     int32_t norm_w32;
     float norm_eps;
-    unsigned long long* norm_part;  // [ntiles][L]
+    float* norm_part;      // [ntiles][L]: sums of squares of each tile's rows
+    uint32_t* norm_count;  // [ntiles / ncb]: tiles of each token chunk done (self-resetting)
 };
 
 // ------------------------------------------------------------------ types
@@ -380,9 +379,8 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
 // one row (a'_t = a_{t+1}, a'_{T-1} = 0): a tensor map based at row 1 with
 // T-1 rows, or, for a decay per row, a guarded load of row t+1.
 // NORM = true (SSD only): the outputs of each token are RMS-normalised over all
-// C channels before they are stored (RMSNorm after the scan).  The ncb tiles
-// of one token chunk, adjacent in blockIdx, exchange per-row sums of squares
-// through tagged records and each waits (bounded) for its siblings' sums.
+// C channels (RMSNorm after the scan).  The last of a token chunk's ncb tiles
+// to finish normalises the chunk's rows from the tiles' sums of squares.
 template <class K, bool FIX = false, bool REV = false, bool NORM = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
     static_assert(!NORM || (K::FORM == FORM_SSD && !FIX && !REV), "RMSNorm epilogue: SSD forward only");
@@ -402,7 +400,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
-    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // the launch's record tag
+    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // NORM: this tile normalises its chunk
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -472,7 +470,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 ep = static_cast<uint32_t>(old >> 32);
             }
             const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
-            if (NORM && lane == 0) *s_tag = tag;  // read by the row warps after the carry barrier
             auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
             float carry[8], carryP[8];
             float2 TA[4], TB[4];  // this tile's map
@@ -838,80 +835,90 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             // RMSNorm epilogue (need_kernels.py:99-107, the reference's GPU
             // rms_norm): y is the scan's output in the stream dtype; per token
             // ss = sum(y^2) / C in fp32, inv = rsqrt(ss + eps), out = y * inv * w
-            // in fp32, rounded once.  The rows stay in registers while the
-            // channel blocks of the token chunk exchange their sums.
-            PS ys[RS][4];
+            // in fp32, rounded once.  Every tile stores its y and its rows' sums of
+            // squares; the last of the token chunk's ncb tiles to finish (a
+            // self-resetting counter) adds the sums in channel-block order and
+            // rewrites the chunk's rows normalised, while they are still in L2.
+            // Nothing waits on another CTA.
             float ss[RS];
 #pragma unroll
             for (int j = 0; j < RS; ++j) {
                 ss[j] = 0.0f;
                 if (j < rend) {
-                    step(r0 + j, ys[j]);
+                    PS o[4];
+                    step(r0 + j, o);
                     float2 acc = splat2(0.0f);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float2 y = widen(ys[j][i]);
+                        const float2 y = widen(o[i]);
                         if (i < 2 ? ok0 : ok1) acc = ffma2(y, y, acc);
                     }
                     ss[j] = acc.x + acc.y;
+                    Row8<TS, SPLIT>::stg(orow + j * ostep, v, o, ok0, ok1);
                 }
             }
 #pragma unroll
             for (int m = 1; m < LPR; m <<= 1)
 #pragma unroll
                 for (int j = 0; j < RS; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], m);
-            const uint32_t tag = *s_tag;
-            unsigned long long* part = p.norm_part + (int64_t)(tile - cblk) * L + r0;  // channel block 0's rows
             if (v == 0) {
 #pragma unroll
                 for (int j = 0; j < RS; ++j)
-                    if (j < rend) st_relaxed_u64(part + (int64_t)cblk * L + j, tagged(ss[j], tag));
+                    if (j < rend) p.norm_part[(int64_t)tile * L + r0 + j] = ss[j];
             }
-            float wv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int c = c0 + chan<SPLIT>(e, v);
-                wv[e] = c >= p.C ? 0.0f
-                        : p.norm_w32 ? static_cast<const float*>(p.norm_w)[c]
-                                     : to_f(static_cast<const TS*>(p.norm_w)[c]);
+            __threadfence();  // this thread's outputs and sums, before the count below
+            named_sync(2, NW * 32);
+            if (tid == 0) {
+                const uint32_t old = atomicInc(&p.norm_count[tile / p.ncb], static_cast<uint32_t>(p.ncb - 1));
+                const bool last = old == static_cast<uint32_t>(p.ncb - 1);
+                if (last) __threadfence();  // the other tiles' outputs and sums, before reading them
+                *s_tag = last ? 1u : 0u;
             }
-            // the sums of all channel blocks, added in block order (bounded wait)
-            float tot[RS];
-            bool got = false;
-            for (uint32_t it = 0; it < kNormPolls; ++it) {
-                bool valid = true;
+            named_sync(2, NW * 32);
+            if (*s_tag != 0u) {
+                // the slots are free once every row warp is past phase 2
+                float* s_inv = reinterpret_cast<float*>(slot_ptr<K>(base, 0));
+                const float* part = p.norm_part + (int64_t)(tile - cblk) * L;  // channel block 0's rows
+                for (int r = tid; r < nvalid; r += NW * 32) {
+                    float tot = 0.0f;
+                    for (int sblk = 0; sblk < p.ncb; ++sblk) tot += __ldcg(part + (int64_t)sblk * L + r);
+                    s_inv[r] = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.C)), p.norm_eps));
+                }
+                named_sync(2, NW * 32);
+                constexpr int VEC = 16 / Ops<TS>::BYTES;  // elements per 16-byte access
+                const int nvec = p.C / VEC;
+                TS* rows = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh;
+                for (int i = tid; i < nvalid * nvec; i += NW * 32) {
+                    const int r = i / nvec, c = (i - r * nvec) * VEC;
+                    const int64_t t = REV ? p.T - 1 - t0 - r : t0 + r;
+                    uint4* ptr = reinterpret_cast<uint4*>(rows + t * p.ost + c);
+                    uint4 x = __ldcg(ptr);
+                    const float inv = s_inv[r];
+                    if constexpr (Ops<TS>::BYTES == 4) {
+                        float* f = reinterpret_cast<float*>(&x);
 #pragma unroll
-                for (int j = 0; j < RS; ++j) {
-                    tot[j] = 0.0f;
-                    if (j < rend) {
-                        for (int s = 0; s < p.ncb; ++s) {
-                            const unsigned long long w = ld_relaxed_u64(part + (int64_t)s * L + j);
-                            valid &= tag_ok(w, tag);
-                            tot[j] += untag(w);
+                        for (int e = 0; e < 4; ++e) {
+                            const float w = p.norm_w32 ? static_cast<const float*>(p.norm_w)[c + e]
+                                                       : to_f(static_cast<const TS*>(p.norm_w)[c + e]);
+                            f[e] = __fmul_rn(__fmul_rn(f[e], inv), w);
+                        }
+                    } else {
+                        PS* h = reinterpret_cast<PS*>(&x);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 y = widen(h[e]);
+                            float w0, w1;
+                            if (p.norm_w32) {
+                                w0 = static_cast<const float*>(p.norm_w)[c + 2 * e];
+                                w1 = static_cast<const float*>(p.norm_w)[c + 2 * e + 1];
+                            } else {
+                                w0 = to_f(static_cast<const TS*>(p.norm_w)[c + 2 * e]);
+                                w1 = to_f(static_cast<const TS*>(p.norm_w)[c + 2 * e + 1]);
+                            }
+                            h[e] = OS::pack(__fmul_rn(__fmul_rn(y.x, inv), w0), __fmul_rn(__fmul_rn(y.y, inv), w1));
                         }
                     }
-                }
-                if (__all_sync(0xffffffffu, valid)) {
-                    got = true;
-                    break;
-                }
-                __nanosleep(64);
-                if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
-            }
-            if (!got && lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_NORM);
-            const float rc = static_cast<float>(p.C);
-#pragma unroll
-            for (int j = 0; j < RS; ++j) {
-                if (j < rend) {
-                    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(tot[j], rc), p.norm_eps));
-                    PS o[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 y = widen(ys[j][i]);
-                        o[i] = OS::pack(__fmul_rn(__fmul_rn(y.x, inv), wv[2 * i]),
-                                        __fmul_rn(__fmul_rn(y.y, inv), wv[2 * i + 1]));
-                    }
-                    Row8<TS, SPLIT>::stg(orow + j * ostep, v, o, ok0, ok1);
+                    *ptr = x;
                 }
             }
         }

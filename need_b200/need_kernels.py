@@ -18,9 +18,13 @@ gradients raises.  ``rms_norm``, ``swiglu``, ``residual_scale_add``,
 ``sparse_moe_combine`` and ``sample_from_logits`` are outside the scan path;
 they are plain PyTorch expressions so that ``need_core`` keeps working.
 
-New entry points (no reference counterpart): ``gated_scan`` (sigmoid-gated
-scan with packed-segment resets, initial and final state), ``ragged_verify`` /
-``commit_states`` (speculative-decode state update), and the pieces of the
+New entry points (no ``need_kernels`` counterpart): ``gated_scan``
+(sigmoid-gated scan with packed-segment resets, initial and final state),
+``ragged_verify`` / ``commit_states`` (speculative-decode state update),
+``segment_starts`` (reset mask of packed token windows), ``ssd_conv_silu`` and
+``ssd_scan_rms_norm`` (the SSD block's prologue, and its scan with the
+out_norm fused), ``linear_associative_memory`` (HierarchicalMemory's
+matrix-state memory, need_core.py:1960-2001), and the pieces of the
 sequence-parallel scan used by ``need_b200.sp``.
 """
 from __future__ import annotations
@@ -559,10 +563,6 @@ def ssd_scan(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tensor, dt_raw
     return out if out.dtype == u.dtype else out.to(u.dtype)
 
 
-# Channels the fused RMSNorm epilogue takes (64 channel tiles of 128 or 256).
-_NORM_MAX_C = {torch.bfloat16: 8192, torch.float16: 8192, torch.float32: 16384}
-
-
 def _rms_norm_gpu(y: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """The reference's GPU rms_norm arithmetic (need_kernels.py:99-107) as torch
     ops: fp32 mean of squares, rsqrt, y * inv * w in fp32, one rounding."""
@@ -583,10 +583,10 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
     token is then normalised over its D channels as the reference's GPU
     ``rms_norm`` computes (need_kernels.py:99-107): ``y * rsqrt(mean(y^2) + eps)
     * weight`` in fp32 from the scan's output in ``u.dtype``, rounded once.  The
-    normalised tensor is written straight from the scan's registers, so the
-    scan's output never makes a round trip through HBM.  Shapes the fused
-    kernel does not take (D not a multiple of 8, or above 8192 channels for
-    16-bit inputs) run :func:`ssd_scan` and the same normalisation as torch ops.
+    last scan tile of each token chunk normalises the chunk's rows while they
+    are still in L2, so the scan's output makes no extra round trip through
+    HBM.  D not a multiple of 8 runs :func:`ssd_scan` and the same
+    normalisation as torch ops.
     """
     del backend
     b, t, d = u.shape
@@ -598,7 +598,7 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
     ts = u.dtype if u.dtype in _DT else torch.float32
     if u.numel() == 0:
         return torch.empty_like(u)
-    if not _channel_ok(d, ts == torch.float32) or d > _NORM_MAX_C[ts]:
+    if not _channel_ok(d, ts == torch.float32):
         y = ssd_scan(u, b_gate, c_gate, dt_raw, out_gate, d_skip, dt_min, dt_max,
                      seg_start=seg_start, h0=h0, h_final=h_final)
         return _rms_norm_gpu(y, norm_weight.reshape(-1), eps)

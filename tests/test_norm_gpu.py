@@ -6,6 +6,7 @@ Tolerances as for the scan: fp32 1e-5 relative; 16-bit 2e-2 relative with at
 least 99% of outputs bit-identical.  Against the same normalisation applied by
 torch ops to this library's own ssd_scan output, the fused kernel differs only
 by the order of the fp32 sum of squares: 99.9% of outputs bit-identical.
+Repeated calls are bit-identical (the sums are added in a fixed order).
 """
 import numpy as np
 import pytest
@@ -80,7 +81,8 @@ def test_matches_reference_fixture(cuda, name):
     (1, 64, 128, torch.bfloat16, False),     # one tile
     (3, 200, 96, torch.float16, True),       # one partial tile
     (2, 130, 520, torch.float32, True),      # fp32: 256-channel tiles
-    (1, 70, 8192, torch.bfloat16, False),    # the largest fused width: 64 channel tiles
+    (1, 70, 8192, torch.bfloat16, False),    # 64 channel tiles per token chunk
+    (2, 50, 8200, torch.bfloat16, True),     # 65 channel tiles, the last one 8 channels wide
 ])
 def test_matches_oracle(cuda, B, T, C, dtype, resets):
     xs, dskip, w, seg = inputs(B, T, C, dtype, seed=C + T, resets=resets)
@@ -129,10 +131,10 @@ def test_weight_in_model_dtype_and_projection_chunks(cuda):
     no_device_error()
 
 
-@pytest.mark.parametrize("C", [100, 8200])
+@pytest.mark.parametrize("C", [100, 36])
 def test_widths_outside_the_fused_kernel(cuda, C):
-    """D not a multiple of 8, or wider than the fused kernel takes: the scan
-    kernel and the normalisation as torch ops, same arithmetic."""
+    """D not a multiple of 8: the scan kernel and the normalisation as torch
+    ops, same arithmetic."""
     xs, dskip, w, _ = inputs(1, 40, C, torch.bfloat16, seed=C)
     got = nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs], dskip.to(cuda), 0.001, 0.2, w.to(cuda), 1e-5)
     want, _ = oracle_norm(xs, dskip, w, None, torch.bfloat16, 1e-5)
@@ -143,3 +145,16 @@ def test_bad_weight_size(cuda):
     xs, dskip, w, _ = inputs(1, 8, 64, torch.bfloat16, seed=0)
     with pytest.raises(ValueError):
         nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs], dskip.to(cuda), 0.001, 0.2, w[:32].to(cuda))
+
+
+def test_repeat_calls_identical_and_workspace_reuse(cuda):
+    """The chunk counters reset themselves: back-to-back calls on one workspace,
+    with different shapes in between, give identical results."""
+    xs, dskip, w, seg = inputs(2, 700, 832, torch.bfloat16, seed=8, resets=True)
+    args = ([x.to(cuda) for x in xs], dskip.to(cuda), w.to(cuda), seg.to(cuda))
+    a = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
+    xs2, d2, w2, _ = inputs(3, 129, 96, torch.bfloat16, seed=9)
+    nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs2], d2.to(cuda), 0.001, 0.2, w2.to(cuda))
+    b = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
+    assert torch.equal(a, b)
+    no_device_error()
