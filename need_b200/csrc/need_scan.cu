@@ -225,7 +225,7 @@ Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) 
 size_t ws_bytes(const Plan& pl, int64_t ntiles) {
     const size_t hdr = WS_HDR_WORDS * 4;
     return hdr + size_t(ntiles) * (size_t(pl.CB) * sizeof(ulonglong2) * 2 +
-                                   (pl.norm_rows ? size_t(pl.norm_rows) * 4 + 4 : 0));
+                                   (pl.norm_rows ? size_t(pl.norm_rows) * 4 + 8 : 0));
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -357,7 +357,7 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * pl->CB;
     P->norm_part = reinterpret_cast<float*>(P->incl + size_t(g.ntiles) * pl->CB);
-    P->norm_count = reinterpret_cast<uint32_t*>(P->norm_part + size_t(g.ntiles) * pl->norm_rows);
+    P->norm_count = reinterpret_cast<unsigned long long*>(P->norm_part + size_t(g.ntiles) * pl->norm_rows);
     return NEED_OK;
 }
 

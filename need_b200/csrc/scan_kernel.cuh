@@ -94,12 +94,12 @@ struct ScanParams {
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
     // RMSNorm over the C channels of each output token (scan_kernel<K, false,
     // false, true>): weight [C] (fp32 when norm_w32, else the stream dtype),
-    // eps, and per tile and row the tagged sum of squares of the tile's outputs
+    // eps, the sum of squares of each tile row and a counter per token chunk
     const void* norm_w;
     int32_t norm_w32;
     float norm_eps;
-    float* norm_part;      // [ntiles][L]: sums of squares of each tile's rows
-    uint32_t* norm_count;  // [ntiles / ncb]: tiles of each token chunk done (self-resetting)
+    float* norm_part;                  // [ntiles][L]: sums of squares of each tile's rows
+    unsigned long long* norm_count;    // [ntiles / ncb]: {launch tag, tiles of the token chunk done}
 };
 
 // ------------------------------------------------------------------ types
@@ -400,7 +400,8 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
-    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // NORM: this tile normalises its chunk
+    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // NORM: the launch's tag, then
+                                                                   // whether this tile normalises its chunk
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -470,6 +471,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 ep = static_cast<uint32_t>(old >> 32);
             }
             const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
+            if (NORM && lane == 0) *s_tag = tag;  // read by the row warps after the carry barrier
             auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
             float carry[8], carryP[8];
             float2 TA[4], TB[4];  // this tile's map
@@ -839,7 +841,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             // squares; the last of the token chunk's ncb tiles to finish (a
             // self-resetting counter) adds the sums in channel-block order and
             // rewrites the chunk's rows normalised, while they are still in L2.
-            // Nothing waits on another CTA.
+            // Nothing waits on another CTA.  The counter word carries the launch's
+            // tag, so a word left by an earlier launch (or by other records in a
+            // shared workspace) counts as zero.
             float ss[RS];
 #pragma unroll
             for (int j = 0; j < RS; ++j) {
@@ -869,13 +873,21 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             __threadfence();  // this thread's outputs and sums, before the count below
             named_sync(2, NW * 32);
             if (tid == 0) {
-                const uint32_t old = atomicInc(&p.norm_count[tile / p.ncb], static_cast<uint32_t>(p.ncb - 1));
-                const bool last = old == static_cast<uint32_t>(p.ncb - 1);
+                const uint32_t tag = *s_tag;
+                unsigned long long* ctr = &p.norm_count[tile / p.ncb];
+                unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(ctr), want;
+                for (;;) {  // {tag, n} -> {tag, n + 1}; a stale word -> {tag, 1}; at most ncb rounds
+                    want = static_cast<uint32_t>(seen >> 32) == tag ? seen + 1 : ((unsigned long long)tag << 32) | 1u;
+                    const unsigned long long prev = atomicCAS(ctr, seen, want);
+                    if (prev == seen) break;
+                    seen = prev;
+                }
+                const bool last = static_cast<uint32_t>(want) == static_cast<uint32_t>(p.ncb);
                 if (last) __threadfence();  // the other tiles' outputs and sums, before reading them
-                *s_tag = last ? 1u : 0u;
+                s_tag[1] = last ? 1u : 0u;
             }
             named_sync(2, NW * 32);
-            if (*s_tag != 0u) {
+            if (s_tag[1] != 0u) {
                 // the slots are free once every row warp is past phase 2
                 float* s_inv = reinterpret_cast<float*>(slot_ptr<K>(base, 0));
                 const float* part = p.norm_part + (int64_t)(tile - cblk) * L;  // channel block 0's rows

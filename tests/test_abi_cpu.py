@@ -77,11 +77,11 @@ def test_sizes_and_chunk_lengths(lib):
     assert ws == 128 + ntiles * 128 * 32  # header + tagged (A, B) and (prod, h) records per channel
     assert lib.need_scan_workspace_size(abi.FORM_GATED, 7, 7, 0, 1, 1, 1, 8) == 0  # unknown dtype
     # SSD: 64-token tiles of 128 channels, plus the RMSNorm sums (4 bytes per tile
-    # row) and a counter per tile
+    # row) and a tagged 64-bit counter per tile
     assert lib.need_scan_chunk_len(abi.FORM_SSD, abi.BF16, abi.BF16, 0) == 64
     ws = lib.need_scan_workspace_size(abi.FORM_SSD, abi.BF16, abi.BF16, 0, 8, 1, 2048, 832)
     ntiles = 8 * 7 * (2048 // 64)
-    assert ws == 128 + ntiles * (128 * 32 + 64 * 4 + 4)
+    assert ws == 128 + ntiles * (128 * 32 + 64 * 4 + 8)
     assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
 
 

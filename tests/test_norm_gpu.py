@@ -148,13 +148,19 @@ def test_bad_weight_size(cuda):
 
 
 def test_repeat_calls_identical_and_workspace_reuse(cuda):
-    """The chunk counters reset themselves: back-to-back calls on one workspace,
-    with different shapes in between, give identical results."""
+    """The chunk counters carry the launch's tag: back-to-back calls on one
+    workspace, with other shapes and forms in between, give identical results."""
     xs, dskip, w, seg = inputs(2, 700, 832, torch.bfloat16, seed=8, resets=True)
     args = ([x.to(cuda) for x in xs], dskip.to(cuda), w.to(cuda), seg.to(cuda))
     a = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
     xs2, d2, w2, _ = inputs(3, 129, 96, torch.bfloat16, seed=9)
     nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs2], d2.to(cuda), 0.001, 0.2, w2.to(cuda))
+    # other scans in between leave their records where this call keeps its counters
+    g = torch.Generator().manual_seed(3)
+    z, gg, x = (torch.randn(4, 1500, 1024, generator=g).to(torch.bfloat16).to(cuda) for _ in range(3))
+    nk.gated_scan(z, gg, x)
+    xs3, d3, w3, _ = inputs(1, 90, 520, torch.float32, seed=10)
+    nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs3], d3.to(cuda), 0.001, 0.2, w3.to(cuda))
     b = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
     assert torch.equal(a, b)
     no_device_error()
