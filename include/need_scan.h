@@ -31,9 +31,10 @@
  *                                   (need_core.py:1620-1622), as one kernel
  *   need_assoc_memory            <- HierarchicalMemory._linear_associative_memory
  *                                   (need_core.py:1960-2001), the matrix-state memory
+ *   need_rms_norm                <- need_kernels.rms_norm (need_kernels.py:266-276; its
+ *                                   GPU kernel need_kernels.py:99-107)
  *   need_ssd_scan_rms_norm       <- need_kernels.ssd_scan followed by the block's
- *                                   out_norm (need_core.py:1624-1643 with
- *                                   need_kernels.rms_norm, need_kernels.py:266-276), fused
+ *                                   out_norm (need_core.py:1624-1643), one call
  *
  * Return codes: NEED_OK (0), or a need_status error; need_last_error() gives a
  * message for the calling thread's last failure.  All entry points are
@@ -160,6 +161,19 @@ typedef struct {
     int64_t seg_stride_b, seg_stride_t;
 } need_conv_args;
 
+/* need_rms_norm: RMSNorm over the C channels of nb x T rows. */
+typedef struct {
+    int32_t dtype;          /* x and out: NEED_BF16, NEED_F16 or NEED_F32 */
+    int32_t weight_dtype;   /* NEED_F32 or `dtype` */
+    int64_t nb, T, C;       /* C a multiple of 16 bytes' worth of elements */
+    const void* x;          /* [nb, T, C], channel stride 1, 16-byte aligned rows */
+    int64_t x_stride_b, x_stride_t;
+    void* out;              /* [nb, T, C], same rules; may be x (in place) */
+    int64_t out_stride_b, out_stride_t;
+    const void* weight;     /* [C], 16-byte aligned */
+    double eps;
+} need_norm_args;
+
 /* need_assoc_memory: the matrix-state associative memory of HierarchicalMemory. */
 typedef struct {
     int32_t dtype;          /* v and out: NEED_BF16 */
@@ -237,17 +251,21 @@ NEED_API int need_ssd_conv_silu(const need_conv_args* args, need_stream_t stream
 /* need_kernels.ssd_scan (need_kernels.py:302-339): args->form == NEED_FORM_SSD. */
 NEED_API int need_ssd_scan(const need_scan_args* args, need_stream_t stream);
 
-/* need_ssd_scan with StructuredDualRetention's out_norm fused after it
+/* need_kernels.rms_norm on the GPU (need_kernels.py:266-276), with the
+ * arithmetic of the reference's GPU kernel (need_kernels.py:99-107): per row,
+ * x in fp32, inv = rsqrt(sum(x^2) / C + eps), out = (x * inv) * weight as two
+ * fp32 products, rounded once to `dtype`.  The row's sum is added in a fixed
+ * order, so repeated calls give identical results. */
+NEED_API int need_rms_norm(const need_norm_args* args, need_stream_t stream);
+
+/* need_ssd_scan followed by StructuredDualRetention's out_norm
  * (need_core.py:1624-1643: out_norm(ssd_scan(...)), an RMSNorm over the C
- * channels of each token).  `out` receives, per token,
- *     y * rsqrt(sum_c(y^2) / C + eps) * weight
- * where y is need_ssd_scan's output in `dtype`; the sum, the scale and the
- * products are fp32 and the result is rounded once to `dtype`, as the
- * reference's GPU rms_norm computes (need_kernels.py:99-107).  weight is [C],
- * NEED_F32 or `dtype` (weight_dtype).  Each scan tile stores its outputs and
- * its rows' sums of squares; the last tile of each token chunk to finish
- * normalises the chunk's rows in place.  Workspace as for need_ssd_scan (it
- * holds the sums and a self-resetting counter per chunk). */
+ * channels of each token) in one call: the scan writes `out`, then
+ * need_rms_norm normalises `out` in place while it is still in L2.  `out`
+ * receives, per token, y * rsqrt(sum_c(y^2) / C + eps) * weight, where y is
+ * need_ssd_scan's output in `dtype` (need_rms_norm's arithmetic).  weight is
+ * [C], NEED_F32 or `dtype` (weight_dtype), 16-byte aligned; nh must be 1.
+ * Workspace as for need_ssd_scan. */
 NEED_API int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, int32_t weight_dtype,
                                     double eps, need_stream_t stream);
 

@@ -71,6 +71,15 @@ class NeedConvArgs(Structure):
     ]
 
 
+class NeedNormArgs(Structure):
+    _fields_ = [
+        ("dtype", c_int32), ("weight_dtype", c_int32), ("nb", c_int64), ("T", c_int64), ("C", c_int64),
+        ("x", c_void_p), ("x_stride_b", c_int64), ("x_stride_t", c_int64),
+        ("out", c_void_p), ("out_stride_b", c_int64), ("out_stride_t", c_int64),
+        ("weight", c_void_p), ("eps", c_double),
+    ]
+
+
 class NeedAssocArgs(Structure):
     _fields_ = [
         ("dtype", c_int32), ("qk_dtype", c_int32),
@@ -95,6 +104,7 @@ SIGNATURES = {
     "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan_rms_norm": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_double, c_void_p]),
+    "need_rms_norm": (c_int32, [POINTER(NeedNormArgs), c_void_p]),
     "need_assoc_memory_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int32]),
     "need_assoc_memory": (c_int32, [POINTER(NeedAssocArgs), c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libneed_scan.so")
-SOURCES = ["need_scan.cu", "decode.cu", "sp.cu", "noalloc.cu", "segments.cu", "prologue.cu", "assoc.cu"]
+SOURCES = ["need_scan.cu", "decode.cu", "sp.cu", "noalloc.cu", "segments.cu", "prologue.cu", "epilogue.cu", "assoc.cu"]
 HEADERS = ["ptx.cuh", "scan_kernel.cuh", "host_common.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

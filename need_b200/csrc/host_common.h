@@ -95,6 +95,11 @@ inline int ensure_context() {
     return e == cudaSuccess ? NEED_OK : cuda_fail(e, "binding the device context");
 }
 
+// RMSNorm over the C channels of nb x T rows (epilogue.cu); launches only.
+int rms_norm_rows(int32_t dtype, const void* x, int64_t xsb, int64_t xst, void* out, int64_t osb, int64_t ost,
+                  int64_t nb, int64_t T, int64_t C, const void* weight, int32_t weight_dtype, double eps,
+                  cudaStream_t stream);
+
 inline int dtype_bytes(int dt) { return dt == NEED_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == NEED_F32 || dt == NEED_BF16 || dt == NEED_F16; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -80,11 +80,9 @@ using RetCfg = ScanCfg<FORM_RETENTION, TS, TD, RD, RetL<TS, TD, RD>::L, RetL<TS,
 struct Plan {
     int L = 0, R = 0, CB = 0, nin = 0, in0 = 0;  // tokens, rows per warp, channels per tile
     bool dstream = false, split = false;
-    int norm_rows = 0;  // SSD: rows of RMSNorm sum records per tile in the workspace (L)
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
     int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;   // gated form only
     int (*launch_rev)(const ScanParams&, cudaStream_t) = nullptr;   // affine form only
-    int (*launch_norm)(const ScanParams&, cudaStream_t) = nullptr;  // SSD form only
 };
 
 template <class K>
@@ -138,18 +136,6 @@ int launch_rev_cfg(const ScanParams& prm, cudaStream_t s) {
     return NEED_OK;
 }
 
-// The SSD scan with the RMSNorm epilogue, one tile per CTA.
-template <class K>
-int launch_norm_cfg(const ScanParams& prm, cudaStream_t s) {
-    static std::atomic<uint64_t> smem_done{0};
-    cudaError_t e = ensure_smem(scan_kernel<K, false, false, true>, K::SMEM, smem_done);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel, rms norm)");
-    scan_kernel<K, false, false, true><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch (rms norm)");
-    return NEED_OK;
-}
-
 template <class K>
 Plan plan_of() {
     Plan p;
@@ -163,10 +149,6 @@ Plan plan_of() {
     p.launch = &launch_cfg<K>;
     if constexpr (K::FORM == FORM_GATED) p.launch_fix = &launch_fix_cfg<K>;
     if constexpr (K::FORM == FORM_AFFINE) p.launch_rev = &launch_rev_cfg<K>;
-    if constexpr (K::FORM == FORM_SSD) {
-        p.norm_rows = K::L;
-        p.launch_norm = &launch_norm_cfg<K>;
-    }
     return p;
 }
 
@@ -220,12 +202,9 @@ Geometry geometry(const Plan& pl, int64_t nb, int64_t nh, int64_t T, int64_t C) 
     return g;
 }
 
-// header, tagged AGG and INCL records, and (SSD) the RMSNorm sums per tile row
-// and a chunk counter per tile
 size_t ws_bytes(const Plan& pl, int64_t ntiles) {
     const size_t hdr = WS_HDR_WORDS * 4;
-    return hdr + size_t(ntiles) * (size_t(pl.CB) * sizeof(ulonglong2) * 2 +
-                                   (pl.norm_rows ? size_t(pl.norm_rows) * 4 + 8 : 0));
+    return hdr + size_t(ntiles) * size_t(pl.CB) * sizeof(ulonglong2) * 2;  // tagged AGG and INCL records
 }
 
 // ------------------------------------------------------------------ TMA descriptors
@@ -356,8 +335,6 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     P->hdr = reinterpret_cast<uint32_t*>(ws);
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * pl->CB;
-    P->norm_part = reinterpret_cast<float*>(P->incl + size_t(g.ntiles) * pl->CB);
-    P->norm_count = reinterpret_cast<unsigned long long*>(P->norm_part + size_t(g.ntiles) * pl->norm_rows);
     return NEED_OK;
 }
 
@@ -455,14 +432,16 @@ int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, 
         return fail(NEED_ERR_UNSUPPORTED, "norm weight dtype %d must be fp32 or the stream dtype %d", weight_dtype,
                     args->dtype);
     if (!(eps >= 0.0)) return fail(NEED_ERR_INVALID, "eps must be >= 0");
+    if (args->nh != 1) return fail(NEED_ERR_UNSUPPORTED, "the RMSNorm epilogue takes nh == 1");
     Plan pl;
     ScanParams P;
     if (int rc = prepare(args, NEED_FORM_SSD, &pl, &P)) return rc;
-    if (pl.launch_norm == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no RMSNorm epilogue for dtype %d", args->dtype);
-    P.norm_w = norm_weight;
-    P.norm_w32 = weight_dtype == NEED_F32 ? 1 : 0;
-    P.norm_eps = static_cast<float>(eps);
-    if (int rc = pl.launch_norm(P, stream)) return rc;
+    if (int rc = pl.launch(P, stream)) return rc;
+    // the normalisation over the rows just written, in place, while they are in L2
+    if (int rc = rms_norm_rows(args->dtype, args->out, args->out_stride_b, args->out_stride_t, args->out,
+                               args->out_stride_b, args->out_stride_t, args->nb, args->T, args->C, norm_weight,
+                               weight_dtype, eps, stream))
+        return rc;
     return ok();
 }
 

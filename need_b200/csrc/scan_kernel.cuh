@@ -30,8 +30,7 @@
 // HBM traffic is the algorithmic minimum (inputs read once, outputs written
 // once) plus 32 bytes of look-back records per channel and tile (normally
 // L2-resident).  The same kernel also runs the sequence-parallel fix-up
-// (FIX), the backward's reversed-time scan (REV) and the SSD scan with an
-// RMSNorm over each token's channels after it (NORM); see scan_kernel below.
+// (FIX) and the backward's reversed-time scan (REV); see scan_kernel below.
 #pragma once
 
 #include <cuda.h>
@@ -92,14 +91,6 @@ struct ScanParams {
     const uint32_t* fix_chunks;
     ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
-    // RMSNorm over the C channels of each output token (scan_kernel<K, false,
-    // false, true>): weight [C] (fp32 when norm_w32, else the stream dtype),
-    // eps, the sum of squares of each tile row and a counter per token chunk
-    const void* norm_w;
-    int32_t norm_w32;
-    float norm_eps;
-    float* norm_part;                  // [ntiles][L]: sums of squares of each tile's rows
-    unsigned long long* norm_count;    // [ntiles / ncb]: {launch tag, tiles of the token chunk done}
 };
 
 // ------------------------------------------------------------------ types
@@ -378,12 +369,8 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
 // output rows are mirrored.  The caller passes the decay already shifted by
 // one row (a'_t = a_{t+1}, a'_{T-1} = 0): a tensor map based at row 1 with
 // T-1 rows, or, for a decay per row, a guarded load of row t+1.
-// NORM = true (SSD only): the outputs of each token are RMS-normalised over all
-// C channels (RMSNorm after the scan).  The last of a token chunk's ncb tiles
-// to finish normalises the chunk's rows from the tiles' sums of squares.
-template <class K, bool FIX = false, bool REV = false, bool NORM = false>
+template <class K, bool FIX = false, bool REV = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
-    static_assert(!NORM || (K::FORM == FORM_SSD && !FIX && !REV), "RMSNorm epilogue: SSD forward only");
     using TS = typename K::TS;
     using TD = typename K::TD;
     using OS = Ops<TS>;
@@ -400,8 +387,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
-    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_bar + NW + 1);  // NORM: the launch's tag, then
-                                                                   // whether this tile normalises its chunk
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -471,7 +456,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 ep = static_cast<uint32_t>(old >> 32);
             }
             const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
-            if (NORM && lane == 0) *s_tag = tag;  // read by the row warps after the carry barrier
             auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
             float carry[8], carryP[8];
             float2 TA[4], TB[4];  // this tile's map
@@ -826,113 +810,11 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
             }
         };
-        if constexpr (!NORM) {
 #pragma unroll 2
-            for (int j = 0; j < rend; ++j, orow += ostep) {
-                PS o[4];
-                step(r0 + j, o);
-                Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
-            }
-        } else {
-            // RMSNorm epilogue (need_kernels.py:99-107, the reference's GPU
-            // rms_norm): y is the scan's output in the stream dtype; per token
-            // ss = sum(y^2) / C in fp32, inv = rsqrt(ss + eps), out = y * inv * w
-            // in fp32, rounded once.  Every tile stores its y and its rows' sums of
-            // squares; the last of the token chunk's ncb tiles to finish (a
-            // self-resetting counter) adds the sums in channel-block order and
-            // rewrites the chunk's rows normalised, while they are still in L2.
-            // Nothing waits on another CTA.  The counter word carries the launch's
-            // tag, so a word left by an earlier launch (or by other records in a
-            // shared workspace) counts as zero.
-            float ss[RS];
-#pragma unroll
-            for (int j = 0; j < RS; ++j) {
-                ss[j] = 0.0f;
-                if (j < rend) {
-                    PS o[4];
-                    step(r0 + j, o);
-                    float2 acc = splat2(0.0f);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 y = widen(o[i]);
-                        if (i < 2 ? ok0 : ok1) acc = ffma2(y, y, acc);
-                    }
-                    ss[j] = acc.x + acc.y;
-                    Row8<TS, SPLIT>::stg(orow + j * ostep, v, o, ok0, ok1);
-                }
-            }
-#pragma unroll
-            for (int m = 1; m < LPR; m <<= 1)
-#pragma unroll
-                for (int j = 0; j < RS; ++j) ss[j] += __shfl_xor_sync(0xffffffffu, ss[j], m);
-            if (v == 0) {
-#pragma unroll
-                for (int j = 0; j < RS; ++j)
-                    if (j < rend) p.norm_part[(int64_t)tile * L + r0 + j] = ss[j];
-            }
-            __threadfence();  // this thread's outputs and sums, before the count below
-            named_sync(2, NW * 32);
-            if (tid == 0) {
-                const uint32_t tag = *s_tag;
-                unsigned long long* ctr = &p.norm_count[tile / p.ncb];
-                unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(ctr), want;
-                for (;;) {  // {tag, n} -> {tag, n + 1}; a stale word -> {tag, 1}; at most ncb rounds
-                    want = static_cast<uint32_t>(seen >> 32) == tag ? seen + 1 : ((unsigned long long)tag << 32) | 1u;
-                    const unsigned long long prev = atomicCAS(ctr, seen, want);
-                    if (prev == seen) break;
-                    seen = prev;
-                }
-                const bool last = static_cast<uint32_t>(want) == static_cast<uint32_t>(p.ncb);
-                if (last) __threadfence();  // the other tiles' outputs and sums, before reading them
-                s_tag[1] = last ? 1u : 0u;
-            }
-            named_sync(2, NW * 32);
-            if (s_tag[1] != 0u) {
-                // the slots are free once every row warp is past phase 2
-                float* s_inv = reinterpret_cast<float*>(slot_ptr<K>(base, 0));
-                const float* part = p.norm_part + (int64_t)(tile - cblk) * L;  // channel block 0's rows
-                for (int r = tid; r < nvalid; r += NW * 32) {
-                    float tot = 0.0f;
-                    for (int sblk = 0; sblk < p.ncb; ++sblk) tot += __ldcg(part + (int64_t)sblk * L + r);
-                    s_inv[r] = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.C)), p.norm_eps));
-                }
-                named_sync(2, NW * 32);
-                constexpr int VEC = 16 / Ops<TS>::BYTES;  // elements per 16-byte access
-                const int nvec = p.C / VEC;
-                TS* rows = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh;
-                for (int i = tid; i < nvalid * nvec; i += NW * 32) {
-                    const int r = i / nvec, c = (i - r * nvec) * VEC;
-                    const int64_t t = REV ? p.T - 1 - t0 - r : t0 + r;
-                    uint4* ptr = reinterpret_cast<uint4*>(rows + t * p.ost + c);
-                    uint4 x = __ldcg(ptr);
-                    const float inv = s_inv[r];
-                    if constexpr (Ops<TS>::BYTES == 4) {
-                        float* f = reinterpret_cast<float*>(&x);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float w = p.norm_w32 ? static_cast<const float*>(p.norm_w)[c + e]
-                                                       : to_f(static_cast<const TS*>(p.norm_w)[c + e]);
-                            f[e] = __fmul_rn(__fmul_rn(f[e], inv), w);
-                        }
-                    } else {
-                        PS* h = reinterpret_cast<PS*>(&x);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 y = widen(h[e]);
-                            float w0, w1;
-                            if (p.norm_w32) {
-                                w0 = static_cast<const float*>(p.norm_w)[c + 2 * e];
-                                w1 = static_cast<const float*>(p.norm_w)[c + 2 * e + 1];
-                            } else {
-                                w0 = to_f(static_cast<const TS*>(p.norm_w)[c + 2 * e]);
-                                w1 = to_f(static_cast<const TS*>(p.norm_w)[c + 2 * e + 1]);
-                            }
-                            h[e] = OS::pack(__fmul_rn(__fmul_rn(y.x, inv), w0), __fmul_rn(__fmul_rn(y.y, inv), w1));
-                        }
-                    }
-                    *ptr = x;
-                }
-            }
+        for (int j = 0; j < rend; ++j, orow += ostep) {
+            PS o[4];
+            step(r0 + j, o);
+            Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
         }
         }  // row warps
         if constexpr (FIX) {  // the stage is refilled by the next tile's TMA

@@ -15,8 +15,10 @@ and conventions (need_kernels.py:229-345):
 The scan itself runs only on CUDA tensors through the C ABI.  There is no CPU
 or eager-PyTorch fallback: a CPU tensor, a missing library or a request for
 gradients raises.  ``rms_norm``, ``swiglu``, ``residual_scale_add``,
-``sparse_moe_combine`` and ``sample_from_logits`` are outside the scan path;
-they are plain PyTorch expressions so that ``need_core`` keeps working.
+``sparse_moe_combine`` and ``sample_from_logits`` are outside the scan path
+and keep working on any device: ``rms_norm`` (the SSD block's out_norm) runs a
+kernel where the reference runs its GPU kernel, and the torch expression
+elsewhere; the others are plain PyTorch expressions.
 
 New entry points (no ``need_kernels`` counterpart): ``gated_scan``
 (sigmoid-gated scan with packed-segment resets, initial and final state),
@@ -576,17 +578,16 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
                       norm_weight: torch.Tensor, eps: float = 1e-6, backend: str = "auto", *,
                       seg_start: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
                       h_final: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``rms_norm(ssd_scan(...), norm_weight, eps)`` in one kernel: the SSD block's
+    """``rms_norm(ssd_scan(...), norm_weight, eps)`` in one call: the SSD block's
     scan and its ``out_norm`` (need_core.py:1624-1643).
 
     The scan is :func:`ssd_scan`'s (same arguments and extensions); each output
     token is then normalised over its D channels as the reference's GPU
     ``rms_norm`` computes (need_kernels.py:99-107): ``y * rsqrt(mean(y^2) + eps)
-    * weight`` in fp32 from the scan's output in ``u.dtype``, rounded once.  The
-    last scan tile of each token chunk normalises the chunk's rows while they
-    are still in L2, so the scan's output makes no extra round trip through
-    HBM.  D not a multiple of 8 runs :func:`ssd_scan` and the same
-    normalisation as torch ops.
+    * weight`` in fp32 from the scan's output in ``u.dtype``, rounded once.  One
+    C call runs the scan and then the RMSNorm kernel in place over its output,
+    which is still in L2.  D not a multiple of 8 runs :func:`ssd_scan` and the
+    same normalisation as torch ops.
     """
     del backend
     b, t, d = u.shape
@@ -610,6 +611,8 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
     if w.dtype not in (torch.float32, ts):
         w = w.float()
     w = w.contiguous()
+    if w.data_ptr() % 16:
+        w = w.clone()
     a = abi.NeedScanArgs()
     _fill_common(a, abi.FORM_SSD, ts, b, 1, t, d, out)
     xu, xbg, xcg, xdt, xog = xs
@@ -746,12 +749,46 @@ def commit_states(states: torch.Tensor, states_k: torch.Tensor, cu_k: torch.Tens
 
 
 # --------------------------------------------------------------------------
-# outside the scan path: plain PyTorch, same contracts as need_kernels.py:266-371
+# outside the scan path, same contracts as need_kernels.py:266-371: rms_norm
+# (the SSD block's out_norm) has a kernel on CUDA, the rest is plain PyTorch
 # --------------------------------------------------------------------------
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, backend: str = "auto") -> torch.Tensor:
+    """need_kernels.rms_norm (need_kernels.py:266-276).  Where the reference runs
+    its GPU kernel (CUDA tensors, contiguous, at most 8192 channels) this runs
+    need_rms_norm with the same arithmetic (fp32 throughout, one rounding), as
+    long as no gradient is required (the kernel has no backward); elsewhere the
+    reference's torch expression (need_kernels.py:276)."""
+    del backend
+    if (x.is_cuda and weight.is_cuda and x.dtype in _DT and x.dim() >= 1 and x.numel() > 0
+            and x.is_contiguous() and weight.is_contiguous() and x.shape[-1] <= 8192
+            and weight.numel() == x.shape[-1] and x.shape[-1] % (16 // x.element_size()) == 0
+            and x.data_ptr() % 16 == 0
+            and not (torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad))):
+        return _rms_norm_kernel(x, weight, eps)
     inv = torch.rsqrt(x.float().pow(2).mean(dim=-1, keepdim=True) + eps).to(x.dtype)
     return x * inv * weight
+
+
+def _rms_norm_kernel(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None):
+    """need_rms_norm over the last dim of a contiguous CUDA tensor."""
+    c = x.shape[-1]
+    w = weight.reshape(-1)
+    if w.dtype not in (torch.float32, x.dtype):
+        w = w.float()
+    w = w.contiguous()
+    if w.data_ptr() % 16:
+        w = w.clone()
+    out = torch.empty_like(x) if out is None else out
+    a = abi.NeedNormArgs()
+    a.dtype, a.weight_dtype = _DT[x.dtype], _DT[w.dtype]
+    a.nb, a.T, a.C = 1, x.numel() // c, c
+    a.x, a.x_stride_b, a.x_stride_t = x.data_ptr(), 0, c
+    a.out, a.out_stride_b, a.out_stride_t = out.data_ptr(), 0, c
+    a.weight, a.eps = w.data_ptr(), float(eps)
+    abi.check("need_rms_norm", _lib().need_rms_norm(ctypes.byref(a), _stream(x.device)))
+    del w
+    return out
 
 
 def swiglu(a: torch.Tensor, b: torch.Tensor, backend: str = "auto") -> torch.Tensor:

@@ -49,6 +49,7 @@ def test_struct_layout_matches_header(tmp_path):
         "need_segment_args": (abi.NeedSegmentArgs, [f[0] for f in abi.NeedSegmentArgs._fields_]),
         "need_conv_args": (abi.NeedConvArgs, [f[0] for f in abi.NeedConvArgs._fields_]),
         "need_assoc_args": (abi.NeedAssocArgs, [f[0] for f in abi.NeedAssocArgs._fields_]),
+        "need_norm_args": (abi.NeedNormArgs, [f[0] for f in abi.NeedNormArgs._fields_]),
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
     for cname, (_, names) in fields.items():
@@ -76,12 +77,10 @@ def test_sizes_and_chunk_lengths(lib):
     ntiles = 16 * (1024 // 128) * (4096 // L)  # 128-channel tiles
     assert ws == 128 + ntiles * 128 * 32  # header + tagged (A, B) and (prod, h) records per channel
     assert lib.need_scan_workspace_size(abi.FORM_GATED, 7, 7, 0, 1, 1, 1, 8) == 0  # unknown dtype
-    # SSD: 64-token tiles of 128 channels, plus the RMSNorm sums (4 bytes per tile
-    # row) and a tagged 64-bit counter per tile
+    # SSD: 64-token tiles of 128 channels
     assert lib.need_scan_chunk_len(abi.FORM_SSD, abi.BF16, abi.BF16, 0) == 64
     ws = lib.need_scan_workspace_size(abi.FORM_SSD, abi.BF16, abi.BF16, 0, 8, 1, 2048, 832)
-    ntiles = 8 * 7 * (2048 // 64)
-    assert ws == 128 + ntiles * (128 * 32 + 64 * 4 + 8)
+    assert ws == 128 + 8 * 7 * (2048 // 64) * 128 * 32
     assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
 
 
@@ -112,6 +111,15 @@ def test_argument_errors_return_status(lib):
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F32, -1.0, None) == abi.ERR_INVALID
     s.T = 0
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F32, 1e-6, None) == abi.ERR_INVALID
+    n = abi.NeedNormArgs()
+    assert lib.need_rms_norm(None, None) == abi.ERR_INVALID
+    n.dtype, n.weight_dtype, n.nb, n.T, n.C = abi.BF16, abi.F32, 1, 4, 832
+    assert lib.need_rms_norm(ctypes.byref(n), None) == abi.ERR_INVALID  # null tensors
+    n.x = n.out = n.weight = 256
+    n.C = 100
+    assert lib.need_rms_norm(ctypes.byref(n), None) == abi.ERR_UNSUPPORTED  # C not a multiple of 8
+    n.C, n.weight_dtype = 832, abi.F16
+    assert lib.need_rms_norm(ctypes.byref(n), None) == abi.ERR_UNSUPPORTED  # weight dtype
     m = abi.NeedAssocArgs()
     assert lib.need_assoc_memory(None, None) == abi.ERR_INVALID
     m.dtype, m.qk_dtype, m.nb, m.T, m.r, m.d = abi.BF16, abi.F32, 1, 16, 64, 64

@@ -1,4 +1,5 @@
-"""The SSD scan with the block's out_norm fused after it (need_core.py:1624-1643:
+"""The SSD block's out_norm: need_rms_norm (need_kernels.rms_norm on CUDA) and
+the scan with the norm after it in one call (need_core.py:1624-1643:
 out_norm(ssd_scan(...))), against the oracle: the reference's ssd_scan followed
 by the reference's GPU rms_norm arithmetic (need_kernels.py:99-107).
 
@@ -148,14 +149,14 @@ def test_bad_weight_size(cuda):
 
 
 def test_repeat_calls_identical_and_workspace_reuse(cuda):
-    """The chunk counters carry the launch's tag: back-to-back calls on one
-    workspace, with other shapes and forms in between, give identical results."""
+    """Back-to-back calls on one workspace, with other shapes and forms in
+    between, give identical results."""
     xs, dskip, w, seg = inputs(2, 700, 832, torch.bfloat16, seed=8, resets=True)
     args = ([x.to(cuda) for x in xs], dskip.to(cuda), w.to(cuda), seg.to(cuda))
     a = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
     xs2, d2, w2, _ = inputs(3, 129, 96, torch.bfloat16, seed=9)
     nk.ssd_scan_rms_norm(*[x.to(cuda) for x in xs2], d2.to(cuda), 0.001, 0.2, w2.to(cuda))
-    # other scans in between leave their records where this call keeps its counters
+    # other scans in between leave their records in the shared workspace
     g = torch.Generator().manual_seed(3)
     z, gg, x = (torch.randn(4, 1500, 1024, generator=g).to(torch.bfloat16).to(cuda) for _ in range(3))
     nk.gated_scan(z, gg, x)
@@ -164,3 +165,37 @@ def test_repeat_calls_identical_and_workspace_reuse(cuda):
     b = nk.ssd_scan_rms_norm(*args[0], args[1], 0.001, 0.2, args[2], 1e-6, seg_start=args[3])
     assert torch.equal(a, b)
     no_device_error()
+
+
+@pytest.mark.parametrize("dtype,wdtype,rows,C", [
+    (torch.bfloat16, torch.float32, 3000, 832),
+    (torch.bfloat16, torch.bfloat16, 17, 8192),
+    (torch.float16, torch.float32, 100, 96),
+    (torch.float32, torch.float32, 50, 520),
+])
+def test_rms_norm_kernel_matches_oracle(cuda, dtype, wdtype, rows, C):
+    """need_kernels.rms_norm on CUDA runs need_rms_norm: the reference's GPU
+    arithmetic, against the oracle; repeated calls are identical."""
+    gen = torch.Generator().manual_seed(rows + C)
+    x = (torch.randn(2, rows, C, generator=gen) * 3.0).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(C, generator=gen)).to(wdtype)
+    got = nk.rms_norm(x.to(cuda), w.to(cuda), 1e-6)
+    assert got.dtype == dtype and got.shape == x.shape
+    want = oracle.rms_norm(x.float().numpy(), w.float().numpy(), 1e-6, dtype=NAME[dtype])
+    g = host(got)
+    assert float(np.abs(g - want).max() / np.abs(want).max()) <= TOL[dtype]
+    assert float(np.mean(g == want)) >= 0.999
+    assert torch.equal(got, nk.rms_norm(x.to(cuda), w.to(cuda), 1e-6))
+
+
+def test_rms_norm_keeps_the_torch_path_elsewhere(cuda):
+    """Under grad, or for shapes the reference's kernel does not take, the
+    reference's torch expression (need_kernels.py:276)."""
+    x = torch.randn(4, 8, 64, device=cuda, requires_grad=True)
+    w = torch.ones(64, device=cuda)
+    y = nk.rms_norm(x, w)
+    y.sum().backward()
+    assert x.grad is not None
+    xc = torch.randn(3, 10, 12).to(torch.bfloat16)  # CPU
+    ref = xc * torch.rsqrt(xc.float().pow(2).mean(dim=-1, keepdim=True) + 1e-6).to(xc.dtype) * torch.ones(12)
+    assert torch.equal(nk.rms_norm(xc, torch.ones(12)), ref)
