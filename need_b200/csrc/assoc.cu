@@ -40,7 +40,7 @@ namespace {
 constexpr int kTok = 128;    // tokens per tile
 constexpr int kCols = 128;   // columns of d per CTA
 constexpr int kRank = 64;    // feature rank, zero padded
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // two warpgroups
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAssocPolls = 1u << 20;  // try_wait polls per wait before giving up
 
@@ -51,8 +51,8 @@ constexpr int OFF_V = OFF_K + 2 * 16384;       // 2 stages x 2 boxes x [128 toke
 constexpr int OFF_P = OFF_V + 2 * 32768;       // 2 K-atoms x [128 tokens][64 tokens]
 constexpr int OFF_S = OFF_P + 32768;           // [128 columns][64 features] (K-major B of Q S)
 constexpr int OFF_O = OFF_S + 16384;           // 2 boxes x [128 tokens][64 columns], TMA store source
-constexpr int OFF_Z = OFF_O + 32768;           // z: 64 fp32, and 64 fp32 of partial column sums
-constexpr int OFF_BAR = OFF_Z + 2 * kRank * 4; // full[2], pbar, obar, tmem base
+constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q.z [2][128], row sums [2][128] (fp32)
+constexpr int OFF_BAR = OFF_Z + (5 * kRank + 4 * kTok) * 4;  // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
 struct AssocParams {
@@ -68,18 +68,25 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 // ------------------------------------------------------------------ main kernel
+// Two warpgroups.  Warp w reads tensor-memory lanes 32 (w % 4) .. + 31, so row
+// (token, or column of d for the state) `row` = 32 (w % 4) + lane belongs to
+// warps w and w + 4; warpgroup g takes half of each epilogue's columns.
 __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constant__ AssocParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* z = reinterpret_cast<float*>(base + OFF_Z);
-    float* zhalf = z + kRank;  // the upper rows' column sums
+    float* z = reinterpret_cast<float*>(base + OFF_Z);  // [64] sum of k over the tiles so far
+    float* zpart = z + kRank;                           // [4][64] column sums of a quarter of the rows
+    float* s_qz = zpart + 4 * kRank;                    // [2][128] q_t . z, per half of the features
+    float* s_rs = s_qz + 2 * kTok;                      // [2][128] masked row sums of P, per half
     uint64_t* full = reinterpret_cast<uint64_t*>(base + OFF_BAR);  // [2] tile loads
     uint64_t* pbar = full + 2;  // P = Q K^T done
     uint64_t* obar = full + 3;  // O and the state update done
     uint32_t* tbase = reinterpret_cast<uint32_t*>(full + 4);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wg = warp >> 2, lw = warp & 3;
+    const int row = lw * 32 + lane;
     const int c0 = blockIdx.x * kCols, b = blockIdx.y;
     const int ntile = (p.T + kTok - 1) / kTok;
     const uint32_t sbase = smem_addr(base);
@@ -100,8 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = *tbase;
-    const uint32_t tP = tmem, tO = tmem + 128, tS = tmem + 256;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;  // this warp's TMEM lanes
+    const uint32_t lane_off = static_cast<uint32_t>(lw * 32) << 16;  // this warp's TMEM lanes
+    const uint32_t tP = tmem + lane_off, tO = tmem + 128 + lane_off, tS = tmem + 256 + lane_off;
+    const uint32_t dP = tmem, dO = tmem + 128, dS = tmem + 256;  // MMA destinations
 
     constexpr uint32_t ID_QK = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
     constexpr uint32_t ID_PV = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::MN_MAJOR);
@@ -133,9 +141,15 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         umma::fence_after_sync();
 #pragma unroll
         for (int k = 0; k < kRank / 16; ++k)
-            umma::mma_bf16(tP, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sK + 32 * k, 16, 1024), ID_QK,
+            umma::mma_bf16(dP, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sK + 32 * k, 16, 1024), ID_QK,
                            k > 0);
         umma::mma_commit(pbar);
+    };
+    auto store_row_chunks = [&](unsigned char* dst, int r, int j0, const uint32_t (&pk)[16]) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+            *reinterpret_cast<uint4*>(dst + umma::sw128(r, j0 + q4)) =
+                make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
     };
     if (tid == 0) issue_qk(0);
     int aborted_at = -1;
@@ -148,50 +162,55 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         const unsigned char* qrow = base + OFF_Q + st * 16384;
         const unsigned char* krow = base + OFF_K + st * 16384;
 
-        // q_t . z over the tiles before this one (this thread's token t = tid); the
-        // tile's loads have landed: thread 0 waited on them before issuing its P
+        // q_t . z over the tiles before this one, this warpgroup's half of the
+        // features (the tile's loads have landed: thread 0 waited on them before
+        // issuing its P)
         ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
-        float qz0 = 0.0f, qz1 = 0.0f;
+        {
+            float qz0 = 0.0f, qz1 = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(tid, j));
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = 4 * wg + jj;
+                const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(row, j));
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                qz0 = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz0);
-                qz1 = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz1);
+                for (int e = 0; e < 4; ++e) {
+                    qz0 = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz0);
+                    qz1 = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz1);
+                }
             }
+            s_qz[wg * kTok + row] = qz0 + qz1;
         }
-        const float qz = qz0 + qz1;
         ok &= mbar_wait_bounded(pbar, pph, kAssocPolls);
         pph ^= 1u;
         umma::fence_after_sync();
 
-        // ---- P epilogue: causal mask, row sum (fp32), bf16 P as the K-major A of P V
-        float rs = 0.0f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-            float v[2][32];
-            umma::tmem_ld32(tP + lane_off + 64 * half, v[0]);
-            umma::tmem_ld32(tP + lane_off + 64 * half + 32, v[1]);
-            umma::tmem_wait_ld();
+        // ---- P epilogue over this warpgroup's 64 columns: blocks of 32 source
+        // tokens above the diagonal are all masked (no load), below it none are
+        {
+            float rs = 0.0f;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const int cb = 2 * half + h;
+                const int cb = 2 * wg + h;  // 32-column block
                 uint32_t pk[16];
+                if (cb > lw) {
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float a0 = (32 * cb + e <= tid) ? v[h][e] : 0.0f;
-                    const float a1 = (32 * cb + e + 1 <= tid) ? v[h][e + 1] : 0.0f;
-                    rs += a0 + a1;
-                    pk[e / 2] = pack_bf16(a0, a1);
+                    for (int e = 0; e < 16; ++e) pk[e] = 0u;
+                } else {
+                    float v[32];
+                    umma::tmem_ld32(tP + 32 * cb, v);
+                    umma::tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float a0 = (cb < lw || e <= lane) ? v[e] : 0.0f;
+                        const float a1 = (cb < lw || e + 1 <= lane) ? v[e + 1] : 0.0f;
+                        rs += a0 + a1;
+                        pk[e / 2] = pack_bf16(a0, a1);
+                    }
                 }
-                unsigned char* prow = base + OFF_P + half * 16384;
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<uint4*>(prow + umma::sw128(tid, h * 4 + q4)) =
-                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                store_row_chunks(base + OFF_P + wg * 16384, row, h * 4, pk);
             }
+            s_rs[wg * kTok + row] = rs;
         }
         fence_proxy_async_shared();  // P and last tile's state copy visible to the tensor cores
         if (tid == 0) umma::tma_store_wait_read();  // last tile's output store has left shared memory
@@ -203,80 +222,69 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             umma::fence_after_sync();
 #pragma unroll
             for (int k = 0; k < kTok / 16; ++k)
-                umma::mma_bf16(tO, umma::smem_desc(sP + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
+                umma::mma_bf16(dO, umma::smem_desc(sP + (k >> 2) * 16384 + 32 * (k & 3), 16, 1024),
                                umma::smem_desc(sV + 2048 * k, 16384, 1024), ID_PV, k > 0);
             if (it > 0) {
 #pragma unroll
                 for (int k = 0; k < kRank / 16; ++k)
-                    umma::mma_bf16(tO, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sS + 32 * k, 16, 1024),
+                    umma::mma_bf16(dO, umma::smem_desc(sQ + 32 * k, 16, 1024), umma::smem_desc(sS + 32 * k, 16, 1024),
                                    ID_QS, true);
             }
 #pragma unroll
             for (int k = 0; k < kTok / 16; ++k)
-                umma::mma_bf16(tS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
+                umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
                                umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
             umma::mma_commit(obar);
             // P of the next tile overlaps this tile's output epilogue (its TMEM
             // columns were read out above)
             if (it + 1 < ntile) issue_qk(it + 1);
         }
-        // z += column sums of this tile's k, after every thread has read z above:
-        // thread c (and c + 64) sums half the rows of feature c
+        // z += column sums of this tile's k (every thread has read z above):
+        // threads c, c + 64, c + 128, c + 192 each sum a quarter of the rows of feature c
         {
-            const int c = tid & 63, r0 = (tid >> 6) * 64;
+            const int c = tid & 63, r0 = (tid >> 6) * 32;
             const int j = c >> 3, e = c & 7;
             float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-            for (int r = 0; r < 64; ++r) {
-                const uint16_t h = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
-                a[r & 3] += __uint_as_float(static_cast<uint32_t>(h) << 16);
+#pragma unroll 8
+            for (int r = 0; r < 32; ++r) {
+                const uint16_t hv = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
+                a[r & 3] += __uint_as_float(static_cast<uint32_t>(hv) << 16);
             }
-            const float part = (a[0] + a[1]) + (a[2] + a[3]);
-            if (tid >= 64) zhalf[c] = part;
+            zpart[(tid >> 6) * kRank + c] = (a[0] + a[1]) + (a[2] + a[3]);
             named_sync(1, kThreads);
-            if (tid < 64) z[c] += part + zhalf[c];
+            if (tid < kRank) z[c] += (zpart[c] + zpart[kRank + c]) + (zpart[2 * kRank + c] + zpart[3 * kRank + c]);
         }
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
         umma::fence_after_sync();
 
-        // ---- outputs: O / max(q.z + rowsum, eps) in bf16, staged for the TMA store
-        const float inv = 1.0f / fmaxf(qz + rs, p.eps);
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        // ---- outputs: O / max(q.z + rowsum, eps) in bf16, this warpgroup's 64
+        // columns (one TMA store box), staged for the store
+        {
+            const float den = (s_qz[row] + s_qz[kTok + row]) + (s_rs[row] + s_rs[kTok + row]);
+            const float inv = 1.0f / fmaxf(den, p.eps);
             float v[2][32];
-            umma::tmem_ld32(tO + lane_off + 64 * half, v[0]);
-            umma::tmem_ld32(tO + lane_off + 64 * half + 32, v[1]);
+            umma::tmem_ld32(tO + 64 * wg, v[0]);
+            umma::tmem_ld32(tO + 64 * wg + 32, v[1]);
             umma::tmem_wait_ld();
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[h][e] * inv, v[h][e + 1] * inv);
-                unsigned char* orow = base + OFF_O + half * 16384;
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<uint4*>(orow + umma::sw128(tid, h * 4 + q4)) =
-                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                store_row_chunks(base + OFF_O + wg * 16384, row, h * 4, pk);
             }
         }
-        // ---- the state after this tile, bf16, as the K-major B of the next Q S (row = column of d)
+        // ---- the state after this tile, bf16, as the K-major B of the next Q S
+        // (row = column of d; this warpgroup's 32 features)
         {
-            float v[2][32];
-            umma::tmem_ld32(tS + lane_off, v[0]);
-            umma::tmem_ld32(tS + lane_off + 32, v[1]);
+            float v[32];
+            umma::tmem_ld32(tS + 32 * wg, v);
             umma::tmem_wait_ld();
+            uint32_t pk[16];
 #pragma unroll
-            for (int cb = 0; cb < 2; ++cb) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[cb][e], v[cb][e + 1]);
-                unsigned char* srow = base + OFF_S;
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<uint4*>(srow + umma::sw128(tid, cb * 4 + q4)) =
-                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-            }
+            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e], v[e + 1]);
+            store_row_chunks(base + OFF_S, row, wg * 4, pk);
         }
         fence_proxy_async_shared();  // staged outputs (TMA store) and S (next MMA) visible to the async proxy
         umma::fence_before_sync();

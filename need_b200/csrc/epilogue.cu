@@ -4,12 +4,13 @@
 // fp32, ss = sum(x^2) / C, inv = rsqrt(ss + eps), out = (x * inv) * w as two
 // fp32 products, rounded once to the row's dtype.
 //
-// One warp per row.  Pass 1 reads the row in 16-byte pieces (lane l takes
-// pieces l, l + 32, ...) and sums their squares in that fixed order, then a
-// butterfly adds the lanes: the result is the same on every call.  Pass 2
-// re-reads the row (from L1; a row is at most a few KB), scales it and writes
-// it; every piece is read and written by the same lane, so `out` may be `x`.
-// Run right after the scan, the rows come from L2.
+// One warp per row.  The row is read in 16-byte pieces (lane l takes pieces
+// l, l + 32, ...) whose squares it sums in that fixed order; a butterfly adds
+// the lanes, so the result is the same on every call.  Rows of up to 256
+// pieces (2048 16-bit channels) stay in registers between the sum and the
+// scaling; longer rows are read a second time (from L1).  Every piece is read
+// and written by the same lane, so `out` may be `x`.  Run right after the
+// scan, the rows come from L2.
 #include "host_common.h"
 #include "need_scan.h"
 #include "scan_kernel.cuh"
@@ -30,7 +31,9 @@ struct NormParams {
 
 constexpr int kRowsPerBlock = 8;  // warps per block
 
-template <typename TS>
+// VPL > 0: the row is read once into registers (at most VPL 16-byte pieces per
+// lane).  VPL == 0: two passes over the row, the second from L1.
+template <typename TS, int VPL>
 __global__ void __launch_bounds__(kRowsPerBlock * 32) rms_norm_kernel(const NormParams p) {
     using PS = typename Ops<TS>::P;
     constexpr int VEC = 16 / Ops<TS>::BYTES;
@@ -42,25 +45,17 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) rms_norm_kernel(const Norm
     TS* out = static_cast<TS*>(p.out) + b * p.osb + t * p.ost;
     const int nvec = p.C / VEC;
 
-    float acc = 0.0f;
-#pragma unroll 4
-    for (int v = lane; v < nvec; v += 32) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + v * VEC);
+    auto sumsq = [](const uint4& u, float acc) {
         const PS* h = reinterpret_cast<const PS*>(&u);
 #pragma unroll
-        for (int e = 0; e < 16 / int(sizeof(PS)); ++e) {
+        for (int e = 0; e < VEC / 2; ++e) {
             const float2 y = widen(h[e]);
             acc = fmaf(y.x, y.x, acc);
             acc = fmaf(y.y, y.y, acc);
         }
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.C)), p.eps));
-
-#pragma unroll 4
-    for (int v = lane; v < nvec; v += 32) {
-        uint4 u = *reinterpret_cast<const uint4*>(x + v * VEC);
+        return acc;
+    };
+    auto scale = [&](uint4 u, int v, float inv) {
         float wv[VEC];
         if (p.w32) {
             const float4* w4 = reinterpret_cast<const float4*>(static_cast<const float*>(p.w) + v * VEC);
@@ -86,7 +81,46 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) rms_norm_kernel(const Norm
                                  __fmul_rn(__fmul_rn(y.y, inv), wv[2 * e + 1]));
         }
         *reinterpret_cast<uint4*>(out + v * VEC) = u;
+    };
+
+    float acc = 0.0f;
+    if constexpr (VPL > 0) {
+        uint4 u[VPL];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) u[k] = *reinterpret_cast<const uint4*>(x + v * VEC);
+        }
+#pragma unroll
+        for (int k = 0; k < VPL; ++k)
+            if (lane + 32 * k < nvec) acc = sumsq(u[k], acc);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.C)), p.eps));
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) scale(u[k], v, inv);
+        }
+    } else {
+#pragma unroll 4
+        for (int v = lane; v < nvec; v += 32) acc = sumsq(*reinterpret_cast<const uint4*>(x + v * VEC), acc);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(acc, static_cast<float>(p.C)), p.eps));
+#pragma unroll 4
+        for (int v = lane; v < nvec; v += 32) scale(*reinterpret_cast<const uint4*>(x + v * VEC), v, inv);
     }
+}
+
+template <typename TS>
+void launch_norm(const NormParams& p, dim3 grid, dim3 block, cudaStream_t s) {
+    const int nvec = p.C / (16 / int(sizeof(TS)));
+    if (nvec <= 32) rms_norm_kernel<TS, 1><<<grid, block, 0, s>>>(p);
+    else if (nvec <= 64) rms_norm_kernel<TS, 2><<<grid, block, 0, s>>>(p);
+    else if (nvec <= 128) rms_norm_kernel<TS, 4><<<grid, block, 0, s>>>(p);
+    else if (nvec <= 256) rms_norm_kernel<TS, 8><<<grid, block, 0, s>>>(p);
+    else rms_norm_kernel<TS, 0><<<grid, block, 0, s>>>(p);
 }
 
 }  // namespace
@@ -116,9 +150,9 @@ int rms_norm_rows(int32_t dtype, const void* x, int64_t xsb, int64_t xst, void* 
     const int64_t blocks = (p.rows + kRowsPerBlock - 1) / kRowsPerBlock;
     if (blocks > INT32_MAX) return fail(NEED_ERR_UNSUPPORTED, "rms norm: too many rows");
     const dim3 grid(static_cast<unsigned>(blocks)), block(kRowsPerBlock * 32);
-    if (dtype == NEED_BF16) rms_norm_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(p);
-    else if (dtype == NEED_F16) rms_norm_kernel<__half><<<grid, block, 0, stream>>>(p);
-    else rms_norm_kernel<float><<<grid, block, 0, stream>>>(p);
+    if (dtype == NEED_BF16) launch_norm<__nv_bfloat16>(p, grid, block, stream);
+    else if (dtype == NEED_F16) launch_norm<__half>(p, grid, block, stream);
+    else launch_norm<float>(p, grid, block, stream);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "rms_norm_kernel launch");
     return NEED_OK;
