@@ -68,6 +68,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 // ------------------------------------------------------------------ main kernel
+// Grid (column blocks, sequences, segments).  Segment s owns tiles [s*tps,
+// (s+1)*tps); its CTA first runs the tiles before them in state-only mode
+// (S^T += V^T K and z, no Q, no outputs) and then its own tiles in full.
 // Two warpgroups.  Warp w reads tensor-memory lanes 32 (w % 4) .. + 31, so row
 // (token, or column of d for the state) `row` = 32 (w % 4) + lane belongs to
 // warps w and w + 4; warpgroup g takes half of each epilogue's columns.
@@ -89,6 +92,10 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     const int row = lw * 32 + lane;
     const int c0 = blockIdx.x * kCols, b = blockIdx.y;
     const int ntile = (p.T + kTok - 1) / kTok;
+    const int tps = (ntile + static_cast<int>(gridDim.z) - 1) / static_cast<int>(gridDim.z);
+    const int start = static_cast<int>(blockIdx.z) * tps;  // this CTA's first own tile
+    const int end = min(ntile, start + tps);
+    if (start >= end) return;  // no tiles (before any allocation or barrier)
     const uint32_t sbase = smem_addr(base);
 
     if (tid == 0) {
@@ -116,20 +123,21 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     constexpr uint32_t ID_QS = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
     constexpr uint32_t ID_VK = umma::idesc_bf16(128, 64, umma::MN_MAJOR, umma::MN_MAJOR);
 
-    auto issue_load = [&](int tile, int st) {
+    auto issue_load = [&](int tile, int st) {  // state-only tiles need no q
         const int t0 = tile * kTok;
         unsigned char* q = base + OFF_Q + st * 16384;
         unsigned char* k = base + OFF_K + st * 16384;
         unsigned char* v = base + OFF_V + st * 32768;
-        mbar_arrive_expect_tx(&full[st], 16384u * 2u + 32768u);
-        umma::tma_load_3d(q, &p.tm_q, 0, t0, b, &full[st]);
+        const bool own = tile >= start;
+        mbar_arrive_expect_tx(&full[st], (own ? 16384u : 0u) + 16384u + 32768u);
+        if (own) umma::tma_load_3d(q, &p.tm_q, 0, t0, b, &full[st]);
         umma::tma_load_3d(k, &p.tm_k, 0, t0, b, &full[st]);
         umma::tma_load_3d(v, &p.tm_v, c0, t0, b, &full[st]);
         umma::tma_load_3d(v + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);  // may lie past d: zero fill
     };
     if (tid == 0) {
         issue_load(0, 0);
-        if (ntile > 1) issue_load(1, 1);
+        if (end > 1) issue_load(1, 1);
     }
 
     bool ok = true;
@@ -151,9 +159,66 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             *reinterpret_cast<uint4*>(dst + umma::sw128(r, j0 + q4)) =
                 make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
     };
-    if (tid == 0) issue_qk(0);
+    // z += column sums of a tile's k: threads c, c + 64, c + 128, c + 192 each
+    // sum a quarter of the rows of feature c (call after every thread has read z)
+    auto add_z = [&](const unsigned char* krow) {
+        const int c = tid & 63, r0 = (tid >> 6) * 32;
+        const int j = c >> 3, e = c & 7;
+        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            const uint16_t hv = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
+            a[r & 3] += __uint_as_float(static_cast<uint32_t>(hv) << 16);
+        }
+        zpart[(tid >> 6) * kRank + c] = (a[0] + a[1]) + (a[2] + a[3]);
+        named_sync(1, kThreads);
+        if (tid < kRank) z[c] += (zpart[c] + zpart[kRank + c]) + (zpart[2 * kRank + c] + zpart[3 * kRank + c]);
+    };
+    // the bf16 copy of the state in TMEM, as the K-major B of the next Q S (row =
+    // column of d; this warpgroup's 32 features)
+    auto copy_state = [&]() {
+        float v[32];
+        umma::tmem_ld32(tS + 32 * wg, v);
+        umma::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e], v[e + 1]);
+        store_row_chunks(base + OFF_S, row, wg * 4, pk);
+    };
+
     int aborted_at = -1;
-    for (int it = 0; it < ntile; ++it) {
+    // ---- state-only tiles before this CTA's segment
+    for (int it = 0; it < start; ++it) {
+        const int st = it & 1;
+        const uint32_t sK = sbase + OFF_K + st * 16384, sV = sbase + OFF_V + st * 32768;
+        ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
+        if (tid == 0) {
+            umma::fence_after_sync();
+#pragma unroll
+            for (int k = 0; k < kTok / 16; ++k)
+                umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
+                               umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
+            umma::mma_commit(obar);
+        }
+        add_z(base + OFF_K + st * 16384);
+        ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
+        oph ^= 1u;
+        umma::fence_after_sync();
+        umma::fence_before_sync();
+        if (!__syncthreads_and(ok)) {
+            aborted_at = it;
+            break;
+        }
+        if (tid == 0 && it + 2 < end) issue_load(it + 2, st);  // the stage's MMAs and readers are done
+    }
+    if (start > 0 && aborted_at < 0) {  // the state entering the segment, for its first Q S
+        copy_state();
+        fence_proxy_async_shared();
+        umma::fence_before_sync();
+        __syncthreads();
+    }
+    if (tid == 0 && aborted_at < 0) issue_qk(start);
+    for (int it = start; it < end && aborted_at < 0; ++it) {
         const int st = it & 1;
         const int t0 = it * kTok;
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
@@ -237,23 +302,9 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             umma::mma_commit(obar);
             // P of the next tile overlaps this tile's output epilogue (its TMEM
             // columns were read out above)
-            if (it + 1 < ntile) issue_qk(it + 1);
+            if (it + 1 < end) issue_qk(it + 1);
         }
-        // z += column sums of this tile's k (every thread has read z above):
-        // threads c, c + 64, c + 128, c + 192 each sum a quarter of the rows of feature c
-        {
-            const int c = tid & 63, r0 = (tid >> 6) * 32;
-            const int j = c >> 3, e = c & 7;
-            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-            for (int r = 0; r < 32; ++r) {
-                const uint16_t hv = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
-                a[r & 3] += __uint_as_float(static_cast<uint32_t>(hv) << 16);
-            }
-            zpart[(tid >> 6) * kRank + c] = (a[0] + a[1]) + (a[2] + a[3]);
-            named_sync(1, kThreads);
-            if (tid < kRank) z[c] += (zpart[c] + zpart[kRank + c]) + (zpart[2 * kRank + c] + zpart[3 * kRank + c]);
-        }
+        add_z(krow);
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
         umma::fence_after_sync();
@@ -275,17 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
                 store_row_chunks(base + OFF_O + wg * 16384, row, h * 4, pk);
             }
         }
-        // ---- the state after this tile, bf16, as the K-major B of the next Q S
-        // (row = column of d; this warpgroup's 32 features)
-        {
-            float v[32];
-            umma::tmem_ld32(tS + 32 * wg, v);
-            umma::tmem_wait_ld();
-            uint32_t pk[16];
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[e], v[e + 1]);
-            store_row_chunks(base + OFF_S, row, wg * 4, pk);
-        }
+        // ---- the state after this tile, for the next tile's Q S
+        if (it + 1 < end) copy_state();
         fence_proxy_async_shared();  // staged outputs (TMA store) and S (next MMA) visible to the async proxy
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) {  // a wait gave up: stop (uniformly) and report
@@ -296,12 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             umma::tma_store_3d(&p.tm_out, base + OFF_O, c0, t0, b);
             if (c0 + 64 < p.d) umma::tma_store_3d(&p.tm_out, base + OFF_O + 16384, c0 + 64, t0, b);
             umma::tma_store_commit();
-            if (it + 2 < ntile) issue_load(it + 2, st);  // this stage's MMAs and readers are done
+            if (it + 2 < end) issue_load(it + 2, st);  // this stage's MMAs and readers are done
         }
     }
     // after a give-up, the next tile's P may still be in flight: its commit
     // covers every MMA issued, so wait (bounded) before freeing tensor memory
-    if (tid == 0 && aborted_at >= 0 && aborted_at + 1 < ntile) mbar_wait_bounded(pbar, pph, kAssocPolls);
+    if (tid == 0 && aborted_at >= start && aborted_at + 1 < end) mbar_wait_bounded(pbar, pph, kAssocPolls);
     if (tid == 0) umma::tma_store_wait_all();
     if (!ok) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
     umma::fence_before_sync();
@@ -313,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
 }
 
 // ------------------------------------------------------------------ feature map
-// One warp per token: q, k -> bf16(elu(x) + 1) (need_core.py:1977-1978), zero past
+// One warp per kFeatRows tokens: q, k -> bf16(elu(x) + 1) (need_core.py:1977-1978), zero past
 // r; with a write mask w = bf16(clamp(mask, 0, 1)): k := bf16(k * w) and
 // v := bf16(v * w) (need_core.py:1979-1984).
 struct FeatArgs {
@@ -337,37 +379,55 @@ __device__ __forceinline__ float ld_any(const void* base, int64_t i, bool f32) {
 }
 __device__ __forceinline__ float feature(float x) { return __bfloat162float(__float2bfloat16_rn((x > 0.0f ? x : expm1f(x)) + 1.0f)); }
 
+constexpr int kFeatRows = 4;  // rows per warp, their loads in flight together
+
 __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= a.nb * a.T) return;
-    const int64_t bi = row / a.T, t = row - bi * a.T;
-    float w = 1.0f;
-    if (a.mask != nullptr)
-        w = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(ld_any(a.mask, bi * a.msb + t * a.mst, a.mask32))),
-                        0.0f),
-                  1.0f);
-    float qv[2], kv[2];
+    const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5)) * kFeatRows;
+    const int64_t nrows = a.nb * a.T;
+    float qv[kFeatRows][2], kv[kFeatRows][2], w[kFeatRows];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-        const int c = 2 * lane + e;
-        qv[e] = c < a.r ? feature(ld_any(a.q, bi * a.qsb + t * a.qst + c, a.qk32)) : 0.0f;
-        kv[e] = c < a.r ? feature(ld_any(a.k, bi * a.ksb + t * a.kst + c, a.qk32)) : 0.0f;
-        if (a.mask != nullptr) kv[e] = __bfloat162float(__float2bfloat16_rn(kv[e] * w));
+    for (int i = 0; i < kFeatRows; ++i) {
+        const int64_t row = row0 + i;
+        const int64_t bi = row / a.T, t = row - bi * a.T;
+        w[i] = 1.0f;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int c = 2 * lane + e;
+            const bool in = row < nrows && c < a.r;
+            qv[i][e] = in ? ld_any(a.q, bi * a.qsb + t * a.qst + c, a.qk32) : 0.0f;
+            kv[i][e] = in ? ld_any(a.k, bi * a.ksb + t * a.kst + c, a.qk32) : 0.0f;
+        }
+        if (a.mask != nullptr && row < nrows) w[i] = ld_any(a.mask, bi * a.msb + t * a.mst, a.mask32);
     }
-    reinterpret_cast<uint32_t*>(a.qf + row * kRank)[lane] = pack_bf16(qv[0], qv[1]);
-    reinterpret_cast<uint32_t*>(a.kf + row * kRank)[lane] = pack_bf16(kv[0], kv[1]);
-    if (a.mask != nullptr) {
-        const __nv_bfloat16* src = a.v + bi * a.vsb + t * a.vst;
-        __nv_bfloat16* dst = a.vm + row * a.d;
-        for (int64_t c = 8 * lane; c < a.d; c += 256) {
-            const uint4 x = *reinterpret_cast<const uint4*>(src + c);
-            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            uint32_t o[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                o[i] = pack_bf16(__uint_as_float(xs[i] << 16) * w, __uint_as_float(xs[i] & 0xffff0000u) * w);
-            *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int i = 0; i < kFeatRows; ++i) {
+        const int64_t row = row0 + i;
+        if (row >= nrows) break;
+        const float wi = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(w[i])), 0.0f), 1.0f);
+        float qf[2], kf[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const bool in = 2 * lane + e < a.r;
+            qf[e] = in ? feature(qv[i][e]) : 0.0f;
+            kf[e] = in ? feature(kv[i][e]) : 0.0f;
+            if (a.mask != nullptr) kf[e] = __bfloat162float(__float2bfloat16_rn(kf[e] * wi));
+        }
+        reinterpret_cast<uint32_t*>(a.qf + row * kRank)[lane] = pack_bf16(qf[0], qf[1]);
+        reinterpret_cast<uint32_t*>(a.kf + row * kRank)[lane] = pack_bf16(kf[0], kf[1]);
+        if (a.mask != nullptr) {
+            const int64_t bi = row / a.T, t = row - bi * a.T;
+            const __nv_bfloat16* src = a.v + bi * a.vsb + t * a.vst;
+            __nv_bfloat16* dst = a.vm + row * a.d;
+            for (int64_t c = 8 * lane; c < a.d; c += 256) {
+                const uint4 x = *reinterpret_cast<const uint4*>(src + c);
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                uint32_t o[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    o[k] = pack_bf16(__uint_as_float(xs[k] << 16) * wi, __uint_as_float(xs[k] & 0xffff0000u) * wi);
+                *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
         }
     }
 }
@@ -482,13 +542,23 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     P.hdr = reinterpret_cast<uint32_t*>(ws);
 
     const int64_t rows = a->nb * a->T;
-    assoc_features_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, stream>>>(f);
+    const int64_t fblocks = (rows + 4 * kFeatRows - 1) / (4 * kFeatRows);
+    if (fblocks > INT32_MAX) return fail(NEED_ERR_UNSUPPORTED, "too many tokens");
+    assoc_features_kernel<<<static_cast<unsigned>(fblocks), 128, 0, stream>>>(f);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "assoc_features_kernel launch");
     static std::atomic<uint64_t> smem_done{0};
     if ((e = ensure_smem(assoc_kernel, SMEM_BYTES, smem_done)) != cudaSuccess)
         return cuda_fail(e, "cudaFuncSetAttribute(assoc_kernel)");
-    const dim3 grid(static_cast<unsigned>((a->d + kCols - 1) / kCols), static_cast<unsigned>(a->nb));
+    // Sequences split into segments so that the CTAs fill the GPU's SMs (one
+    // CTA per SM); each later segment first sums the state of the tiles before it.
+    int dev = 0, sms = 148;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    const int64_t ncb = (a->d + kCols - 1) / kCols, ntile = (a->T + kTok - 1) / kTok;
+    const int64_t nseg = std::max<int64_t>(1, std::min<int64_t>({ntile, sms / (ncb * a->nb), 16}));
+    const dim3 grid(static_cast<unsigned>(ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(nseg));
     assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");
     return ok();
