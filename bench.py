@@ -49,7 +49,8 @@ def parse_args():
     ap.add_argument("--no-side", action="store_true", help="skip the sequence-parallel and decode side runs")
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup"], default="prefill",
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "assoc"],
+                    default="prefill",
                     help="with --profile: which kernel's workload to run (one GPU)")
     return ap.parse_args()
 
@@ -398,9 +399,27 @@ def profile_side_case(args, dev, nk, sp, workloads):
     """One-GPU workloads of the other kernels, for ncu: ``decode`` replays the
     verify + commit graph of 256 sequences x 4 drafted tokens; ``sp-fixup``
     scans the 8 slices of a B=1, T=65536, C=4096 sequence, stacks their
-    summaries as the all-gather would and fixes up the last slice."""
+    summaries as the all-gather would and fixes up the last slice; ``ssd-norm``
+    runs the SSD scan with the RMSNorm kernel after it, and ``assoc`` the
+    associative memory (feature map + tensor-core kernel), both at NEED's 350M
+    shape (B=8, T=2048, d_model=832, memory_rank=64, bf16)."""
     import torch
-    if args.profile_case == "decode":
+    if args.profile_case in ("ssd-norm", "assoc"):
+        g0 = torch.Generator(device=dev).manual_seed(1)
+        Bm, Tm, d = 8, 2048, 832
+        xs = [torch.randn(Bm, Tm, d, device=dev, generator=g0).to(torch.bfloat16) for _ in range(5)]
+        q = torch.randn(Bm, Tm, 64, device=dev, generator=g0)
+        k = torch.randn(Bm, Tm, 64, device=dev, generator=g0)
+        dskip, w = torch.full((d,), 0.1, device=dev), torch.ones(d, device=dev)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            if args.profile_case == "ssd-norm":
+                nk.ssd_scan_rms_norm(*xs, dskip, 0.001, 0.2, w, 1e-6)
+            else:
+                nk.linear_associative_memory(q, k, xs[0])
+        torch.cuda.synchronize()
+        if nk.workspace_error() != 0:
+            raise RuntimeError("a device-side wait gave up")
+    elif args.profile_case == "decode":
         w = workloads.verify(dev, N=256, C=1024, k=4, seed=11)
         pool = w.states.clone()
         y, sk = torch.empty_like(w.x), torch.empty_like(w.x)
