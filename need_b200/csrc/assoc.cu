@@ -377,7 +377,14 @@ struct FeatArgs {
 __device__ __forceinline__ float ld_any(const void* base, int64_t i, bool f32) {
     return f32 ? static_cast<const float*>(base)[i] : __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
 }
-__device__ __forceinline__ float feature(float x) { return __bfloat162float(__float2bfloat16_rn((x > 0.0f ? x : expm1f(x)) + 1.0f)); }
+// elu(x) + 1 rounded to bf16: x + 1 above 0, exp(x) = expm1(x) + 1 at or below
+// 0 (one hardware 2^x; its few-ulp fp32 error only moves the bf16 result
+// where the value lies within those ulp of a rounding tie)
+__device__ __forceinline__ float feature(float x) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fminf(x, 0.0f) * 1.4426950408889634f));
+    return __bfloat162float(__float2bfloat16_rn(x > 0.0f ? x + 1.0f : e));
+}
 
 constexpr int kFeatRows = 4;  // rows per warp, their loads in flight together
 
@@ -385,11 +392,16 @@ __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
     const int lane = threadIdx.x & 31;
     const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5)) * kFeatRows;
     const int64_t nrows = a.nb * a.T;
+    // row -> (sequence, token) in 32 bits (the host limits nb * T below 2^31)
+    const uint32_t T32 = static_cast<uint32_t>(a.T);
+    const uint32_t b0 = static_cast<uint32_t>(row0) / T32, tt0 = static_cast<uint32_t>(row0) - b0 * T32;
     float qv[kFeatRows][2], kv[kFeatRows][2], w[kFeatRows];
 #pragma unroll
     for (int i = 0; i < kFeatRows; ++i) {
         const int64_t row = row0 + i;
-        const int64_t bi = row / a.T, t = row - bi * a.T;
+        uint32_t bu = b0, tu = tt0 + i;
+        while (tu >= T32) tu -= T32, ++bu;  // at most kFeatRows steps
+        const int64_t bi = bu, t = tu;
         w[i] = 1.0f;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -416,7 +428,9 @@ __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
         reinterpret_cast<uint32_t*>(a.qf + row * kRank)[lane] = pack_bf16(qf[0], qf[1]);
         reinterpret_cast<uint32_t*>(a.kf + row * kRank)[lane] = pack_bf16(kf[0], kf[1]);
         if (a.mask != nullptr) {
-            const int64_t bi = row / a.T, t = row - bi * a.T;
+            uint32_t bu = b0, tu = tt0 + i;
+            while (tu >= T32) tu -= T32, ++bu;
+            const int64_t bi = bu, t = tu;
             const __nv_bfloat16* src = a.v + bi * a.vsb + t * a.vst;
             __nv_bfloat16* dst = a.vm + row * a.d;
             for (int64_t c = 8 * lane; c < a.d; c += 256) {
@@ -479,7 +493,7 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
         return fail(NEED_ERR_UNSUPPORTED, "q_raw / k_raw must be fp32 or bf16 (dtype %d)", a->qk_dtype);
     if (a->r > kRank) return fail(NEED_ERR_UNSUPPORTED, "r=%lld: at most %d features", (long long)a->r, kRank);
     if (a->d % 8 != 0) return fail(NEED_ERR_UNSUPPORTED, "d=%lld must be a multiple of 8", (long long)a->d);
-    if (a->T > INT32_MAX / 2 || a->d > INT32_MAX / 2 || a->nb > 65535)
+    if (a->T > INT32_MAX / 2 || a->d > INT32_MAX / 2 || a->nb > 65535 || a->nb * a->T > INT32_MAX / 2)
         return fail(NEED_ERR_UNSUPPORTED, "sizes out of range");
     if (a->q_raw == nullptr || a->k_raw == nullptr || a->v == nullptr || a->out == nullptr)
         return fail(NEED_ERR_INVALID, "q_raw, k_raw, v and out must be non-null");
