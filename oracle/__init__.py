@@ -50,8 +50,9 @@ def _lib():
         lib.ora_stream_step.argtypes = [i32, p, p, p, p, p, p, p, p, i64, i64, d, d, i32]
         lib.ora_rms_norm.argtypes = [p, p, p, i64, i64, d, i32]
         lib.ora_assoc_memory.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i32, i32]
+        lib.ora_assoc_step.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i32]
         for fn in ("ora_round", "ora_affine_scan", "ora_affine_scan_seq", "ora_gated_prep",
-                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory"):
+                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory", "ora_assoc_step"):
             getattr(lib, fn).restype = None
         del f
         _LIB = lib
@@ -192,6 +193,20 @@ def assoc_memory(q_raw, k_raw, v, write_mask=None, *, chunk: int = 32, dtype: st
     _lib().ora_assoc_memory(_ptr(q), _ptr(k), _ptr(v), _ptr(wm), _ptr(out), b, t, r, d, int(chunk),
                             MODE[dtype], _threads(nthreads))
     return out
+
+
+def assoc_step(q_raw, k_raw, v, state, denom, write_mask=None, *, dtype: str = "bf16"):
+    """One token of HierarchicalMemory.stream_step's associative memory
+    (need_core.py:2067-2080): q_raw, k_raw [N, r] fp32, v [N, d], state [N, r, d]
+    and denom [N, r] in ``dtype`` values; returns (out [N, d], state, denom)."""
+    q, k, v = _f32(q_raw), _f32(k_raw), _f32(v)
+    st, dn = _f32(state).copy(), _f32(denom).copy()
+    n, r = q.shape
+    d = v.shape[-1]
+    wm = None if write_mask is None else _f32(write_mask).reshape(n)
+    out = np.empty((n, d), np.float32)
+    _lib().ora_assoc_step(_ptr(q), _ptr(k), _ptr(v), _ptr(wm), _ptr(st), _ptr(dn), _ptr(out), n, r, d, MODE[dtype])
+    return out, st, dn
 
 
 def stream_step(form: str, state, p0, p1, p2, p3=None, p4=None, dskip=None,

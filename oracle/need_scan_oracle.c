@@ -28,6 +28,7 @@
  *   ora_ssd_epilogue
  *   ora_assoc_memory     need_core.py:1960-2001 (HierarchicalMemory's linear
  *                        associative memory, the matrix-state recurrence).
+ *   ora_assoc_step       need_core.py:2067-2080 (its one-token streaming step).
  *   ora_rms_norm         need_kernels.py:99-107 (rms_norm's GPU kernel), the SSD
  *                        block's out_norm after ssd_scan (need_core.py:1643).
  *   ora_stream_step      need_core.py:6420-6428 (_stream_retention_step) and
@@ -442,6 +443,47 @@ static void assoc_row(void* ctx_, int64_t b) {
         memcpy(denom_state, dc, sizeof(float) * (size_t)r);
     }
     free(state); free(denom_state); free(acc); free(acck); free(sc); free(dc); free(qf); free(kf); free(vv);
+}
+
+/* One token of HierarchicalMemory.stream_step's associative memory
+ * (need_core.py:2067-2080), in place on the model-dtype state [N, r, d] and
+ * denom [N, r]:
+ *   state = rnd(state + rnd(kf (x) v)), denom = rnd(denom + kf),
+ *   out = rnd(rnd(sum_i qf_i state_i) / max(rnd(sum_i rnd(qf_i denom_i)), rnd(1e-6)))
+ * with qf, kf and the write mask as in ora_assoc_memory.  q_raw, k_raw [N, r]
+ * fp32; v [N, d]; wm [N] or NULL; out [N, d]. */
+ORA_API void ora_assoc_step(const float* q_raw, const float* k_raw, const float* v, const float* wm, float* state,
+                            float* denom, float* out, int64_t N, int64_t r, int64_t d, int mode) {
+    const float eps = rnd(1e-6f, mode);
+    float* qf = malloc(sizeof(float) * (size_t)r);
+    float* kf = malloc(sizeof(float) * (size_t)r);
+    float* vv = malloc(sizeof(float) * (size_t)d);
+    for (int64_t n = 0; n < N; ++n) {
+        const float w = wm ? rnd(fminf(fmaxf(wm[n], 0.0f), 1.0f), mode) : 1.0f;
+        for (int64_t i = 0; i < r; ++i) {
+            const float qv = q_raw[n * r + i], kv = k_raw[n * r + i];
+            qf[i] = rnd((qv > 0.0f ? qv : expm1f(qv)) + 1.0f, mode);
+            kf[i] = rnd((kv > 0.0f ? kv : expm1f(kv)) + 1.0f, mode);
+            if (wm) kf[i] = rnd(kf[i] * w, mode);
+        }
+        for (int64_t j = 0; j < d; ++j) vv[j] = wm ? rnd(v[n * d + j] * w, mode) : v[n * d + j];
+        float* st = state + n * r * d;
+        float* dn = denom + n * r;
+        float den = 0.0f;
+        for (int64_t i = 0; i < r; ++i) {
+            dn[i] = rnd(dn[i] + kf[i], mode);
+            den += rnd(qf[i] * dn[i], mode);
+            for (int64_t j = 0; j < d; ++j) st[i * d + j] = rnd(st[i * d + j] + rnd(kf[i] * vv[j], mode), mode);
+        }
+        den = rnd(den, mode);
+        if (den < eps) den = eps;
+        for (int64_t j = 0; j < d; ++j) {
+            float num = 0.0f;
+            for (int64_t i = 0; i < r; ++i) num += qf[i] * st[i * d + j];
+            out[n * d + j] = rnd(rnd(num, mode) / den, mode);
+        }
+    }
+    free(qf); free(kf); free(vv);
 }
 
 ORA_API void ora_assoc_memory(const float* q_raw, const float* k_raw, const float* v, const float* wm, float* out,

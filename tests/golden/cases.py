@@ -83,6 +83,8 @@ CASES = {
     "assoc_bf16": dict(kind="assoc", seed=11, b=2, t=100, r=16, d=48, dtype="bf16", mask=False),
     "assoc_bf16_mask": dict(kind="assoc", seed=12, b=2, t=70, r=8, d=24, dtype="bf16", mask=True),
     "assoc_fp32": dict(kind="assoc", seed=13, b=1, t=80, r=16, d=32, dtype="fp32", mask=False),
+    # its one-token streaming step from given states, 5 steps, a write mask on some
+    "assoc_step_bf16": dict(kind="assoc_step", seed=14, n=3, r=8, d=24, steps=5, dtype="bf16"),
     # streaming one-token steps (ragged verify oracle)
     "stream_gated_bf16": dict(kind="stream", form="gated", seed=7, s=5, c=64, kmax=4, dtype="bf16"),
     "stream_ssd_bf16": dict(kind="stream", form="ssd", seed=8, s=5, c=64, kmax=4, dtype="bf16"),
@@ -130,6 +132,19 @@ def assoc_case(seed: int, b: int, t: int, r: int, d: int, dtype: str, mask: bool
     return out
 
 
+def assoc_step_case(seed: int, n: int, r: int, d: int, steps: int, dtype: str):
+    rs = np.random.RandomState(seed)
+    return {
+        "q": rs.standard_normal((steps, n, r)).astype(F32),
+        "k": rs.standard_normal((steps, n, r)).astype(F32),
+        "v": cast(rs.standard_normal((steps, n, d)), dtype),
+        "state": cast(0.5 * rs.standard_normal((n, r, d)), dtype),
+        "denom": cast(rs.uniform(0.0, 5.0, (n, r)), dtype),
+        "wm": np.where(rs.uniform(size=(steps, n)) < 0.5, 1.0,
+                       np.clip(rs.uniform(-0.3, 1.3, (steps, n)), 0.0, 1.0)).astype(F32),
+    }
+
+
 def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
     rs = np.random.RandomState(seed)
     k = rs.randint(0, kmax + 1, size=s)
@@ -163,6 +178,8 @@ def make_inputs(name: str):
         return ssd_norm_case(**spec)
     if kind == "assoc":
         return assoc_case(**spec)
+    if kind == "assoc_step":
+        return assoc_step_case(**spec)
     if kind == "stream":
         return stream_case(**spec)
     raise KeyError(kind)

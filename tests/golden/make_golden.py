@@ -16,6 +16,7 @@ guards against drift).  Reference entry points used (file:line in NEED):
   need_kernels.ssd_scan (torch path)        need_kernels.py:302-339
   need_kernels.rms_norm (torch path)        need_kernels.py:266-276 (with need_core.RMSNorm)
   HierarchicalMemory._linear_associative_memory  need_core.py:1960-2001
+  HierarchicalMemory.stream_step (its associative memory)  need_core.py:2043-2080
   StructuredDualRetention.stream_step       need_core.py:1653-1686
   the one-token formula of                  need_core.py:6420-6428
 
@@ -170,8 +171,72 @@ def check_module_stream_step():
             assert torch.equal(rec, state["scan_state"]), f"stream_step formula mismatch at t={t}"
 
 
+def assoc_step(q_raw, k_raw, v, state, denom, wm=None):
+    """One token of HierarchicalMemory.stream_step's associative memory
+    (need_core.py:2067-2080), in the model dtype of ``v``: returns
+    (associative [N, d], new state [N, r, d], new denom [N, r])."""
+    dt = v.dtype
+    qf = (torch.nn.functional.elu(q_raw.float()) + 1.0).to(dt)
+    kf = (torch.nn.functional.elu(k_raw.float()) + 1.0).to(dt)
+    vv = v
+    if wm is not None:
+        w = wm.to(dtype=dt).view(wm.size(0), -1)[:, :1].clamp(0.0, 1.0)
+        kf = kf * w
+        vv = vv * w
+    st = state.to(dt) + kf.unsqueeze(-1) * vv.unsqueeze(1)
+    dn = denom.to(dt) + kf
+    numer = torch.einsum("br,brd->bd", qf, st)
+    den = (qf * dn).sum(dim=-1, keepdim=True).clamp_min(1e-6)
+    return numer / den, st, dn
+
+
+def check_module_assoc_step():
+    """assoc_step against the real HierarchicalMemory.stream_step: its state and
+    its mixed output (semantic and cue recomputed as the module does)."""
+    import torch.nn.functional as F
+    torch.manual_seed(0)
+    cfg = need_core.NeedConfig(d_model=16, n_heads=2, n_layers=1, block_size=32)
+    cfg.memory_rank = 8
+    mod = need_core.HierarchicalMemory(cfg).eval()
+    state = {}
+    b = 3
+    st = torch.zeros(b, 8, 16, dtype=torch.bfloat16)
+    dn = torch.zeros(b, 8, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for t in range(4):
+            x = torch.randn(b, 1, 16).to(torch.bfloat16)
+            wm = None if t % 2 == 0 else torch.tensor([[1.0], [0.0], [0.6]])
+            mixed, _ = mod.stream_step(x, state, write_mask=None if wm is None else wm.view(b, 1, 1))
+            qs, ws, _, _, _ = mod._compose_inputs(x, None, None)
+            q_raw, k_raw = mod.q(qs.float())[:, 0], mod.k(ws.float())[:, 0]
+            v = mod.v(ws.float()).to(x.dtype)[:, 0]
+            assoc, st, dn = assoc_step(q_raw, k_raw, v, st, dn, wm)
+            assert torch.equal(st, state["assoc_state"]) and torch.equal(dn, state["assoc_denom"]), t
+            qn = F.normalize(mod.q(qs.float()), dim=-1)
+            sem = torch.einsum("br,sr->bs", qn[:, 0], F.normalize(mod.semantic_slots.float(), dim=-1))
+            semantic = torch.einsum("bs,sd->bd", F.softmax(sem, dim=-1).to(x.dtype), mod.semantic_values.to(x.dtype))
+            cue = mod.cue(ws[:, 0].float()).to(x.dtype)
+            want = mod.out(torch.cat([semantic, assoc, cue], dim=-1).float()).to(x.dtype).unsqueeze(1)
+            assert torch.equal(want, mixed), f"assoc stream step formula mismatch at t={t}"
+
+
+def ref_assoc_step(inp, dtype):
+    """k one-token steps from the given states, the outputs and states after each."""
+    st, dn = T(inp["state"], dtype), T(inp["denom"], dtype)
+    ys, sts, dns = [], [], []
+    for j in range(inp["q"].shape[0]):
+        wm = None if "wm" not in inp else torch.from_numpy(inp["wm"][j])
+        y, st, dn = assoc_step(torch.from_numpy(inp["q"][j]), torch.from_numpy(inp["k"][j]),
+                               T(inp["v"][j], dtype), st, dn, wm)
+        ys.append(npf(y))
+        sts.append(npf(st))
+        dns.append(npf(dn))
+    return {"y": np.stack(ys), "state": np.stack(sts), "denom": np.stack(dns)}
+
+
 def main():
     check_module_stream_step()
+    check_module_assoc_step()
     for name, spec in cases.CASES.items():
         inp = cases.make_inputs(name)
         kind, dtype = spec["kind"], spec["dtype"]
@@ -185,6 +250,8 @@ def main():
             out = ref_ssd_norm(inp, dtype)
         elif kind == "assoc":
             out = ref_assoc(inp, dtype)
+        elif kind == "assoc_step":
+            out = ref_assoc_step(inp, dtype)
         else:
             out = ref_stream(inp, spec["form"], dtype)
         if inp.get("x") is not None and inp["x"].size > 250_000:

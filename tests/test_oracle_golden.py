@@ -118,6 +118,17 @@ def test_assoc_memory(name):
         assert rel(y, g["y"]) < FP32_TOL
 
 
+def test_assoc_stream_step():
+    """HierarchicalMemory.stream_step's associative memory, 5 steps from given
+    states with a write mask: outputs and states bit for bit."""
+    inp, g = load("assoc_step_bf16")
+    st, dn = inp["state"], inp["denom"]
+    for j in range(inp["q"].shape[0]):
+        y, st, dn = oracle.assoc_step(inp["q"][j], inp["k"][j], inp["v"][j], st, dn, inp["wm"][j])
+        assert np.array_equal(st, g["state"][j]) and np.array_equal(dn, g["denom"][j]), j
+        assert np.array_equal(y, g["y"][j]), j
+
+
 @pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16"])
 def test_stream_steps(name):
     inp, g = load(name)
