@@ -610,12 +610,22 @@ def run_assoc(dev, nk, barrier, max_over_ranks):
 
     kern_us = timed(graphed(lambda: nk.linear_associative_memory(q, k, v)), 30)
     torch_us = timed(graphed(chunked), 3)
+    # decode: one token for each of 256 sequences against their states (r x d, bf16)
+    Ns = 256
+    st = torch.zeros(Ns, r, d, device=dev, dtype=torch.bfloat16)
+    dn = torch.zeros(Ns, r, device=dev, dtype=torch.bfloat16)
+    qs, ks = torch.randn(Ns, r, device=dev, generator=g0), torch.randn(Ns, r, device=dev, generator=g0)
+    vs = torch.randn(Ns, d, device=dev, generator=g0).to(torch.bfloat16)
+    step_us = timed(graphed(lambda: nk.assoc_memory_step(qs, ks, vs, st, dn)), 100)
+    step_bytes = Ns * (2 * r * d * 2 + 2 * r * 2 + 2 * d * 2 + 2 * r * 4)  # state, denom r/w; v, out; q, k
     nbytes = 2 * Bm * Tm * r * 4 + 2 * Bm * Tm * d * 2  # q, k (fp32) and v in, out
     tiles = Bm * -(-Tm // 128) * -(-d // 128)
     flops = tiles * 2 * 128 * (128 * 64 + 128 * 128 + 64 * 128 + 128 * 64)  # QK^T, PV, QS, V^T K per tile
     return {"workload": "linear associative memory, B=8, T=2048, d=832, r=64, bf16 values",
             "kernels_us": kern_us, "hbm_gbs": nbytes / (kern_us / 1e6) / 1e9,
-            "tensor_tflops": flops / (kern_us / 1e6) / 1e12, "torch_ops_us": torch_us}
+            "tensor_tflops": flops / (kern_us / 1e6) / 1e12, "torch_ops_us": torch_us,
+            "decode_step": {"workload": "one token for 256 sequences, state 64 x 832 bf16 each",
+                            "us": step_us, "hbm_gbs": step_bytes / (step_us / 1e6) / 1e9}}
 
 
 def run_ssd_block(dev, nk, barrier, max_over_ranks):

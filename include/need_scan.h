@@ -31,6 +31,8 @@
  *                                   (need_core.py:1620-1622), as one kernel
  *   need_assoc_memory            <- HierarchicalMemory._linear_associative_memory
  *                                   (need_core.py:1960-2001), the matrix-state memory
+ *   need_assoc_memory_step       <- its one-token step in HierarchicalMemory.stream_step
+ *                                   (need_core.py:2067-2080)
  *   need_rms_norm                <- need_kernels.rms_norm (need_kernels.py:266-276; its
  *                                   GPU kernel need_kernels.py:99-107)
  *   need_ssd_scan_rms_norm       <- need_kernels.ssd_scan followed by the block's
@@ -196,6 +198,30 @@ typedef struct {
     size_t workspace_bytes;
 } need_assoc_args;
 
+/* need_assoc_memory_step: one token of the associative memory per sequence,
+ * against per-sequence states kept between calls (decode). */
+typedef struct {
+    int32_t dtype;          /* v, out, state and denom: the model dtype (NEED_BF16, NEED_F16, NEED_F32) */
+    int32_t qk_dtype;       /* q_raw and k_raw: NEED_F32 or NEED_BF16 */
+    int64_t nseq, r, d;     /* r <= 256; d a multiple of 16 bytes' worth of elements */
+    const void* q_raw;      /* [nseq, r], feature stride 1 */
+    int64_t q_stride;
+    const void* k_raw;      /* [nseq, r], feature stride 1 */
+    int64_t k_stride;
+    const void* v;          /* [nseq, d], 16-byte aligned rows */
+    int64_t v_stride;
+    const void* write_mask; /* optional [nseq] contiguous, rounded to the model dtype and clamped to [0, 1] */
+    int32_t mask_dtype;     /* NEED_F32 or NEED_BF16 */
+    void* state;            /* [nslots, r, d], column stride 1, 16-byte aligned rows; updated in place */
+    int64_t state_stride_n, state_stride_r;
+    void* denom;            /* [nslots, r], feature stride 1; updated in place */
+    int64_t denom_stride_n;
+    const int32_t* slot;    /* optional [nseq]: state row of sequence i (default i) */
+    void* out;              /* [nseq, d], 16-byte aligned rows */
+    int64_t out_stride;
+    double eps;             /* denominator floor (the reference's 1e-6) */
+} need_assoc_step_args;
+
 /* Version of this header the library was built from. */
 NEED_API int need_abi_version(void);
 
@@ -318,6 +344,18 @@ NEED_API size_t need_assoc_memory_workspace_size(int64_t nb, int64_t T, int64_t 
  * second product) with fp32 accumulation, and the denominator is fp32.  The
  * chunk length therefore does not enter. */
 NEED_API int need_assoc_memory(const need_assoc_args* args, need_stream_t stream);
+
+/* HierarchicalMemory.stream_step's associative memory for one token of each
+ * sequence (need_core.py:2067-2080), with the reference's model-dtype
+ * arithmetic: q = elu(q_raw) + 1 and k = elu(k_raw) + 1 rounded to the model
+ * dtype (k and v scaled by the write mask, rounded); then, each op rounded to
+ * the model dtype,
+ *     state += k (x) v,   denom += k,
+ *     out = (q . state) / max(sum_i q_i denom_i, eps),
+ * where q . state and the sum are fp32 sums over the features in feature
+ * order.  state and denom are read and written in place (one sequence per
+ * row, or per slot[i]); sequences must not share a slot within one call. */
+NEED_API int need_assoc_memory_step(const need_assoc_step_args* args, need_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Ragged decode / speculative verify                                        */

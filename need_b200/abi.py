@@ -93,6 +93,17 @@ class NeedAssocArgs(Structure):
     ]
 
 
+class NeedAssocStepArgs(Structure):
+    _fields_ = [
+        ("dtype", c_int32), ("qk_dtype", c_int32), ("nseq", c_int64), ("r", c_int64), ("d", c_int64),
+        ("q_raw", c_void_p), ("q_stride", c_int64), ("k_raw", c_void_p), ("k_stride", c_int64),
+        ("v", c_void_p), ("v_stride", c_int64), ("write_mask", c_void_p), ("mask_dtype", c_int32),
+        ("state", c_void_p), ("state_stride_n", c_int64), ("state_stride_r", c_int64),
+        ("denom", c_void_p), ("denom_stride_n", c_int64), ("slot", c_void_p),
+        ("out", c_void_p), ("out_stride", c_int64), ("eps", c_double),
+    ]
+
+
 # every symbol the header declares, with (restype, argtypes)
 SIGNATURES = {
     "need_abi_version": (c_int32, []),
@@ -107,6 +118,7 @@ SIGNATURES = {
     "need_rms_norm": (c_int32, [POINTER(NeedNormArgs), c_void_p]),
     "need_assoc_memory_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int32]),
     "need_assoc_memory": (c_int32, [POINTER(NeedAssocArgs), c_void_p]),
+    "need_assoc_memory_step": (c_int32, [POINTER(NeedAssocStepArgs), c_void_p]),
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

@@ -446,6 +446,120 @@ __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
     }
 }
 
+// ------------------------------------------------------------------ one-token step
+// HierarchicalMemory.stream_step's associative memory (need_core.py:2067-2080)
+// for one token of each sequence, every op in the model dtype TS as the
+// reference rounds it: the state [r, d] and denominator [r] are updated in
+// place, the output is (q . state) / max(q . denom, eps).  One CTA per
+// sequence; thread i < r maps feature i, then each thread owns 16-byte column
+// pieces and walks the r rows of the state.  The sums over features are taken
+// in feature order with separately rounded fp32 products and adds.
+constexpr int kStepThreads = 128;
+constexpr int kStepMaxRank = 256;
+
+struct StepParams {
+    const void* q;
+    const void* k;
+    int64_t qs, ks;
+    int32_t qk32;
+    const void* v;
+    int64_t vs;
+    const void* mask;
+    int32_t mask32;
+    void* state;
+    int64_t sn, sr;
+    void* denom;
+    int64_t dn;
+    const int32_t* slot;
+    void* out;
+    int64_t os;
+    int32_t r, d;
+    float eps;
+};
+
+template <typename TS>
+__device__ __forceinline__ float rnd_to(float x) {
+    return to_f(static_cast<TS>(x));
+}
+template <>
+__device__ __forceinline__ float rnd_to<float>(float x) {
+    return x;
+}
+
+template <typename TS>
+__global__ void __launch_bounds__(kStepThreads) assoc_step_kernel(const StepParams p) {
+    using PS = typename Ops<TS>::P;
+    constexpr int VEC = 16 / Ops<TS>::BYTES;
+    __shared__ float s_q[kStepMaxRank], s_k[kStepMaxRank], s_dq[kStepMaxRank];
+    __shared__ float s_w, s_den;
+    const int n = blockIdx.x, tid = threadIdx.x;
+    const int64_t slot = p.slot != nullptr ? p.slot[n] : n;
+    TS* st = static_cast<TS*>(p.state) + slot * p.sn;
+    TS* dn = static_cast<TS*>(p.denom) + slot * p.dn;
+    const bool masked = p.mask != nullptr;
+    const float w = masked ? fminf(fmaxf(rnd_to<TS>(ld_any(p.mask, n, p.mask32)), 0.0f), 1.0f) : 1.0f;
+    for (int i = tid; i < p.r; i += kStepThreads) {
+        const float qv = ld_any(p.q, n * p.qs + i, p.qk32), kv = ld_any(p.k, n * p.ks + i, p.qk32);
+        const float qf = rnd_to<TS>((qv > 0.0f ? qv : expm1f(qv)) + 1.0f);
+        float kf = rnd_to<TS>((kv > 0.0f ? kv : expm1f(kv)) + 1.0f);
+        if (masked) kf = rnd_to<TS>(__fmul_rn(kf, w));
+        const float d_new = rnd_to<TS>(__fadd_rn(to_f(dn[i]), kf));
+        dn[i] = static_cast<TS>(d_new);
+        s_q[i] = qf;
+        s_k[i] = kf;
+        s_dq[i] = rnd_to<TS>(__fmul_rn(qf, d_new));
+    }
+    if (tid == 0) s_w = w;
+    __syncthreads();
+    if (tid == 0) {
+        float den = 0.0f;
+        for (int i = 0; i < p.r; ++i) den = __fadd_rn(den, s_dq[i]);
+        s_den = fmaxf(rnd_to<TS>(den), rnd_to<TS>(p.eps));
+    }
+    __syncthreads();
+    const float den = s_den;
+    const TS* v = static_cast<const TS*>(p.v) + n * p.vs;
+    TS* out = static_cast<TS*>(p.out) + n * p.os;
+    for (int c = tid * VEC; c < p.d; c += kStepThreads * VEC) {
+        float vv[VEC], acc[VEC];
+        {
+            const uint4 u = *reinterpret_cast<const uint4*>(v + c);
+            const PS* h = reinterpret_cast<const PS*>(&u);
+#pragma unroll
+            for (int e = 0; e < VEC / 2; ++e) {
+                const float2 f = widen(h[e]);
+                vv[2 * e] = masked ? rnd_to<TS>(__fmul_rn(f.x, w)) : f.x;
+                vv[2 * e + 1] = masked ? rnd_to<TS>(__fmul_rn(f.y, w)) : f.y;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < p.r; ++i) {
+            uint4* ptr = reinterpret_cast<uint4*>(st + i * p.sr + c);
+            uint4 u = *ptr;
+            PS* h = reinterpret_cast<PS*>(&u);
+            const float kf = s_k[i], qf = s_q[i];
+#pragma unroll
+            for (int e = 0; e < VEC / 2; ++e) {
+                const float2 f = widen(h[e]);
+                const float s0 = rnd_to<TS>(__fadd_rn(f.x, rnd_to<TS>(__fmul_rn(kf, vv[2 * e]))));
+                const float s1 = rnd_to<TS>(__fadd_rn(f.y, rnd_to<TS>(__fmul_rn(kf, vv[2 * e + 1]))));
+                h[e] = Ops<TS>::pack(s0, s1);
+                acc[2 * e] = __fadd_rn(acc[2 * e], __fmul_rn(qf, s0));
+                acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], __fmul_rn(qf, s1));
+            }
+            *ptr = u;
+        }
+        uint4 o;
+        PS* oh = reinterpret_cast<PS*>(&o);
+#pragma unroll
+        for (int e = 0; e < VEC / 2; ++e)
+            oh[e] = Ops<TS>::pack(__fdiv_rn(rnd_to<TS>(acc[2 * e]), den), __fdiv_rn(rnd_to<TS>(acc[2 * e + 1]), den));
+        *reinterpret_cast<uint4*>(out + c) = o;
+    }
+}
+
 // ------------------------------------------------------------------ host
 size_t align128(size_t x) { return (x + 127) & ~size_t(127); }
 
@@ -575,6 +689,38 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     const dim3 grid(static_cast<unsigned>(ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(nseg));
     assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");
+    return ok();
+}
+
+int need_assoc_memory_step(const need_assoc_step_args* a, need_stream_t stream) {
+    if (a == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (!dtype_ok(a->dtype)) return fail(NEED_ERR_UNSUPPORTED, "dtype %d", a->dtype);
+    if (a->qk_dtype != NEED_F32 && a->qk_dtype != NEED_BF16)
+        return fail(NEED_ERR_UNSUPPORTED, "q_raw / k_raw must be fp32 or bf16 (dtype %d)", a->qk_dtype);
+    if (a->nseq < 1 || a->r < 1 || a->d < 1) return fail(NEED_ERR_INVALID, "sizes must be >= 1");
+    if (a->r > kStepMaxRank) return fail(NEED_ERR_UNSUPPORTED, "r=%lld: at most %d features", (long long)a->r, kStepMaxRank);
+    const int64_t vec = 16 / dtype_bytes(a->dtype);
+    if (a->d % vec != 0 || a->d > INT32_MAX / 2 || a->nseq > INT32_MAX)
+        return fail(NEED_ERR_UNSUPPORTED, "d=%lld must be a multiple of %lld", (long long)a->d, (long long)vec);
+    if (a->q_raw == nullptr || a->k_raw == nullptr || a->v == nullptr || a->state == nullptr ||
+        a->denom == nullptr || a->out == nullptr)
+        return fail(NEED_ERR_INVALID, "q_raw, k_raw, v, state, denom and out must be non-null");
+    if (a->write_mask != nullptr && a->mask_dtype != NEED_F32 && a->mask_dtype != NEED_BF16)
+        return fail(NEED_ERR_UNSUPPORTED, "write_mask must be fp32 or bf16 (dtype %d)", a->mask_dtype);
+    if (!aligned16(a->v) || !aligned16(a->state) || !aligned16(a->out) || a->v_stride % vec != 0 ||
+        a->out_stride % vec != 0 || a->state_stride_n % vec != 0 || a->state_stride_r % vec != 0)
+        return fail(NEED_ERR_UNSUPPORTED, "v, state and out need 16-byte aligned rows");
+    if (!(a->eps >= 0.0)) return fail(NEED_ERR_INVALID, "eps must be >= 0");
+    StepParams p{a->q_raw, a->k_raw, a->q_stride, a->k_stride, a->qk_dtype == NEED_F32 ? 1 : 0, a->v, a->v_stride,
+                 a->write_mask, a->mask_dtype == NEED_F32 ? 1 : 0, a->state, a->state_stride_n, a->state_stride_r,
+                 a->denom, a->denom_stride_n, a->slot, a->out, a->out_stride, static_cast<int32_t>(a->r),
+                 static_cast<int32_t>(a->d), static_cast<float>(a->eps)};
+    const dim3 grid(static_cast<unsigned>(a->nseq));
+    if (a->dtype == NEED_BF16) assoc_step_kernel<__nv_bfloat16><<<grid, kStepThreads, 0, stream>>>(p);
+    else if (a->dtype == NEED_F16) assoc_step_kernel<__half><<<grid, kStepThreads, 0, stream>>>(p);
+    else assoc_step_kernel<float><<<grid, kStepThreads, 0, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "assoc_step_kernel launch");
     return ok();
 }
 

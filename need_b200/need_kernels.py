@@ -693,6 +693,61 @@ def linear_associative_memory(q_raw: torch.Tensor, k_raw: torch.Tensor, v: torch
     return out
 
 
+def assoc_memory_step(q_raw: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor, state: torch.Tensor,
+                      denom: torch.Tensor, write_mask: Optional[torch.Tensor] = None, *,
+                      slot: Optional[torch.Tensor] = None, eps: float = 1e-6) -> torch.Tensor:
+    """One token of HierarchicalMemory.stream_step's associative memory
+    (need_core.py:2067-2080) for each of N sequences, with the reference's
+    model-dtype arithmetic.  q_raw, k_raw [N, r]; v [N, d] in the model dtype;
+    ``state`` [S, r, d] and ``denom`` [S, r] (the module's ``assoc_state`` /
+    ``assoc_denom``, model dtype) are updated in place for the sequences' rows
+    (``slot`` [N] int32 picks rows of a pool; default row i).  ``write_mask``
+    [N] (or [N, 1, 1]) scales k and v.  Returns the associative read [N, d].
+    """
+    _require_cuda(q_raw, k_raw, v, state, denom, write_mask, slot)
+    _no_grad(q_raw, k_raw, v, state, denom)
+    if q_raw.dim() == 3:
+        q_raw, k_raw, v = q_raw[:, 0], k_raw[:, 0], v[:, 0]
+    n, r = q_raw.shape
+    d = v.shape[-1]
+    if (k_raw.shape != q_raw.shape or v.shape != (n, d) or state.dim() != 3 or state.shape[1:] != (r, d)
+            or denom.dim() != 2 or denom.shape[1] != r or state.dtype != v.dtype or denom.dtype != v.dtype):
+        raise ValueError("assoc_memory_step: q_raw, k_raw [N, r], v [N, d], state [S, r, d] and denom [S, r] "
+                         "in v's dtype")
+    if v.dtype not in _DT:
+        raise NotImplementedError(f"assoc_memory_step: dtype {v.dtype}")
+    if state.stride(-1) != 1 or denom.stride(-1) != 1 or state.data_ptr() % 16 or (
+            state.stride(1) * state.element_size()) % 16 or (state.stride(0) * state.element_size()) % 16:
+        raise ValueError("assoc_memory_step: state needs contiguous, 16-byte aligned rows (it is updated in place)")
+    qk = torch.float32 if q_raw.dtype == torch.float32 else torch.bfloat16
+    q = q_raw if q_raw.dtype == qk and q_raw.stride(-1) == 1 else q_raw.to(qk).contiguous()
+    k = k_raw if k_raw.dtype == qk and k_raw.stride(-1) == 1 else k_raw.to(qk).contiguous()
+    vv = v if v.stride(-1) == 1 and v.data_ptr() % 16 == 0 and (v.stride(0) * v.element_size()) % 16 == 0 \
+        else v.contiguous()
+    out = torch.empty((n, d), dtype=v.dtype, device=v.device)
+    a = abi.NeedAssocStepArgs()
+    a.dtype, a.qk_dtype, a.nseq, a.r, a.d = _DT[v.dtype], _DT[qk], n, r, d
+    a.q_raw, a.q_stride, a.k_raw, a.k_stride = q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0)
+    a.v, a.v_stride = vv.data_ptr(), vv.stride(0)
+    m = None
+    if write_mask is not None:
+        m = write_mask.reshape(n)
+        if m.dtype not in (torch.float32, torch.bfloat16):
+            m = m.float()
+        m = m.contiguous()
+        a.write_mask, a.mask_dtype = m.data_ptr(), _DT[m.dtype]
+    a.state, a.state_stride_n, a.state_stride_r = state.data_ptr(), state.stride(0), state.stride(1)
+    a.denom, a.denom_stride_n = denom.data_ptr(), denom.stride(0)
+    sl = None
+    if slot is not None:
+        sl = slot.to(torch.int32).contiguous()
+        a.slot = sl.data_ptr()
+    a.out, a.out_stride, a.eps = out.data_ptr(), out.stride(0), float(eps)
+    abi.check("need_assoc_memory_step", _lib().need_assoc_memory_step(ctypes.byref(a), _stream(v.device)))
+    del q, k, vv, m, sl
+    return out
+
+
 # --------------------------------------------------------------------------
 # ragged decode / speculative verify
 # --------------------------------------------------------------------------

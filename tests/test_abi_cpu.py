@@ -50,6 +50,7 @@ def test_struct_layout_matches_header(tmp_path):
         "need_conv_args": (abi.NeedConvArgs, [f[0] for f in abi.NeedConvArgs._fields_]),
         "need_assoc_args": (abi.NeedAssocArgs, [f[0] for f in abi.NeedAssocArgs._fields_]),
         "need_norm_args": (abi.NeedNormArgs, [f[0] for f in abi.NeedNormArgs._fields_]),
+        "need_assoc_step_args": (abi.NeedAssocStepArgs, [f[0] for f in abi.NeedAssocStepArgs._fields_]),
     }
     lines = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void) {"]
     for cname, (_, names) in fields.items():
@@ -120,6 +121,12 @@ def test_argument_errors_return_status(lib):
     assert lib.need_rms_norm(ctypes.byref(n), None) == abi.ERR_UNSUPPORTED  # C not a multiple of 8
     n.C, n.weight_dtype = 832, abi.F16
     assert lib.need_rms_norm(ctypes.byref(n), None) == abi.ERR_UNSUPPORTED  # weight dtype
+    sa = abi.NeedAssocStepArgs()
+    assert lib.need_assoc_memory_step(None, None) == abi.ERR_INVALID
+    sa.dtype, sa.qk_dtype, sa.nseq, sa.r, sa.d = abi.BF16, abi.F32, 4, 300, 64
+    assert lib.need_assoc_memory_step(ctypes.byref(sa), None) == abi.ERR_UNSUPPORTED  # rank above 256
+    sa.r = 64
+    assert lib.need_assoc_memory_step(ctypes.byref(sa), None) == abi.ERR_INVALID  # null tensors
     m = abi.NeedAssocArgs()
     assert lib.need_assoc_memory(None, None) == abi.ERR_INVALID
     m.dtype, m.qk_dtype, m.nb, m.T, m.r, m.d = abi.BF16, abi.F32, 1, 16, 64, 64

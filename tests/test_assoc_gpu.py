@@ -123,3 +123,48 @@ def test_rejects_what_it_does_not_take(cuda):
         nk.linear_associative_memory(q[..., :64], q[..., :64], v.float())  # fp32 values
     with pytest.raises(ValueError):
         nk.linear_associative_memory(q[..., :64], q[..., :64], v[:, :4])
+
+
+# ------------------------------------------------------------------ one-token streaming step
+
+def test_step_matches_reference_fixture(cuda):
+    """HierarchicalMemory.stream_step's associative memory, 5 steps from given
+    states with a write mask, against the reference's own outputs and states."""
+    inp = cases.make_inputs("assoc_step_bf16")
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/assoc_step_bf16.npz")
+    bf = torch.bfloat16
+    st = torch.from_numpy(inp["state"]).to(bf).to(cuda)
+    dn = torch.from_numpy(inp["denom"]).to(bf).to(cuda)
+    for j in range(inp["q"].shape[0]):
+        y = nk.assoc_memory_step(torch.from_numpy(inp["q"][j]).to(cuda), torch.from_numpy(inp["k"][j]).to(cuda),
+                                 torch.from_numpy(inp["v"][j]).to(bf).to(cuda), st, dn,
+                                 torch.from_numpy(inp["wm"][j]).to(cuda))
+        assert np.mean(host(st) == g["state"][j]) >= 0.999 and np.mean(host(dn) == g["denom"][j]) >= 0.999, j
+        assert np.mean(host(y) == g["y"][j]) >= 0.99 and rel(host(y), g["y"][j]) <= TOL, j
+
+
+@pytest.mark.parametrize("dtype,name", [(torch.bfloat16, "bf16"), (torch.float16, "fp16"), (torch.float32, "fp32")])
+def test_step_matches_oracle_with_a_pool(cuda, dtype, name):
+    """64 sequences at NEED's shape (r=64, d=832) in a pool of 100 state rows,
+    3 steps with a write mask, against the oracle."""
+    gen = torch.Generator().manual_seed(31)
+    N, S, r, d = 64, 100, 64, 832
+    pool = (0.5 * torch.randn(S, r, d, generator=gen)).to(dtype)
+    pden = (5.0 * torch.rand(S, r, generator=gen)).to(dtype)
+    slot = torch.randperm(S, generator=gen)[:N].to(torch.int32)
+    st, dn = pool.to(cuda), pden.to(cuda)
+    want_st, want_dn = pool[slot.long()].float().numpy(), pden[slot.long()].float().numpy()
+    for step in range(3):
+        q, k = torch.randn(N, r, generator=gen), torch.randn(N, r, generator=gen)
+        v = torch.randn(N, d, generator=gen).to(dtype)
+        wm = torch.rand(N, generator=gen) * 1.4 - 0.2 if step == 1 else None
+        y = nk.assoc_memory_step(q.to(cuda), k.to(cuda), v.to(cuda), st, dn,
+                                 None if wm is None else wm.to(cuda), slot=slot.to(cuda))
+        want_y, want_st, want_dn = oracle.assoc_step(q.numpy(), k.numpy(), v.float().numpy(), want_st, want_dn,
+                                                     None if wm is None else wm.numpy(), dtype=name)
+        got_st = host(st)[slot.long().numpy()]
+        eq = 0.999 if dtype != torch.float32 else 0.0
+        assert np.mean(got_st == want_st) >= eq and rel(got_st, want_st) <= 1e-2, step
+        assert rel(host(y), want_y) <= (1e-5 if dtype == torch.float32 else TOL), step
+    untouched = np.setdiff1d(np.arange(S), slot.numpy())
+    assert np.array_equal(host(st)[untouched], pool[untouched].float().numpy())
