@@ -534,22 +534,30 @@ __global__ void __launch_bounds__(kStepThreads) assoc_step_kernel(const StepPara
         }
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-#pragma unroll 4
-        for (int i = 0; i < p.r; ++i) {
-            uint4* ptr = reinterpret_cast<uint4*>(st + i * p.sr + c);
-            uint4 u = *ptr;
-            PS* h = reinterpret_cast<PS*>(&u);
-            const float kf = s_k[i], qf = s_q[i];
+        // rows in batches of U: the batch's loads are issued together, before its stores
+        constexpr int U = 8;
+        for (int i0 = 0; i0 < p.r; i0 += U) {
+            uint4 u[U];
 #pragma unroll
-            for (int e = 0; e < VEC / 2; ++e) {
-                const float2 f = widen(h[e]);
-                const float s0 = rnd_to<TS>(__fadd_rn(f.x, rnd_to<TS>(__fmul_rn(kf, vv[2 * e]))));
-                const float s1 = rnd_to<TS>(__fadd_rn(f.y, rnd_to<TS>(__fmul_rn(kf, vv[2 * e + 1]))));
-                h[e] = Ops<TS>::pack(s0, s1);
-                acc[2 * e] = __fadd_rn(acc[2 * e], __fmul_rn(qf, s0));
-                acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], __fmul_rn(qf, s1));
+            for (int k = 0; k < U; ++k)
+                if (i0 + k < p.r) u[k] = *reinterpret_cast<const uint4*>(st + (int64_t)(i0 + k) * p.sr + c);
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const int i = i0 + k;
+                if (i >= p.r) break;
+                PS* h = reinterpret_cast<PS*>(&u[k]);
+                const float kf = s_k[i], qf = s_q[i];
+#pragma unroll
+                for (int e = 0; e < VEC / 2; ++e) {
+                    const float2 f = widen(h[e]);
+                    const float s0 = rnd_to<TS>(__fadd_rn(f.x, rnd_to<TS>(__fmul_rn(kf, vv[2 * e]))));
+                    const float s1 = rnd_to<TS>(__fadd_rn(f.y, rnd_to<TS>(__fmul_rn(kf, vv[2 * e + 1]))));
+                    h[e] = Ops<TS>::pack(s0, s1);
+                    acc[2 * e] = __fadd_rn(acc[2 * e], __fmul_rn(qf, s0));
+                    acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], __fmul_rn(qf, s1));
+                }
+                *reinterpret_cast<uint4*>(st + (int64_t)i * p.sr + c) = u[k];
             }
-            *ptr = u;
         }
         uint4 o;
         PS* oh = reinterpret_cast<PS*>(&o);
