@@ -362,7 +362,7 @@ NEED_API int need_assoc_memory_step(const need_assoc_step_args* args, need_strea
 /* ------------------------------------------------------------------------ */
 
 typedef struct {
-    int32_t form;          /* NEED_FORM_GATED or NEED_FORM_SSD */
+    int32_t form;          /* NEED_FORM_GATED, NEED_FORM_SSD or NEED_FORM_RETENTION */
     int32_t dtype;         /* NEED_BF16, NEED_F16 or NEED_F32: states, inputs and outputs */
     int64_t nseq, C;
     void* states;          /* [nslots, C] state pool, read only here */
@@ -370,15 +370,20 @@ typedef struct {
     const int32_t* cu_k;   /* [nseq + 1] offsets of each sequence's drafted tokens */
     int64_t total_k;       /* cu_k[nseq] (rows of the packed inputs) */
     const void* in[5];     /* packed [total_k, C] contiguous: GATED z, g, x;
-                              SSD dt_raw, b_gate, u, c_gate, out_gate */
+                              SSD dt_raw, b_gate, u, c_gate, out_gate;
+                              RETENTION in[0] = decay [total_k, C / head_dim] (one value
+                              per head), in[1..3] = k, v, q */
     const float* d_skip;   /* SSD: [C] fp32 */
     double dt_min, dt_max;
     void* y;               /* [total_k, C] output of each drafted token */
     void* states_k;        /* [total_k, C] state after each drafted token */
+    int64_t head_dim;      /* RETENTION: channels per head (a multiple of 8 dividing C) */
 } need_verify_args;
 
 /* k_i one-token steps per sequence from its pooled state, in the model dtype's
- * arithmetic (need_core.py:6420-6428).  The pool is not modified. */
+ * arithmetic (need_core.py:6420-6428; RETENTION: SelectiveRetention's step
+ * state = decay * state + k * v, y = q * state, need_core.py:1590-1592).  The
+ * pool is not modified. */
 NEED_API int need_ragged_verify(const need_verify_args* args, need_stream_t stream);
 
 /* states[slot[i]] := states_k[cu_k[i] + accept_len[i] - 1] when accept_len[i] > 0;

@@ -46,7 +46,7 @@ class NeedVerifyArgs(Structure):
         ("form", c_int32), ("dtype", c_int32), ("nseq", c_int64), ("C", c_int64),
         ("states", c_void_p), ("slot", c_void_p), ("cu_k", c_void_p), ("total_k", c_int64),
         ("in_", c_void_p * 5), ("d_skip", c_void_p), ("dt_min", c_double), ("dt_max", c_double),
-        ("y", c_void_p), ("states_k", c_void_p),
+        ("y", c_void_p), ("states_k", c_void_p), ("head_dim", c_int64),
     ]
 
 

@@ -2,8 +2,9 @@
 //
 // need_ragged_verify runs k_i one-token recurrent steps for each of nseq
 // sequences from its pooled state, in the model dtype's arithmetic of the
-// reference's streaming step (need_core.py:6420-6428: every op rounded to the
-// state dtype), and records the output and the state after every drafted
+// reference's streaming steps (need_core.py:6420-6428 for the SSD / gated
+// block, :1590-1592 and :6440-6444 for SelectiveRetention: every op rounded to
+// the state dtype), and records the output and the state after every drafted
 // token.  need_commit_states then keeps, per sequence, the state after its
 // accepted prefix (the reference keeps the accepted tokens, generate.py:1078-1083,
 // and recomputes its whole context on the next verify, generate.py:909-913).
@@ -33,6 +34,7 @@ struct VerifyParams {
     float dt_min, dt_scale;
     void* y;
     void* states_k;
+    int64_t H, head_dim;  // RETENTION: in[0] is the decay per (token, head) [sum k, H]
 };
 
 template <typename T>
@@ -71,7 +73,9 @@ template <typename T, int FORM>
 __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
     using O = Ops<T>;
     using P = typename O::P;
-    constexpr int NIN = FORM == FORM_GATED ? 3 : 5;
+    // streamed [C] inputs: GATED z, g, x; SSD dt, bg, u, cg, og; RETENTION k, v, q (in[1..3])
+    constexpr int NIN = FORM == FORM_SSD ? 5 : 3;
+    constexpr int IN0 = FORM == FORM_RETENTION ? 1 : 0;
     const int64_t i = blockIdx.y;
     const int64_t c = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
     if (i >= p.nseq || c >= p.C) return;
@@ -84,18 +88,36 @@ __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) dsk[q] = O::pack(p.dskip[c + 2 * q], p.dskip[c + 2 * q + 1]);
     }
+    const int64_t head = FORM == FORM_RETENTION ? c / p.head_dim : 0;  // a thread's 8 channels share a head
     for (int64_t j0 = kb; j0 < ke; j0 += 4) {
         P x[4][NIN][4];
+        T dh[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-            if (j0 + u < ke)
+            if (j0 + u < ke) {
 #pragma unroll
                 for (int k = 0; k < NIN; ++k)
-                    Vec8<T>::ld(reinterpret_cast<const T*>(p.in[k]) + (j0 + u) * p.C + c, x[u][k]);
+                    Vec8<T>::ld(reinterpret_cast<const T*>(p.in[IN0 + k]) + (j0 + u) * p.C + c, x[u][k]);
+                if constexpr (FORM == FORM_RETENTION) dh[u] = reinterpret_cast<const T*>(p.in[0])[(j0 + u) * p.H + head];
+            }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             if (j0 + u >= ke) break;
             P yo[4];
+            if constexpr (FORM == FORM_RETENTION) {
+                // need_core.py:1590-1592: state = decay * state + k * v; y = q * state,
+                // each op in the state dtype
+                const float df = to_f(dh[u]);
+                const P dec = O::pack(df, df);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    st[q] = O::add(O::mul(dec, st[q]), O::mul(x[u][0][q], x[u][1][q]));
+                    yo[q] = O::mul(x[u][2][q], st[q]);
+                }
+                Vec8<T>::st(reinterpret_cast<T*>(p.y) + (j0 + u) * p.C + c, yo);
+                Vec8<T>::st(reinterpret_cast<T*>(p.states_k) + (j0 + u) * p.C + c, st);
+                continue;
+            }
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float2 f0 = O::unpack(x[u][0][q]);
@@ -170,14 +192,19 @@ extern "C" {
 
 int need_ragged_verify(const need_verify_args* a, need_stream_t stream) {
     if (a == nullptr) return fail(NEED_ERR_INVALID, "args is null");
-    if (a->form != NEED_FORM_GATED && a->form != NEED_FORM_SSD)
-        return fail(NEED_ERR_INVALID, "form must be GATED or SSD");
+    if (a->form != NEED_FORM_GATED && a->form != NEED_FORM_SSD && a->form != NEED_FORM_RETENTION)
+        return fail(NEED_ERR_INVALID, "form must be GATED, SSD or RETENTION");
     if (int rc = check_rows(a->dtype, a->nseq, a->C)) return rc;
+    if (a->form == NEED_FORM_RETENTION &&
+        (a->head_dim < 8 || a->head_dim % 8 != 0 || a->C % a->head_dim != 0))
+        return fail(NEED_ERR_UNSUPPORTED, "head_dim=%lld must be a multiple of 8 that divides C=%lld",
+                    (long long)a->head_dim, (long long)a->C);
     if (a->nseq == 0 || a->total_k == 0) return ok();
-    const int nin = a->form == NEED_FORM_GATED ? 3 : 5;
+    const int nin = a->form == NEED_FORM_SSD ? 5 : a->form == NEED_FORM_RETENTION ? 4 : 3;
     if (!a->states || !a->cu_k || !a->y || !a->states_k) return fail(NEED_ERR_INVALID, "null pointer");
     for (int k = 0; k < nin; ++k)
-        if (!a->in[k] || !aligned16(a->in[k])) return fail(NEED_ERR_INVALID, "in[%d] null or not 16-byte aligned", k);
+        if (!a->in[k] || (!aligned16(a->in[k]) && !(a->form == NEED_FORM_RETENTION && k == 0)))
+            return fail(NEED_ERR_INVALID, "in[%d] null or not 16-byte aligned", k);
     if (!aligned16(a->states) || !aligned16(a->y) || !aligned16(a->states_k))
         return fail(NEED_ERR_UNSUPPORTED, "states / y / states_k must be 16-byte aligned");
     if (a->form == NEED_FORM_SSD && !a->d_skip) return fail(NEED_ERR_INVALID, "d_skip is null");
@@ -193,12 +220,19 @@ int need_ragged_verify(const need_verify_args* a, need_stream_t stream) {
     p.dt_scale = static_cast<float>(a->dt_max - a->dt_min);
     p.y = a->y;
     p.states_k = a->states_k;
+    p.head_dim = a->form == NEED_FORM_RETENTION ? a->head_dim : 8;
+    p.H = a->C / p.head_dim;
     const cudaStream_t s = stream;
     int rc;
-    const bool g = a->form == NEED_FORM_GATED;
-    if (a->dtype == NEED_BF16) rc = g ? launch_verify<__nv_bfloat16, FORM_GATED>(p, s) : launch_verify<__nv_bfloat16, FORM_SSD>(p, s);
-    else if (a->dtype == NEED_F16) rc = g ? launch_verify<__half, FORM_GATED>(p, s) : launch_verify<__half, FORM_SSD>(p, s);
-    else rc = g ? launch_verify<float, FORM_GATED>(p, s) : launch_verify<float, FORM_SSD>(p, s);
+    auto by_form = [&](auto tag) {
+        using T = decltype(tag);
+        return a->form == NEED_FORM_GATED ? launch_verify<T, FORM_GATED>(p, s)
+               : a->form == NEED_FORM_SSD ? launch_verify<T, FORM_SSD>(p, s)
+                                          : launch_verify<T, FORM_RETENTION>(p, s);
+    };
+    if (a->dtype == NEED_BF16) rc = by_form(__nv_bfloat16{});
+    else if (a->dtype == NEED_F16) rc = by_form(__half{});
+    else rc = by_form(float{});
     return rc ? rc : ok();
 }
 

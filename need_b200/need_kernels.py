@@ -760,10 +760,13 @@ def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str
 
     ``states`` [S, C] pool (not modified); ``cu_k`` int32 [N+1] offsets of each
     sequence's drafted tokens in the packed inputs; ``inputs`` is
-    (decay_logit, gate_logit, x) for ``form="gated"`` or
-    (dt_raw, b_gate, u, c_gate, out_gate) for ``form="ssd"``, each [sum k, C].
-    Arithmetic follows the reference's streaming step (need_core.py:6420-6428),
-    every op in the state dtype.  Returns (y, states_k), both [sum k, C].
+    (decay_logit, gate_logit, x) for ``form="gated"``,
+    (dt_raw, b_gate, u, c_gate, out_gate) for ``form="ssd"``, each [sum k, C],
+    or (decay [sum k, H], k, v, q) for ``form="retention"`` (SelectiveRetention,
+    H heads of C / H channels; states are its ``state`` [S, H, hd] flattened).
+    Arithmetic follows the reference's streaming steps (need_core.py:6420-6428,
+    :1590-1592), every op in the state dtype.  Returns (y, states_k), both
+    [sum k, C].
     """
     _require_cuda(states, cu_k, *inputs)
     nseq = cu_k.numel() - 1
@@ -772,7 +775,9 @@ def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str
     y, sk = out if out is not None else (torch.empty(total, C, dtype=states.dtype, device=states.device),
                                          torch.empty(total, C, dtype=states.dtype, device=states.device))
     a = abi.NeedVerifyArgs()
-    a.form = abi.FORM_GATED if form == "gated" else abi.FORM_SSD
+    a.form = {"gated": abi.FORM_GATED, "ssd": abi.FORM_SSD, "retention": abi.FORM_RETENTION}[form]
+    if form == "retention":
+        a.head_dim = C // inputs[0].shape[1]
     a.dtype = _DT[states.dtype]
     a.nseq, a.C = nseq, C
     a.states = states.data_ptr()

@@ -215,13 +215,14 @@ def stream_step(form: str, state, p0, p1, p2, p3=None, p4=None, dskip=None,
 
     form "gated": p0=decay logit, p1=input-gate logit, p2=x.
     form "ssd":   p0=dt_raw, p1=b_gate, p2=u_act, p3=c_gate, p4=out_gate, dskip=[C].
+    form "retention": p0=decay per channel (a head's value repeated), p1=k, p2=v, p3=q.
     """
     st = _f32(state).copy()
     n, c = st.shape
     ps = [_f32(p) if p is not None else None for p in (p0, p1, p2, p3, p4)]
     ds = None if dskip is None else _f32(dskip).reshape(-1)
     y = np.empty_like(st)
-    _lib().ora_stream_step(0 if form == "gated" else 1, _ptr(st), *[_ptr(p) for p in ps], _ptr(ds), _ptr(y),
+    _lib().ora_stream_step({"gated": 0, "ssd": 1, "retention": 2}[form], _ptr(st), *[_ptr(p) for p in ps], _ptr(ds), _ptr(y),
                            n, c, float(dt_min), float(dt_max), MODE[dtype])
     return st, y
 

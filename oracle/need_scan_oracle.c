@@ -496,7 +496,10 @@ ORA_API void ora_assoc_memory(const float* q_raw, const float* k_raw, const floa
 /* one-token recurrent step (streaming decode)                         */
 /* ------------------------------------------------------------------ */
 
-/* form 0 (gated):  dec = sigmoid(p0); upd = (1-dec)*(sigmoid(p1)*p2)
+/* form 2 (selective retention, need_core.py:1590-1592 and :6440-6444):
+ *                  state = decay*state + k*v; y = q*state, with p0 = decay (the
+ *                  per-head value repeated over its channels), p1 = k, p2 = v, p3 = q
+ * form 0 (gated):  dec = sigmoid(p0); upd = (1-dec)*(sigmoid(p1)*p2)
  *                  state = dec*state + upd; y = state
  * form 1 (ssd):    p0=dt_raw, p1=b_gate, p2=u_act, p3=c_gate, p4=out_gate
  *                  dec = exp(-(dt_min + (dt_max-dt_min)*sigmoid(p0)))
@@ -509,6 +512,14 @@ ORA_API void ora_stream_step(int form, float* state, const float* p0, const floa
                              const float* dskip, float* y, int64_t N, int64_t C,
                              double dt_min, double dt_max, int mode) {
     const float scale = (float)(dt_max - dt_min), off = (float)dt_min;
+    if (form == 2) { /* selective retention: p0 = decay (per channel), p1 = k, p2 = v, p3 = q */
+        for (int64_t i = 0; i < N * C; ++i) {
+            const float st = rnd(rnd(p0[i] * state[i], mode) + rnd(p1[i] * p2[i], mode), mode);
+            state[i] = st;
+            y[i] = rnd(p3[i] * st, mode);
+        }
+        return;
+    }
     for (int64_t n = 0; n < N; ++n)
         for (int64_t c = 0; c < C; ++c) {
             const int64_t i = n * C + c;

@@ -88,6 +88,8 @@ CASES = {
     # streaming one-token steps (ragged verify oracle)
     "stream_gated_bf16": dict(kind="stream", form="gated", seed=7, s=5, c=64, kmax=4, dtype="bf16"),
     "stream_ssd_bf16": dict(kind="stream", form="ssd", seed=8, s=5, c=64, kmax=4, dtype="bf16"),
+    # SelectiveRetention's step: decay per head (4 heads of 16 channels), k, v, q
+    "stream_retention_bf16": dict(kind="stream", form="retention", seed=15, s=5, c=64, kmax=4, dtype="bf16"),
 }
 
 
@@ -158,6 +160,11 @@ def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
         out["p0"] = cast(rs.standard_normal((tot, c)) + 4.0, dtype)
         out["p1"] = cast(rs.standard_normal((tot, c)), dtype)
         out["p2"] = cast(rs.standard_normal((tot, c)), dtype)
+    elif form == "retention":
+        heads = 4
+        out["decay"] = cast(np.clip(rs.uniform(0.7, 0.999, (tot, heads)), 0.05, 0.999), dtype)  # [sum k, H]
+        for i in (1, 2, 3):  # k, v, q
+            out[f"p{i}"] = cast(rs.standard_normal((tot, c)), dtype)
     else:
         for i in range(5):
             out[f"p{i}"] = cast(rs.standard_normal((tot, c)), dtype)

@@ -123,7 +123,13 @@ def ref_stream(inp, form, dtype):
     for i in range(states.shape[0]):
         rec = states[i:i + 1].clone()
         for j in range(int(cu[i]), int(cu[i + 1])):
-            if form == "gated":
+            if form == "retention":  # need_core.py:1590-1592 / :6440-6444, heads of c // H channels
+                dec = T(inp["decay"][j:j + 1], dtype)
+                dec = dec.repeat_interleave(c // dec.shape[1], dim=1)
+                kk, vv, qq = (T(inp[f"p{k}"][j:j + 1], dtype) for k in (1, 2, 3))
+                rec = dec * rec + kk * vv
+                y = qq * rec
+            elif form == "gated":
                 decay = torch.sigmoid(T(inp["p0"][j:j + 1], dtype))
                 bg = torch.sigmoid(T(inp["p1"][j:j + 1], dtype))
                 u_act = T(inp["p2"][j:j + 1], dtype)
@@ -190,6 +196,27 @@ def assoc_step(q_raw, k_raw, v, state, denom, wm=None):
     return numer / den, st, dn
 
 
+def check_module_selective_step():
+    """The retention form of ref_stream against SelectiveRetention.stream_step."""
+    torch.manual_seed(0)
+    cfg = need_core.NeedConfig(d_model=16, n_heads=2, n_layers=1, block_size=32)
+    mod = need_core.SelectiveRetention(cfg).to(torch.bfloat16).eval()
+    state = {}
+    b, h, hd = 3, mod.heads, mod.head_dim
+    rec = torch.zeros(b, h, hd, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for t in range(4):
+            x = torch.randn(b, 1, 16).to(torch.bfloat16)
+            mod.stream_step(x, state)
+            q, k, v = mod.in_proj(x).chunk(3, dim=-1)
+            q, k, v = (z.view(b, h, hd) for z in (q, k, v))
+            dyn = torch.sigmoid(mod.decay_proj(x)).transpose(1, 2).squeeze(-1).unsqueeze(-1)
+            base = mod.base_decay.squeeze(0).squeeze(-1).to(dtype=x.dtype)
+            decay = (base.unsqueeze(0) + cfg.retention_dynamic_scale * (dyn - 0.5) * 0.05).clamp(0.05, 0.999)
+            rec = decay * rec + k * v
+            assert torch.equal(rec, state["state"]), f"selective stream step mismatch at t={t}"
+
+
 def check_module_assoc_step():
     """assoc_step against the real HierarchicalMemory.stream_step: its state and
     its mixed output (semantic and cue recomputed as the module does)."""
@@ -236,6 +263,7 @@ def ref_assoc_step(inp, dtype):
 
 def main():
     check_module_stream_step()
+    check_module_selective_step()
     check_module_assoc_step()
     for name, spec in cases.CASES.items():
         inp = cases.make_inputs(name)

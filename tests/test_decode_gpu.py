@@ -1,5 +1,6 @@
 """Ragged decode / speculative verify and commit against the oracle's
-sequential one-token steps (need_core.py:6420-6428 arithmetic)."""
+sequential one-token steps (need_core.py:6420-6428 arithmetic; SelectiveRetention's
+step need_core.py:1590-1592)."""
 import numpy as np
 import pytest
 import torch
@@ -100,3 +101,49 @@ def test_verify_graph_capture(cuda):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(pool, ref_pool) and torch.equal(y, y2)
+
+
+def test_selective_retention_verify_matches_reference_fixture(cuda):
+    """SelectiveRetention's one-token step (need_core.py:1590-1592): the
+    reference's own states and outputs, bit for bit."""
+    inp = cases.make_inputs("stream_retention_bf16")
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/stream_retention_bf16.npz")
+    bf = lambda k: torch.from_numpy(inp[k]).to(cuda).to(torch.bfloat16)  # noqa: E731
+    states = bf("states")
+    cu = torch.from_numpy(inp["cu_k"].astype(np.int32)).to(cuda)
+    y, sk = nk.ragged_verify(states, cu, (bf("decay"), bf("p1"), bf("p2"), bf("p3")), form="retention")
+    np.testing.assert_array_equal(host(sk), g["states_k"])
+    np.testing.assert_array_equal(host(y), g["y"])
+
+
+@pytest.mark.parametrize("dtype,mode", [(torch.bfloat16, "bf16"), (torch.float16, "fp16"), (torch.float32, "fp32")])
+def test_selective_retention_verify_and_commit(cuda, dtype, mode):
+    """128 sequences of 13 heads x 64 channels (NEED's 350M shape), ragged k,
+    pooled slots, against the oracle; then the commit keeps the accepted state."""
+    rs = np.random.RandomState(5)
+    N, H, hd = 128, 13, 64
+    C = H * hd
+    ks = rs.randint(0, 5, N).astype(np.int32)
+    tot = int(ks.sum())
+    cu = np.concatenate([[0], np.cumsum(ks)]).astype(np.int32)
+    gen = torch.Generator().manual_seed(6)
+    pool = (0.5 * torch.randn(150, C, generator=gen)).to(dtype)
+    slot = rs.permutation(150)[:N].astype(np.int32)
+    decay = (0.7 + 0.29 * torch.rand(tot, H, generator=gen)).to(dtype)
+    k, v, q = (torch.randn(tot, C, generator=gen).to(dtype) for _ in range(3))
+    dev = lambda t: t.to(cuda)  # noqa: E731
+    pool_d = dev(pool)
+    y, sk = nk.ragged_verify(pool_d, dev(torch.from_numpy(cu)), (dev(decay), dev(k), dev(v), dev(q)),
+                             form="retention", slot=dev(torch.from_numpy(slot)))
+    want_y, want_sk = oracle.ragged_verify("retention", host(pool)[slot], cu,
+                                           np.repeat(host(decay), hd, axis=1), host(k), host(v), host(q),
+                                           dtype=mode)
+    np.testing.assert_array_equal(host(sk), want_sk)
+    np.testing.assert_array_equal(host(y), want_y)
+    accept = np.minimum(rs.randint(0, 5, N), ks).astype(np.int32)
+    nk.commit_states(pool_d, sk, dev(torch.from_numpy(cu)), dev(torch.from_numpy(accept)),
+                     slot=dev(torch.from_numpy(slot)))
+    got = host(pool_d)
+    for i in range(N):
+        want = want_sk[cu[i] + accept[i] - 1] if accept[i] > 0 else host(pool)[slot[i]]
+        np.testing.assert_array_equal(got[slot[i]], want)

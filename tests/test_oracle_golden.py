@@ -129,11 +129,15 @@ def test_assoc_stream_step():
         assert np.array_equal(y, g["y"][j]), j
 
 
-@pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16"])
+@pytest.mark.parametrize("name", ["stream_gated_bf16", "stream_ssd_bf16", "stream_retention_bf16"])
 def test_stream_steps(name):
     inp, g = load(name)
     spec = cases.CASES[name]
-    y, sk = oracle.ragged_verify(spec["form"], inp["states"], inp["cu_k"], inp["p0"], inp["p1"], inp["p2"],
+    p0 = inp.get("p0")
+    if spec["form"] == "retention":  # the per-head decay repeated over each head's channels
+        c = inp["states"].shape[1]
+        p0 = np.repeat(inp["decay"], c // inp["decay"].shape[1], axis=1)
+    y, sk = oracle.ragged_verify(spec["form"], inp["states"], inp["cu_k"], p0, inp["p1"], inp["p2"],
                                  inp.get("p3"), inp.get("p4"), inp.get("dskip"), dtype=spec["dtype"])
     assert np.array_equal(y, g["y"]) and np.array_equal(sk, g["states_k"])
 
