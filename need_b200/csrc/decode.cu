@@ -114,33 +114,31 @@ __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
                     st[q] = O::add(O::mul(dec, st[q]), O::mul(x[u][0][q], x[u][1][q]));
                     yo[q] = O::mul(x[u][2][q], st[q]);
                 }
-                Vec8<T>::st(reinterpret_cast<T*>(p.y) + (j0 + u) * p.C + c, yo);
-                Vec8<T>::st(reinterpret_cast<T*>(p.states_k) + (j0 + u) * p.C + c, st);
-                continue;
-            }
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 f0 = O::unpack(x[u][0][q]);
-                const float2 f1 = O::unpack(x[u][1][q]);
-                P dec;
-                if constexpr (FORM == FORM_GATED) {
-                    dec = O::pack(sigm<T>(f0.x), sigm<T>(f0.y));
-                } else {
-                    const float dx = __fadd_rn(__fmul_rn(sigm<T>(f0.x), p.dt_scale), p.dt_min);
-                    const float dy = __fadd_rn(__fmul_rn(sigm<T>(f0.y), p.dt_scale), p.dt_min);
-                    dec = O::pack(expo<T>(-dx), expo<T>(-dy));
-                }
-                const P gs = O::pack(sigm<T>(f1.x), sigm<T>(f1.y));
-                // rec = decay * rec + (1 - decay) * (bg * u)
-                st[q] = O::add(O::mul(dec, st[q]), O::mul(O::sub(O::one(), dec), O::mul(gs, x[u][2][q])));
-                if constexpr (FORM == FORM_GATED) {
-                    yo[q] = st[q];
-                } else {
-                    const float2 f3 = O::unpack(x[u][3][q]);
-                    const float2 f4 = O::unpack(x[u][4][q]);
-                    const P cgs = O::pack(sigm<T>(f3.x), sigm<T>(f3.y));
-                    const P ogs = O::pack(sigm<T>(f4.x), sigm<T>(f4.y));
-                    yo[q] = O::mul(O::add(O::mul(cgs, st[q]), O::mul(dsk[q], x[u][2][q])), ogs);
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f0 = O::unpack(x[u][0][q]);
+                    const float2 f1 = O::unpack(x[u][1][q]);
+                    P dec;
+                    if constexpr (FORM == FORM_GATED) {
+                        dec = O::pack(sigm<T>(f0.x), sigm<T>(f0.y));
+                    } else {
+                        const float dx = __fadd_rn(__fmul_rn(sigm<T>(f0.x), p.dt_scale), p.dt_min);
+                        const float dy = __fadd_rn(__fmul_rn(sigm<T>(f0.y), p.dt_scale), p.dt_min);
+                        dec = O::pack(expo<T>(-dx), expo<T>(-dy));
+                    }
+                    const P gs = O::pack(sigm<T>(f1.x), sigm<T>(f1.y));
+                    // rec = decay * rec + (1 - decay) * (bg * u)
+                    st[q] = O::add(O::mul(dec, st[q]), O::mul(O::sub(O::one(), dec), O::mul(gs, x[u][2][q])));
+                    if constexpr (FORM == FORM_GATED) {
+                        yo[q] = st[q];
+                    } else {
+                        const float2 f3 = O::unpack(x[u][3][q]);
+                        const float2 f4 = O::unpack(x[u][4][q]);
+                        const P cgs = O::pack(sigm<T>(f3.x), sigm<T>(f3.y));
+                        const P ogs = O::pack(sigm<T>(f4.x), sigm<T>(f4.y));
+                        yo[q] = O::mul(O::add(O::mul(cgs, st[q]), O::mul(dsk[q], x[u][2][q])), ogs);
+                    }
                 }
             }
             Vec8<T>::st(reinterpret_cast<T*>(p.y) + (j0 + u) * p.C + c, yo);
