@@ -363,6 +363,7 @@ struct FeatArgs {
     const void* k;
     int64_t qsb, qst, ksb, kst;
     int32_t qk32;  // q, k are fp32 (else bf16)
+    int32_t pairs; // fp32 q, k with 8-byte aligned rows: each lane loads its two features at once
     const void* mask;
     int32_t mask32;
     int64_t msb, mst;
@@ -377,14 +378,15 @@ struct FeatArgs {
 __device__ __forceinline__ float ld_any(const void* base, int64_t i, bool f32) {
     return f32 ? static_cast<const float*>(base)[i] : __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
 }
-// elu(x) + 1 rounded to bf16: x + 1 above 0, exp(x) = expm1(x) + 1 at or below
-// 0 (one hardware 2^x; its few-ulp fp32 error only moves the bf16 result
-// where the value lies within those ulp of a rounding tie)
-__device__ __forceinline__ float feature(float x) {
+// elu(x) + 1 before its rounding to bf16: x + 1 above 0, exp(x) = expm1(x) + 1
+// at or below 0 (one hardware 2^x; its few-ulp fp32 error only moves the bf16
+// result where the value lies within those ulp of a rounding tie)
+__device__ __forceinline__ float feature_raw(float x) {
     float e;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fminf(x, 0.0f) * 1.4426950408889634f));
-    return __bfloat162float(__float2bfloat16_rn(x > 0.0f ? x + 1.0f : e));
+    return x > 0.0f ? x + 1.0f : e;
 }
+__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 constexpr int kFeatRows = 4;  // rows per warp, their loads in flight together
 
@@ -403,12 +405,23 @@ __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
         while (tu >= T32) tu -= T32, ++bu;  // at most kFeatRows steps
         const int64_t bi = bu, t = tu;
         w[i] = 1.0f;
+        if (a.pairs) {
+            const bool in = row < nrows && 2 * lane < a.r;
+            const float2 qq = in ? *reinterpret_cast<const float2*>(static_cast<const float*>(a.q) + bi * a.qsb +
+                                                                     t * a.qst + 2 * lane)
+                                 : make_float2(0.0f, 0.0f);
+            const float2 kk = in ? *reinterpret_cast<const float2*>(static_cast<const float*>(a.k) + bi * a.ksb +
+                                                                     t * a.kst + 2 * lane)
+                                 : make_float2(0.0f, 0.0f);
+            qv[i][0] = qq.x, qv[i][1] = qq.y, kv[i][0] = kk.x, kv[i][1] = kk.y;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int c = 2 * lane + e;
-            const bool in = row < nrows && c < a.r;
-            qv[i][e] = in ? ld_any(a.q, bi * a.qsb + t * a.qst + c, a.qk32) : 0.0f;
-            kv[i][e] = in ? ld_any(a.k, bi * a.ksb + t * a.kst + c, a.qk32) : 0.0f;
+            for (int e = 0; e < 2; ++e) {
+                const int c = 2 * lane + e;
+                const bool in = row < nrows && c < a.r;
+                qv[i][e] = in ? ld_any(a.q, bi * a.qsb + t * a.qst + c, a.qk32) : 0.0f;
+                kv[i][e] = in ? ld_any(a.k, bi * a.ksb + t * a.kst + c, a.qk32) : 0.0f;
+            }
         }
         if (a.mask != nullptr && row < nrows) w[i] = ld_any(a.mask, bi * a.msb + t * a.mst, a.mask32);
     }
@@ -417,13 +430,13 @@ __global__ void __launch_bounds__(128) assoc_features_kernel(const FeatArgs a) {
         const int64_t row = row0 + i;
         if (row >= nrows) break;
         const float wi = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(w[i])), 0.0f), 1.0f);
-        float qf[2], kf[2];
+        float qf[2], kf[2];  // rounded to bf16 once, by the packing below
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const bool in = 2 * lane + e < a.r;
-            qf[e] = in ? feature(qv[i][e]) : 0.0f;
-            kf[e] = in ? feature(kv[i][e]) : 0.0f;
-            if (a.mask != nullptr) kf[e] = __bfloat162float(__float2bfloat16_rn(kf[e] * wi));
+            qf[e] = in ? feature_raw(qv[i][e]) : 0.0f;
+            kf[e] = in ? feature_raw(kv[i][e]) : 0.0f;
+            if (a.mask != nullptr) kf[e] = rbf(rbf(kf[e]) * wi);
         }
         reinterpret_cast<uint32_t*>(a.qf + row * kRank)[lane] = pack_bf16(qf[0], qf[1]);
         reinterpret_cast<uint32_t*>(a.kf + row * kRank)[lane] = pack_bf16(kf[0], kf[1]);
@@ -646,6 +659,9 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     f.ksb = a->k_stride_b;
     f.kst = a->k_stride_t;
     f.qk32 = a->qk_dtype == NEED_F32;
+    f.pairs = f.qk32 && a->r % 2 == 0 && (reinterpret_cast<uintptr_t>(a->q_raw) & 7u) == 0 &&
+              (reinterpret_cast<uintptr_t>(a->k_raw) & 7u) == 0 && a->q_stride_t % 2 == 0 &&
+              a->k_stride_t % 2 == 0 && a->q_stride_b % 2 == 0 && a->k_stride_b % 2 == 0;
     f.mask = a->write_mask;
     f.mask32 = a->mask_dtype == NEED_F32;
     f.msb = a->mask_stride_b;
