@@ -49,7 +49,8 @@ def parse_args():
     ap.add_argument("--no-side", action="store_true", help="skip the sequence-parallel and decode side runs")
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "assoc"],
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "assoc", "prologue",
+                                               "assoc-step"],
                     default="prefill",
                     help="with --profile: which kernel's workload to run (one GPU)")
     return ap.parse_args()
@@ -416,11 +417,29 @@ def profile_side_case(args, dev, nk, sp, workloads):
     verify + commit graph of 256 sequences x 4 drafted tokens; ``sp-fixup``
     scans the 8 slices of a B=1, T=65536, C=4096 sequence, stacks their
     summaries as the all-gather would and fixes up the last slice; ``ssd-norm``
-    runs the SSD scan with the RMSNorm kernel after it, and ``assoc`` the
-    associative memory (feature map + tensor-core kernel), both at NEED's 350M
-    shape (B=8, T=2048, d_model=832, memory_rank=64, bf16)."""
+    runs the SSD scan with the RMSNorm kernel after it, ``assoc`` the
+    associative memory (feature map + tensor-core kernel) and ``prologue`` the
+    conv + SiLU prologue, all at NEED's 350M shape (B=8, T=2048, d_model=832,
+    memory_rank=64, bf16); ``assoc-step`` runs the memory's decode step for 256
+    sequences."""
     import torch
-    if args.profile_case in ("ssd-norm", "assoc"):
+    if args.profile_case == "prologue":
+        g0 = torch.Generator(device=dev).manual_seed(8)
+        u = torch.randn(8, 2048, 832, device=dev, generator=g0).to(torch.bfloat16)
+        w = (torch.randn(832, 1, 3, device=dev, generator=g0) * 0.5).to(torch.bfloat16)
+        b = (torch.randn(832, device=dev, generator=g0) * 0.1).to(torch.bfloat16)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk.ssd_conv_silu(u, w, b)
+    elif args.profile_case == "assoc-step":
+        g0 = torch.Generator(device=dev).manual_seed(9)
+        Ns, r, d = 256, 64, 832
+        st = torch.zeros(Ns, r, d, device=dev, dtype=torch.bfloat16)
+        dn = torch.zeros(Ns, r, device=dev, dtype=torch.bfloat16)
+        qs, ks = torch.randn(Ns, r, device=dev, generator=g0), torch.randn(Ns, r, device=dev, generator=g0)
+        vs = torch.randn(Ns, d, device=dev, generator=g0).to(torch.bfloat16)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk.assoc_memory_step(qs, ks, vs, st, dn)
+    elif args.profile_case in ("ssd-norm", "assoc"):
         g0 = torch.Generator(device=dev).manual_seed(1)
         Bm, Tm, d = 8, 2048, 832
         xs = [torch.randn(Bm, Tm, d, device=dev, generator=g0).to(torch.bfloat16) for _ in range(5)]
