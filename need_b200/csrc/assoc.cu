@@ -55,11 +55,14 @@ constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q
 constexpr int OFF_BAR = OFF_Z + (5 * kRank + 4 * kTok) * 4;  // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
+constexpr int kMaxSeg = 16;  // segments per sequence
+
 struct AssocParams {
     CUtensorMap tm_q, tm_k, tm_v, tm_out;  // 3-D maps (column, token, sequence), 64 x 128 boxes, 128-byte swizzle
     int32_t T, d;
     float eps;
     uint32_t* hdr;  // workspace header: error word
+    int32_t seg[kMaxSeg + 1];  // segment s owns tiles seg[s] .. seg[s + 1] - 1
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -68,9 +71,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 }
 
 // ------------------------------------------------------------------ main kernel
-// Grid (column blocks, sequences, segments).  Segment s owns tiles [s*tps,
-// (s+1)*tps); its CTA first runs the tiles before them in state-only mode
-// (S^T += V^T K and z, no Q, no outputs) and then its own tiles in full.
+// Grid (column blocks, sequences, segments).  Segment s owns tiles [seg[s],
+// seg[s+1]); its CTA first runs the tiles before them in state-only mode
+// (S^T += V^T K and z, no Q, no outputs), two tiles per load stage in the
+// buffers of Q, P and O that mode leaves idle, and then its own tiles in full.
+// Every CTA adds the tiles' products in the same order, so the outputs do not
+// depend on where the segments start.
 // Two warpgroups.  Warp w reads tensor-memory lanes 32 (w % 4) .. + 31, so row
 // (token, or column of d for the state) `row` = 32 (w % 4) + lane belongs to
 // warps w and w + 4; warpgroup g takes half of each epilogue's columns.
@@ -91,10 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     const int wg = warp >> 2, lw = warp & 3;
     const int row = lw * 32 + lane;
     const int c0 = blockIdx.x * kCols, b = blockIdx.y;
-    const int ntile = (p.T + kTok - 1) / kTok;
-    const int tps = (ntile + static_cast<int>(gridDim.z) - 1) / static_cast<int>(gridDim.z);
-    const int start = static_cast<int>(blockIdx.z) * tps;  // this CTA's first own tile
-    const int end = min(ntile, start + tps);
+    const int start = p.seg[blockIdx.z];  // this CTA's first own tile
+    const int end = p.seg[blockIdx.z + 1];
     if (start >= end) return;  // no tiles (before any allocation or barrier)
     const uint32_t sbase = smem_addr(base);
 
@@ -123,29 +127,54 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     constexpr uint32_t ID_QS = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
     constexpr uint32_t ID_VK = umma::idesc_bf16(128, 64, umma::MN_MAJOR, umma::MN_MAJOR);
 
-    auto issue_load = [&](int tile, int st) {  // state-only tiles need no q
-        const int t0 = tile * kTok;
-        unsigned char* q = base + OFF_Q + st * 16384;
-        unsigned char* k = base + OFF_K + st * 16384;
-        unsigned char* v = base + OFF_V + st * 32768;
-        const bool own = tile >= start;
-        mbar_arrive_expect_tx(&full[st], (own ? 16384u : 0u) + 16384u + 32768u);
-        if (own) umma::tma_load_3d(q, &p.tm_q, 0, t0, b, &full[st]);
-        umma::tma_load_3d(k, &p.tm_k, 0, t0, b, &full[st]);
-        umma::tma_load_3d(v, &p.tm_v, c0, t0, b, &full[st]);
-        umma::tma_load_3d(v + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);  // may lie past d: zero fill
+    // Own tile `it` sits in stage (it - start) & 1.  State-only step j holds
+    // tiles 2j and 2j + 1 in stage j & 1: the first in the stage's K / V slots,
+    // the second in P (K) and O or Q (V).  fpar holds the phase each stage's
+    // barrier completes next; pend (thread 0) the stages with a load in flight.
+    const int nsteps = (start + 1) >> 1;
+    uint32_t fpar = 0, pend = 0;
+    auto own_stage = [&](int it) { return (it - start) & 1; };
+    auto pre_k = [](int st, int h) { return h == 0 ? OFF_K + st * 16384 : OFF_P + st * 16384; };
+    auto pre_v = [](int st, int h) { return h == 0 ? OFF_V + st * 32768 : (st == 0 ? OFF_O : OFF_Q); };
+    auto load_kv = [&](int koff, int voff, int t0, uint64_t* bar) {
+        umma::tma_load_3d(base + koff, &p.tm_k, 0, t0, b, bar);
+        umma::tma_load_3d(base + voff, &p.tm_v, c0, t0, b, bar);
+        umma::tma_load_3d(base + voff + 16384, &p.tm_v, c0 + 64, t0, b, bar);  // may lie past d: zero fill
+    };
+    auto issue_own = [&](int tile) {
+        const int st = own_stage(tile), t0 = tile * kTok;
+        pend |= 1u << st;
+        mbar_arrive_expect_tx(&full[st], 16384u + 16384u + 32768u);
+        umma::tma_load_3d(base + OFF_Q + st * 16384, &p.tm_q, 0, t0, b, &full[st]);
+        load_kv(OFF_K + st * 16384, OFF_V + st * 32768, t0, &full[st]);
+    };
+    auto issue_pre = [&](int j) {
+        const int st = j & 1, n = min(2, start - 2 * j);
+        pend |= 1u << st;
+        mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(n) * (16384u + 32768u));
+        for (int h = 0; h < n; ++h) load_kv(pre_k(st, h), pre_v(st, h), (2 * j + h) * kTok, &full[st]);
     };
     if (tid == 0) {
-        issue_load(0, 0);
-        if (end > 1) issue_load(1, 1);
+        if (start > 0) {
+            issue_pre(0);
+            if (nsteps > 1) issue_pre(1);
+        } else {
+            issue_own(start);
+            if (start + 1 < end) issue_own(start + 1);
+        }
     }
 
     bool ok = true;
     uint32_t pph = 0, oph = 0;  // phases of the P barrier and the O / state barrier
+    auto wait_full = [&](int st) {  // a stage's loads, by every thread
+        const bool got = mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
+        ok &= got;
+        if (got) fpar ^= 1u << st, pend &= ~(1u << st);
+    };
     auto issue_qk = [&](int tile) {  // P = Q K^T of `tile` (its loads waited for here)
-        const int st = tile & 1;
+        const int st = own_stage(tile);
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
-        ok &= mbar_wait_bounded(&full[st], (tile >> 1) & 1, kAssocPolls);
+        ok &= mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);  // thread 0, ahead of wait_full
         umma::fence_after_sync();
 #pragma unroll
         for (int k = 0; k < kRank / 16; ++k)
@@ -187,31 +216,41 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     };
 
     int aborted_at = -1;
-    // ---- state-only tiles before this CTA's segment
-    for (int it = 0; it < start; ++it) {
-        const int st = it & 1;
-        const uint32_t sK = sbase + OFF_K + st * 16384, sV = sbase + OFF_V + st * 32768;
-        ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
+    // ---- state-only tiles before this CTA's segment, two per step
+    for (int j = 0; j < nsteps; ++j) {
+        const int st = j & 1, n = min(2, start - 2 * j);
+        wait_full(st);
         if (tid == 0) {
             umma::fence_after_sync();
+            for (int h = 0; h < n; ++h) {
+                const uint32_t sK = sbase + pre_k(st, h), sV = sbase + pre_v(st, h);
 #pragma unroll
-            for (int k = 0; k < kTok / 16; ++k)
-                umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
-                               umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
+                for (int k = 0; k < kTok / 16; ++k)
+                    umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
+                                   umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, j > 0 || h > 0 || k > 0);
+            }
             umma::mma_commit(obar);
         }
-        add_z(base + OFF_K + st * 16384);
+        add_z(base + pre_k(st, 0));
+        if (n > 1) {
+            named_sync(1, kThreads);  // the first tile's column sums are read
+            add_z(base + pre_k(st, 1));
+        }
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
         umma::fence_after_sync();
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) {
-            aborted_at = it;
+            aborted_at = 2 * j;
             break;
         }
-        if (tid == 0 && it + 2 < end) issue_load(it + 2, st);  // the stage's MMAs and readers are done
+        if (tid == 0 && j + 2 < nsteps) issue_pre(j + 2);  // the stage's MMAs and readers are done
     }
     if (start > 0 && aborted_at < 0) {  // the state entering the segment, for its first Q S
+        if (tid == 0) {  // every buffer of the state-only steps is free now
+            issue_own(start);
+            if (start + 1 < end) issue_own(start + 1);
+        }
         copy_state();
         fence_proxy_async_shared();
         umma::fence_before_sync();
@@ -219,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     }
     if (tid == 0 && aborted_at < 0) issue_qk(start);
     for (int it = start; it < end && aborted_at < 0; ++it) {
-        const int st = it & 1;
+        const int st = own_stage(it);
         const int t0 = it * kTok;
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
         const uint32_t sV = sbase + OFF_V + st * 32768;
@@ -230,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         // q_t . z over the tiles before this one, this warpgroup's half of the
         // features (the tile's loads have landed: thread 0 waited on them before
         // issuing its P)
-        ok &= mbar_wait_bounded(&full[st], (it >> 1) & 1, kAssocPolls);
+        wait_full(st);
         {
             float qz0 = 0.0f, qz1 = 0.0f;
 #pragma unroll
@@ -338,12 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             umma::tma_store_3d(&p.tm_out, base + OFF_O, c0, t0, b);
             if (c0 + 64 < p.d) umma::tma_store_3d(&p.tm_out, base + OFF_O + 16384, c0 + 64, t0, b);
             umma::tma_store_commit();
-            if (it + 2 < end) issue_load(it + 2, st);  // this stage's MMAs and readers are done
+            if (it + 2 < end) issue_own(it + 2);  // this stage's MMAs and readers are done
         }
     }
     // after a give-up, the next tile's P may still be in flight: its commit
     // covers every MMA issued, so wait (bounded) before freeing tensor memory
     if (tid == 0 && aborted_at >= start && aborted_at + 1 < end) mbar_wait_bounded(pbar, pph, kAssocPolls);
+    if (tid == 0 && aborted_at >= 0) {  // loads still in flight land before the CTA exits
+        for (int st = 0; st < 2; ++st)
+            if (pend & (1u << st)) mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
+    }
     if (tid == 0) umma::tma_store_wait_all();
     if (!ok) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
     umma::fence_before_sync();
@@ -604,6 +647,39 @@ int encode_bf16(CUtensorMap* tm, const void* ptr, int64_t width, int64_t T, int6
     return NEED_OK;
 }
 
+#ifndef NEED_ASSOC_PREFIX_COST
+#define NEED_ASSOC_PREFIX_COST 0.25  // a state-only tile, in own tiles (two per load, no Q, no outputs)
+#endif
+#ifndef NEED_ASSOC_SWITCH_COST
+#define NEED_ASSOC_SWITCH_COST 1.0  // the first own tile's load after the state-only tiles
+#endif
+
+// Boundaries of at most `nseg` segments over `ntile` tiles that even out the
+// CTAs' times: a segment starting at tile a with n own tiles costs n, plus
+// a * prefix + switch when a > 0.  The smallest budget whose greedy cover fits
+// is found by bisection; returns the number of segments used.
+int assoc_segments(int ntile, int nseg, int32_t* seg) {
+    const double pre = NEED_ASSOC_PREFIX_COST, sw = NEED_ASSOC_SWITCH_COST;
+    auto cover = [&](double budget, int32_t* out) {
+        int a = 0, s = 0;
+        if (out) out[0] = 0;
+        while (a < ntile && s < nseg) {
+            const double left = budget - (a > 0 ? pre * a + sw : 0.0);
+            const int n = std::max(1, static_cast<int>(left + 1e-9));
+            a = std::min(ntile, a + n);
+            if (out) out[s + 1] = a;
+            ++s;
+        }
+        return a == ntile ? s : -1;
+    };
+    double lo = 0.0, hi = ntile;  // one segment with every tile fits `hi`
+    for (int i = 0; i < 50; ++i) {
+        const double mid = 0.5 * (lo + hi);
+        (cover(mid, nullptr) > 0 ? hi : lo) = mid;
+    }
+    return cover(hi, seg);
+}
+
 size_t assoc_ws(int64_t nb, int64_t T, int64_t d, bool mask) {
     const size_t feat = align128(size_t(nb) * size_t(T) * kRank * 2);
     return WS_HDR_WORDS * 4 + 2 * feat + (mask ? align128(size_t(nb) * size_t(T) * size_t(d) * 2) : 0);
@@ -709,7 +785,8 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
         return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
     const int64_t ncb = (a->d + kCols - 1) / kCols, ntile = (a->T + kTok - 1) / kTok;
-    const int64_t nseg = std::max<int64_t>(1, std::min<int64_t>({ntile, sms / (ncb * a->nb), 16}));
+    const int64_t most = std::max<int64_t>(1, std::min<int64_t>({ntile, sms / (ncb * a->nb), kMaxSeg}));
+    const int nseg = assoc_segments(static_cast<int>(ntile), static_cast<int>(most), P.seg);
     const dim3 grid(static_cast<unsigned>(ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(nseg));
     assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");

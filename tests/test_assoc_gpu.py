@@ -114,6 +114,25 @@ def test_repeat_calls_are_identical(cuda):
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("T", [2048, 1700])
+def test_segments_do_not_change_the_result(cuda, T):
+    """Alone, a sequence of 16 (14) tiles is cut into one-tile segments whose
+    CTAs first run every tile before them state-only (odd and even counts, a
+    last step of one tile); copied 12 and 36 times it gets 6 and 2 segments.
+    Every CTA adds the tiles' products in the same order: the copies match the
+    single sequence bit for bit."""
+    gen = torch.Generator().manual_seed(T)
+    q, k = torch.randn(1, T, 64, generator=gen).to(cuda), torch.randn(1, T, 64, generator=gen).to(cuda)
+    v = torch.randn(1, T, 256, generator=gen).to(torch.bfloat16).to(cuda)
+    one = nk.linear_associative_memory(q, k, v)
+    for copies in (12, 36):
+        many = nk.linear_associative_memory(q.repeat(copies, 1, 1), k.repeat(copies, 1, 1), v.repeat(copies, 1, 1))
+        assert torch.equal(many, one.expand_as(many)), copies
+    ex = host(exact(q, k, v))
+    assert rel(host(one), ex) <= 1e-2 and rel_l2(host(one), ex) <= 5e-3
+    no_device_error()
+
+
 def test_rejects_what_it_does_not_take(cuda):
     q = torch.randn(1, 8, 80, device=cuda)
     v = torch.randn(1, 8, 64, device=cuda).to(torch.bfloat16)
