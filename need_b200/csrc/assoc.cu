@@ -55,15 +55,41 @@ constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q
 constexpr int OFF_BAR = OFF_Z + (5 * kRank + 4 * kTok) * 4;  // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
-constexpr int kMaxSeg = 16;  // segments per sequence
+constexpr int kMaxSeg = 16;    // segments per sequence
+constexpr int kMaxChunk = 64;  // state chunks per sequence
+constexpr int kScanAbove = 4;  // more chunks than this: prefix-summed by a kernel of their own
 
 struct AssocParams {
     CUtensorMap tm_q, tm_k, tm_v, tm_out;  // 3-D maps (column, token, sequence), 64 x 128 boxes, 128-byte swizzle
     int32_t T, d;
     float eps;
     uint32_t* hdr;  // workspace header: error word
-    int32_t seg[kMaxSeg + 1];  // segment s owns tiles seg[s] .. seg[s + 1] - 1
+    float* cs;      // chunk states [chunk][sequence][column block][128 columns][64 features] fp32
+    float* cz;      // chunk feature sums [chunk][sequence][64] fp32
+    int32_t nb, ncb;
+    int32_t kchunk;   // chunks per segment before the last
+    int32_t scanned;  // cs / cz hold running sums over the chunks (else each chunk's own)
+    int32_t recompute;  // a later segment sums the tiles before it itself (no chunk states)
+    int32_t seg[kMaxSeg + 1];      // segment s owns tiles seg[s] .. seg[s + 1] - 1
+    int32_t chunk[kMaxChunk + 1];  // chunk c sums tiles chunk[c] .. chunk[c + 1] - 1
 };
+
+// z += column sums of a tile's k (bf16 [128 tokens][64 features], 128-byte
+// swizzle): threads c, c + 64, c + 128, c + 192 each sum a quarter of the rows
+// of feature c, thread c adds them to z[c] (call after every thread has read z)
+__device__ __forceinline__ void add_z(const unsigned char* krow, float* z, float* zpart, int tid) {
+    const int c = tid & 63, r0 = (tid >> 6) * 32;
+    const int j = c >> 3, e = c & 7;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+    for (int r = 0; r < 32; ++r) {
+        const uint16_t hv = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
+        a[r & 3] += __uint_as_float(static_cast<uint32_t>(hv) << 16);
+    }
+    zpart[(tid >> 6) * kRank + c] = (a[0] + a[1]) + (a[2] + a[3]);
+    named_sync(1, 256);
+    if (tid < kRank) z[c] += (zpart[c] + zpart[kRank + c]) + (zpart[2 * kRank + c] + zpart[3 * kRank + c]);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
@@ -72,11 +98,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 // ------------------------------------------------------------------ main kernel
 // Grid (column blocks, sequences, segments).  Segment s owns tiles [seg[s],
-// seg[s+1]); its CTA first runs the tiles before them in state-only mode
-// (S^T += V^T K and z, no Q, no outputs), two tiles per load stage in the
-// buffers of Q, P and O that mode leaves idle, and then its own tiles in full.
-// Every CTA adds the tiles' products in the same order, so the outputs do not
-// depend on where the segments start.
+// seg[s+1]).  A later segment starts from the state of the tiles before it:
+// the sum, in chunk order, of the chunk states that assoc_state_kernel left in
+// the workspace (or the running sum at its last chunk, after the chunk scan).
 // Two warpgroups.  Warp w reads tensor-memory lanes 32 (w % 4) .. + 31, so row
 // (token, or column of d for the state) `row` = 32 (w % 4) + lane belongs to
 // warps w and w + 4; warpgroup g takes half of each epilogue's columns.
@@ -127,35 +151,39 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     constexpr uint32_t ID_QS = umma::idesc_bf16(128, 128, umma::K_MAJOR, umma::K_MAJOR);
     constexpr uint32_t ID_VK = umma::idesc_bf16(128, 64, umma::MN_MAJOR, umma::MN_MAJOR);
 
-    // Own tile `it` sits in stage (it - start) & 1.  State-only step j holds
-    // tiles 2j and 2j + 1 in stage j & 1: the first in the stage's K / V slots,
-    // the second in P (K) and O or Q (V).  fpar holds the phase each stage's
-    // barrier completes next; pend (thread 0) the stages with a load in flight.
-    const int nsteps = (start + 1) >> 1;
+    // Own tile `it` sits in stage (it - start) & 1.  fpar holds the phase each
+    // stage's barrier completes next; pend (thread 0) the stages with a load in flight.
     uint32_t fpar = 0, pend = 0;
     auto own_stage = [&](int it) { return (it - start) & 1; };
-    auto pre_k = [](int st, int h) { return h == 0 ? OFF_K + st * 16384 : OFF_P + st * 16384; };
-    auto pre_v = [](int st, int h) { return h == 0 ? OFF_V + st * 32768 : (st == 0 ? OFF_O : OFF_Q); };
-    auto load_kv = [&](int koff, int voff, int t0, uint64_t* bar) {
-        umma::tma_load_3d(base + koff, &p.tm_k, 0, t0, b, bar);
-        umma::tma_load_3d(base + voff, &p.tm_v, c0, t0, b, bar);
-        umma::tma_load_3d(base + voff + 16384, &p.tm_v, c0 + 64, t0, b, bar);  // may lie past d: zero fill
-    };
     auto issue_own = [&](int tile) {
         const int st = own_stage(tile), t0 = tile * kTok;
         pend |= 1u << st;
         mbar_arrive_expect_tx(&full[st], 16384u + 16384u + 32768u);
         umma::tma_load_3d(base + OFF_Q + st * 16384, &p.tm_q, 0, t0, b, &full[st]);
-        load_kv(OFF_K + st * 16384, OFF_V + st * 32768, t0, &full[st]);
+        umma::tma_load_3d(base + OFF_K + st * 16384, &p.tm_k, 0, t0, b, &full[st]);
+        umma::tma_load_3d(base + OFF_V + st * 32768, &p.tm_v, c0, t0, b, &full[st]);
+        umma::tma_load_3d(base + OFF_V + st * 32768 + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);  // may lie past d
     };
+    // With p.recompute a later segment first runs the tiles before it
+    // state-only, two per step: step j holds tiles 2j and 2j + 1 in stage j & 1,
+    // the first in the stage's K / V slots, the second in P (K) and O or Q (V),
+    // buffers that this mode leaves idle.
+    const int nsteps = p.recompute ? (start + 1) >> 1 : 0;
+    auto pre_k = [](int st, int h) { return h == 0 ? OFF_K + st * 16384 : OFF_P + st * 16384; };
+    auto pre_v = [](int st, int h) { return h == 0 ? OFF_V + st * 32768 : (st == 0 ? OFF_O : OFF_Q); };
     auto issue_pre = [&](int j) {
         const int st = j & 1, n = min(2, start - 2 * j);
         pend |= 1u << st;
         mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(n) * (16384u + 32768u));
-        for (int h = 0; h < n; ++h) load_kv(pre_k(st, h), pre_v(st, h), (2 * j + h) * kTok, &full[st]);
+        for (int h = 0; h < n; ++h) {
+            const int t0 = (2 * j + h) * kTok;
+            umma::tma_load_3d(base + pre_k(st, h), &p.tm_k, 0, t0, b, &full[st]);
+            umma::tma_load_3d(base + pre_v(st, h), &p.tm_v, c0, t0, b, &full[st]);
+            umma::tma_load_3d(base + pre_v(st, h) + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);
+        }
     };
     if (tid == 0) {
-        if (start > 0) {
+        if (nsteps > 0) {
             issue_pre(0);
             if (nsteps > 1) issue_pre(1);
         } else {
@@ -171,10 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         ok &= got;
         if (got) fpar ^= 1u << st, pend &= ~(1u << st);
     };
-    auto issue_qk = [&](int tile) {  // P = Q K^T of `tile` (its loads waited for here)
+    bool qk_ahead = false;  // thread 0: the next tile's P is issued already
+    auto issue_qk = [&](int tile) {  // P = Q K^T of `tile`, whose loads have landed
         const int st = own_stage(tile);
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
-        ok &= mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);  // thread 0, ahead of wait_full
         umma::fence_after_sync();
 #pragma unroll
         for (int k = 0; k < kRank / 16; ++k)
@@ -187,21 +215,6 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         for (int q4 = 0; q4 < 4; ++q4)
             *reinterpret_cast<uint4*>(dst + umma::sw128(r, j0 + q4)) =
                 make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-    };
-    // z += column sums of a tile's k: threads c, c + 64, c + 128, c + 192 each
-    // sum a quarter of the rows of feature c (call after every thread has read z)
-    auto add_z = [&](const unsigned char* krow) {
-        const int c = tid & 63, r0 = (tid >> 6) * 32;
-        const int j = c >> 3, e = c & 7;
-        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-        for (int r = 0; r < 32; ++r) {
-            const uint16_t hv = *reinterpret_cast<const uint16_t*>(krow + umma::sw128(r0 + r, j) + 2 * e);
-            a[r & 3] += __uint_as_float(static_cast<uint32_t>(hv) << 16);
-        }
-        zpart[(tid >> 6) * kRank + c] = (a[0] + a[1]) + (a[2] + a[3]);
-        named_sync(1, kThreads);
-        if (tid < kRank) z[c] += (zpart[c] + zpart[kRank + c]) + (zpart[2 * kRank + c] + zpart[3 * kRank + c]);
     };
     // the bf16 copy of the state in TMEM, as the K-major B of the next Q S (row =
     // column of d; this warpgroup's 32 features)
@@ -231,10 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             }
             umma::mma_commit(obar);
         }
-        add_z(base + pre_k(st, 0));
+        add_z(base + pre_k(st, 0), z, zpart, tid);
         if (n > 1) {
             named_sync(1, kThreads);  // the first tile's column sums are read
-            add_z(base + pre_k(st, 1));
+            add_z(base + pre_k(st, 1), z, zpart, tid);
         }
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
@@ -246,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         }
         if (tid == 0 && j + 2 < nsteps) issue_pre(j + 2);  // the stage's MMAs and readers are done
     }
-    if (start > 0 && aborted_at < 0) {  // the state entering the segment, for its first Q S
+    if (nsteps > 0 && aborted_at < 0) {  // the state entering the segment, for its first Q S
         if (tid == 0) {  // every buffer of the state-only steps is free now
             issue_own(start);
             if (start + 1 < end) issue_own(start + 1);
@@ -256,7 +269,36 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         umma::fence_before_sync();
         __syncthreads();
     }
-    if (tid == 0 && aborted_at < 0) issue_qk(start);
+    if (start > 0 && !p.recompute) {  // the state entering the segment: chunk sums in chunk order
+        const int chi = static_cast<int>(blockIdx.z) * p.kchunk, clo = p.scanned ? chi - 1 : 0;
+        float acc[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
+        for (int c = clo; c < chi; ++c) {
+            const float4* src = reinterpret_cast<const float4*>(
+                p.cs + ((static_cast<size_t>(c) * p.nb + b) * p.ncb + blockIdx.x) * (kCols * kRank) + row * kRank +
+                32 * wg);
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+                const float4 f = src[q4];
+                acc[4 * q4] += f.x, acc[4 * q4 + 1] += f.y, acc[4 * q4 + 2] += f.z, acc[4 * q4 + 3] += f.w;
+            }
+        }
+        umma::tmem_st32(tS + 32 * wg, acc);
+        if (tid < kRank) {
+            float zz = 0.0f;
+            for (int c = clo; c < chi; ++c) zz += p.cz[(static_cast<size_t>(c) * p.nb + b) * kRank + tid];
+            z[tid] = zz;
+        }
+        umma::tmem_wait_st();
+        umma::fence_before_sync();
+        __syncthreads();
+        umma::fence_after_sync();
+        copy_state();
+        fence_proxy_async_shared();
+        umma::fence_before_sync();
+        __syncthreads();
+    }
     for (int it = start; it < end && aborted_at < 0; ++it) {
         const int st = own_stage(it);
         const int t0 = it * kTok;
@@ -270,6 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         // features (the tile's loads have landed: thread 0 waited on them before
         // issuing its P)
         wait_full(st);
+        if (tid == 0 && !qk_ahead) issue_qk(it);
+        qk_ahead = false;
         {
             float qz0 = 0.0f, qz1 = 0.0f;
 #pragma unroll
@@ -339,14 +383,24 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
                 umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
                                umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
             umma::mma_commit(obar);
-            // P of the next tile overlaps this tile's output epilogue (its TMEM
-            // columns were read out above)
-            if (it + 1 < end) issue_qk(it + 1);
         }
-        add_z(krow);
+        add_z(krow, z, zpart, tid);
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
         umma::fence_after_sync();
+        if (tid == 0) {
+            // every reader of this stage is done (the MMAs by the barrier, q.z
+            // and the column sums by the block barriers before it): refill it
+            // now, a whole output epilogue ahead of the end of the tile
+            if (it + 2 < end) issue_own(it + 2);
+            // the next tile's P overlaps this tile's output epilogue (its TMEM
+            // columns were read out above) when its loads are in already
+            const int nx = own_stage(it + 1);
+            if (it + 1 < end && mbar_test_wait(&full[nx], (fpar >> nx) & 1u)) {
+                issue_qk(it + 1);
+                qk_ahead = true;
+            }
+        }
 
         // ---- outputs: O / max(q.z + rowsum, eps) in bf16, this warpgroup's 64
         // columns (one TMA store box), staged for the store
@@ -377,12 +431,11 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             umma::tma_store_3d(&p.tm_out, base + OFF_O, c0, t0, b);
             if (c0 + 64 < p.d) umma::tma_store_3d(&p.tm_out, base + OFF_O + 16384, c0 + 64, t0, b);
             umma::tma_store_commit();
-            if (it + 2 < end) issue_own(it + 2);  // this stage's MMAs and readers are done
         }
     }
     // after a give-up, the next tile's P may still be in flight: its commit
     // covers every MMA issued, so wait (bounded) before freeing tensor memory
-    if (tid == 0 && aborted_at >= start && aborted_at + 1 < end) mbar_wait_bounded(pbar, pph, kAssocPolls);
+    if (tid == 0 && aborted_at >= 0 && qk_ahead) mbar_wait_bounded(pbar, pph, kAssocPolls);
     if (tid == 0 && aborted_at >= 0) {  // loads still in flight land before the CTA exits
         for (int st = 0; st < 2; ++st)
             if (pend & (1u << st)) mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
@@ -394,6 +447,139 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     if (warp == 0) {
         umma::fence_after_sync();
         umma::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ chunk states
+// Grid (column blocks, sequences, chunks).  A CTA sums its chunk's tiles:
+// S^T = sum V^T K on the tensor cores (fp32 in tensor memory) and z = sum k;
+// it writes them to cs / cz (z from column block 0 only: every block computes
+// the same).  A ring of four K / V stages keeps three tiles' loads in flight
+// while one is summed.
+constexpr int kRing = 4;
+constexpr int CS_OFF_K = 0;                         // 4 x [128 tokens][64 features] bf16
+constexpr int CS_OFF_V = CS_OFF_K + kRing * 16384;  // 4 x 2 boxes x [128 tokens][64 columns]
+constexpr int CS_OFF_Z = CS_OFF_V + kRing * 32768;  // z [64], column sums [4][64] (fp32)
+constexpr int CS_OFF_BAR = CS_OFF_Z + 5 * kRank * 4;  // full[4], done, tmem base
+constexpr int CS_SMEM_BYTES = CS_OFF_BAR + 64 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1) assoc_state_kernel(const __grid_constant__ AssocParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* z = reinterpret_cast<float*>(base + CS_OFF_Z);
+    float* zpart = z + kRank;
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + CS_OFF_BAR);
+    uint64_t* done = full + kRing;  // the tile's MMAs have read its stage
+    uint32_t* tbase = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wg = warp >> 2, row = (warp & 3) * 32 + lane;
+    const int cb = blockIdx.x, c0 = cb * kCols, b = blockIdx.y, chunk = blockIdx.z;
+    const int t_lo = p.chunk[chunk], n = p.chunk[chunk + 1] - t_lo;
+    if (n <= 0) return;
+    const bool zsum = cb == 0;
+    const uint32_t sbase = smem_addr(base);
+
+    if (tid == 0) {
+        for (int i = 0; i < kRing; ++i) mbar_init(&full[i], 1);
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (tid < kRank) z[tid] = 0.0f;
+    if (warp == 0) {
+        umma::tmem_alloc(tbase, 64);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = *tbase;
+    const uint32_t tS = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    constexpr uint32_t ID_VK = umma::idesc_bf16(128, 64, umma::MN_MAJOR, umma::MN_MAJOR);
+
+    uint32_t fpar = 0, pend = 0;  // per stage: the phase completing next; a load in flight (thread 0)
+    auto issue = [&](int i) {
+        const int st = i % kRing, t0 = (t_lo + i) * kTok;
+        pend |= 1u << st;
+        mbar_arrive_expect_tx(&full[st], 16384u + 32768u);
+        umma::tma_load_3d(base + CS_OFF_K + st * 16384, &p.tm_k, 0, t0, b, &full[st]);
+        umma::tma_load_3d(base + CS_OFF_V + st * 32768, &p.tm_v, c0, t0, b, &full[st]);
+        umma::tma_load_3d(base + CS_OFF_V + st * 32768 + 16384, &p.tm_v, c0 + 64, t0, b, &full[st]);
+    };
+    if (tid == 0)
+        for (int i = 0; i < min(kRing, n); ++i) issue(i);
+
+    bool ok = true;
+    uint32_t dph = 0;
+    int i = 0;
+    for (; i < n; ++i) {
+        const int st = i % kRing;
+        const bool got = mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
+        ok &= got;
+        if (got) fpar ^= 1u << st, pend &= ~(1u << st);
+        if (tid == 0) {
+            umma::fence_after_sync();
+            const uint32_t sK = sbase + CS_OFF_K + st * 16384, sV = sbase + CS_OFF_V + st * 32768;
+#pragma unroll
+            for (int k = 0; k < kTok / 16; ++k)
+                umma::mma_bf16(tmem, umma::smem_desc(sV + 2048 * k, 16384, 1024),
+                               umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, i > 0 || k > 0);
+            umma::mma_commit(done);
+        }
+        if (zsum) add_z(base + CS_OFF_K + st * 16384, z, zpart, tid);
+        ok &= mbar_wait_bounded(done, dph, kAssocPolls);
+        dph ^= 1u;
+        umma::fence_after_sync();
+        umma::fence_before_sync();
+        if (!__syncthreads_and(ok)) break;
+        if (tid == 0 && i + kRing < n) issue(i + kRing);  // the stage's MMAs and readers are done
+    }
+    if (i == n) {
+        float v[32];
+        umma::tmem_ld32(tS + 32 * wg, v);
+        umma::tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(
+            p.cs + ((static_cast<size_t>(chunk) * p.nb + b) * p.ncb + cb) * (kCols * kRank) + row * kRank + 32 * wg);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) dst[q4] = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        if (zsum && tid < kRank) p.cz[(static_cast<size_t>(chunk) * p.nb + b) * kRank + tid] = z[tid];
+    } else if (tid == 0) {  // a wait gave up: loads still in flight land before the CTA exits
+        for (int st = 0; st < kRing; ++st)
+            if (pend & (1u << st)) mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
+        atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        umma::fence_after_sync();
+        umma::tmem_dealloc(tmem, 64);
+    }
+}
+
+// Running sums over the chunks, in place and in chunk order: cs[c] := cs[0] +
+// ... + cs[c], the same for cz.  Thread i owns one float4 of every chunk; its
+// loads go out eight chunks at a time.
+__global__ void __launch_bounds__(256) assoc_chunk_scan_kernel(float* __restrict__ cs, float* __restrict__ cz,
+                                                               int64_t cs4, int64_t cz4, int nchunk) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    float4* col;
+    int64_t stride;
+    if (i < cs4) col = reinterpret_cast<float4*>(cs) + i, stride = cs4;
+    else if (i < cs4 + cz4) col = reinterpret_cast<float4*>(cz) + (i - cs4), stride = cz4;
+    else return;
+    float4 acc = col[0];
+    for (int c0 = 1; c0 < nchunk; c0 += 8) {
+        float4 f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (c0 + j < nchunk) f[j] = __ldcg(col + (c0 + j) * stride);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (c0 + j < nchunk) {
+                acc.x += f[j].x, acc.y += f[j].y, acc.z += f[j].z, acc.w += f[j].w;
+                col[(c0 + j) * stride] = acc;
+            }
     }
 }
 
@@ -655,9 +841,10 @@ int encode_bf16(CUtensorMap* tm, const void* ptr, int64_t width, int64_t T, int6
 #endif
 
 // Boundaries of at most `nseg` segments over `ntile` tiles that even out the
-// CTAs' times: a segment starting at tile a with n own tiles costs n, plus
-// a * prefix + switch when a > 0.  The smallest budget whose greedy cover fits
-// is found by bisection; returns the number of segments used.
+// CTAs' times when later segments run the tiles before them state-only: a
+// segment starting at tile a with n own tiles costs n, plus a * prefix +
+// switch when a > 0.  The smallest budget whose greedy cover fits is found by
+// bisection; returns the number of segments used.
 int assoc_segments(int ntile, int nseg, int32_t* seg) {
     const double pre = NEED_ASSOC_PREFIX_COST, sw = NEED_ASSOC_SWITCH_COST;
     auto cover = [&](double budget, int32_t* out) {
@@ -680,9 +867,68 @@ int assoc_segments(int ntile, int nseg, int32_t* seg) {
     return cover(hi, seg);
 }
 
-size_t assoc_ws(int64_t nb, int64_t T, int64_t d, bool mask) {
-    const size_t feat = align128(size_t(nb) * size_t(T) * kRank * 2);
-    return WS_HDR_WORDS * 4 + 2 * feat + (mask ? align128(size_t(nb) * size_t(T) * size_t(d) * 2) : 0);
+// How a launch splits the sequences into `nseg` segments per sequence (the
+// CTAs of all segments fill the SMs once).  Two segments: the second re-sums
+// the first's tiles state-only (cheaper than a launch of its own), at
+// boundaries that balance the two.  More: equal segments, and the tiles before
+// the last segment in `nchunk` chunks, `kchunk` per segment, whose states the
+// chunk kernel sums first on as many SMs again.
+struct AssocPlan {
+    int nseg = 1, kchunk = 0, nchunk = 0, recompute = 0;
+    int32_t seg[kMaxSeg + 1] = {};
+    int32_t chunk[kMaxChunk + 1] = {};
+};
+
+int device_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;
+    }
+    return sms;
+}
+
+AssocPlan assoc_plan(int64_t nb, int64_t T, int64_t d, int sms) {
+    AssocPlan pl;
+    const int64_t ncb = (d + kCols - 1) / kCols, ntile = (T + kTok - 1) / kTok, per = ncb * nb;
+    pl.nseg = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({ntile, sms / per, kMaxSeg})));
+    if (pl.nseg <= 2) {
+        pl.recompute = pl.nseg > 1;
+        pl.nseg = assoc_segments(static_cast<int>(ntile), pl.nseg, pl.seg);
+        return pl;
+    }
+    for (int s = 0; s <= pl.nseg; ++s) pl.seg[s] = static_cast<int32_t>(s * ntile / pl.nseg);
+    if (pl.nseg > 1) {
+        const int64_t shortest = ntile / pl.nseg;  // >= 1 tile
+        pl.kchunk = static_cast<int>(std::max<int64_t>(
+            1, std::min<int64_t>({sms / (per * (pl.nseg - 1)), shortest, kMaxChunk / (pl.nseg - 1)})));
+        pl.nchunk = (pl.nseg - 1) * pl.kchunk;
+        for (int s = 0; s + 1 < pl.nseg; ++s) {
+            const int len = pl.seg[s + 1] - pl.seg[s];
+            for (int j = 0; j < pl.kchunk; ++j) pl.chunk[s * pl.kchunk + j] = pl.seg[s] + j * len / pl.kchunk;
+        }
+        pl.chunk[pl.nchunk] = pl.seg[pl.nseg - 1];
+    }
+    return pl;
+}
+
+// workspace: header | q features | k features | masked v | chunk states | chunk z
+struct AssocLayout {
+    size_t feat, vm, cs, cz, total;
+};
+AssocLayout assoc_layout(int64_t nb, int64_t T, int64_t d, bool mask, const AssocPlan& pl) {
+    AssocLayout l;
+    const int64_t ncb = (d + kCols - 1) / kCols;
+    l.feat = align128(size_t(nb) * size_t(T) * kRank * 2);
+    l.vm = mask ? align128(size_t(nb) * size_t(T) * size_t(d) * 2) : 0;
+    l.cs = align128(size_t(pl.nchunk) * size_t(nb) * size_t(ncb) * kCols * kRank * 4);
+    l.cz = align128(size_t(pl.nchunk) * size_t(nb) * kRank * 4);
+    l.total = WS_HDR_WORDS * 4 + 2 * l.feat + l.vm + l.cs + l.cz;
+    return l;
+}
+
+AssocPlan plan_for(int64_t nb, int64_t T, int64_t d) {
+    return assoc_plan(nb, T, d, T > kTok ? device_sms() : 1);  // one tile: one segment, no device query
 }
 
 }  // namespace
@@ -690,8 +936,8 @@ size_t assoc_ws(int64_t nb, int64_t T, int64_t d, bool mask) {
 extern "C" {
 
 size_t need_assoc_memory_workspace_size(int64_t nb, int64_t T, int64_t d, int32_t has_mask) {
-    if (nb < 1 || T < 1 || d < 1) return WS_HDR_WORDS * 4;
-    return assoc_ws(nb, T, d, has_mask != 0);
+    if (nb < 1 || T < 1 || d < 1 || T > INT32_MAX / 2 || d > INT32_MAX / 2) return WS_HDR_WORDS * 4;
+    return assoc_layout(nb, T, d, has_mask != 0, plan_for(nb, T, d)).total;
 }
 
 int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
@@ -714,18 +960,21 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     if (a->eps < 0.0) return fail(NEED_ERR_INVALID, "eps must be >= 0");
     if (a->workspace == nullptr || !aligned16(a->workspace))
         return fail(NEED_ERR_WORKSPACE, "workspace is null or not 16-byte aligned");
-    const size_t need = assoc_ws(a->nb, a->T, a->d, mask);
-    if (a->workspace_bytes < need)
-        return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, need);
+    const AssocPlan pl = plan_for(a->nb, a->T, a->d);
+    const AssocLayout lay = assoc_layout(a->nb, a->T, a->d, mask, pl);
+    if (a->workspace_bytes < lay.total)
+        return fail(NEED_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", a->workspace_bytes, lay.total);
     if (!aligned16(a->v)) return fail(NEED_ERR_UNSUPPORTED, "v is not 16-byte aligned");
     if ((a->v_stride_t % 8) != 0 || (a->nb > 1 && (a->v_stride_b % 8) != 0))
         return fail(NEED_ERR_UNSUPPORTED, "v strides must be multiples of 8 elements");
 
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
-    const size_t feat = align128(size_t(a->nb) * size_t(a->T) * kRank * 2);
-    __nv_bfloat16* qf = reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4);
-    __nv_bfloat16* kf = reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4 + feat);
-    __nv_bfloat16* vm = mask ? reinterpret_cast<__nv_bfloat16*>(ws + WS_HDR_WORDS * 4 + 2 * feat) : nullptr;
+    unsigned char* wp = ws + WS_HDR_WORDS * 4;
+    __nv_bfloat16* qf = reinterpret_cast<__nv_bfloat16*>(wp);
+    __nv_bfloat16* kf = reinterpret_cast<__nv_bfloat16*>(wp + lay.feat);
+    __nv_bfloat16* vm = mask ? reinterpret_cast<__nv_bfloat16*>(wp + 2 * lay.feat) : nullptr;
+    float* cs = reinterpret_cast<float*>(wp + 2 * lay.feat + lay.vm);
+    float* cz = reinterpret_cast<float*>(wp + 2 * lay.feat + lay.vm + lay.cs);
 
     FeatArgs f{};
     f.q = a->q_raw;
@@ -768,6 +1017,15 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     P.d = int32_t(a->d);
     P.eps = static_cast<float>(a->eps);
     P.hdr = reinterpret_cast<uint32_t*>(ws);
+    P.cs = cs;
+    P.cz = cz;
+    P.nb = static_cast<int32_t>(a->nb);
+    P.ncb = static_cast<int32_t>((a->d + kCols - 1) / kCols);
+    P.kchunk = pl.kchunk;
+    P.scanned = pl.nchunk > kScanAbove ? 1 : 0;
+    P.recompute = pl.recompute;
+    std::copy(pl.seg, pl.seg + kMaxSeg + 1, P.seg);
+    std::copy(pl.chunk, pl.chunk + kMaxChunk + 1, P.chunk);
 
     const int64_t rows = a->nb * a->T;
     const int64_t fblocks = (rows + 4 * kFeatRows - 1) / (4 * kFeatRows);
@@ -775,19 +1033,24 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
     assoc_features_kernel<<<static_cast<unsigned>(fblocks), 128, 0, stream>>>(f);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "assoc_features_kernel launch");
-    static std::atomic<uint64_t> smem_done{0};
+    static std::atomic<uint64_t> smem_done{0}, cs_smem_done{0};
     if ((e = ensure_smem(assoc_kernel, SMEM_BYTES, smem_done)) != cudaSuccess)
         return cuda_fail(e, "cudaFuncSetAttribute(assoc_kernel)");
-    // Sequences split into segments so that the CTAs fill the GPU's SMs (one
-    // CTA per SM); each later segment first sums the state of the tiles before it.
-    int dev = 0, sms = 148;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
-    const int64_t ncb = (a->d + kCols - 1) / kCols, ntile = (a->T + kTok - 1) / kTok;
-    const int64_t most = std::max<int64_t>(1, std::min<int64_t>({ntile, sms / (ncb * a->nb), kMaxSeg}));
-    const int nseg = assoc_segments(static_cast<int>(ntile), static_cast<int>(most), P.seg);
-    const dim3 grid(static_cast<unsigned>(ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(nseg));
+    const dim3 grid(static_cast<unsigned>(P.ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(pl.nseg));
+    if (pl.nchunk > 0) {  // the states entering the later segments
+        if ((e = ensure_smem(assoc_state_kernel, CS_SMEM_BYTES, cs_smem_done)) != cudaSuccess)
+            return cuda_fail(e, "cudaFuncSetAttribute(assoc_state_kernel)");
+        const dim3 cgrid(static_cast<unsigned>(P.ncb), static_cast<unsigned>(a->nb), static_cast<unsigned>(pl.nchunk));
+        assoc_state_kernel<<<cgrid, kThreads, CS_SMEM_BYTES, stream>>>(P);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_state_kernel launch");
+        if (P.scanned) {
+            const int64_t cs4 = int64_t(a->nb) * P.ncb * kCols * kRank / 4, cz4 = int64_t(a->nb) * kRank / 4;
+            const int64_t threads = cs4 + cz4;
+            assoc_chunk_scan_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(cs, cz, cs4, cz4,
+                                                                                                    pl.nchunk);
+            if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_chunk_scan_kernel launch");
+        }
+    }
     assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");
     return ok();
