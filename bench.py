@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
     ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "assoc", "prologue",
-                                               "assoc-step"],
+                                               "assoc-step", "assoc-long"],
                     default="prefill",
                     help="with --profile: which kernel's workload to run (one GPU)")
     return ap.parse_args()
@@ -454,6 +454,16 @@ def profile_side_case(args, dev, nk, sp, workloads):
         torch.cuda.synchronize()
         if nk.workspace_error() != 0:
             raise RuntimeError("a device-side wait gave up")
+    elif args.profile_case == "assoc-long":  # one T=16384 sequence: chunk states, their scan, 16 segments
+        g0 = torch.Generator(device=dev).manual_seed(1)
+        q = torch.randn(1, 16384, 64, device=dev, generator=g0)
+        k = torch.randn(1, 16384, 64, device=dev, generator=g0)
+        v = torch.randn(1, 16384, 832, device=dev, generator=g0).to(torch.bfloat16)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk.linear_associative_memory(q, k, v)
+        torch.cuda.synchronize()
+        if nk.workspace_error() != 0:
+            raise RuntimeError("a device-side wait gave up")
     elif args.profile_case == "decode":
         w = workloads.verify(dev, N=256, C=1024, k=4, seed=11)
         pool = w.states.clone()
@@ -653,6 +663,12 @@ def run_assoc(dev, nk, barrier, max_over_ranks):
     vs = torch.randn(Ns, d, device=dev, generator=g0).to(torch.bfloat16)
     step_us = timed(graphed(lambda: nk.assoc_memory_step(qs, ks, vs, st, dn)), 100)
     step_bytes = Ns * (2 * r * d * 2 + 2 * r * 2 + 2 * d * 2 + 2 * r * 4)  # state, denom r/w; v, out; q, k
+    # one long sequence: its segments start from chunk states summed once
+    Tl = 16384
+    ql, kl = torch.randn(1, Tl, r, device=dev, generator=g0), torch.randn(1, Tl, r, device=dev, generator=g0)
+    vl = torch.randn(1, Tl, d, device=dev, generator=g0).to(torch.bfloat16)
+    long_us = timed(graphed(lambda: nk.linear_associative_memory(ql, kl, vl)), 30)
+    long_bytes = 2 * Tl * r * 4 + 2 * Tl * d * 2
     nbytes = 2 * Bm * Tm * r * 4 + 2 * Bm * Tm * d * 2  # q, k (fp32) and v in, out
     tiles = Bm * -(-Tm // 128) * -(-d // 128)
     flops = tiles * 2 * 128 * (128 * 64 + 128 * 128 + 64 * 128 + 128 * 64)  # QK^T, PV, QS, V^T K per tile
@@ -660,7 +676,9 @@ def run_assoc(dev, nk, barrier, max_over_ranks):
             "kernels_us": kern_us, "hbm_gbs": nbytes / (kern_us / 1e6) / 1e9,
             "tensor_tflops": flops / (kern_us / 1e6) / 1e12, "torch_ops_us": torch_us,
             "decode_step": {"workload": "one token for 256 sequences, state 64 x 832 bf16 each",
-                            "us": step_us, "hbm_gbs": step_bytes / (step_us / 1e6) / 1e9}}
+                            "us": step_us, "hbm_gbs": step_bytes / (step_us / 1e6) / 1e9},
+            "long_sequence": {"workload": "one sequence, T=16384, d=832, r=64", "kernels_us": long_us,
+                              "hbm_gbs": long_bytes / (long_us / 1e6) / 1e9}}
 
 
 def run_ssd_block(dev, nk, barrier, max_over_ranks):

@@ -329,8 +329,11 @@ NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
 NEED_API int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t stream);
 
 /* Workspace bytes need_assoc_memory needs: a 128-byte header, the bf16
- * feature-mapped q and k ([nb, T, 64] each) and, with a write mask, the masked
- * values [nb, T, d]. */
+ * feature-mapped q and k ([nb, T, 64] each), with a write mask the masked
+ * values [nb, T, d], and when the sequences are cut into more than two
+ * segments the fp32 chunk states that start the later segments (at most one
+ * 32 KB state per SM).  The split follows the current device's SM count: ask
+ * on the device that runs the call. */
 NEED_API size_t need_assoc_memory_workspace_size(int64_t nb, int64_t T, int64_t d, int32_t has_mask);
 
 /* HierarchicalMemory._linear_associative_memory (need_core.py:1960-2001):
