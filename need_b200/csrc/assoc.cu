@@ -41,6 +41,7 @@ constexpr int kTok = 128;    // tokens per tile
 constexpr int kCols = 128;   // columns of d per CTA
 constexpr int kRank = 64;    // feature rank, zero padded
 constexpr int kThreads = 256;  // two warpgroups
+constexpr int kMainThreads = kThreads + 32;  // and, in the main kernel, one warp that issues the MMAs
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAssocPolls = 1u << 20;  // try_wait polls per wait before giving up
 
@@ -51,8 +52,8 @@ constexpr int OFF_V = OFF_K + 2 * 16384;       // 2 stages x 2 boxes x [128 toke
 constexpr int OFF_P = OFF_V + 2 * 32768;       // 2 K-atoms x [128 tokens][64 tokens]
 constexpr int OFF_S = OFF_P + 32768;           // [128 columns][64 features] (K-major B of Q S)
 constexpr int OFF_O = OFF_S + 16384;           // 2 boxes x [128 tokens][64 columns], TMA store source
-constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q.z [2][128], row sums [2][128] (fp32)
-constexpr int OFF_BAR = OFF_Z + (5 * kRank + 4 * kTok) * 4;  // full[2], pbar, obar, tmem base
+constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q.z [2 tiles][2][128], row sums [2][128] (fp32)
+constexpr int OFF_BAR = OFF_Z + (5 * kRank + 6 * kTok) * 4;  // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
 constexpr int kMaxSeg = 16;    // segments per sequence
@@ -101,17 +102,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // seg[s+1]).  A later segment starts from the state of the tiles before it:
 // the sum, in chunk order, of the chunk states that assoc_state_kernel left in
 // the workspace (or the running sum at its last chunk, after the chunk scan).
-// Two warpgroups.  Warp w reads tensor-memory lanes 32 (w % 4) .. + 31, so row
-// (token, or column of d for the state) `row` = 32 (w % 4) + lane belongs to
-// warps w and w + 4; warpgroup g takes half of each epilogue's columns.
-__global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constant__ AssocParams p) {
+// Two warpgroups run the CUDA-core work.  Warp w reads tensor-memory lanes
+// 32 (w % 4) .. + 31, so row (token, or column of d for the state) `row` =
+// 32 (w % 4) + lane belongs to warps w and w + 4; warpgroup g takes half of each
+// epilogue's columns.  A ninth warp issues the MMAs: an issuing thread stalls
+// while the tensor pipe drains, and the warpgroups' column sums and the next
+// tile's q.z run meanwhile.
+__global__ void __launch_bounds__(kMainThreads, 1) assoc_kernel(const __grid_constant__ AssocParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* z = reinterpret_cast<float*>(base + OFF_Z);  // [64] sum of k over the tiles so far
     float* zpart = z + kRank;                           // [4][64] column sums of a quarter of the rows
-    float* s_qz = zpart + 4 * kRank;                    // [2][128] q_t . z, per half of the features
-    float* s_rs = s_qz + 2 * kTok;                      // [2][128] masked row sums of P, per half
+    float* s_qz = zpart + 4 * kRank;                    // [2 tiles][2][128] q_t . z, per half of the features
+    float* s_rs = s_qz + 4 * kTok;                      // [2][128] masked row sums of P, per half
     uint64_t* full = reinterpret_cast<uint64_t*>(base + OFF_BAR);  // [2] tile loads
     uint64_t* pbar = full + 2;  // P = Q K^T done
     uint64_t* obar = full + 3;  // O and the state update done
@@ -120,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wg = warp >> 2, lw = warp & 3;
     const int row = lw * 32 + lane;
+    const bool compute = warp < kThreads / 32, mma_thread = tid == kThreads;
     const int c0 = blockIdx.x * kCols, b = blockIdx.y;
     const int start = p.seg[blockIdx.z];  // this CTA's first own tile
     const int end = p.seg[blockIdx.z + 1];
@@ -199,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         ok &= got;
         if (got) fpar ^= 1u << st, pend &= ~(1u << st);
     };
-    bool qk_ahead = false;  // thread 0: the next tile's P is issued already
+    bool qk_ahead = false;  // the MMA thread: the next tile's P is issued already
     auto issue_qk = [&](int tile) {  // P = Q K^T of `tile`, whose loads have landed
         const int st = own_stage(tile);
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     for (int j = 0; j < nsteps; ++j) {
         const int st = j & 1, n = min(2, start - 2 * j);
         wait_full(st);
-        if (tid == 0) {
+        if (mma_thread) {
             umma::fence_after_sync();
             for (int h = 0; h < n; ++h) {
                 const uint32_t sK = sbase + pre_k(st, h), sV = sbase + pre_v(st, h);
@@ -244,10 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             }
             umma::mma_commit(obar);
         }
-        add_z(base + pre_k(st, 0), z, zpart, tid);
-        if (n > 1) {
-            named_sync(1, kThreads);  // the first tile's column sums are read
-            add_z(base + pre_k(st, 1), z, zpart, tid);
+        if (compute) {
+            add_z(base + pre_k(st, 0), z, zpart, tid);
+            if (n > 1) {
+                named_sync(1, kThreads);  // the first tile's column sums are read
+                add_z(base + pre_k(st, 1), z, zpart, tid);
+            }
         }
         ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
         oph ^= 1u;
@@ -264,12 +271,12 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             issue_own(start);
             if (start + 1 < end) issue_own(start + 1);
         }
-        copy_state();
+        if (compute) copy_state();
         fence_proxy_async_shared();
         umma::fence_before_sync();
         __syncthreads();
     }
-    if (start > 0 && !p.recompute) {  // the state entering the segment: chunk sums in chunk order
+    if (start > 0 && !p.recompute && compute) {  // the state entering the segment: chunk sums in chunk order
         const int chi = static_cast<int>(blockIdx.z) * p.kchunk, clo = p.scanned ? chi - 1 : 0;
         float acc[32];
 #pragma unroll
@@ -291,51 +298,62 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
             z[tid] = zz;
         }
         umma::tmem_wait_st();
+    }
+    if (start > 0 && !p.recompute) {
         umma::fence_before_sync();
         __syncthreads();
         umma::fence_after_sync();
-        copy_state();
+        if (compute) copy_state();
         fence_proxy_async_shared();
         umma::fence_before_sync();
         __syncthreads();
     }
+    // q_t . z over the tiles before `it`, this warpgroup's half of the features,
+    // into the tile's q.z slot (its loads have landed)
+    auto qdotz = [&](int it) {
+        const unsigned char* qrow = base + OFF_Q + own_stage(it) * 16384;
+        float qz0 = 0.0f, qz1 = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int j = 4 * wg + jj;
+            const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(row, j));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                qz0 = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz0);
+                qz1 = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz1);
+            }
+        }
+        s_qz[((it - start) & 1) * 2 * kTok + wg * kTok + row] = qz0 + qz1;
+    };
+    if (aborted_at < 0 && start < end) {  // the first tile's loads, P and q.z
+        wait_full(own_stage(start));
+        if (mma_thread) {
+            issue_qk(start);
+            qk_ahead = true;
+        }
+        if (compute) qdotz(start);
+    }
+    // ---- own tiles.  Tile it: its P epilogue; its MMA group on the tensor
+    // cores, with the next tile's Q K^T behind it, while the warpgroups add its
+    // k to z and take the next tile's q.z; then its outputs and state copy.
     for (int it = start; it < end && aborted_at < 0; ++it) {
-        const int st = own_stage(it);
+        const int st = own_stage(it), qs = (it - start) & 1;
+        const bool next = it + 1 < end;
         const int t0 = it * kTok;
         const uint32_t sQ = sbase + OFF_Q + st * 16384, sK = sbase + OFF_K + st * 16384;
         const uint32_t sV = sbase + OFF_V + st * 32768;
         const uint32_t sP = sbase + OFF_P, sS = sbase + OFF_S;
-        const unsigned char* qrow = base + OFF_Q + st * 16384;
         const unsigned char* krow = base + OFF_K + st * 16384;
 
-        // q_t . z over the tiles before this one, this warpgroup's half of the
-        // features (the tile's loads have landed: thread 0 waited on them before
-        // issuing its P)
-        wait_full(st);
-        if (tid == 0 && !qk_ahead) issue_qk(it);
-        qk_ahead = false;
-        {
-            float qz0 = 0.0f, qz1 = 0.0f;
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = 4 * wg + jj;
-                const uint4 w = *reinterpret_cast<const uint4*>(qrow + umma::sw128(row, j));
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    qz0 = fmaf(__uint_as_float(ws[e] << 16), z[8 * j + 2 * e], qz0);
-                    qz1 = fmaf(__uint_as_float(ws[e] & 0xffff0000u), z[8 * j + 2 * e + 1], qz1);
-                }
-            }
-            s_qz[wg * kTok + row] = qz0 + qz1;
-        }
         ok &= mbar_wait_bounded(pbar, pph, kAssocPolls);
         pph ^= 1u;
+        qk_ahead = false;
         umma::fence_after_sync();
 
         // ---- P epilogue over this warpgroup's 64 columns: blocks of 32 source
         // tokens above the diagonal are all masked (no load), below it none are
-        {
+        if (compute) {
             float rs = 0.0f;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -365,8 +383,9 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
         umma::fence_before_sync();
         __syncthreads();
 
-        // ---- O = P V + Q S; S^T += V^T K; then the next tile's P
-        if (tid == 0) {
+        // ---- O = P V + Q S; S^T += V^T K; then the next tile's P (its TMEM
+        // columns were read out above)
+        if (mma_thread) {
             umma::fence_after_sync();
 #pragma unroll
             for (int k = 0; k < kTok / 16; ++k)
@@ -383,29 +402,34 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
                 umma::mma_bf16(dS, umma::smem_desc(sV + 2048 * k, 16384, 1024),
                                umma::smem_desc(sK + 2048 * k, 16384, 1024), ID_VK, it > 0 || k > 0);
             umma::mma_commit(obar);
-        }
-        add_z(krow, z, zpart, tid);
-        ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
-        oph ^= 1u;
-        umma::fence_after_sync();
-        if (tid == 0) {
-            // every reader of this stage is done (the MMAs by the barrier, q.z
-            // and the column sums by the block barriers before it): refill it
-            // now, a whole output epilogue ahead of the end of the tile
-            if (it + 2 < end) issue_own(it + 2);
-            // the next tile's P overlaps this tile's output epilogue (its TMEM
-            // columns were read out above) when its loads are in already
-            const int nx = own_stage(it + 1);
-            if (it + 1 < end && mbar_test_wait(&full[nx], (fpar >> nx) & 1u)) {
+            if (next) {
+                const int nx = own_stage(it + 1);
+                ok &= mbar_wait_bounded(&full[nx], (fpar >> nx) & 1u, kAssocPolls);  // ahead of wait_full
                 issue_qk(it + 1);
                 qk_ahead = true;
             }
         }
+        if (compute) {
+            add_z(krow, z, zpart, tid);
+            named_sync(1, kThreads);  // z with this tile, for the next q.z
+        }
+        if (next) {
+            wait_full(own_stage(it + 1));
+            if (compute) qdotz(it + 1);
+        }
+        ok &= mbar_wait_bounded(obar, oph, kAssocPolls);
+        oph ^= 1u;
+        umma::fence_after_sync();
+        // every reader of this stage is done (the MMAs by the barrier, q.z and
+        // the column sums before the barriers above): refill it now
+        if (tid == 0 && it + 2 < end) issue_own(it + 2);
 
         // ---- outputs: O / max(q.z + rowsum, eps) in bf16, this warpgroup's 64
-        // columns (one TMA store box), staged for the store
-        {
-            const float den = (s_qz[row] + s_qz[kTok + row]) + (s_rs[row] + s_rs[kTok + row]);
+        // columns (one TMA store box), staged for the store; then the state
+        // after this tile, for the next tile's Q S
+        if (compute) {
+            const float* qz = s_qz + qs * 2 * kTok;
+            const float den = (qz[row] + qz[kTok + row]) + (s_rs[row] + s_rs[kTok + row]);
             const float inv = 1.0f / fmaxf(den, p.eps);
             float v[2][32];
             umma::tmem_ld32(tO + 64 * wg, v[0]);
@@ -418,9 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
                 for (int e = 0; e < 32; e += 2) pk[e / 2] = pack_bf16(v[h][e] * inv, v[h][e + 1] * inv);
                 store_row_chunks(base + OFF_O + wg * 16384, row, h * 4, pk);
             }
+            if (next) copy_state();
         }
-        // ---- the state after this tile, for the next tile's Q S
-        if (it + 1 < end) copy_state();
         fence_proxy_async_shared();  // staged outputs (TMA store) and S (next MMA) visible to the async proxy
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) {  // a wait gave up: stop (uniformly) and report
@@ -435,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_kernel(const __grid_constan
     }
     // after a give-up, the next tile's P may still be in flight: its commit
     // covers every MMA issued, so wait (bounded) before freeing tensor memory
-    if (tid == 0 && aborted_at >= 0 && qk_ahead) mbar_wait_bounded(pbar, pph, kAssocPolls);
+    if (mma_thread && aborted_at >= 0 && qk_ahead) mbar_wait_bounded(pbar, pph, kAssocPolls);
     if (tid == 0 && aborted_at >= 0) {  // loads still in flight land before the CTA exits
         for (int st = 0; st < 2; ++st)
             if (pend & (1u << st)) mbar_wait_bounded(&full[st], (fpar >> st) & 1u, kAssocPolls);
@@ -1051,7 +1074,7 @@ int need_assoc_memory(const need_assoc_args* a, need_stream_t stream) {
             if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_chunk_scan_kernel launch");
         }
     }
-    assoc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(P);
+    assoc_kernel<<<grid, kMainThreads, SMEM_BYTES, stream>>>(P);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "assoc_kernel launch");
     return ok();
 }
