@@ -862,13 +862,23 @@ int encode_bf16(CUtensorMap* tm, const void* ptr, int64_t width, int64_t T, int6
 #ifndef NEED_ASSOC_SWITCH_COST
 #define NEED_ASSOC_SWITCH_COST 1.0  // the first own tile's load after the state-only tiles
 #endif
+// the chunk-state alternative, in own tiles: its launch, a tile of it, the chunk scan
+#ifndef NEED_ASSOC_STATE_LAUNCH_COST
+#define NEED_ASSOC_STATE_LAUNCH_COST 3.0
+#endif
+#ifndef NEED_ASSOC_STATE_TILE_COST
+#define NEED_ASSOC_STATE_TILE_COST 0.5
+#endif
+#ifndef NEED_ASSOC_SCAN_COST
+#define NEED_ASSOC_SCAN_COST 1.0
+#endif
 
 // Boundaries of at most `nseg` segments over `ntile` tiles that even out the
 // CTAs' times when later segments run the tiles before them state-only: a
 // segment starting at tile a with n own tiles costs n, plus a * prefix +
 // switch when a > 0.  The smallest budget whose greedy cover fits is found by
-// bisection; returns the number of segments used.
-int assoc_segments(int ntile, int nseg, int32_t* seg) {
+// bisection; returns the number of segments used and the budget in *cost.
+int assoc_segments(int ntile, int nseg, int32_t* seg, double* cost) {
     const double pre = NEED_ASSOC_PREFIX_COST, sw = NEED_ASSOC_SWITCH_COST;
     auto cover = [&](double budget, int32_t* out) {
         int a = 0, s = 0;
@@ -887,15 +897,18 @@ int assoc_segments(int ntile, int nseg, int32_t* seg) {
         const double mid = 0.5 * (lo + hi);
         (cover(mid, nullptr) > 0 ? hi : lo) = mid;
     }
+    *cost = hi;
     return cover(hi, seg);
 }
 
 // How a launch splits the sequences into `nseg` segments per sequence (the
-// CTAs of all segments fill the SMs once).  Two segments: the second re-sums
-// the first's tiles state-only (cheaper than a launch of its own), at
-// boundaries that balance the two.  More: equal segments, and the tiles before
-// the last segment in `nchunk` chunks, `kchunk` per segment, whose states the
-// chunk kernel sums first on as many SMs again.
+// CTAs of all segments fill the SMs once).  Of two plans, the cheaper by the
+// cost model above:
+//  * two segments, the second re-summing the first's tiles state-only, at
+//    boundaries that balance the two;
+//  * as many equal segments as the SMs take, after a launch that sums the
+//    tiles before the last segment in `nchunk` chunks (`kchunk` per segment)
+//    on as many SMs again.
 struct AssocPlan {
     int nseg = 1, kchunk = 0, nchunk = 0, recompute = 0;
     int32_t seg[kMaxSeg + 1] = {};
@@ -914,12 +927,13 @@ int device_sms() {
 AssocPlan assoc_plan(int64_t nb, int64_t T, int64_t d, int sms) {
     AssocPlan pl;
     const int64_t ncb = (d + kCols - 1) / kCols, ntile = (T + kTok - 1) / kTok, per = ncb * nb;
-    pl.nseg = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({ntile, sms / per, kMaxSeg})));
-    if (pl.nseg <= 2) {
-        pl.recompute = pl.nseg > 1;
-        pl.nseg = assoc_segments(static_cast<int>(ntile), pl.nseg, pl.seg);
-        return pl;
-    }
+    const int most = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({ntile, sms / per, kMaxSeg})));
+    AssocPlan re;  // at most two segments, no chunk states
+    double re_cost = 0.0;
+    re.recompute = most > 1;
+    re.nseg = assoc_segments(static_cast<int>(ntile), std::min(most, 2), re.seg, &re_cost);
+    if (most <= 2) return re;
+    pl.nseg = most;
     for (int s = 0; s <= pl.nseg; ++s) pl.seg[s] = static_cast<int32_t>(s * ntile / pl.nseg);
     if (pl.nseg > 1) {
         const int64_t shortest = ntile / pl.nseg;  // >= 1 tile
@@ -932,7 +946,12 @@ AssocPlan assoc_plan(int64_t nb, int64_t T, int64_t d, int sms) {
         }
         pl.chunk[pl.nchunk] = pl.seg[pl.nseg - 1];
     }
-    return pl;
+    int longest_seg = 0, longest_chunk = 0;
+    for (int s = 0; s < pl.nseg; ++s) longest_seg = std::max(longest_seg, pl.seg[s + 1] - pl.seg[s]);
+    for (int c = 0; c < pl.nchunk; ++c) longest_chunk = std::max(longest_chunk, pl.chunk[c + 1] - pl.chunk[c]);
+    const double cost = NEED_ASSOC_STATE_LAUNCH_COST + NEED_ASSOC_STATE_TILE_COST * longest_chunk +
+                        (pl.nchunk > kScanAbove ? NEED_ASSOC_SCAN_COST : 0.0) + longest_seg;
+    return cost < re_cost ? pl : re;
 }
 
 // workspace: header | q features | k features | masked v | chunk states | chunk z

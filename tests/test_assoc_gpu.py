@@ -116,13 +116,14 @@ def test_repeat_calls_are_identical(cuda):
 
 @pytest.mark.parametrize("T", [2048, 1700])
 def test_segmentations_agree(cuda, T):
-    """Alone, a sequence of 16 (14) tiles is cut into one-tile segments whose
-    entering states are running sums over 15 (13) chunk states (the chunk scan
-    kernel); copied 12 times it gets 6 segments (5 chunks, scanned), 24 times
-    3 segments (2 chunks, summed in the main kernel), 36 times 2 segments (the
-    second re-sums the first's tiles itself), 80 times one segment.  The states
-    differ only in the order of their fp32 sums: the outputs agree to about one
-    bf16 rounding, and each layout repeats bit for bit."""
+    """At d=256 the launch plan depends on the batch.  Alone, a sequence of 16
+    (14) tiles gets one-tile segments whose entering states are running sums
+    over 15 (13) chunk states (the chunk scan kernel).  Copied 12 times it
+    gets 6 segments (5 chunks, scanned); 14 times, 5 segments (4 chunks,
+    summed in the main kernel); 36 times, 2 segments, the second re-summing
+    the first's tiles itself; 80 times, one segment.  The states differ only
+    in the order of their fp32 sums: the outputs agree to about one bf16
+    rounding, and each layout repeats bit for bit."""
     gen = torch.Generator().manual_seed(T)
     q, k = torch.randn(1, T, 64, generator=gen).to(cuda), torch.randn(1, T, 64, generator=gen).to(cuda)
     v = torch.randn(1, T, 256, generator=gen).to(torch.bfloat16).to(cuda)
@@ -130,7 +131,7 @@ def test_segmentations_agree(cuda, T):
     assert torch.equal(one, nk.linear_associative_memory(q, k, v))
     ex = host(exact(q, k, v))
     assert rel(host(one), ex) <= 1e-2 and rel_l2(host(one), ex) <= 5e-3
-    for copies in (12, 24, 36, 80):
+    for copies in (12, 14, 36, 80):
         many = nk.linear_associative_memory(q.repeat(copies, 1, 1), k.repeat(copies, 1, 1), v.repeat(copies, 1, 1))
         d = (many.float() - one.float().expand_as(many)).abs()
         assert float(d.max()) <= 2.0 ** -7 * float(one.float().abs().max()), copies
