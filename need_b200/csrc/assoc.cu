@@ -799,13 +799,15 @@ __global__ void __launch_bounds__(kStepThreads) assoc_step_kernel(const StepPara
         }
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-        // rows in batches of U: the batch's loads are issued together, before its stores
+        // rows in batches of U, in row order; the next batch's loads are issued
+        // before this batch is updated and stored, so one batch is always in flight
         constexpr int U = 8;
-        for (int i0 = 0; i0 < p.r; i0 += U) {
-            uint4 u[U];
+        auto load = [&](uint4 (&u)[U], int i0) {
 #pragma unroll
             for (int k = 0; k < U; ++k)
                 if (i0 + k < p.r) u[k] = *reinterpret_cast<const uint4*>(st + (int64_t)(i0 + k) * p.sr + c);
+        };
+        auto update = [&](uint4 (&u)[U], int i0) {
 #pragma unroll
             for (int k = 0; k < U; ++k) {
                 const int i = i0 + k;
@@ -823,6 +825,15 @@ __global__ void __launch_bounds__(kStepThreads) assoc_step_kernel(const StepPara
                 }
                 *reinterpret_cast<uint4*>(st + (int64_t)i * p.sr + c) = u[k];
             }
+        };
+        uint4 ua[U], ub[U];
+        load(ua, 0);
+        for (int i0 = 0; i0 < p.r; i0 += 2 * U) {
+            if (i0 + U < p.r) load(ub, i0 + U);
+            update(ua, i0);
+            if (i0 + U >= p.r) break;
+            if (i0 + 2 * U < p.r) load(ua, i0 + 2 * U);
+            update(ub, i0 + U);
         }
         uint4 o;
         PS* oh = reinterpret_cast<PS*>(&o);
