@@ -5,15 +5,18 @@
 // [r] over feature-mapped keys k = elu(k_raw) + 1, and reads
 //     out_t = (q_t . S_t) / max(q_t . z_t, eps)      q = elu(q_raw) + 1.
 // The reference materialises S_t for every token of a 32-token chunk.  Here a
-// CTA owns one sequence and 128 columns of d and walks the sequence in tiles
-// of 128 tokens with the chunked (linear-attention) form, every product on
-// tcgen05 tensor cores with fp32 accumulators in tensor memory:
+// CTA owns a segment of one sequence and 128 columns of d and walks the
+// segment in tiles of 128 tokens with the chunked (linear-attention) form,
+// every product on tcgen05 tensor cores with fp32 accumulators in tensor memory:
 //     P   = Q K^T                 (128 x 128, masked to s <= t)    TMEM cols   0..127
 //     O   = P V + Q S             (128 tokens x 128 columns)       TMEM cols 128..255
 //     S^T += V^T K                (128 columns x 64 features)      TMEM cols 256..319
 // with the denominator q_t . z + sum_{s<=t} P[t, s] in fp32 on the CUDA cores.
-// The state stays in tensor memory in fp32 for the whole sequence; its bf16
-// copy in shared memory is the B operand of the next tile's Q S.
+// The state stays in tensor memory in fp32 for the whole segment; its bf16
+// copy in shared memory is the B operand of the next tile's Q S.  A later
+// segment starts from the state of the tiles before it: re-summed state-only
+// in the same kernel, or summed once per chunk by assoc_state_kernel
+// (assoc_plan picks the cheaper).
 //
 // Operands arrive by TMA with the 128-byte swizzle (no multicast); every tile
 // is a canonical UMMA layout (umma.cuh), so the same shared-memory tile of V
@@ -22,7 +25,8 @@
 // tile overlap the current one (two stages); outputs leave through a TMA store.
 //
 // A prologue kernel applies the feature map (and the optional write mask) and
-// writes q, k as bf16 [B, T, 64] (features past r zero) into the workspace.
+// writes q, k as bf16 [B, T, 64] (features past r zero) into the workspace;
+// the chunk states, when the plan has them, follow in the same workspace.
 #include <algorithm>
 #include <atomic>
 #include <climits>
