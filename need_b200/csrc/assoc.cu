@@ -60,7 +60,10 @@ constexpr int OFF_Z = OFF_O + 32768;           // z [64], column sums [4][64], q
 constexpr int OFF_BAR = OFF_Z + (5 * kRank + 6 * kTok) * 4;  // full[2], pbar, obar, tmem base
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
-constexpr int kMaxSeg = 16;    // segments per sequence
+#ifndef NEED_ASSOC_MAX_SEG
+#define NEED_ASSOC_MAX_SEG 24
+#endif
+constexpr int kMaxSeg = NEED_ASSOC_MAX_SEG;  // segments per sequence
 constexpr int kMaxChunk = 64;  // state chunks per sequence
 constexpr int kScanAbove = 4;  // more chunks than this: prefix-summed by a kernel of their own
 
@@ -586,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) assoc_state_kernel(const __grid_c
 
 // Running sums over the chunks, in place and in chunk order: cs[c] := cs[0] +
 // ... + cs[c], the same for cz.  Thread i owns one float4 of every chunk; its
-// loads go out eight chunks at a time.
+// loads go out sixteen chunks at a time.
 __global__ void __launch_bounds__(256) assoc_chunk_scan_kernel(float* __restrict__ cs, float* __restrict__ cz,
                                                                int64_t cs4, int64_t cz4, int nchunk) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -595,14 +598,15 @@ __global__ void __launch_bounds__(256) assoc_chunk_scan_kernel(float* __restrict
     if (i < cs4) col = reinterpret_cast<float4*>(cs) + i, stride = cs4;
     else if (i < cs4 + cz4) col = reinterpret_cast<float4*>(cz) + (i - cs4), stride = cz4;
     else return;
-    float4 acc = col[0];
-    for (int c0 = 1; c0 < nchunk; c0 += 8) {
-        float4 f[8];
+    constexpr int kBatch = 16;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // 0 + cs[0] is cs[0]: the main kernel's sums start so too
+    for (int c0 = 0; c0 < nchunk; c0 += kBatch) {
+        float4 f[kBatch];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kBatch; ++j)
             if (c0 + j < nchunk) f[j] = __ldcg(col + (c0 + j) * stride);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kBatch; ++j)
             if (c0 + j < nchunk) {
                 acc.x += f[j].x, acc.y += f[j].y, acc.z += f[j].z, acc.w += f[j].w;
                 col[(c0 + j) * stride] = acc;
