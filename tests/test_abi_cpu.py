@@ -136,3 +136,22 @@ def test_argument_errors_return_status(lib):
     m.r, m.dtype = 64, abi.F32
     assert lib.need_assoc_memory(ctypes.byref(m), None) == abi.ERR_UNSUPPORTED  # fp32 values
     assert lib.need_assoc_memory_workspace_size(2, 100, 64, 0) == 128 + 2 * ((2 * 100 * 64 * 2 + 127) // 128 * 128)
+
+
+def test_assoc_workspace_follows_the_launch_plan(lib):
+    """The associative memory's workspace holds the fp32 chunk states of the
+    plan the launch will use (B200: 148 SMs; without a GPU the library assumes
+    the same).  At d=832 (7 column blocks): 8 sequences of 2048 tokens take two
+    segments, the second re-summing the first's tiles, so no chunk states; 4 of
+    4096 take 5 segments after 4 chunk states; one of 16384 takes 21 segments
+    after 20 chunk states, each [7 blocks][128 columns][64 features] plus z."""
+
+    def feats(nb, t):
+        return 2 * ((nb * t * 64 * 2 + 127) // 128 * 128)
+
+    def chunks(n, nb):
+        return n * nb * 7 * 128 * 64 * 4 + (n * nb * 64 * 4 + 127) // 128 * 128
+
+    assert lib.need_assoc_memory_workspace_size(8, 2048, 832, 0) == 128 + feats(8, 2048)
+    assert lib.need_assoc_memory_workspace_size(4, 4096, 832, 0) == 128 + feats(4, 4096) + chunks(4, 4)
+    assert lib.need_assoc_memory_workspace_size(1, 16384, 832, 0) == 128 + feats(1, 16384) + chunks(20, 1)
