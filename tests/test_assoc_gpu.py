@@ -140,6 +140,41 @@ def test_segmentations_agree(cuda, T):
     no_device_error()
 
 
+def exact_blocked(q_raw, k_raw, v, eps=1e-6, block=2048):
+    """exact() one block of query tokens at a time (float64 on the GPU), for
+    sequences whose full score matrix would not fit."""
+    bf = torch.bfloat16
+    qf = (F.elu(q_raw.float()) + 1.0).to(bf).double()
+    kf = (F.elu(k_raw.float()) + 1.0).to(bf).double()
+    vv = v.double()
+    out = torch.empty(v.shape, dtype=torch.float64, device=v.device)
+    T = v.shape[1]
+    for t0 in range(0, T, block):
+        t1 = min(T, t0 + block)
+        a = torch.einsum("btr,bsr->bts", qf[:, t0:t1], kf[:, :t1])
+        a[:, :, t0:t1] = a[:, :, t0:t1].tril()
+        out[:, t0:t1] = (a @ vv[:, :t1]) / a.sum(-1, keepdim=True).clamp_min(eps)
+    return out
+
+
+@pytest.mark.parametrize("B,T", [(8, 2048), (1, 16384)])
+def test_full_size_matches_exact_sums(cuda, B, T):
+    """The bench workload (8 sequences of 2048 tokens at NEED's d_model 832: two
+    segments, the second re-summing the first's tiles) and one sequence of
+    16384 tokens (21 segments after 20 chunk states) against exact float64 sums
+    of the same bf16 features and values."""
+    gen = torch.Generator().manual_seed(B + T)
+    q = torch.randn(B, T, 64, generator=gen).to(cuda)
+    k = torch.randn(B, T, 64, generator=gen).to(cuda)
+    v = torch.randn(B, T, 832, generator=gen).to(torch.bfloat16).to(cuda)
+    y = nk.linear_associative_memory(q, k, v)
+    ex = exact_blocked(q, k, v)
+    d = (y.double() - ex).abs()
+    assert float(d.max()) <= 1e-2 * float(ex.abs().max())
+    assert float(torch.linalg.norm(y.double() - ex) / torch.linalg.norm(ex)) <= 5e-3
+    no_device_error()
+
+
 def test_rejects_what_it_does_not_take(cuda):
     q = torch.randn(1, 8, 80, device=cuda)
     v = torch.randn(1, 8, 64, device=cuda).to(torch.bfloat16)
