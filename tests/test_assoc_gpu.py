@@ -73,6 +73,7 @@ def test_matches_reference_fixture(cuda, name):
     (2, 300, 64, 832, False),    # NEED's d_model: a partial token tile and a half-full column block
     (3, 1000, 16, 96, True),     # rank below 64, one partial column block, a write mask
     (1, 2048, 64, 256, False),   # 16 tiles: the state carried across the whole sequence
+    (1, 2048, 64, 256, True),    # the same with a write mask: the chunk states read the masked values
 ])
 def test_matches_oracle(cuda, B, T, r, d, mask):
     gen = torch.Generator().manual_seed(B * 1000 + T + r + d)
