@@ -205,12 +205,15 @@ def test_step_matches_reference_fixture(cuda):
         assert np.mean(host(y) == g["y"][j]) >= 0.99 and rel(host(y), g["y"][j]) <= TOL, j
 
 
+@pytest.mark.parametrize("r", [64, 37, 200])
 @pytest.mark.parametrize("dtype,name", [(torch.bfloat16, "bf16"), (torch.float16, "fp16"), (torch.float32, "fp32")])
-def test_step_matches_oracle_with_a_pool(cuda, dtype, name):
-    """64 sequences at NEED's shape (r=64, d=832) in a pool of 100 state rows,
-    3 steps with a write mask, against the oracle."""
-    gen = torch.Generator().manual_seed(31)
-    N, S, r, d = 64, 100, 64, 832
+def test_step_matches_oracle_with_a_pool(cuda, dtype, name, r):
+    """64 sequences at NEED's width (d=832) in a pool of 100 state rows, 3 steps
+    with a write mask, against the oracle: NEED's rank 64, a rank that leaves
+    the last batch of state rows partial (37), and one above the CTA's thread
+    count (200)."""
+    gen = torch.Generator().manual_seed(31 + r)
+    N, S, d = 64, 100, 832
     pool = (0.5 * torch.randn(S, r, d, generator=gen)).to(dtype)
     pden = (5.0 * torch.rand(S, r, generator=gen)).to(dtype)
     slot = torch.randperm(S, generator=gen)[:N].to(torch.int32)
