@@ -319,14 +319,27 @@ NEED_API int need_gated_scan(const need_scan_args* args, need_stream_t stream);
  * every GPU that loads this library holds until the process exits.  A call
  * whose scan needs more scratch than that (more tiles than the array has
  * records for; need_scan_workspace_size gives the bytes a scan needs) fails
- * with NEED_ERR_WORKSPACE and launches nothing.  The first call on each device looks up the array's device
- * address and zero-fills it (a synchronous cudaMemset), so make that first call
- * before any stream capture.  Each call then clears the array's error word on
- * `stream` and launches the same kernel as need_gated_scan.  All calls share
- * the one array: calls that overlap on the GPU (different streams or host
- * threads at once) race on it; calls that run one after another, on any
- * stream, are fine.  It allocates nothing (no cudaMalloc or cudaFree). */
+ * with NEED_ERR_WORKSPACE and launches nothing.  The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress) and zero-fills the
+ * array with cudaMemsetAsync on `stream`, ordered before that call's launch;
+ * make that first call before any stream capture.  The address is kept for the
+ * life of the process, so after cudaDeviceReset neither this entry point nor
+ * need_gated_scan_noalloc_error may be called again.  Each call clears the
+ * array's error word on `stream` (so that a wait that gave up in an earlier
+ * call does not cut this call's waits short) and launches the same kernel as
+ * need_gated_scan, with the same results bit for bit.  All calls share the one
+ * array: calls that overlap on the GPU (different streams or host threads at
+ * once) race on it; calls that run one after another, on any stream, are fine.
+ * It allocates nothing (no cudaMalloc or cudaFree). */
 NEED_API int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t stream);
+
+/* Reads and clears the error word of need_gated_scan_noalloc's static array:
+ * bit 0 = a look-back wait gave up, bit 1 = a tile load wait gave up, as for
+ * need_workspace_error; after either the call's outputs are not valid.  Synchronises `stream`.
+ * Call it after a need_gated_scan_noalloc call and before the next one (the
+ * next call clears the word).  Like need_workspace_error for a caller's
+ * workspace.  No counterpart in the reference. */
+NEED_API int need_gated_scan_noalloc_error(uint32_t* error_out, need_stream_t stream);
 
 /* Workspace bytes need_assoc_memory needs: a 128-byte header, the bf16
  * feature-mapped q and k ([nb, T, 64] each), with a write mask the masked

@@ -122,6 +122,7 @@ SIGNATURES = {
     "need_recurrent_retention_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_gated_scan_noalloc": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
+    "need_gated_scan_noalloc_error": (c_int32, [POINTER(c_uint32), c_void_p]),
     "need_ragged_verify": (c_int32, [POINTER(NeedVerifyArgs), c_void_p]),
     "need_segment_starts": (c_int32, [POINTER(NeedSegmentArgs), c_void_p]),
     "need_ssd_conv_silu": (c_int32, [POINTER(NeedConvArgs), c_void_p]),

@@ -22,8 +22,13 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of g_scratch on the current device, zero-filled on first use.
-int scratch_address(void** out) {
+// Device address of g_scratch on the current device.  The first call on a
+// device looks the address up and zero-fills the array with cudaMemsetAsync on
+// `stream`, so the fill is ordered before that call's launch on any stream
+// (the look-back records must start untagged).  The address is kept for the
+// life of the process: after cudaDeviceReset it is stale, and the entry points
+// must not be used again in that process.
+int scratch_address(cudaStream_t stream, void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return need::cuda_fail(e, "cudaGetDevice");
@@ -33,8 +38,8 @@ int scratch_address(void** out) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_scratch);
         if (e != cudaSuccess) return need::cuda_fail(e, "cudaGetSymbolAddress(scratch)");
-        e = cudaMemset(p, 0, kScratchBytes);  // the look-back records must start untagged
-        if (e != cudaSuccess) return need::cuda_fail(e, "cudaMemset(scratch)");
+        e = cudaMemsetAsync(p, 0, kScratchBytes, stream);
+        if (e != cudaSuccess) return need::cuda_fail(e, "cudaMemsetAsync(scratch)");
         g_scratch_ptr[dev] = p;
     }
     *out = g_scratch_ptr[dev];
@@ -59,7 +64,7 @@ extern "C" int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t
                           static_cast<long long>(need_scan_chunk_len(args->form, args->dtype, args->dtype, 0)));
     }
     void* scratch = nullptr;
-    if (int rc = scratch_address(&scratch)) return rc;
+    if (int rc = scratch_address(static_cast<cudaStream_t>(stream), &scratch)) return rc;
     // a bounded wait that gave up in an earlier call must not shorten this call's waits
     const cudaError_t e =
         cudaMemsetAsync(static_cast<unsigned char*>(scratch) + kErrorWordOffset, 0, sizeof(uint32_t), stream);
@@ -68,4 +73,12 @@ extern "C" int need_gated_scan_noalloc(const need_scan_args* args, need_stream_t
     a.workspace = scratch;
     a.workspace_bytes = kScratchBytes;
     return need_gated_scan(&a, stream);
+}
+
+extern "C" int need_gated_scan_noalloc_error(uint32_t* error_out, need_stream_t stream) {
+    if (error_out == nullptr) return need::fail(NEED_ERR_INVALID, "error_out is null");
+    void* scratch = nullptr;
+    if (int rc = scratch_address(static_cast<cudaStream_t>(stream), &scratch)) return rc;
+    // the array's workspace header holds the error word where a caller's workspace does
+    return need_workspace_error(scratch, error_out, stream);
 }
