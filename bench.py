@@ -130,25 +130,42 @@ def profiled_traffic():
         return None
 
 
-def cpu_sample_rate(rows: int, nthreads: int, repeats: int = 3):
-    """Oracle (C restatement of the reference's chunked scan) tokens/s on `rows`
-    sequences of the prefill workload, all gate math included."""
+def cpu_inputs(rows: int):
+    """The prefill workload's first `rows` sequences as the oracle takes them
+    (fp32 arrays of bf16-rounded values, uint8 reset mask)."""
     import numpy as np
     import oracle
     from need_b200 import workloads
-    rs = np.random.RandomState(0)
+    rng = np.random.default_rng(0)
     shape = (rows, T, C)
-    x = oracle.round_to(rs.standard_normal(shape).astype(np.float32), "bf16")
-    z = oracle.round_to((rs.standard_normal(shape) + 4.0).astype(np.float32), "bf16")
-    g = oracle.round_to(rs.standard_normal(shape).astype(np.float32), "bf16")
+    x = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), "bf16")
+    z = oracle.round_to(rng.standard_normal(shape, dtype=np.float32) + np.float32(4.0), "bf16")
+    g = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), "bf16")
     seg = workloads.segment_starts(rows, T, seed=0, kind="lognormal", lo=16, hi=4096)
+    return x, z, g, seg
+
+
+CPU_ROWS = B  # the CPU legs time the whole workload: all 16 sequences per step
+
+
+def cpu_sample_rate(nthreads: int, repeats: int = 3):
+    """Oracle (C restatement of the reference's chunked scan) tokens/s on the
+    whole prefill workload, all gate math included; median of `repeats` runs."""
+    import oracle
+    x, z, g, seg = cpu_inputs(CPU_ROWS)
     oracle.gated_scan(x[:1, :256], z[:1, :256], g[:1, :256], seg[:1, :256], dtype="bf16", nthreads=nthreads)
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
         oracle.gated_scan(x, z, g, seg, dtype="bf16", nthreads=nthreads)
         times.append(time.perf_counter() - t0)
-    return rows * T / statistics.median(times), statistics.median(times)
+    return CPU_ROWS * T / statistics.median(times), statistics.median(times)
+
+
+def cpu_sample_text(nthreads: int) -> str:
+    return (f"the whole workload per step ({CPU_ROWS} x {T} tokens x {C} channels, bf16-rounded gates, resets); "
+            f"C restatement of need_kernels.py:177-226 + the gate math of :330-336, {nthreads} threads "
+            f"(work split over (sequence, 64-channel block) in the scan and (sequence, 64-token block) in the gates)")
 
 
 # ------------------------------------------------------------------ reference arm
@@ -156,31 +173,22 @@ def run_reference(args, rank: int):
     if rank != 0:
         return
     nthreads = os.cpu_count() or 1
-    rows = 1
-    import numpy as np
     import oracle
-    from need_b200 import workloads
-    rs = np.random.RandomState(0)
-    shape = (rows, T, C)
-    x = oracle.round_to(rs.standard_normal(shape).astype(np.float32), "bf16")
-    z = oracle.round_to((rs.standard_normal(shape) + 4.0).astype(np.float32), "bf16")
-    g = oracle.round_to(rs.standard_normal(shape).astype(np.float32), "bf16")
-    seg = workloads.segment_starts(rows, T, seed=0, kind="lognormal", lo=16, hi=4096)
+    x, z, g, seg = cpu_inputs(CPU_ROWS)
     for _ in range(args.warmup):
         oracle.gated_scan(x, z, g, seg, dtype="bf16", nthreads=nthreads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         oracle.gated_scan(x, z, g, seg, dtype="bf16", nthreads=nthreads)
     el = time.perf_counter() - t0
-    tps = args.steps * rows * T / el
-    sample = (f"1 of the 16 sequences per step (1 x 4096 tokens x 1024 channels, bf16-rounded gates, resets), "
-              f"C restatement of need_kernels.py:177-226 + gate math, {nthreads} threads")
+    tps = args.steps * CPU_ROWS * T / el
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(),
-        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": nthreads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                         "sample": cpu_sample_text(nthreads)},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -356,10 +364,9 @@ def main():
     cpu = None
     if rank == 0 and world == 1:
         nthreads = os.cpu_count() or 1
-        rate, secs = cpu_sample_rate(4, nthreads)
+        rate, secs = cpu_sample_rate(nthreads)
         cpu = {"value": rate, "unit": "tokens/s", "cores": nthreads, "kind": "port",
-               "sample": f"4 of the 16 sequences (4 x 4096 tokens x 1024 channels), median of 3 runs of "
-                         f"{secs:.2f} s; C restatement of the reference's chunked scan + bf16 gate math"}
+               "sample": cpu_sample_text(nthreads) + f"; median of 3 runs of {secs:.2f} s"}
 
     if rank == 0:
         line = {

@@ -236,6 +236,12 @@ ORA_API void ora_affine_scan_seq(const float* a, const float* b, const float* h0
 /* gate arithmetic                                                     */
 /* ------------------------------------------------------------------ */
 
+/* The gate and epilogue passes are elementwise: a work row is (sequence n,
+ * block of ORA_TBLK tokens), so one long sequence still spreads over every
+ * thread.  Splitting changes no result. */
+#define ORA_TBLK 64
+static inline int64_t tblocks(int64_t T) { return (T + ORA_TBLK - 1) / ORA_TBLK; }
+
 typedef struct {
     const float *x, *z, *g;
     const uint8_t* seg;
@@ -244,10 +250,12 @@ typedef struct {
     int mode;
 } gated_ctx;
 
-static void gated_row(void* ctx_, int64_t n) {
+static void gated_row(void* ctx_, int64_t row) {
     gated_ctx* s = (gated_ctx*)ctx_;
     const int m = s->mode;
-    for (int64_t t = 0; t < s->T; ++t) {
+    const int64_t n = row / tblocks(s->T), t0 = (row % tblocks(s->T)) * ORA_TBLK;
+    const int64_t t1 = t0 + ORA_TBLK < s->T ? t0 + ORA_TBLK : s->T;
+    for (int64_t t = t0; t < t1; ++t) {
         const int reset = s->seg ? (s->seg[n * s->T + t] != 0) : 0;
         for (int64_t c = 0; c < s->C; ++c) {
             const int64_t i = (n * s->T + t) * s->C + c;
@@ -267,7 +275,7 @@ ORA_API void ora_gated_prep(const float* x, const float* z, const float* g, cons
                             float* a, float* b, int64_t N, int64_t T, int64_t C, int mode,
                             int nthreads) {
     gated_ctx s = {x, z, g, seg, a, b, T, C, mode};
-    run_rows(gated_row, &s, N, nthreads);
+    run_rows(gated_row, &s, N * tblocks(T), nthreads);
 }
 
 typedef struct {
@@ -279,10 +287,12 @@ typedef struct {
     int mode;
 } ssdp_ctx;
 
-static void ssd_prep_row(void* ctx_, int64_t n) {
+static void ssd_prep_row(void* ctx_, int64_t row) {
     ssdp_ctx* s = (ssdp_ctx*)ctx_;
     const int m = s->mode;
-    for (int64_t t = 0; t < s->T; ++t) {
+    const int64_t n = row / tblocks(s->T), t0 = (row % tblocks(s->T)) * ORA_TBLK;
+    const int64_t t1 = t0 + ORA_TBLK < s->T ? t0 + ORA_TBLK : s->T;
+    for (int64_t t = t0; t < t1; ++t) {
         const int reset = s->seg ? (s->seg[n * s->T + t] != 0) : 0;
         for (int64_t c = 0; c < s->C; ++c) {
             const int64_t i = (n * s->T + t) * s->C + c;
@@ -307,7 +317,7 @@ ORA_API void ora_ssd_prep(const float* u, const float* bg, const float* dt, cons
                           float* a, float* b, int64_t N, int64_t T, int64_t C, double dt_min,
                           double dt_max, int mode, int nthreads) {
     ssdp_ctx s = {u, bg, dt, seg, a, b, T, C, (float)(dt_max - dt_min), (float)dt_min, mode};
-    run_rows(ssd_prep_row, &s, N, nthreads);
+    run_rows(ssd_prep_row, &s, N * tblocks(T), nthreads);
 }
 
 typedef struct {
@@ -317,10 +327,12 @@ typedef struct {
     int mode;
 } ssde_ctx;
 
-static void ssd_epi_row(void* ctx_, int64_t n) {
+static void ssd_epi_row(void* ctx_, int64_t row) {
     ssde_ctx* s = (ssde_ctx*)ctx_;
     const int m = s->mode;
-    for (int64_t t = 0; t < s->T; ++t)
+    const int64_t n = row / tblocks(s->T), t0 = (row % tblocks(s->T)) * ORA_TBLK;
+    const int64_t t1 = t0 + ORA_TBLK < s->T ? t0 + ORA_TBLK : s->T;
+    for (int64_t t = t0; t < t1; ++t)
         for (int64_t c = 0; c < s->C; ++c) {
             const int64_t i = (n * s->T + t) * s->C + c;
             const float cgs = rnd(sigm(s->cg[i]), m);
@@ -339,7 +351,7 @@ ORA_API void ora_ssd_epilogue(const float* h, const float* u, const float* cg, c
                               const float* dskip, float* y, int64_t N, int64_t T, int64_t C,
                               int mode, int nthreads) {
     ssde_ctx s = {h, u, cg, og, dskip, y, T, C, mode};
-    run_rows(ssd_epi_row, &s, N, nthreads);
+    run_rows(ssd_epi_row, &s, N * tblocks(T), nthreads);
 }
 
 /* ------------------------------------------------------------------ */
