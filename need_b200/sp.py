@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass, field
+from datetime import timedelta
 from typing import List, Optional
 
 import torch
@@ -89,20 +90,43 @@ def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> 
         ctypes.byref(a), all_summary.data_ptr(), int(nranks), int(rank), nk._stream(dev)))
 
 
+def exchange_summaries(summary: torch.Tensor, group: Optional[dist.ProcessGroup] = None,
+                       timeout: Optional[timedelta] = None) -> torch.Tensor:
+    """Step 2: every rank's slice map, ``[P, B, C, 2]`` fp32, gathered into this
+    rank's memory (rank order = T order).
+
+    One ``all_gather_into_tensor`` of 2*B*C*4 bytes per rank, into a buffer of
+    the concatenated shape every backend takes (NCCL on GPUs, gloo on CPU).
+    With ``timeout`` the host waits for the collective and raises
+    ``RuntimeError`` when a rank has left or does not join in time; without it
+    the call returns at once on NCCL (the stream waits) and the process
+    group's own timeout bounds the collective.
+    """
+    world = dist.get_world_size(group)
+    summary = summary.contiguous()
+    flat = torch.empty((world * summary.shape[0],) + tuple(summary.shape[1:]), dtype=summary.dtype,
+                       device=summary.device)
+    work = dist.all_gather_into_tensor(flat, summary, group=group, async_op=True)
+    if timeout is None:
+        work.wait()
+    elif not work.wait(timeout=timeout):
+        raise RuntimeError(f"sequence-parallel exchange did not complete within {timeout}")
+    return flat.view((world,) + tuple(summary.shape))
+
+
 def sp_gated_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Tensor, *,
                   group: Optional[dist.ProcessGroup] = None, seg_start: Optional[torch.Tensor] = None,
-                  return_final_state: bool = False):
+                  return_final_state: bool = False, timeout: Optional[timedelta] = None):
     """The gated scan of a sequence whose T is split over the ranks of ``group``.
 
     Every rank passes its own contiguous [B, T/P, C] slice (ranks in T order);
     each gets back the exact outputs of its slice, and with
     ``return_final_state`` the fp32 state after its slice's last token.
+    ``timeout`` bounds the exchange on the host (see ``exchange_summaries``).
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     loc = local_scan(x, decay_logit, gate_logit, seg_start=seg_start)
     if world > 1:
-        gathered = torch.empty((world,) + tuple(loc.summary.shape), dtype=torch.float32, device=x.device)
-        dist.all_gather_into_tensor(gathered, loc.summary, group=group)
-        fixup(loc, gathered, world, rank)
+        fixup(loc, exchange_summaries(loc.summary, group, timeout), world, rank)
     return (loc.out, loc.h_final) if return_final_state else loc.out
