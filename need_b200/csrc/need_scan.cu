@@ -188,6 +188,10 @@ bool select_plan(int form, int dt, int ddt, int rd, Plan* out) {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Look-back polls before a wait gives up, for the launches that follow; 0 =
+// the default kLookbackPolls.  Set only by need_test_set_lookback_polls.
+std::atomic<uint32_t> g_lookback_polls{0};
+
 
 struct Geometry {
     int64_t ncb, nchains, nchunks, ntiles;
@@ -333,6 +337,8 @@ int prepare(const need_scan_args* a, int expect_form, Plan* pl, ScanParams* P, b
     P->tile_carry = a->tile_carry;
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P->hdr = reinterpret_cast<uint32_t*>(ws);
+    const uint32_t polls = g_lookback_polls.load(std::memory_order_relaxed);
+    P->lb_polls = polls != 0 ? polls : kLookbackPolls;
     P->agg = reinterpret_cast<ulonglong2*>(ws + WS_HDR_WORDS * 4);
     P->incl = P->agg + size_t(g.ntiles) * pl->CB;
     return NEED_OK;
@@ -393,6 +399,8 @@ size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t decay_dtype
     if (nb < 1 || nh < 1 || T < 1 || C < 1) return ws_bytes(pl, 0);
     return ws_bytes(pl, geometry(pl, nb, nh, T, C).ntiles);
 }
+
+void need_test_set_lookback_polls(uint32_t polls) { g_lookback_polls.store(polls, std::memory_order_relaxed); }
 
 int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream) {
     if (workspace == nullptr || error_out == nullptr) return fail(NEED_ERR_INVALID, "null argument");

@@ -14,19 +14,22 @@
 //      computes a, b for its rows (gate math per form; 16-bit inputs are
 //      rounded where the reference's torch path rounds), writes them back in
 //      place for phase 2, and reduces its rows to one affine map (A, B):
-//      h_out = A*h_in + B, written to shared memory.
+//      h_out = A*h_in + B.  The row groups of a warp combine their maps by
+//      shuffles into in-warp prefixes, and the warp's total map goes to
+//      shared memory.
 //   3. The look-back warp, from the CTA's start, polls the records of the
 //      kLookbackDepth tiles before this one along T (their maps, AGG) and the
 //      inclusive state (INCL) of the tile before those, composing them in that
-//      fixed order, so results are bit-reproducible; it composes and
-//      publishes this tile's map the moment the row maps are in, hands the
-//      carry to the row warps and publishes the inclusive state.  Records
-//      carry the launch's tag in every 64-bit word, so neither side needs a
-//      fence or a flag.  Every wait is bounded; on give-up an error bit is set
-//      and the tile continues.
-//   4. Phase 2: every thread composes the maps of the rows before its own,
-//      restarts its rows from the exact carry and writes the outputs straight
-//      to global memory (16-byte stores).
+//      fixed order, so results are bit-reproducible; it composes the warps'
+//      totals into this tile's map and publishes it the moment they are in,
+//      then walks the carry through the warp totals, leaving in shared memory
+//      the state entering each warp's rows, and publishes the inclusive
+//      state.  Records carry the launch's tag in every 64-bit word, so neither
+//      side needs a fence or a flag.  Every wait is bounded; on give-up an
+//      error bit is set and the tile continues.
+//   4. Phase 2: every thread takes its warp's entering state, applies its
+//      in-warp prefix, restarts its rows from there and writes the outputs
+//      straight to global memory (16-byte stores).
 // HBM traffic is the algorithmic minimum (inputs read once, outputs written
 // once) plus 32 bytes of look-back records per channel and tile (normally
 // L2-resident).  The same kernel also runs the sequence-parallel fix-up
@@ -51,7 +54,9 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_CHUNKS = 8, WS_HDR_WORDS = 32 };
 enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
 
-constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst case
+// look-back polls before a wait gives up (each poll is an L2 round trip plus a
+// 64 ns sleep: a few seconds at most); need_test_set_lookback_polls lowers it
+constexpr uint32_t kLookbackPolls = 1u << 22;
 #ifndef NEED_LOOKBACK_DEPTH
 #define NEED_LOOKBACK_DEPTH 3
 #endif
@@ -59,6 +64,14 @@ constexpr uint32_t kLookbackPolls = 1u << 22;  // x ~64 ns sleeps: ~0.3 s worst 
 constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
 static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
+#ifndef NEED_P1_UNROLL
+#define NEED_P1_UNROLL 2
+#endif
+#ifndef NEED_P2_UNROLL
+#define NEED_P2_UNROLL 2
+#endif
+constexpr int kPhase1Unroll = NEED_P1_UNROLL;  // rows per unrolled step of phase 1
+constexpr int kPhase2Unroll = NEED_P2_UNROLL;  // and of phase 2
 // registers per thread the occupancy bound plans for
 #ifndef NEED_REG_BUDGET
 #define NEED_REG_BUDGET 112
@@ -82,6 +95,7 @@ struct ScanParams {
     float* tile_prod;
     float* tile_carry;
     uint32_t* hdr;
+    uint32_t lb_polls;  // look-back polls before a wait gives up
     // sequence-parallel fix-up (scan_kernel<K, true>): the local scan's
     // per-tile entering product and state, the carry entering the slice per
     // (sequence, channel) in .x, and the number of leading chunks to rewrite
@@ -335,8 +349,8 @@ struct ScanCfg {
     static constexpr int AGG_STRIDE = AGG_SLOT >= 0 ? (L * CBW * Ops<TS>::BYTES / NW) : 4 * 32 * 16;
     static_assert(AGG_SLOT < 0 || AGG_STRIDE >= 4 * 32 * 16, "a warp's rows must hold its map");
     static constexpr int OFF_AGG = slots_bytes();
-    static constexpr int OFF_CARRY = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
-    static constexpr int OFF_ROWDEC = OFF_CARRY + 8 * 32 * 8;  // (carry, prod) per channel
+    static constexpr int OFF_HIN = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
+    static constexpr int OFF_ROWDEC = OFF_HIN + NW * CBW * 4;  // fp32 state entering each warp's rows
     static constexpr int OFF_RESET = OFF_ROWDEC + (ROWDEC ? L * 4 : 0);
     static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
     static constexpr int SMEM = OFF_MISC + (NW + 1) * 8 + 16 + 128;  // mbarriers, misc, alignment slack
@@ -382,7 +396,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     unsigned char* s_agg = K::AGG_SLOT >= 0 ? slot_ptr<K>(base, K::AGG_SLOT) : base + K::OFF_AGG;
-    float2* s_cc = reinterpret_cast<float2*>(base + K::OFF_CARRY);  // (carry, prod) per channel
+    float* s_hin = reinterpret_cast<float*>(base + K::OFF_HIN);  // [NW][CBW] state entering each warp
     float* s_rowdec = reinterpret_cast<float*>(base + K::OFF_ROWDEC);
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
@@ -416,35 +430,98 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         const int t0 = chunk * L, c0 = cblk * CBW;
         const int nvalid = min(L, p.T - t0);  // rows of this tile inside T
 
+        // The look-back warp's layout: each lane owns NE = 8 / SS channels of one
+        // channel vector -- elements q*NE .. q*NE+NE-1 of vector v -- so all 32
+        // lanes work; NP = NE / 2 channel pairs.
+        constexpr int NE = 8 / SS, NP = NE / 2;
+        auto lbchan = [&](int k) { return chan<SPLIT>(q * NE + k, v); };  // channel of element k
+        // warp w's total map (the in-warp inclusive map of its last row group)
+        // for this lane's pair k
+        auto wtotal = [&](int w, int k) { return agg4(w)[(q * NP + k) * 32 + (SS - 1) * LPR + v]; };
+        // One pass over the warp totals in row order, each batch of WB warps'
+        // loads issued ahead of the chain: with `hand`, walks h (the carry entering the tile)
+        // through them, leaving in s_hin the state entering each warp's rows, and
+        // releases the row warps; with `comp`, composes this tile's map (TA, TB).
+        constexpr int WB = NP >= 4 ? 2 : 4;  // warps per batch of map loads (8 float4 in flight)
+        auto pass = [&](float (&h)[NE], float2 (&TA)[NP], float2 (&TB)[NP], bool hand, bool comp) {
+            if (comp) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    TA[k] = splat2(1.0f);
+                    TB[k] = splat2(0.0f);
+                }
+            }
+#pragma unroll
+            for (int w0 = 0; w0 < NW; w0 += WB) {
+                float4 m[WB][NP];
+#pragma unroll
+                for (int dw = 0; dw < WB; ++dw)
+#pragma unroll
+                    for (int k = 0; k < NP; ++k)
+                        if (w0 + dw < NW) m[dw][k] = wtotal(w0 + dw, k);
+#pragma unroll
+                for (int dw = 0; dw < WB; ++dw) {
+                    if (w0 + dw >= NW) break;
+                    if (hand) {
+                        float* dst = s_hin + (w0 + dw) * CBW;
+                        if constexpr (NE >= 4) {
+#pragma unroll
+                            for (int g = 0; g < NE / 4; ++g)
+                                *reinterpret_cast<float4*>(dst + lbchan(4 * g)) =
+                                    make_float4(h[4 * g], h[4 * g + 1], h[4 * g + 2], h[4 * g + 3]);
+                        } else {
+                            *reinterpret_cast<float2*>(dst + lbchan(0)) = make_float2(h[0], h[1]);
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+                        const float4 mm = m[dw][k];
+                        if (hand) {
+                            h[2 * k] = fmaf(mm.x, h[2 * k], mm.z);
+                            h[2 * k + 1] = fmaf(mm.y, h[2 * k + 1], mm.w);
+                        }
+                        if (comp) {
+                            TB[k] = ffma2(make_float2(mm.x, mm.y), TB[k], make_float2(mm.z, mm.w));
+                            TA[k] = fmul2(make_float2(mm.x, mm.y), TA[k]);
+                        }
+                    }
+                }
+            }
+            if (hand) {
+                __syncwarp();
+                named_arrive(1, K::NT);  // the row warps may run phase 2
+            }
+        };
+        auto el = [](const float2 (&x)[NP], int k) { return (k & 1) ? x[k >> 1].y : x[k >> 1].x; };
+
         if (FIX && warp == K::LB) {
             // ------------------------------------------------------ fix-up carry
             // The state entering this tile of the slice: the local scan's state plus
             // the carry entering the slice times the product of a before the tile.
             const int64_t ti0 = ((int64_t)seq * p.nchunks + chunk) * p.C;
-            if (lane < LPR) {
+            float h[NE];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int c = c0 + chan<SPLIT>(e, v);
-                    float h = 0.0f;
-                    if (c < p.C) h = fmaf(p.fix_tile_prod[ti0 + c], p.fix_carry[(int64_t)seq * p.C + c].x, p.fix_tile_carry[ti0 + c]);
-                    s_cc[e * LPR + v] = make_float2(h, 0.0f);
-                }
+            for (int k = 0; k < NE; ++k) {
+                const int c = c0 + lbchan(k);
+                h[k] = c < p.C ? fmaf(p.fix_tile_prod[ti0 + c], p.fix_carry[(int64_t)seq * p.C + c].x,
+                                      p.fix_tile_carry[ti0 + c])
+                               : 0.0f;
             }
-            __syncwarp();
-            named_arrive(1, K::NT);  // the row warps may run phase 2
+            if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+            float2 TA[NP], TB[NP];
+            pass(h, TA, TB, true, false);
         } else if (warp == K::LB) {
             // ------------------------------------------------------ look-back warp
             // It owns no rows.  From the start of the CTA it polls the predecessors'
             // records -- the maps of the up to kLookbackDepth tiles before this one
             // and the inclusive state of the tile before those, composed in that
             // fixed order, so results are bit-reproducible -- while the row warps
-            // load and run phase 1.  It releases the carry to the row warps (named
-            // barrier) as soon as the records are in, publishes this tile's map (AGG)
-            // the moment the row warps' maps are in -- never held back by a
-            // predecessor -- and then the inclusive state.  Records carry the launch
-            // epoch in every 64-bit word, so publishing needs no fence and a poll
-            // returns the data itself.  Lanes >= LPR duplicate lane % LPR and store nothing.
-            const bool act = lane < LPR;
+            // load and run phase 1.  When the warps' totals are in it composes this
+            // tile's map and publishes it (AGG) -- never held back by a predecessor
+            // -- and, with the carry known (usually by then), in the same pass hands
+            // the row warps their entering states (named barrier); then it publishes
+            // the inclusive state.  Records carry the launch epoch in every 64-bit
+            // word, so publishing needs no fence and a poll returns the data itself.
             uint32_t ep = 0;
             if (lane == 0) {
                 // Every CTA of a launch gets the same epoch: the low half counts CTAs
@@ -456,96 +533,69 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 ep = static_cast<uint32_t>(old >> 32);
             }
             const uint32_t tag = (__shfl_sync(0xffffffffu, ep, 0) & 0x7fffffffu) | 0x80000000u;
-            auto el = [](const float2 (&x)[4], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
-            float carry[8], carryP[8];
-            float2 TA[4], TB[4];  // this tile's map
+            float carry[NE], carryP[NE];
+            float2 TA[NP], TB[NP];  // this tile's map
             const int nagg = chunk == 0 ? 0 : min(chunk - 1, kLookbackDepth);
             bool pread = chunk == 0, mapped = false, agg_pub = chunk == 0;  // chunk 0 publishes no bare map
-            bool released = false;
+            bool handed = false;
             if (chunk == 0) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int c = c0 + chan<SPLIT>(e, v);
-                    carry[e] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
-                    carryP[e] = 1.0f;
+                for (int k = 0; k < NE; ++k) {
+                    const int c = c0 + lbchan(k);
+                    carry[k] = (p.h0 != nullptr && c < p.C) ? p.h0[(int64_t)seq * p.C + c] : 0.0f;
+                    carryP[k] = 1.0f;
                 }
             }
-            auto release = [&]() {
-                if (act) {
+            ulonglong2* const my_agg = p.agg + (int64_t)tile * CBW;
+            auto publish_agg = [&]() {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) s_cc[e * LPR + v] = make_float2(carry[e], carryP[e]);
-                }
-                __syncwarp();
-                named_arrive(1, K::NT);  // the row warps may run phase 2
-                released = true;
+                for (int k = 0; k < NE; ++k)
+                    st_relaxed_v2u64(&my_agg[(q * NE + k) * LPR + v], tagged(el(TA, k), tag), tagged(el(TB, k), tag));
+                agg_pub = true;
             };
-            auto compose_map = [&]() {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    TA[i] = splat2(1.0f);
-                    TB[i] = splat2(0.0f);
-                }
-                for (int w = 0; w < NW; ++w)
-                    for (int qq = 0; qq < SS; ++qq) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float4 m = agg4(w)[i * 32 + qq * LPR + v];
-                            TB[i] = ffma2(make_float2(m.x, m.y), TB[i], make_float2(m.z, m.w));
-                            TA[i] = fmul2(make_float2(m.x, m.y), TA[i]);
-                        }
-                    }
-            };
-            if (pread) release();
             bool ok = false;
-            for (uint32_t it = 0; it < kLookbackPolls; ++it) {
+            for (uint32_t it = 0; it < p.lb_polls; ++it) {
                 bool progressed = false;
                 if (!pread) {
                     bool valid = true;
-                    float accA[8], accB[8];
+                    float accA[NE], accB[NE];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        accA[e] = 1.0f;
-                        accB[e] = 0.0f;
+                    for (int k = 0; k < NE; ++k) {
+                        accA[k] = 1.0f;
+                        accB[k] = 0.0f;
                     }
                     for (int j = 0; j < nagg; ++j) {
                         const ulonglong2* src = p.agg + (int64_t)(tile - (j + 1) * p.nchains) * CBW;
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (A, B)
+                        for (int k = 0; k < NE; ++k) {
+                            const ulonglong2 m = ld_relaxed_v2u64(&src[(q * NE + k) * LPR + v]);  // (A, B)
                             valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                            accB[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                            accA[e] = accA[e] * untag(m.x);
+                            accB[k] = fmaf(accA[k], untag(m.y), accB[k]);
+                            accA[k] = accA[k] * untag(m.x);
                         }
                     }
                     const ulonglong2* src = p.incl + (int64_t)(tile - (nagg + 1) * p.nchains) * CBW;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const ulonglong2 m = ld_relaxed_v2u64(&src[e * LPR + v]);  // (prod, h)
+                    for (int k = 0; k < NE; ++k) {
+                        const ulonglong2 m = ld_relaxed_v2u64(&src[(q * NE + k) * LPR + v]);  // (prod, h)
                         valid &= tag_ok(m.x, tag) & tag_ok(m.y, tag);
-                        carry[e] = fmaf(accA[e], untag(m.y), accB[e]);
-                        carryP[e] = accA[e] * untag(m.x);
+                        carry[k] = fmaf(accA[k], untag(m.y), accB[k]);
+                        carryP[k] = accA[k] * untag(m.x);
                     }
-                    if (__all_sync(0xffffffffu, valid)) {
-                        pread = progressed = true;
-                        release();
-                    }
+                    if (__all_sync(0xffffffffu, valid)) pread = progressed = true;
                 }
                 if (!mapped && __all_sync(0xffffffffu, mbar_test_wait(s_p1, par))) {
-                    compose_map();
+                    float h[NE];
+#pragma unroll
+                    for (int k = 0; k < NE; ++k) h[k] = carry[k];
+                    pass(h, TA, TB, pread, true);  // with the carry in, the hand-out rides along
+                    handed = pread;
                     mapped = progressed = true;
+                    if (!agg_pub) publish_agg();  // successors may compose this map before our carry is in
                 }
                 if (mapped && pread) {
                     ok = true;
                     break;
-                }
-                if (mapped && !agg_pub) {
-                    ulonglong2* my = p.agg + (int64_t)tile * CBW;
-                    if (act) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            st_relaxed_v2u64(&my[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
-                    }
-                    agg_pub = progressed = true;
                 }
                 if (!progressed && it >= 2) __nanosleep(64);
                 if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
@@ -554,48 +604,50 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 if (lane == 0) atomicOr(&p.hdr[WS_ERROR], ERR_LOOKBACK);
                 if (!pread) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        carry[e] = 0.0f;
-                        carryP[e] = 0.0f;
+                    for (int k = 0; k < NE; ++k) {
+                        carry[k] = 0.0f;
+                        carryP[k] = 0.0f;
                     }
                 }
-                if (!released) release();
                 if (!mapped) {
                     mbar_wait_bounded(s_p1, par, kTmaPolls);
-                    compose_map();
+                    float h[NE];
+                    pass(h, TA, TB, false, true);
                 }
+            }
+            if (!handed) {
+                float h[NE];
+#pragma unroll
+                for (int k = 0; k < NE; ++k) h[k] = carry[k];
+                pass(h, TA, TB, true, false);
             }
             // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
             // the final state, the slice summary and the per-tile products
-            float inclP[8], inclH[8];
+            float inclP[NE], inclH[NE];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                inclP[e] = el(TA, e) * carryP[e];
-                inclH[e] = fmaf(el(TA, e), carry[e], el(TB, e));
+            for (int k = 0; k < NE; ++k) {
+                inclP[k] = el(TA, k) * carryP[k];
+                inclH[k] = fmaf(el(TA, k), carry[k], el(TB, k));
             }
-            if (act) {
-                if (chunk + 1 < p.nchunks) {
-                    ulonglong2* ma = p.agg + (int64_t)tile * CBW;
-                    ulonglong2* mi = p.incl + (int64_t)tile * CBW;
+            if (chunk + 1 < p.nchunks) {
+                if (!agg_pub) publish_agg();
+                ulonglong2* mi = p.incl + (int64_t)tile * CBW;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        if (!agg_pub) st_relaxed_v2u64(&ma[e * LPR + v], tagged(el(TA, e), tag), tagged(el(TB, e), tag));
-                        st_relaxed_v2u64(&mi[e * LPR + v], tagged(inclP[e], tag), tagged(inclH[e], tag));
-                    }
-                }
+                for (int k = 0; k < NE; ++k)
+                    st_relaxed_v2u64(&mi[(q * NE + k) * LPR + v], tagged(inclP[k], tag), tagged(inclH[k], tag));
+            }
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int c = c0 + chan<SPLIT>(e, v);
-                    if (c < p.C) {
-                        const int64_t ti = ((int64_t)seq * p.nchunks + chunk) * p.C + c;
-                        if (p.tile_prod != nullptr) p.tile_prod[ti] = carryP[e];
-                        if (p.tile_carry != nullptr) p.tile_carry[ti] = carry[e];
-                        if (chunk + 1 == p.nchunks) {
-                            if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[e];
-                            if (p.summary != nullptr)
-                                reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
-                                    make_float2(inclP[e], inclH[e]);
-                        }
+            for (int k = 0; k < NE; ++k) {
+                const int c = c0 + lbchan(k);
+                if (c < p.C) {
+                    const int64_t ti = ((int64_t)seq * p.nchunks + chunk) * p.C + c;
+                    if (p.tile_prod != nullptr) p.tile_prod[ti] = carryP[k];
+                    if (p.tile_carry != nullptr) p.tile_carry[ti] = carry[k];
+                    if (chunk + 1 == p.nchunks) {
+                        if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = inclH[k];
+                        if (p.summary != nullptr)
+                            reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] =
+                                make_float2(inclP[k], inclH[k]);
                     }
                 }
             }
@@ -729,7 +781,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             A[i] = splat2(1.0f);
             B[i] = splat2(0.0f);
         }
-#pragma unroll 2
+#pragma unroll kPhase1Unroll
         for (int j = 0; j < rend; ++j) {  // rows past T act as the identity
             float2 a[4], b[4];
             gates(r0 + j, true, a, b);
@@ -739,35 +791,49 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 A[i] = fmul2(a[i], A[i]);
             }
         }
+        // ---------------------------------------------------------- in-warp prefix
+        // The row groups q of a warp hold consecutive rows: their inclusive maps
+        // (rows of groups 0..q) by a Kogge-Stone scan over shuffles, and the
+        // exclusive one (the rows before this thread's) from the group before.
+#pragma unroll
+        for (int d = 1; d < SS; d *= 2) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 oA = make_float2(__shfl_up_sync(0xffffffffu, A[i].x, d * LPR),
+                                              __shfl_up_sync(0xffffffffu, A[i].y, d * LPR));
+                const float2 oB = make_float2(__shfl_up_sync(0xffffffffu, B[i].x, d * LPR),
+                                              __shfl_up_sync(0xffffffffu, B[i].y, d * LPR));
+                if (q >= d) {
+                    B[i] = ffma2(A[i], oB, B[i]);
+                    A[i] = fmul2(A[i], oA);
+                }
+            }
+        }
+        float2 EA[4], EB[4];  // map of the warp's rows before this thread's rows
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 pA = make_float2(__shfl_up_sync(0xffffffffu, A[i].x, LPR), __shfl_up_sync(0xffffffffu, A[i].y, LPR));
+            const float2 pB = make_float2(__shfl_up_sync(0xffffffffu, B[i].x, LPR), __shfl_up_sync(0xffffffffu, B[i].y, LPR));
+            EA[i] = q > 0 ? pA : splat2(1.0f);
+            EB[i] = q > 0 ? pB : splat2(0.0f);
+        }
+        // every lane's inclusive map; the last group's is the warp total the look-back warp reads
         if constexpr (K::AGG_SLOT >= 0) __syncwarp();  // every lane is done with the slot rows the map overwrites
 #pragma unroll
         for (int i = 0; i < 4; ++i) agg4(warp)[i * 32 + lane] = make_float4(A[i].x, A[i].y, B[i].x, B[i].y);
         mbar_arrive(s_p1);
-        if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
-
-        // ---------------------------------------------------------- compose
-        float2 EA[4], EB[4];  // map of the rows before this thread's rows
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            EA[i] = splat2(1.0f);
-            EB[i] = splat2(0.0f);
-        }
-        for (int w = 0; w <= warp; ++w)
-            for (int qq = 0; qq < (w < warp ? SS : q); ++qq) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 m = agg4(w)[i * 32 + qq * LPR + v];
-                    EB[i] = ffma2(make_float2(m.x, m.y), EB[i], make_float2(m.z, m.w));
-                    EA[i] = fmul2(make_float2(m.x, m.y), EA[i]);
-                }
-            }
-        named_sync(1, K::NT);  // the look-back warp has put the carry in s_cc
+        named_sync(1, K::NT);  // the look-back warp has put this warp's entering state in s_hin
 
         // ---------------------------------------------------------- phase 2
         float2 h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            h[i] = ffma2(EA[i], make_float2(s_cc[(2 * i) * LPR + v].x, s_cc[(2 * i + 1) * LPR + v].x), EB[i]);
+        {
+            const float4 h0 = *reinterpret_cast<const float4*>(s_hin + warp * CBW + chan<SPLIT>(0, v));
+            const float4 h1 = *reinterpret_cast<const float4*>(s_hin + warp * CBW + chan<SPLIT>(4, v));
+            h[0] = ffma2(EA[0], make_float2(h0.x, h0.y), EB[0]);
+            h[1] = ffma2(EA[1], make_float2(h0.z, h0.w), EB[1]);
+            h[2] = ffma2(EA[2], make_float2(h1.x, h1.y), EB[2]);
+            h[3] = ffma2(EA[3], make_float2(h1.z, h1.w), EB[3]);
+        }
         const bool ok0 = c0 + chan<SPLIT>(0, v) < p.C;
         const bool ok1 = c0 + chan<SPLIT>(4, v) < p.C;
         const int64_t ostep = REV ? -p.ost : p.ost;  // REV: rows are written in decreasing t
@@ -810,7 +876,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 for (int i = 0; i < 4; ++i) o[i] = OS::mul(qp[i], o[i]);
             }
         };
-#pragma unroll 2
+#pragma unroll kPhase2Unroll
         for (int j = 0; j < rend; ++j, orow += ostep) {
             PS o[4];
             step(r0 + j, o);
