@@ -241,6 +241,14 @@ NEED_API size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t de
  * Synchronises `stream`. */
 NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream);
 
+/* Test hook, no counterpart in the reference: the number of look-back polls
+ * after which a scan's wait for a predecessor tile gives up (sets bit 0 of the
+ * workspace error word, takes a zero carry and lets the launch finish), for
+ * every scan launched afterwards in this process; 0 restores the default
+ * (2^22 polls, a few seconds).  Lets a test make a wait run out quickly
+ * without a fault. */
+NEED_API void need_test_set_lookback_polls(uint32_t polls);
+
 /* need_kernels.affine_recurrence_scan (need_kernels.py:229-264): args->form must be
  * NEED_FORM_AFFINE. */
 NEED_API int need_affine_recurrence_scan(const need_scan_args* args, need_stream_t stream);
@@ -394,6 +402,23 @@ typedef struct {
     void* y;               /* [total_k, C] output of each drafted token */
     void* states_k;        /* [total_k, C] state after each drafted token */
     int64_t head_dim;      /* RETENTION: channels per head (a multiple of 8 dividing C) */
+    /* SSD only, optional: the block's causal depthwise conv (need_core.py:6395-6414).
+     * With conv_k in 2..4, in[2] holds the raw u, and every drafted token first
+     * takes the conv step from its sequence's history and SiLU, in the model
+     * dtype: full = [hist, u]; u_conv = sum_j (full_j * w[c, j]) (each product
+     * rounded, the sum in fp32 in tap order, rounded) + bias (rounded);
+     * hist := full[1:]; u_act = silu(u_conv) (fp32, rounded).  conv_k = 0: in[2]
+     * is u_act and the conv fields are unused. */
+    int32_t conv_k;
+    const void* conv_weight; /* [C, conv_k] contiguous, in `dtype` (the fp32 weight cast as
+                                the reference casts it) */
+    const void* conv_bias;   /* optional [C] in `dtype` */
+    const void* conv_hist;   /* [nslots, C, conv_k - 1] in `dtype`: the raw u of each pool
+                                row's last conv_k - 1 tokens, oldest first (the reference's
+                                ssd_conv_hist); read only here */
+    void* conv_hist_k;       /* [total_k, C, conv_k - 1]: the history after each drafted
+                                token; commit it with need_commit_states over rows of
+                                C * (conv_k - 1) elements */
 } need_verify_args;
 
 /* k_i one-token steps per sequence from its pooled state, in the model dtype's
@@ -403,7 +428,9 @@ typedef struct {
 NEED_API int need_ragged_verify(const need_verify_args* args, need_stream_t stream);
 
 /* states[slot[i]] := states_k[cu_k[i] + accept_len[i] - 1] when accept_len[i] > 0;
- * accept_len[i] must lie in [0, cu_k[i+1] - cu_k[i]] (clamped on device). */
+ * accept_len[i] must lie in [0, cu_k[i+1] - cu_k[i]] (clamped on device).  Rows
+ * are C elements; the SSD conv history commits with the same call over rows of
+ * C * (conv_k - 1) elements (conv_hist, conv_hist_k). */
 NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* states,
                        const int32_t* slot, const void* states_k, const int32_t* cu_k,
                        const int32_t* accept_len, need_stream_t stream);

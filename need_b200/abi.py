@@ -47,6 +47,8 @@ class NeedVerifyArgs(Structure):
         ("states", c_void_p), ("slot", c_void_p), ("cu_k", c_void_p), ("total_k", c_int64),
         ("in_", c_void_p * 5), ("d_skip", c_void_p), ("dt_min", c_double), ("dt_max", c_double),
         ("y", c_void_p), ("states_k", c_void_p), ("head_dim", c_int64),
+        ("conv_k", c_int32), ("conv_weight", c_void_p), ("conv_bias", c_void_p),
+        ("conv_hist", c_void_p), ("conv_hist_k", c_void_p),
     ]
 
 
@@ -111,6 +113,7 @@ SIGNATURES = {
     "need_scan_chunk_len": (c_int64, [c_int32, c_int32, c_int32, c_int32]),
     "need_scan_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int64, c_int64, c_int64, c_int64]),
     "need_workspace_error": (c_int32, [c_void_p, POINTER(c_uint32), c_void_p]),
+    "need_test_set_lookback_polls": (None, [c_uint32]),
     "need_affine_recurrence_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),

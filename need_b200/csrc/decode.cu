@@ -9,6 +9,11 @@
 // accepted prefix (the reference keeps the accepted tokens, generate.py:1078-1083,
 // and recomputes its whole context on the next verify, generate.py:909-913).
 //
+// The SSD form optionally runs the block's causal depthwise conv per drafted
+// token (need_core.py:6395-6414, _stream_depthwise_conv1d_step and SiLU) from
+// each sequence's conv history, and records the history after every token so
+// that a commit can keep it at the accepted prefix together with the state.
+//
 // One thread owns 8 channels of one sequence; a sequence's drafted tokens are
 // processed four at a time with all their loads issued before the dependent
 // arithmetic.  Both kernels are latency-bound (a decode step moves ~12 MB at
@@ -35,6 +40,12 @@ struct VerifyParams {
     void* y;
     void* states_k;
     int64_t H, head_dim;  // RETENTION: in[0] is the decay per (token, head) [sum k, H]
+    // SSD with the conv step: weight [C, K], bias [C] or null, history [nslots, C, K-1]
+    // (read) and after every drafted token [total_k, C, K-1] (written)
+    const void* conv_w;
+    const void* conv_b;
+    const void* conv_hist;
+    void* conv_hist_k;
 };
 
 template <typename T>
@@ -69,10 +80,31 @@ struct Vec8 {
     }
 };
 
-template <typename T, int FORM>
+// x / (1 + exp(-x)) in fp32, rounded to T: SiLU at the reference's rounding
+// points (the 16-bit paths use the hardware exp2 approximation, a few ulp)
+template <typename T>
+__device__ __forceinline__ float silu_rounded(float x) {
+    float d;
+    if constexpr (Ops<T>::BYTES == 4) d = __fadd_rn(1.0f, expf(-x));
+    else d = __fadd_rn(1.0f, exp_approx(-x));
+    const float r = __fdiv_rn(x, d);
+    if constexpr (Ops<T>::BYTES == 4) return r;
+    else return to_f(Ops<T>::pack(r, r).x);
+}
+
+template <typename T>
+__device__ __forceinline__ float rnd_to(float x) {
+    if constexpr (Ops<T>::BYTES == 4) return x;
+    else return to_f(Ops<T>::pack(x, x).x);
+}
+
+// KC: conv taps of the SSD form's conv step (0: in[2] is already u_act)
+template <typename T, int FORM, int KC = 0>
 __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
     using O = Ops<T>;
     using P = typename O::P;
+    constexpr int KH = KC > 1 ? KC - 1 : 1;  // history taps kept per channel
+    constexpr int TB = KC > 0 ? 2 : 4;       // drafted tokens loaded together (fewer with the conv state)
     // streamed [C] inputs: GATED z, g, x; SSD dt, bg, u, cg, og; RETENTION k, v, q (in[1..3])
     constexpr int NIN = FORM == FORM_SSD ? 5 : 3;
     constexpr int IN0 = FORM == FORM_RETENTION ? 1 : 0;
@@ -89,11 +121,25 @@ __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
         for (int q = 0; q < 4; ++q) dsk[q] = O::pack(p.dskip[c + 2 * q], p.dskip[c + 2 * q + 1]);
     }
     const int64_t head = FORM == FORM_RETENTION ? c / p.head_dim : 0;  // a thread's 8 channels share a head
-    for (int64_t j0 = kb; j0 < ke; j0 += 4) {
-        P x[4][NIN][4];
-        T dh[4];
+    // conv step state: this thread's 8 channels' weights, bias and history
+    float cw[8][KC > 0 ? KC : 1], cb[8], hist[8][KH];
+    if constexpr (KC > 0) {
+        const T* w = static_cast<const T*>(p.conv_w) + c * KC;
+        const T* hs = static_cast<const T*>(p.conv_hist) + (row * p.C + c) * (KC - 1);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int e = 0; e < 8; ++e) {
+            cb[e] = p.conv_b != nullptr ? to_f(static_cast<const T*>(p.conv_b)[c + e]) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < KC; ++j) cw[e][j] = to_f(w[e * KC + j]);
+#pragma unroll
+            for (int j = 0; j < KC - 1; ++j) hist[e][j] = to_f(hs[e * (KC - 1) + j]);
+        }
+    }
+    for (int64_t j0 = kb; j0 < ke; j0 += TB) {
+        P x[TB][NIN][4];
+        T dh[TB];
+#pragma unroll
+        for (int u = 0; u < TB; ++u)
             if (j0 + u < ke) {
 #pragma unroll
                 for (int k = 0; k < NIN; ++k)
@@ -101,7 +147,7 @@ __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
                 if constexpr (FORM == FORM_RETENTION) dh[u] = reinterpret_cast<const T*>(p.in[0])[(j0 + u) * p.H + head];
             }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < TB; ++u) {
             if (j0 + u >= ke) break;
             P yo[4];
             if constexpr (FORM == FORM_RETENTION) {
@@ -115,6 +161,35 @@ __global__ void __launch_bounds__(128) verify_kernel(const VerifyParams p) {
                     yo[q] = O::mul(x[u][2][q], st[q]);
                 }
             } else {
+                if constexpr (KC > 0) {
+                    // need_core.py:6395-6409, :6413-6414: u_act = silu(conv step), in[2] raw u
+                    T* hk = static_cast<T*>(p.conv_hist_k) + ((j0 + u) * p.C + c) * (KC - 1);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 ur = O::unpack(x[u][2][q]);
+                        float ua[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int e = 2 * q + h;
+                            const float un = h ? ur.y : ur.x;
+                            float acc = 0.0f;
+#pragma unroll
+                            for (int j = 0; j < KC; ++j)
+                                acc = __fadd_rn(acc, rnd_to<T>(__fmul_rn(j < KC - 1 ? hist[e][j] : un, cw[e][j])));
+                            float uc = rnd_to<T>(acc);
+                            if (p.conv_b != nullptr) uc = rnd_to<T>(__fadd_rn(uc, cb[e]));
+#pragma unroll
+                            for (int j = 0; j + 1 < KC - 1; ++j) hist[e][j] = hist[e][j + 1];
+                            hist[e][KC - 2] = un;
+                            ua[h] = silu_rounded<T>(uc);
+                        }
+                        x[u][2][q] = O::pack(ua[0], ua[1]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+#pragma unroll
+                        for (int j = 0; j < KC - 1; ++j) hk[e * (KC - 1) + j] = O::pack(hist[e][j], 0.0f).x;
+                }
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const float2 f0 = O::unpack(x[u][0][q]);
@@ -177,9 +252,9 @@ int check_rows(int dtype, int64_t nseq, int64_t C) {
     return NEED_OK;
 }
 
-template <typename T, int FORM>
+template <typename T, int FORM, int KC = 0>
 int launch_verify(const VerifyParams& p, cudaStream_t s) {
-    verify_kernel<T, FORM><<<grid_for(p.nseq, p.C), 128, 0, s>>>(p);
+    verify_kernel<T, FORM, KC><<<grid_for(p.nseq, p.C), 128, 0, s>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? NEED_OK : cuda_fail(e, "verify_kernel launch");
 }
@@ -206,6 +281,13 @@ int need_ragged_verify(const need_verify_args* a, need_stream_t stream) {
     if (!aligned16(a->states) || !aligned16(a->y) || !aligned16(a->states_k))
         return fail(NEED_ERR_UNSUPPORTED, "states / y / states_k must be 16-byte aligned");
     if (a->form == NEED_FORM_SSD && !a->d_skip) return fail(NEED_ERR_INVALID, "d_skip is null");
+    const int kc = a->conv_k;
+    if (kc != 0) {
+        if (a->form != NEED_FORM_SSD) return fail(NEED_ERR_INVALID, "conv_k is for the SSD form only");
+        if (kc < 2 || kc > 4) return fail(NEED_ERR_UNSUPPORTED, "conv_k=%d must be 0 or 2..4", kc);
+        if (!a->conv_weight || !a->conv_hist || !a->conv_hist_k)
+            return fail(NEED_ERR_INVALID, "conv_weight, conv_hist and conv_hist_k are required with conv_k");
+    }
     VerifyParams p{};
     p.nseq = a->nseq;
     p.C = a->C;
@@ -220,12 +302,20 @@ int need_ragged_verify(const need_verify_args* a, need_stream_t stream) {
     p.states_k = a->states_k;
     p.head_dim = a->form == NEED_FORM_RETENTION ? a->head_dim : 8;
     p.H = a->C / p.head_dim;
+    p.conv_w = a->conv_weight;
+    p.conv_b = a->conv_bias;
+    p.conv_hist = a->conv_hist;
+    p.conv_hist_k = a->conv_hist_k;
     const cudaStream_t s = stream;
     int rc;
     auto by_form = [&](auto tag) {
         using T = decltype(tag);
+        if (a->form == NEED_FORM_SSD)
+            return kc == 2 ? launch_verify<T, FORM_SSD, 2>(p, s)
+                   : kc == 3 ? launch_verify<T, FORM_SSD, 3>(p, s)
+                   : kc == 4 ? launch_verify<T, FORM_SSD, 4>(p, s)
+                             : launch_verify<T, FORM_SSD>(p, s);
         return a->form == NEED_FORM_GATED ? launch_verify<T, FORM_GATED>(p, s)
-               : a->form == NEED_FORM_SSD ? launch_verify<T, FORM_SSD>(p, s)
                                           : launch_verify<T, FORM_RETENTION>(p, s);
     };
     if (a->dtype == NEED_BF16) rc = by_form(__nv_bfloat16{});

@@ -755,7 +755,9 @@ def assoc_memory_step(q_raw: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor,
 def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str = "gated",
                   slot: Optional[torch.Tensor] = None, d_skip: Optional[torch.Tensor] = None,
                   dt_min: float = 0.001, dt_max: float = 0.2,
-                  out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+                  out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                  conv_hist: Optional[torch.Tensor] = None, conv_weight: Optional[torch.Tensor] = None,
+                  conv_bias: Optional[torch.Tensor] = None, conv_hist_out: Optional[torch.Tensor] = None):
     """k_i one-token recurrent steps for each sequence, from its pooled state.
 
     ``states`` [S, C] pool (not modified); ``cu_k`` int32 [N+1] offsets of each
@@ -767,6 +769,14 @@ def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str
     Arithmetic follows the reference's streaming steps (need_core.py:6420-6428,
     :1590-1592), every op in the state dtype.  Returns (y, states_k), both
     [sum k, C].
+
+    SSD with the block's depthwise conv: pass ``conv_hist`` [S, C, K-1] (the
+    reference's ``ssd_conv_hist`` per pool row, raw u of the last K-1 tokens,
+    oldest first) and ``conv_weight`` (the Conv1d weight, [C, 1, K] or [C, K];
+    ``conv_bias`` [C] optional).  ``inputs[2]`` is then the raw u, each drafted
+    token first takes the conv step and SiLU (need_core.py:6395-6414), and the
+    result is (y, states_k, hist_k) with hist_k [sum k, C, K-1] the history
+    after every token; commit it with ``commit_states(conv_hist, hist_k, ...)``.
     """
     _require_cuda(states, cu_k, *inputs)
     nseq = cu_k.numel() - 1
@@ -792,17 +802,43 @@ def ragged_verify(states: torch.Tensor, cu_k: torch.Tensor, inputs, *, form: str
         a.d_skip = ds.data_ptr()
     a.dt_min, a.dt_max = float(dt_min), float(dt_max)
     a.y, a.states_k = y.data_ptr(), sk.data_ptr()
+    keep = []
+    hk = None
+    if conv_hist is not None:
+        if form != "ssd" or conv_weight is None:
+            raise ValueError("conv_hist needs form='ssd' and conv_weight")
+        _require_cuda(conv_hist, conv_weight)
+        w = conv_weight.reshape(C, -1).to(states.dtype).contiguous()  # the reference casts it to the model dtype
+        K = w.shape[1]
+        if conv_hist.dtype != states.dtype or tuple(conv_hist.shape[1:]) != (C, K - 1) or not conv_hist.is_contiguous():
+            raise ValueError(f"conv_hist must be a contiguous [S, {C}, {K - 1}] {states.dtype} tensor")
+        hk = conv_hist_out if conv_hist_out is not None else torch.empty(
+            total, C, K - 1, dtype=states.dtype, device=states.device)
+        a.conv_k = K
+        a.conv_weight, a.conv_hist, a.conv_hist_k = w.data_ptr(), conv_hist.data_ptr(), hk.data_ptr()
+        keep.append(w)
+        if conv_bias is not None:
+            b = conv_bias.to(states.dtype).contiguous()
+            a.conv_bias = b.data_ptr()
+            keep.append(b)
     abi.check("need_ragged_verify", _lib().need_ragged_verify(ctypes.byref(a), _stream(states.device)))
-    return y, sk
+    del keep
+    return (y, sk) if hk is None else (y, sk, hk)
 
 
 def commit_states(states: torch.Tensor, states_k: torch.Tensor, cu_k: torch.Tensor,
                   accept_len: torch.Tensor, slot: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """In place: ``states[slot[i]] = states_k[cu_k[i] + L_i - 1]`` where ``L_i > 0``."""
+    """In place: ``states[slot[i]] = states_k[cu_k[i] + L_i - 1]`` where ``L_i > 0``.
+
+    A row is everything after the first dimension, so the SSD conv history
+    ([S, C, K-1] with its per-token [sum k, C, K-1]) commits the same way."""
     _require_cuda(states, states_k, cu_k, accept_len)
     nseq = cu_k.numel() - 1
+    width = states[0].numel() if states.dim() > 1 else 1
+    if not states.is_contiguous() or not states_k.is_contiguous() or states_k[0].numel() != width:
+        raise ValueError("states and states_k must be contiguous with rows of the same width")
     abi.check("need_commit_states", _lib().need_commit_states(
-        _DT[states.dtype], nseq, states.shape[1], states.data_ptr(),
+        _DT[states.dtype], nseq, width, states.data_ptr(),
         slot.data_ptr() if slot is not None else None, states_k.data_ptr(), cu_k.data_ptr(),
         accept_len.data_ptr(), _stream(states.device)))
     return states

@@ -51,8 +51,10 @@ def _lib():
         lib.ora_rms_norm.argtypes = [p, p, p, i64, i64, d, i32]
         lib.ora_assoc_memory.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i32, i32]
         lib.ora_assoc_step.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i32]
+        lib.ora_conv_step.argtypes = [p, p, p, p, p, i64, i64, i64, i32]
         for fn in ("ora_round", "ora_affine_scan", "ora_affine_scan_seq", "ora_gated_prep",
-                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory", "ora_assoc_step"):
+                   "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory", "ora_assoc_step",
+                   "ora_conv_step"):
             getattr(lib, fn).restype = None
         del f
         _LIB = lib
@@ -227,13 +229,36 @@ def stream_step(form: str, state, p0, p1, p2, p3=None, p4=None, dskip=None,
     return st, y
 
 
+def conv_step(hist, u, w, bias=None, *, dtype: str = "bf16"):
+    """One token of the SSD block's causal depthwise conv from its history,
+    then SiLU, in the model dtype (need_core.py:6395-6409, :6413-6414).
+
+    hist: [N, C, K-1] raw inputs of the previous K-1 tokens, oldest first;
+    u: [N, C] this token's raw input; w: [C, K] (fp32 parameter); bias: [C].
+    Returns (new_hist, u_act)."""
+    h = _f32(hist).copy()
+    n, c = _f32(u).shape
+    w = _f32(w).reshape(c, -1)
+    k = w.shape[1]
+    if h.shape != (n, c, k - 1):
+        raise ValueError(f"hist must be [{n}, {c}, {k - 1}]; got {h.shape}")
+    ua = np.empty((n, c), np.float32)
+    b = None if bias is None else _f32(bias).reshape(-1)
+    _lib().ora_conv_step(_ptr(h), _ptr(_f32(u)), _ptr(w), _ptr(b), _ptr(ua), n, c, k, MODE[dtype])
+    return h, ua
+
+
 def ragged_verify(form: str, states, cu_k, p0, p1, p2, p3=None, p4=None, dskip=None,
-                  dt_min: float = 0.001, dt_max: float = 0.2, *, dtype: str = "bf16"):
+                  dt_min: float = 0.001, dt_max: float = 0.2, *, dtype: str = "bf16",
+                  conv_hist=None, conv_w=None, conv_b=None):
     """k_i sequential stream steps per sequence from its own state.
 
     states: [S, C]; cu_k: [S+1] offsets into the packed [sum k, C] inputs.
     Returns (y [sum k, C], states_k [sum k, C]) where states_k[j] is the state
-    after packed token j.
+    after packed token j.  With ``conv_hist`` ([S, C, K-1]) and ``conv_w``
+    (form "ssd"), p2 holds the raw u: every token first takes the conv step
+    (``conv_step``) from its sequence's history, and a third result
+    [sum k, C, K-1] holds the history after every token.
     """
     states = _f32(states)
     cu = np.asarray(cu_k, dtype=np.int64)
@@ -242,14 +267,22 @@ def ragged_verify(form: str, states, cu_k, p0, p1, p2, p3=None, p4=None, dskip=N
     y = np.zeros((tot, c), np.float32)
     sk = np.zeros((tot, c), np.float32)
     ps = [None if p is None else _f32(p) for p in (p0, p1, p2, p3, p4)]
+    conv = conv_hist is not None
+    if conv:
+        hist_all = _f32(conv_hist)
+        hk = np.zeros((tot,) + hist_all.shape[1:], np.float32)
     for i in range(states.shape[0]):
         st = states[i:i + 1]
+        hist = hist_all[i:i + 1] if conv else None
         for j in range(int(cu[i]), int(cu[i + 1])):
             sl = [None if p is None else p[j:j + 1] for p in ps]
+            if conv:
+                hist, sl[2] = conv_step(hist, sl[2], conv_w, conv_b, dtype=dtype)
+                hk[j] = hist[0]
             st, yy = stream_step(form, st, *sl, dskip=dskip, dt_min=dt_min, dt_max=dt_max, dtype=dtype)
             y[j] = yy[0]
             sk[j] = st[0]
-    return y, sk
+    return (y, sk, hk) if conv else (y, sk)
 
 
 def commit_states(states, states_k, cu_k, accept_len):

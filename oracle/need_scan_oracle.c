@@ -34,6 +34,9 @@
  *   ora_stream_step      need_core.py:6420-6428 (_stream_retention_step) and
  *                        :1674-1685 (StructuredDualRetention.stream_step): one
  *                        token, state kept in the model dtype.
+ *   ora_conv_step        need_core.py:6395-6409 (_stream_depthwise_conv1d_step)
+ *                        and the SiLU of :6414: the SSD block's causal depthwise
+ *                        conv for one token from its history, in the model dtype.
  *
  * Extensions with no reference counterpart, defined by reduction to the above:
  *   resets   : decay[t] := 0 at a segment start (the update is unchanged);
@@ -519,6 +522,36 @@ ORA_API void ora_assoc_memory(const float* q_raw, const float* k_raw, const floa
  *                  y = (sigmoid(p3)*state + D*p2) * sigmoid(p4)
  * (need_core.py:6420-6428 and :1674-1685).  Every op rounds to `mode`;
  * state is [N, C] in the model dtype; p* are [N, C]. */
+/* One token of the SSD block's causal depthwise conv from its history, then
+ * SiLU, in the model dtype (need_core.py:6395-6409 and :6413-6414):
+ *   full = [hist_0 .. hist_{K-2}, u]          (oldest first)
+ *   u_conv = rnd(rnd(sum_j rnd(full_j * rnd(w[c, j]))) + rnd(b[c]))
+ *   hist := full[1:], u_act = rnd(u_conv / (1 + exp(-u_conv)))
+ * The tap products are separately rounded (a bf16 elementwise product), their
+ * sum is accumulated in fp32 in tap order and rounded once (torch's bf16
+ * sum), and SiLU is computed in fp32 (torch's CPU silu for 16-bit inputs).
+ * hist: [N, C, K-1] in/out; u, u_act: [N, C]; w: [C, K] fp32; bias: [C] or
+ * NULL. */
+ORA_API void ora_conv_step(float* hist, const float* u, const float* w, const float* bias, float* u_act,
+                           int64_t N, int64_t C, int64_t K, int mode) {
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t c = 0; c < C; ++c) {
+            float* h = hist + (n * C + c) * (K - 1);
+            const float un = u[n * C + c];
+            float acc = 0.0f;
+            for (int64_t j = 0; j < K; ++j) {
+                const float fj = j < K - 1 ? h[j] : un;
+                acc = acc + rnd(fj * rnd(w[c * K + j], mode), mode);
+            }
+            float uc = rnd(acc, mode);
+            if (bias) uc = rnd(uc + rnd(bias[c], mode), mode);
+            for (int64_t j = 0; j + 1 < K - 1; ++j) h[j] = h[j + 1];
+            if (K > 1) h[K - 2] = un;
+            const float e = expf(-uc);
+            u_act[n * C + c] = rnd(uc / (1.0f + e), mode);
+        }
+}
+
 ORA_API void ora_stream_step(int form, float* state, const float* p0, const float* p1,
                              const float* p2, const float* p3, const float* p4,
                              const float* dskip, float* y, int64_t N, int64_t C,

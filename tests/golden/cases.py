@@ -88,6 +88,9 @@ CASES = {
     # streaming one-token steps (ragged verify oracle)
     "stream_gated_bf16": dict(kind="stream", form="gated", seed=7, s=5, c=64, kmax=4, dtype="bf16"),
     "stream_ssd_bf16": dict(kind="stream", form="ssd", seed=8, s=5, c=64, kmax=4, dtype="bf16"),
+    # the SSD step with its depthwise conv (K=3): raw u in p2, the conv history
+    # [s, c, 2] each sequence carries, the conv weight [c, 3] and bias [c]
+    "stream_ssd_conv_bf16": dict(kind="stream", form="ssd_conv", seed=9, s=6, c=64, kmax=4, dtype="bf16"),
     # SelectiveRetention's step: decay per head (4 heads of 16 channels), k, v, q
     "stream_retention_bf16": dict(kind="stream", form="retention", seed=15, s=5, c=64, kmax=4, dtype="bf16"),
 }
@@ -169,6 +172,11 @@ def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
         for i in range(5):
             out[f"p{i}"] = cast(rs.standard_normal((tot, c)), dtype)
         out["dskip"] = (0.1 + 0.05 * rs.standard_normal(c)).astype(F32)
+        if form == "ssd_conv":
+            taps = 3
+            out["conv_w"] = (0.5 * rs.standard_normal((c, taps))).astype(F32)   # nn.Conv1d weight, fp32
+            out["conv_b"] = (0.1 * rs.standard_normal(c)).astype(F32)
+            out["hist"] = cast(rs.standard_normal((s, c, taps - 1)), dtype)     # raw u of the last 2 tokens
     return out
 
 

@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Generate golden fixtures by running the reference's own functions on CPU.
 
-Run in a container that has the reference checked out (default
-/root/reference; override with NEED_REFERENCE):
+The reference is imported from $NEED_REFERENCE, or else from the repository's
+git-ignored baseline/_ref (made by baseline/fetch_reference.sh):
 
+    baseline/fetch_reference.sh
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
 
 Each fixture ``<case>.npz`` holds the reference outputs for the seeded inputs
@@ -19,6 +20,8 @@ guards against drift).  Reference entry points used (file:line in NEED):
   HierarchicalMemory.stream_step (its associative memory)  need_core.py:2043-2080
   StructuredDualRetention.stream_step       need_core.py:1653-1686
   the one-token formula of                  need_core.py:6420-6428
+  NeedModel._stream_retention_step with     need_core.py:6410-6431 and its conv step
+    _stream_depthwise_conv1d_step           need_core.py:6395-6409
 
 The gated form (decay = sigmoid(z), update = (1 - decay)*(sigmoid(g)*x)) is the
 gate arithmetic of need_kernels.py:330-336 with a sigmoid decay; it is built
@@ -37,7 +40,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import cases  # noqa: E402
 
-REF = os.environ.get("NEED_REFERENCE", "/root/reference")
+REF = os.environ.get("NEED_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "baseline", "_ref")
+if not os.path.exists(os.path.join(REF, "need_kernels.py")):
+    sys.exit(f"no reference at {REF}: set NEED_REFERENCE or run baseline/fetch_reference.sh")
 sys.dont_write_bytecode = True
 sys.path.insert(0, REF)
 import need_core  # noqa: E402
@@ -149,6 +154,55 @@ def ref_stream(inp, form, dtype):
             ys[j] = y[0]
             sk[j] = rec[0]
     return {"y": npf(ys), "states_k": npf(sk)}
+
+
+class _Feed(torch.nn.Module):
+    """Stands in for a block's in_proj: returns the drafted token's five chunks."""
+
+    def __init__(self):
+        super().__init__()
+        self.chunks = None
+
+    def forward(self, x):
+        return self.chunks.view(1, 1, -1)
+
+
+def ref_stream_ssd_conv(inp, dtype):
+    """k_i drafted tokens per sequence through the reference's own
+    NeedModel._stream_retention_step (need_core.py:6410-6431): the depthwise
+    conv step from each sequence's history (need_core.py:6395-6409), SiLU, the
+    SSD recurrence and the output gates, all in the model dtype.  The block's
+    in_proj is replaced by the drafted token's chunks and its out_norm and out
+    by identities, so the step returns y itself."""
+    dt = TD[dtype]
+    c = inp["states"].shape[1]
+    taps = inp["conv_w"].shape[1]
+    cfg = need_core.NeedConfig(d_model=c, n_heads=2, n_layers=1, block_size=32, ssd_conv_kernel=taps,
+                               ssd_dt_min=0.001, ssd_dt_max=0.2)
+    mod = need_core.StructuredDualRetention(cfg).eval()
+    with torch.no_grad():
+        mod.dwconv.weight.copy_(torch.from_numpy(inp["conv_w"]).view(c, 1, taps))
+        mod.dwconv.bias.copy_(torch.from_numpy(inp["conv_b"]))
+        mod.D.copy_(torch.from_numpy(inp["dskip"]))
+    feed = _Feed()
+    mod.in_proj, mod.out_norm, mod.out = feed, torch.nn.Identity(), torch.nn.Identity()
+    step = need_core.NeedModel._stream_retention_step
+    holder = types.SimpleNamespace(
+        _stream_depthwise_conv1d_step=lambda conv, x, h: need_core.NeedModel._stream_depthwise_conv1d_step(
+            None, conv, x, h))
+    cu = inp["cu_k"]
+    tot = int(cu[-1])
+    ys = np.zeros((tot, c), np.float32)
+    sk = np.zeros((tot, c), np.float32)
+    hk = np.zeros((tot, c, taps - 1), np.float32)
+    for i in range(inp["states"].shape[0]):
+        state = {"ssd_state": T(inp["states"][i:i + 1], dtype), "ssd_conv_hist": T(inp["hist"][i:i + 1], dtype)}
+        for j in range(int(cu[i]), int(cu[i + 1])):
+            feed.chunks = torch.cat([T(inp[f"p{k}"][j:j + 1], dtype) for k in (2, 1, 3, 0, 4)], dim=-1)
+            with torch.no_grad():
+                y = step(holder, mod, torch.zeros(1, c, dtype=dt), state)
+            ys[j], sk[j], hk[j] = npf(y[0]), npf(state["ssd_state"][0]), npf(state["ssd_conv_hist"][0])
+    return {"y": ys, "states_k": sk, "hist_k": hk}
 
 
 def check_module_stream_step():
@@ -280,6 +334,8 @@ def main():
             out = ref_assoc(inp, dtype)
         elif kind == "assoc_step":
             out = ref_assoc_step(inp, dtype)
+        elif spec["form"] == "ssd_conv":
+            out = ref_stream_ssd_conv(inp, dtype)
         else:
             out = ref_stream(inp, spec["form"], dtype)
         if inp.get("x") is not None and inp["x"].size > 250_000:

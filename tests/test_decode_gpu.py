@@ -147,3 +147,41 @@ def test_selective_retention_verify_and_commit(cuda, dtype, mode):
     for i in range(N):
         want = want_sk[cu[i] + accept[i] - 1] if accept[i] > 0 else host(pool)[slot[i]]
         np.testing.assert_array_equal(got[slot[i]], want)
+
+
+def test_ssd_verify_with_conv_history_and_rollback(cuda):
+    """The SSD step with the block's depthwise conv (need_core.py:6395-6414):
+    y, the state and the conv history after every drafted token against the
+    fixture made by the reference's NeedModel._stream_retention_step, then a
+    commit that keeps state and history at each sequence's accepted prefix."""
+    name = "stream_ssd_conv_bf16"
+    inp = cases.make_inputs(name)
+    g = np.load(f"{cases.__file__.rsplit('/', 1)[0]}/{name}.npz")
+    bf = lambda k: torch.from_numpy(inp[k]).to(cuda).to(torch.bfloat16)  # noqa: E731
+    states, hist = bf("states"), bf("hist").contiguous()
+    cu = torch.from_numpy(inp["cu_k"].astype(np.int32)).to(cuda)
+    ins = tuple(bf(f"p{i}") for i in range(5))  # p2: the raw u
+    w = torch.from_numpy(inp["conv_w"]).to(cuda).view(-1, 1, 3)  # nn.Conv1d weight [C, 1, K], fp32
+    b = torch.from_numpy(inp["conv_b"]).to(cuda)
+    y, sk, hk = nk.ragged_verify(states, cu, ins, form="ssd", d_skip=torch.from_numpy(inp["dskip"]).to(cuda),
+                                 conv_hist=hist, conv_weight=w, conv_bias=b)
+    np.testing.assert_array_equal(host(hk), g["hist_k"])  # the history holds raw inputs: exact
+    assert np.mean(host(y) == g["y"]) >= 0.99 and np.mean(host(sk) == g["states_k"]) >= 0.99
+    assert np.abs(host(y) - g["y"]).max() <= 2e-2 * np.abs(g["y"]).max()
+    assert np.abs(host(sk) - g["states_k"]).max() <= 2e-2 * np.abs(g["states_k"]).max()
+    assert torch.equal(hist, bf("hist")) and torch.equal(states, bf("states")), "the pools must not change"
+
+    # roll back: keep state and history at the accepted prefix (0 = unchanged)
+    ks = np.diff(inp["cu_k"])
+    accept = np.array([min(int(k), a) for k, a in zip(ks, [3, 0, 2, 1, 4, 0])], np.int32)
+    acc = torch.from_numpy(accept).to(cuda)
+    nk.commit_states(states, sk, cu, acc)
+    nk.commit_states(hist, hk, cu, acc)
+    for i, L in enumerate(accept):
+        if L == 0:
+            np.testing.assert_array_equal(host(states[i]), inp["states"][i])
+            np.testing.assert_array_equal(host(hist[i]), inp["hist"][i])
+        else:
+            j = int(inp["cu_k"][i]) + L - 1
+            np.testing.assert_array_equal(host(states[i]), host(sk[j]))
+            np.testing.assert_array_equal(host(hist[i]), g["hist_k"][j])

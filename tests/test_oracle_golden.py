@@ -187,3 +187,15 @@ def test_bf16_roundtrip_helpers():
     back = oracle.bf16_bits_to_f32(bits)
     assert np.array_equal(back, oracle.round_to(x, "bf16"))
     assert back[2] == 1.0  # tie rounds to even
+
+
+def test_stream_step_with_conv_history():
+    """The SSD step with its depthwise conv: each drafted token takes the conv
+    step from its sequence's history (need_core.py:6395-6409), SiLU, then the
+    recurrence; y, the state and the conv history after every token, bit for
+    bit against NeedModel._stream_retention_step."""
+    inp, g = load("stream_ssd_conv_bf16")
+    y, sk, hk = oracle.ragged_verify("ssd", inp["states"], inp["cu_k"], *[inp[f"p{k}"] for k in range(5)],
+                                     dskip=inp["dskip"], dtype="bf16", conv_hist=inp["hist"],
+                                     conv_w=inp["conv_w"], conv_b=inp["conv_b"])
+    assert np.array_equal(y, g["y"]) and np.array_equal(sk, g["states_k"]) and np.array_equal(hk, g["hist_k"])
