@@ -1,0 +1,128 @@
+"""NEED's model forward with every recurrent layer routed through the drop-in.
+
+The reference model (need_core.NeedModel, need_core.py:3984-4230) imports the
+kernel module by name (need_core.py:33-36) and calls it at run time: with the
+preset's retention_impl="ssd", StructuredDualRetention's ssd_scan under no_grad
+(need_core.py:1624-1629), once per layer, plus rms_norm and swiglu.  (The
+reference's own ssd_scan runs its torch path through affine_recurrence_scan,
+need_kernels.py:336-337; the drop-in's ssd_scan is one kernel.)  This test builds the
+~350M preset of config_for_size.model_config_for_params (d_model=832, 14
+layers, block_size raised to 2048 for 2048-token rows), seeded N(0, 0.02)
+weights from the model's own _init_weights, eval, and runs one forward over an
+8 x 2048 batch of token ids ~ U[0, vocab) in bf16 the way the reference runs
+inference (fp32 weights under torch.autocast(dtype=bfloat16), generate.py:1334),
+so the scans see bf16 streams, twice:
+
+* with the reference's own need_kernels on its torch path (Triton off: the
+  path whose rounding points the CUDA kernels follow), and
+* with need_b200.need_kernels bound in its place,
+
+and requires the logits to agree within the bf16 budget (max |diff| / max |ref|
+<= 2e-2) with all 14 ssd_scan calls made through libneed_scan.so.  The reference's Triton path (fp32 gate math) is run as well
+and its distance reported.  The reference model takes no reset mask, so no
+arm uses resets.  Both arms run with the config's image_2d_scan off: that
+module calls affine_recurrence_scan_torch directly (need_core.py:1769), not the
+kernel module, and under CUDA autocast it writes its bf16 result into a float32
+buffer (need_core.py:1779, :1820) and raises once a random image span is long
+enough to form a grid.
+
+The reference is imported from baseline/_ref (an unmodified copy made by
+baseline/fetch_reference.sh, git-ignored); without it the test is skipped.
+"""
+import os
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+B, T = 8, 2048
+
+
+def reference_modules():
+    if not os.path.exists(os.path.join(REF, "need_core.py")):
+        pytest.skip("baseline/_ref has no copy of the reference (run baseline/fetch_reference.sh)")
+    sys.dont_write_bytecode = True
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import config_for_size  # noqa: E402
+    import need_core  # noqa: E402
+    import need_kernels  # noqa: E402  (the reference's module of that name)
+    return need_core, need_kernels, config_for_size
+
+
+def build_model(need_core, config_for_size, dev):
+    cfg, _ = config_for_size.model_config_for_params(350_000_000, block_size=T)
+    cfg["image_2d_scan"] = False
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = need_core.NeedModel(need_core.NeedConfig(**cfg))
+    return model.eval(), cfg
+
+
+def forward_logits(model, ids):
+    with torch.no_grad(), torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        out = model(ids)
+    torch.cuda.synchronize()
+    return out[0].float()
+
+
+def rel(a, b):
+    return float((a - b).abs().max() / b.abs().max()), float((a - b).norm() / b.norm())
+
+
+def test_need_model_forward_through_the_drop_in(cuda):
+    need_core, ref_nk, config_for_size = reference_modules()
+    from need_b200 import need_kernels as nk
+
+    model, cfg = build_model(need_core, config_for_size, cuda)
+    assert (cfg["d_model"], cfg["n_layers"]) == (832, 14)
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    ids = torch.randint(0, model.cfg.vocab_size, (B, T), device=cuda, generator=gen)
+
+    saved_binding, saved_triton = need_core.need_kernels, ref_nk.HAS_TRITON
+    try:
+        # the reference's torch path
+        need_core.need_kernels = ref_nk
+        ref_nk.HAS_TRITON = False
+        want = forward_logits(model, ids)
+        # the reference's Triton path (informational)
+        ref_nk.HAS_TRITON = saved_triton
+        triton_logits = forward_logits(model, ids) if saved_triton else None
+
+        # the drop-in, counting the scan calls that reach the library
+        calls = {"ssd_scan": 0, "affine_recurrence_scan": 0}
+
+        class Counting:
+            def __getattr__(self, name):
+                fn = getattr(nk, name)
+                if name not in calls:
+                    return fn
+
+                def counted(*a, **k):
+                    calls[name] += 1
+                    return fn(*a, **k)
+                return counted
+
+        need_core.need_kernels = Counting()
+        got = forward_logits(model, ids)
+    finally:
+        need_core.need_kernels = saved_binding
+        ref_nk.HAS_TRITON = saved_triton
+
+    assert calls == {"ssd_scan": 14, "affine_recurrence_scan": 0}, calls
+    assert nk.workspace_error() == 0
+    assert torch.isfinite(got).all()
+    err, l2 = rel(got, want)
+    print(f"\nlogits vs the reference's torch path: max rel {err:.3e}, rel L2 {l2:.3e}")
+    if triton_logits is not None:
+        terr, tl2 = rel(got, triton_logits)
+        rerr, rl2 = rel(want, triton_logits)
+        print(f"logits vs the reference's Triton path: max rel {terr:.3e}, rel L2 {tl2:.3e} "
+              f"(the reference's own torch path vs its Triton path: {rerr:.3e}, {rl2:.3e})")
+    assert err <= BF16_TOL, f"logits differ from the reference's: max rel {err}"
