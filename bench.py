@@ -199,8 +199,8 @@ def workload_config():
                         "x~N(0,1), decay logits~N(4,1), input-gate logits~N(0,1)",
             "B": B, "T": T, "H": H, "D": D, "parallelism": "batch-sharded replicas (no collective)",
             "l2": "inputs 403 MB per launch > 126 MB L2: no flush between steps",
-            "timing": "device time (CUDA events) of CUDA-graph replays of the public gated_scan call; "
-                      "e2e runs the call from the host every step"}
+            "timing": "device time (CUDA events) of back-to-back calls of the public gated_scan API on "
+                      "resident inputs; e2e adds the host copies of every step's inputs and outputs"}
 
 
 # ------------------------------------------------------------------ our arm
@@ -262,26 +262,18 @@ def main():
             step()
         torch.cuda.synchronize()
 
-    # The timed steps replay the public call from a CUDA graph: every step
-    # launches the full scan over the same resident inputs, and the host's
-    # per-call work (Python, argument checks, tensor-map encoding) cannot leave
-    # the GPU idle between steps.  The end-to-end number below keeps the host path.
-    side_stream = torch.cuda.Stream(dev)
-    side_stream.wait_stream(stream)
-    with torch.cuda.stream(side_stream):
-        step()
-    stream.wait_stream(side_stream)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    for _ in range(3):
-        graph.replay()
+    # The timed steps are calls of the public API, each a full scan over the
+    # same resident inputs.  The host's per-call work (argument checks,
+    # tensor-map encoding) takes a fraction of a launch, so the stream stays
+    # ahead of the GPU and only the first call's host time is exposed.
+    # (Replaying a one-kernel CUDA graph per step was measured ~8 us slower per
+    # step on B200: graph-launch overhead between back-to-back kernels.)
     K = args.steps
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
     barrier()
     ev[0].record(stream)
     for i in range(K):
-        graph.replay()
+        step()
         ev[i + 1].record(stream)
     barrier()
     clocks = sampler.stop() if not args.profile else None

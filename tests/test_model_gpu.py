@@ -17,8 +17,11 @@ so the scans see bf16 streams, twice:
   path whose rounding points the CUDA kernels follow), and
 * with need_b200.need_kernels bound in its place,
 
-and requires the logits to agree within the bf16 budget (max |diff| / max |ref|
-<= 2e-2) with all 14 ssd_scan calls made through libneed_scan.so.  The reference's Triton path (fp32 gate math) is run as well
+and requires all 14 ssd_scan calls to go through libneed_scan.so, each call's
+output to agree with the reference's torch-path ssd_scan on that call's own
+inputs within the bf16 budget (max |diff| / max |ref| <= 2e-2), and the logits,
+where the 14 layers compound the gates' last-bit roundings, to agree within
+the same budget.  The reference's Triton path (fp32 gate math) is run as well
 and its distance reported.  The reference model takes no reset mask, so no
 arm uses resets.  Both arms run with the config's image_2d_scan off: that
 module calls affine_recurrence_scan_torch directly (need_core.py:1769), not the
@@ -95,8 +98,10 @@ def test_need_model_forward_through_the_drop_in(cuda):
         ref_nk.HAS_TRITON = saved_triton
         triton_logits = forward_logits(model, ids) if saved_triton else None
 
-        # the drop-in, counting the scan calls that reach the library
+        # the drop-in, counting the scan calls that reach the library and
+        # keeping each ssd_scan call's inputs and output
         calls = {"ssd_scan": 0, "affine_recurrence_scan": 0}
+        recorded = []
 
         class Counting:
             def __getattr__(self, name):
@@ -106,7 +111,10 @@ def test_need_model_forward_through_the_drop_in(cuda):
 
                 def counted(*a, **k):
                     calls[name] += 1
-                    return fn(*a, **k)
+                    y = fn(*a, **k)
+                    if name == "ssd_scan":
+                        recorded.append(([t.clone() if isinstance(t, torch.Tensor) else t for t in a], y.clone()))
+                    return y
                 return counted
 
         need_core.need_kernels = Counting()
@@ -117,6 +125,19 @@ def test_need_model_forward_through_the_drop_in(cuda):
 
     assert calls == {"ssd_scan": 14, "affine_recurrence_scan": 0}, calls
     assert nk.workspace_error() == 0
+    # every layer's scan against the reference's torch path on the same inputs
+    ref_nk.HAS_TRITON = False
+    try:
+        worst = 0.0
+        for i, (args, y) in enumerate(recorded):
+            with torch.no_grad():
+                want_y = ref_nk.ssd_scan(*args)
+            e, _ = rel(y.float(), want_y.float())
+            worst = max(worst, e)
+            assert e <= BF16_TOL, f"layer {i}: ssd_scan max rel {e}"
+    finally:
+        ref_nk.HAS_TRITON = saved_triton
+    print(f"\nper-layer ssd_scan vs the reference's torch path: worst max rel {worst:.3e}")
     assert torch.isfinite(got).all()
     err, l2 = rel(got, want)
     print(f"\nlogits vs the reference's torch path: max rel {err:.3e}, rel L2 {l2:.3e}")
