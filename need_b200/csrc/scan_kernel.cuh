@@ -584,7 +584,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     }
                     if (__all_sync(0xffffffffu, valid)) pread = progressed = true;
                 }
-                if (!mapped && __all_sync(0xffffffffu, mbar_test_wait(s_p1, par))) {
+                // with the carry in, nothing else is polled: suspend on the barrier
+                // (try_wait wakes when the phase completes) instead of spinning
+                if (!mapped && __all_sync(0xffffffffu, pread ? mbar_try_wait(s_p1, par) : mbar_test_wait(s_p1, par))) {
                     float h[NE];
 #pragma unroll
                     for (int k = 0; k < NE; ++k) h[k] = carry[k];
@@ -597,7 +599,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     ok = true;
                     break;
                 }
-                if (!progressed && it >= 2) __nanosleep(64);
+                if (!progressed && !pread && it >= 2) __nanosleep(64);
                 if ((it & 1023u) == 1023u && ld_volatile_u32(&p.hdr[WS_ERROR]) != 0) break;  // fail fast
             }
             if (!ok) {
