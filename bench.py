@@ -351,6 +351,8 @@ def main():
         side["ssd_prologue"] = run_prologue(dev, nk, barrier, max_over_ranks)
         side["ssd_block"] = run_ssd_block(dev, nk, barrier, max_over_ranks)
         side["assoc_memory"] = run_assoc(dev, nk, barrier, max_over_ranks)
+        if world == 1:
+            side["reference_gpu"] = run_reference_gpu(dev, nk, workloads)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -359,6 +361,9 @@ def main():
         rate, secs = cpu_sample_rate(nthreads)
         cpu = {"value": rate, "unit": "tokens/s", "cores": nthreads, "kind": "port",
                "sample": cpu_sample_text(nthreads) + f"; median of 3 runs of {secs:.2f} s"}
+        ref_cpu = reference_cpu_torch(nthreads)
+        if ref_cpu is not None:
+            cpu["reference_torch_cpu"] = ref_cpu
 
     if rank == 0:
         line = {
@@ -385,6 +390,119 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_kernels():
+    """The reference's own need_kernels module from baseline/_ref (an unmodified
+    copy made by baseline/fetch_reference.sh), or None when it is not there."""
+    if not os.path.exists(os.path.join(REF_DIR, "need_kernels.py")):
+        return None
+    sys.dont_write_bytecode = True
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import need_kernels as ref_nk  # noqa: E402  (the reference's module of that name)
+    return ref_nk
+
+
+def run_reference_gpu(dev, nk, workloads):
+    """The reference's own GPU code for the same work, on this B200, beside this
+    repository's kernels (the reference publishes no numbers of its own):
+
+    * ssd_scan with its Triton kernel (need_kernels.py:119-144, launched at
+      :325-329) at NEED's 350M model shape (B=8, T=2048, C=832) and at the
+      prefill shape (B=16, T=4096, C=1024), bf16;
+    * the headline gated prefill (B=16, T=4096, C=1024 bf16, no resets: the
+      reference has none) the way the reference computes it on a GPU: the
+      gates as torch ops in bf16 (need_kernels.py:330-336 with a sigmoid
+      decay) and affine_recurrence_scan, which on CUDA takes torch's
+      associative_scan (need_kernels.py:245-262) or, when that raises, its
+      chunked torch scan (:177-226).
+
+    Device time with CUDA events, after a warm-up call (Triton compiles then)."""
+    import torch
+    ref_nk = reference_kernels()
+    if ref_nk is None:
+        return {"unavailable": "baseline/_ref holds no copy of the reference (run baseline/fetch_reference.sh)"}
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, k, warm=2):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / k
+
+    out = {"triton": bool(ref_nk.HAS_TRITON)}
+    g0 = torch.Generator(device=dev).manual_seed(23)
+    for name, (Bm, Tm, d) in (("ssd_scan_model_shape", (8, 2048, 832)), ("ssd_scan_prefill_shape", (16, 4096, 1024))):
+        xs = [torch.randn(Bm, Tm, d, device=dev, generator=g0).to(torch.bfloat16) for _ in range(5)]
+        dskip = torch.full((d,), 0.1, device=dev)
+        ref_ms = timed(lambda: ref_nk.ssd_scan(*xs, dskip, 0.001, 0.2), 10)
+        our_ms = timed(lambda: nk.ssd_scan(*xs, dskip, 0.001, 0.2), 20)
+        out[name] = {"workload": f"ssd_scan B={Bm}, T={Tm}, C={d} bf16",
+                     "reference_triton_us": 1e3 * ref_ms, "ours_us": 1e3 * our_ms, "speedup": ref_ms / our_ms}
+        del xs
+    w = workloads.gated_inputs(B, T, C, z_mean=4.0, dtype=torch.bfloat16, device=dev, seed=24, resets=None)
+    path = "associative_scan"
+    try:  # the same call the reference makes; it catches a failing associative_scan itself
+        scan = ref_nk._get_associative_scan()
+        if scan is None:
+            path = "chunked torch scan (no associative_scan in this torch)"
+        else:
+            a = torch.rand(2, 8, 4, device=dev)
+            scan(lambda l, r: (r[0] * l[0], r[1] + r[0] * l[1]), (a, a), dim=0)
+    except Exception as e:  # noqa: BLE001 -- reported, the reference falls back the same way
+        path = f"chunked torch scan (associative_scan raised {type(e).__name__})"
+
+    def reference_gated():
+        decay = torch.sigmoid(w.z)
+        update = (1.0 - decay) * (torch.sigmoid(w.g) * w.x)
+        return ref_nk.affine_recurrence_scan(decay, update, dim=1)
+
+    ref_ms = timed(reference_gated, 3, warm=1)
+    our_ms = timed(lambda: nk.gated_scan(w.x, w.z, w.g), 20)
+    out["gated_prefill"] = {"workload": "gated scan B=16, T=4096, C=1024 bf16, no resets",
+                            "reference_path": f"torch gate ops + affine_recurrence_scan ({path})",
+                            "reference_us": 1e3 * ref_ms, "ours_us": 1e3 * our_ms, "speedup": ref_ms / our_ms}
+    return out
+
+
+def reference_cpu_torch(nthreads: int):
+    """The reference's own CPU path for the headline workload, on the host
+    cores: the gates as torch ops in bf16 and affine_recurrence_scan on CPU
+    tensors (need_kernels.py:229-264 -> the chunked scan of :177-226); one
+    sequence of the prefill workload (1 x 4096 x 1024, no resets), median of 3."""
+    import torch
+    ref_nk = reference_kernels()
+    if ref_nk is None:
+        return None
+    torch.set_num_threads(nthreads)
+    g = torch.Generator().manual_seed(25)
+    x, z, gg = (torch.randn(1, T, C, generator=g).to(torch.bfloat16) for _ in range(3))
+    z = (z.float() + 4.0).to(torch.bfloat16)
+
+    def run():
+        decay = torch.sigmoid(z)
+        return ref_nk.affine_recurrence_scan(decay, (1.0 - decay) * (torch.sigmoid(gg) * x), dim=1)
+
+    run()
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": T / sec, "unit": "tokens/s", "cores": nthreads, "kind": "reference",
+            "sample": f"1 of the 16 sequences (1 x {T} tokens x {C} channels, no resets), the reference's "
+                      f"torch CPU path, median of 3 runs of {sec:.2f} s"}
 
 
 def run_sp(dev, world, rank, barrier, max_over_ranks, sp, workloads):
