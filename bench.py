@@ -199,8 +199,9 @@ def workload_config():
                         "x~N(0,1), decay logits~N(4,1), input-gate logits~N(0,1)",
             "B": B, "T": T, "H": H, "D": D, "parallelism": "batch-sharded replicas (no collective)",
             "l2": "inputs 403 MB per launch > 126 MB L2: no flush between steps",
-            "timing": "device time (CUDA events) of back-to-back calls of the public gated_scan API on "
-                      "resident inputs; e2e adds the host copies of every step's inputs and outputs"}
+            "timing": "device time (CUDA events) of K public gated_scan calls on resident inputs, captured "
+                      "in one CUDA graph; direct_calls_ms_per_step times them as back-to-back host calls; "
+                      "e2e adds the host copies of every step's inputs and outputs"}
 
 
 # ------------------------------------------------------------------ our arm
@@ -262,26 +263,44 @@ def main():
             step()
         torch.cuda.synchronize()
 
-    # The timed steps are calls of the public API, each a full scan over the
-    # same resident inputs.  The host's per-call work (argument checks,
-    # tensor-map encoding) takes a fraction of a launch, so the stream stays
-    # ahead of the GPU and only the first call's host time is exposed.
-    # (Replaying a one-kernel CUDA graph per step was measured ~8 us slower per
-    # step on B200: graph-launch overhead between back-to-back kernels.)
+    # The K timed steps are K calls of the public API captured in one CUDA
+    # graph: each is a full scan over the same resident inputs, and nothing but
+    # the kernels runs between them.  (Back-to-back direct calls are reported
+    # beside it: the host's per-call work then adds ~2-4 us of launch gap per
+    # step; a one-call graph per step added ~8 us.)
     K = args.steps
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    side_stream = torch.cuda.Stream(dev)
+    side_stream.wait_stream(stream)
+    with torch.cuda.stream(side_stream):
+        step()
+    stream.wait_stream(side_stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(K):
+            step()
+    graph.replay()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     barrier()
     ev[0].record(stream)
-    for i in range(K):
-        step()
-        ev[i + 1].record(stream)
+    graph.replay()
+    ev[1].record(stream)
     barrier()
-    clocks = sampler.stop() if not args.profile else None
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(K)]
-    elapsed_ms = max_over_ranks(ev[0].elapsed_time(ev[K]))
+    elapsed_ms = max_over_ranks(ev[0].elapsed_time(ev[1]))
     ms_step = elapsed_ms / K
     value = world * B * T / (ms_step / 1e3)
-    launch_ms = statistics.mean(per)
+    launch_ms = ev[0].elapsed_time(ev[1]) / K  # this rank's kernel, one launch per step
+    del graph
+    # the same K steps as back-to-back direct calls (host work between launches)
+    ed = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    barrier()
+    ed[0].record(stream)
+    for _ in range(K):
+        step()
+    ed[1].record(stream)
+    barrier()
+    direct_ms_step = max_over_ranks(ed[0].elapsed_time(ed[1])) / K
+    clocks = sampler.stop() if not args.profile else None
     peak, peak_kind = measured_peak()
     achieved = algorithmic_bytes() / (launch_ms / 1e3) / 1e9
 
@@ -368,7 +387,7 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "direct_calls_ms_per_step": direct_ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
