@@ -372,6 +372,7 @@ def main():
         side["assoc_memory"] = run_assoc(dev, nk, barrier, max_over_ranks)
         if world == 1:
             side["reference_gpu"] = run_reference_gpu(dev, nk, workloads)
+            side["need_model"] = run_need_model(dev, nk)
 
     # ---------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
@@ -492,6 +493,82 @@ def run_reference_gpu(dev, nk, workloads):
                             "reference_path": f"torch gate ops + affine_recurrence_scan ({path})",
                             "reference_us": 1e3 * ref_ms, "ours_us": 1e3 * our_ms, "speedup": ref_ms / our_ms}
     return out
+
+
+def run_need_model(dev, nk):
+    """NEED's own model at config 5: the ~350M preset (config_for_size.py,
+    block_size raised to 2048), seeded N(0, 0.02) weights, eval, bf16 autocast
+    (the reference's inference setting), one forward over 8 x 2048 random token
+    ids.  Timed three ways on this B200: with the reference's kernels (Triton),
+    with this repository's need_kernels bound in their place (every ssd_scan on
+    libneed_scan.so), and the time the drop-in's 14 scan calls take inside that
+    forward (CUDA events around each call)."""
+    import torch
+    ref_nk = reference_kernels()
+    if ref_nk is None:
+        return {"unavailable": "baseline/_ref holds no copy of the reference (run baseline/fetch_reference.sh)"}
+    import config_for_size  # noqa: E402  (from baseline/_ref)
+    import need_core  # noqa: E402
+    Bm, Tm = 8, 2048
+    cfg, _ = config_for_size.model_config_for_params(350_000_000, block_size=Tm)
+    cfg["image_2d_scan"] = False  # not on the kernel path; raises under CUDA autocast
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = need_core.NeedModel(need_core.NeedConfig(**cfg)).eval()
+    g0 = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(0, model.cfg.vocab_size, (Bm, Tm), device=dev, generator=g0)
+    stream = torch.cuda.current_stream(dev)
+
+    def forward():
+        with torch.no_grad(), torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            return model(ids)[0]
+
+    def timed(k=5):
+        forward()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            forward()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / k
+
+    saved = need_core.need_kernels
+    scan_events = []
+
+    class Timed:
+        def __getattr__(self, name):
+            fn = getattr(nk, name)
+            if name != "ssd_scan":
+                return fn
+
+            def wrapped(*a, **k):
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record(stream)
+                y = fn(*a, **k)
+                ev[1].record(stream)
+                scan_events.append(ev)
+                return y
+            return wrapped
+    try:
+        need_core.need_kernels = ref_nk
+        ref_ms = timed()
+        need_core.need_kernels = nk
+        our_ms = timed()
+        need_core.need_kernels = Timed()
+        forward()
+        torch.cuda.synchronize()
+        scan_ms = sum(a.elapsed_time(b) for a, b in scan_events)
+    finally:
+        need_core.need_kernels = saved
+    params = sum(p.numel() for p in model.parameters())
+    del model
+    return {"workload": f"NeedModel forward, {params / 1e6:.0f}M params (d_model={cfg['d_model']}, "
+                        f"{cfg['n_layers']} layers), B={Bm}, T={Tm}, bf16 autocast, random weights",
+            "reference_kernels_ms": ref_ms, "drop_in_ms": our_ms,
+            "drop_in_tokens_per_s": Bm * Tm / (our_ms / 1e3), "reference_tokens_per_s": Bm * Tm / (ref_ms / 1e3),
+            "scan_calls": len(scan_events), "scan_ms": scan_ms, "scan_share": scan_ms / our_ms}
 
 
 def reference_cpu_torch(nthreads: int):
