@@ -78,10 +78,10 @@ def test_sizes_and_chunk_lengths(lib):
     ntiles = 16 * (1024 // 128) * (4096 // L)  # 128-channel tiles
     assert ws == 128 + ntiles * 128 * 32  # header + tagged (A, B) and (prod, h) records per channel
     assert lib.need_scan_workspace_size(abi.FORM_GATED, 7, 7, 0, 1, 1, 1, 8) == 0  # unknown dtype
-    # SSD: 64-token tiles of 128 channels
+    # SSD: 64-token tiles of 64 channels (13 channel blocks for C=832)
     assert lib.need_scan_chunk_len(abi.FORM_SSD, abi.BF16, abi.BF16, 0) == 64
     ws = lib.need_scan_workspace_size(abi.FORM_SSD, abi.BF16, abi.BF16, 0, 8, 1, 2048, 832)
-    assert ws == 128 + 8 * 7 * (2048 // 64) * 128 * 32
+    assert ws == 128 + 8 * 13 * (2048 // 64) * 64 * 32
     assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
 
 
