@@ -439,16 +439,28 @@ NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* st
 /* Sequence parallelism (T sharded over ranks)                               */
 /* ------------------------------------------------------------------------ */
 
+/* Step 1 of the sequence-parallel gated scan on rank `rank`: the scan of this
+ * rank's T-slice from a zero state (form GATED; `summary`, `tile_prod` and
+ * `tile_carry` required), as need_gated_scan.  For rank > 0 the tiles that
+ * need_sp_fixup will rewrite -- those whose product of a before them exceeds
+ * 2^-24 on some channel -- are scanned for their maps but their outputs are
+ * not written: call need_sp_fixup on the same args before reading `out`.
+ * Replaces no reference interface (the reference has no distributed scan). */
+NEED_API int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t stream);
+
 /* After a rank scanned its T-slice from a zero state (with `summary`,
  * `tile_prod` and `tile_carry` requested) and gathered every rank's summary
  * into `all_summary` [nranks, nb*nh, C, 2], this applies the carry from ranks
- * < rank: carry = compose(summary[0..rank-1]); every tile whose entering
- * correction prod(a) * carry exceeds 2^-24 * |carry| on some channel is
+ * < rank: carry = compose(summary[0..rank-1]); the affected tiles are
  * re-scanned from the corrected fp32 state tile_carry + tile_prod * carry, with
- * the scan's own arithmetic, and its outputs rewritten; later tiles are left
- * as they are (their correction is below fp32 resolution of the carry).  It
- * also corrects h_final / summary when given.  `args` is the description the
- * local scan got (form AFFINE or GATED). */
+ * the scan's own arithmetic, and their outputs rewritten; later tiles are left
+ * as they are (their correction is below fp32 resolution of the carry).
+ * GATED: a tile is rewritten while tile_prod exceeds 2^-24 on some channel of
+ * it (the tiles need_sp_local_scan leaves unwritten).  AFFINE: while the
+ * correction is non-zero on some channel.  It also corrects h_final / summary
+ * when given.  `args` is the description the local scan got; for GATED the
+ * workspace must also hold 128 B + nb*nh*C*8 B + (chains + tiles) * 4 B, which
+ * need_scan_workspace_size always covers. */
 NEED_API int need_sp_fixup(const need_scan_args* args, const float* all_summary, int32_t nranks,
                   int32_t rank, need_stream_t stream);
 

@@ -131,6 +131,7 @@ SIGNATURES = {
     "need_ssd_conv_silu": (c_int32, [POINTER(NeedConvArgs), c_void_p]),
     "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
+    "need_sp_local_scan": (c_int32, [POINTER(NeedScanArgs), c_int32, c_void_p]),
     "need_sp_fixup": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_int32, c_void_p]),
 }
 

@@ -359,11 +359,25 @@ int run(const need_scan_args* a, int form, cudaStream_t s) {
 }  // namespace
 
 namespace need {
+// Tiles of the gated scan of `a`: channels per tile, chains (sequence x channel
+// block) and chunks.  0, or a status for a dtype without a kernel.
+int gated_geometry(const need_scan_args* a, int* cbw, int64_t* nchains, int64_t* nchunks) {
+    Plan pl;
+    if (!select_plan(NEED_FORM_GATED, a->dtype, a->dtype, 0, &pl))
+        return fail(NEED_ERR_UNSUPPORTED, "no kernel for dtype %d", a->dtype);
+    const Geometry g = geometry(pl, a->nb, a->nh, a->T, a->C);
+    *cbw = pl.CB;
+    *nchains = g.nchains;
+    *nchunks = g.nchunks;
+    return NEED_OK;
+}
+
 // The gated scan kernel in fix-up mode over the slice described by `a`, whose
-// tile_prod / tile_carry the local scan filled (sp.cu prepares fix_carry and
-// fix_chunks).  Writes only the rewritten tiles' outputs.
-int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_chunks,
-                       cudaStream_t stream) {
+// tile_prod / tile_carry the local scan filled: it rewrites the fix_count
+// tiles of fix_list (sp.cu prepares them and fix_carry).  Writes only the
+// rewritten tiles' outputs.
+int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_count,
+                       const uint32_t* fix_list, cudaStream_t stream) {
     Plan pl;
     ScanParams P;
     if (int rc = prepare(a, NEED_FORM_GATED, &pl, &P)) return rc;
@@ -371,7 +385,8 @@ int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const u
     P.fix_tile_prod = a->tile_prod;
     P.fix_tile_carry = a->tile_carry;
     P.fix_carry = fix_carry;
-    P.fix_chunks = fix_chunks;
+    P.fix_count = fix_count;
+    P.fix_list = fix_list;
     P.tile_prod = nullptr;
     P.tile_carry = nullptr;
     P.h_final = nullptr;
@@ -459,6 +474,19 @@ int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, 
 
 int need_recurrent_retention_scan(const need_scan_args* args, need_stream_t stream) {
     return run(args, NEED_FORM_RETENTION, stream);
+}
+
+int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t stream) {
+    if (args == nullptr) return fail(NEED_ERR_INVALID, "args is null");
+    if (rank < 0) return fail(NEED_ERR_INVALID, "rank %d", rank);
+    if (args->summary == nullptr || args->tile_prod == nullptr || args->tile_carry == nullptr)
+        return fail(NEED_ERR_INVALID, "the local scan of a slice needs summary, tile_prod and tile_carry");
+    Plan pl;
+    ScanParams P;
+    if (int rc = prepare(args, NEED_FORM_GATED, &pl, &P)) return rc;
+    P.sp_defer = rank > 0 ? 1 : 0;
+    if (int rc = pl.launch(P, stream)) return rc;
+    return ok();
 }
 
 int need_gated_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_GATED, stream); }

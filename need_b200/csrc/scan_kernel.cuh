@@ -50,8 +50,9 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 
 // workspace header words (uint32)
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
-// word 8: leading chunks a sequence-parallel fix-up rewrites
-enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_CHUNKS = 8, WS_HDR_WORDS = 32 };
+// word 8: tiles a sequence-parallel fix-up rewrites (entries of its list)
+// word 9: blocks of the fix-up's preparation that are done (the last builds the list)
+enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_COUNT = 8, WS_FIX_TICKET = 9, WS_HDR_WORDS = 32 };
 enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
 
 // look-back polls before a wait gives up (each poll is an L2 round trip plus a
@@ -64,6 +65,11 @@ constexpr uint32_t kLookbackPolls = 1u << 22;
 constexpr int kLookbackDepth = NEED_LOOKBACK_DEPTH;
 static_assert(kLookbackDepth >= 1 && kLookbackDepth <= 31, "look-back depth must be 1..31");
 constexpr uint32_t kTmaPolls = 1u << 22;
+// A sequence-parallel fix-up rewrites a tile while the product of a before it
+// (from the slice start) exceeds 2^-24 on some channel of the tile: past that
+// the carry entering the slice changes no state above fp32 resolution of the
+// carry.  The local scan (sp_defer) and the fix-up's preparation both use it.
+constexpr float kFixTau = 0x1p-24f;
 #ifndef NEED_P1_UNROLL
 #define NEED_P1_UNROLL 2
 #endif
@@ -96,13 +102,19 @@ struct ScanParams {
     float* tile_carry;
     uint32_t* hdr;
     uint32_t lb_polls;  // look-back polls before a wait gives up
+    // Local scan of a sequence-parallel slice after the first: tiles whose
+    // entering product of a exceeds kFixTau on some channel skip phase 2 (their
+    // outputs are written by the fix-up, which rewrites exactly those tiles).
+    int32_t sp_defer;
     // sequence-parallel fix-up (scan_kernel<K, true>): the local scan's
     // per-tile entering product and state, the carry entering the slice per
-    // (sequence, channel) in .x, and the number of leading chunks to rewrite
+    // (sequence, channel) in .x, and the list of tiles to rewrite (fix_count
+    // entries of fix_list, tile ids as the scan numbers them)
     const float* fix_tile_prod;
     const float* fix_tile_carry;
     const float2* fix_carry;
-    const uint32_t* fix_chunks;
+    const uint32_t* fix_count;
+    const uint32_t* fix_list;
     ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
 };
@@ -401,6 +413,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
+    uint32_t* s_defer = reinterpret_cast<uint32_t*>(s_p1 + 1);  // this tile skips phase 2 (sp_defer)
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -418,10 +431,15 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         fence_barrier_init();
     }
     __syncthreads();
-    const int ntl = FIX ? min(p.ntiles, static_cast<int>(*p.fix_chunks) * p.nchains) : p.ntiles;
+    const int ntl = FIX ? min(p.ntiles, static_cast<int>(*p.fix_count)) : p.ntiles;
     const int stride = FIX ? static_cast<int>(gridDim.x) : p.ntiles;
     uint32_t par = 0;  // mbarrier phase of this CTA's current tile
-    for (int tile = static_cast<int>(blockIdx.x); tile < ntl; tile += stride, par ^= 1u) {
+    // FIX: entry `item` of the list names the tile; the next entry is read one tile ahead
+    int next_tile = static_cast<int>(blockIdx.x);
+    if (FIX && next_tile < ntl) next_tile = static_cast<int>(p.fix_list[next_tile]);
+    for (int item = static_cast<int>(blockIdx.x); item < ntl; item += stride, par ^= 1u) {
+        const int tile = next_tile;
+        if (FIX && item + stride < ntl) next_tile = static_cast<int>(p.fix_list[item + stride]);
         const int chunk = tile / p.nchains;
         const int chain = tile - chunk * p.nchains;
         const int seq = chain / p.ncb;
@@ -508,6 +526,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                                : 0.0f;
             }
             if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
+            if (lane == 0) *s_defer = 0u;
             float2 TA[NP], TB[NP];
             pass(h, TA, TB, true, false);
         } else if (warp == K::LB) {
@@ -547,6 +566,18 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 }
             }
             ulonglong2* const my_agg = p.agg + (int64_t)tile * CBW;
+            // sp_defer: with the product before this tile known, does some channel
+            // still exceed kFixTau (then the fix-up writes the outputs)?  Written to
+            // s_defer before the row warps are released.
+            auto set_defer = [&]() {
+                bool d = false;
+                if (p.sp_defer) {
+#pragma unroll
+                    for (int k = 0; k < NE; ++k) d |= (c0 + lbchan(k) < p.C) && carryP[k] > kFixTau;
+                }
+                d = __any_sync(0xffffffffu, d);
+                if (lane == 0) *s_defer = d ? 1u : 0u;
+            };
             auto publish_agg = [&]() {
 #pragma unroll
                 for (int k = 0; k < NE; ++k)
@@ -590,6 +621,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                     float h[NE];
 #pragma unroll
                     for (int k = 0; k < NE; ++k) h[k] = carry[k];
+                    if (pread) set_defer();
                     pass(h, TA, TB, pread, true);  // with the carry in, the hand-out rides along
                     handed = pread;
                     mapped = progressed = true;
@@ -621,6 +653,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 float h[NE];
 #pragma unroll
                 for (int k = 0; k < NE; ++k) h[k] = carry[k];
+                set_defer();
                 pass(h, TA, TB, true, false);
             }
             // the inclusive state: for the successors kLookbackDepth + 1 chunks on,
@@ -827,6 +860,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         named_sync(1, K::NT);  // the look-back warp has put this warp's entering state in s_hin
 
         // ---------------------------------------------------------- phase 2
+        if (*s_defer == 0u) {  // else the sequence-parallel fix-up writes this tile
         float2 h[4];
         {
             const float4 h0 = *reinterpret_cast<const float4*>(s_hin + warp * CBW + chan<SPLIT>(0, v));
@@ -884,6 +918,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             step(r0 + j, o);
             Row8<TS, SPLIT>::stg(orow, v, o, ok0, ok1);
         }
+        }  // phase 2
         }  // row warps
         if constexpr (FIX) {  // the stage is refilled by the next tile's TMA
             fence_proxy_async_shared();

@@ -78,15 +78,16 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def workspace(dev: torch.device, nbytes: int, kind: str = "scan") -> torch.Tensor:
+def workspace(dev: torch.device, nbytes: int, kind: str = "scan", stream: Optional[int] = None) -> torch.Tensor:
     """Zero-initialised scratch, one per (device, stream, kind).
 
     ``"scan"`` holds the look-back records: the kernels leave it ready for the
     next launch on the same stream, so it is allocated (and zeroed) only when a
     larger one is needed, and nothing else writes into it.  ``"assoc"`` holds the
-    associative memory's feature-mapped q, k.
+    associative memory's feature-mapped q, k.  ``stream``: the raw handle of the
+    current stream, when the caller has already looked it up.
     """
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream, kind)
+    key = (dev.index, _stream(dev) if stream is None else stream, kind)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -139,16 +140,32 @@ def _fill_state(a: abi.NeedScanArgs, dev, nb: int, nh: int, C: int, seg_start, h
     return keep
 
 
+_ws_sizes = {}
+
+
+def _scan_workspace_size(lib, form: int, dtype: int, decay_dtype: int, rowdec: int, nb: int, nh: int, T: int,
+                         C: int) -> int:
+    """need_scan_workspace_size, remembered per argument tuple (it depends on nothing else)."""
+    key = (form, dtype, decay_dtype, rowdec, nb, nh, T, C)
+    n = _ws_sizes.get(key)
+    if n is None:
+        n = int(lib.need_scan_workspace_size(form, dtype, decay_dtype, rowdec, nb, nh, T, C))
+        if len(_ws_sizes) < 4096:
+            _ws_sizes[key] = n
+    return n
+
+
 def _launch(fn_name: str, a: abi.NeedScanArgs, dev: torch.device, rowdec: int = 0, extra: tuple = ()) -> None:
     """Runs ``fn_name(&a, *extra, stream)`` with this stream's workspace."""
     lib = _lib()
-    nbytes = lib.need_scan_workspace_size(a.form, a.dtype, a.decay_dtype, rowdec, a.nb, a.nh, a.T, a.C)
+    nbytes = _scan_workspace_size(lib, a.form, a.dtype, a.decay_dtype, rowdec, a.nb, a.nh, a.T, a.C)
     if nbytes == 0:
         raise abi.NeedError(fn_name, abi.ERR_UNSUPPORTED, "unsupported dtype combination")
-    ws = workspace(dev, nbytes)
+    stream = _stream(dev)
+    ws = workspace(dev, nbytes, stream=stream)
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
-    abi.check(fn_name, getattr(lib, fn_name)(ctypes.byref(a), *extra, _stream(dev)))
+    abi.check(fn_name, getattr(lib, fn_name)(ctypes.byref(a), *extra, stream))
 
 
 def _channel_ok(C: int, split: bool) -> bool:
@@ -469,7 +486,9 @@ def recurrent_retention_scan(q: torch.Tensor, kv: torch.Tensor, decay: torch.Ten
 def _bt_c_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
     if t.dim() != 3:
         raise ValueError(f"{name} must be [B, T, C]; got {tuple(t.shape)}")
-    if t.stride(-1) != 1 or t.data_ptr() % 16 != 0 or any((s * t.element_size()) % 16 for s in t.stride()[:2]):
+    sb, st, sc = t.stride()
+    es = t.element_size()
+    if sc != 1 or t.data_ptr() % 16 != 0 or (sb * es) % 16 or (st * es) % 16:
         t = t.contiguous()
     return t
 

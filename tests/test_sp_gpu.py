@@ -22,31 +22,59 @@ def host(t):
     return t.detach().float().cpu().numpy()
 
 
-def emulate(w, P):
+def emulate(w, P, defer=True):
+    """Ranks 0..P-1 on one device.  With ``defer`` each rank's local scan is
+    told its rank (ranks > 0 leave the tiles the fix-up rewrites unwritten),
+    into outputs filled with NaN beforehand, so an output neither the local
+    scan nor the fix-up writes stays NaN."""
     T = w.x.shape[1]
     bounds = [T * r // P for r in range(P + 1)]
     locs = []
     for r in range(P):
         sl = slice(bounds[r], bounds[r + 1])
         seg = None if w.seg is None else w.seg[:, sl].contiguous()
-        locs.append(sp.local_scan(w.x[:, sl], w.z[:, sl], w.g[:, sl], seg_start=seg))
+        out = torch.full_like(w.x[:, sl], float("nan"))
+        locs.append(sp.local_scan(w.x[:, sl], w.z[:, sl], w.g[:, sl], seg_start=seg, rank=r if defer else 0,
+                                  out=out))
     gathered = torch.stack([loc.summary for loc in locs])
     for r, loc in enumerate(locs):
         sp.fixup(loc, gathered, P, r)
-    return torch.cat([loc.out for loc in locs], dim=1), locs[-1].h_final
+    got = torch.cat([loc.out for loc in locs], dim=1)
+    assert not torch.isnan(got).any(), "an output of the slices was never written"
+    return got, locs[-1].h_final
 
 
+@pytest.mark.parametrize("defer", [True, False])
 @pytest.mark.parametrize("P", [2, 3, 8])
 @pytest.mark.parametrize("z_mean,resets", [(5.0, None), (2.0, "uniform"), (8.0, None)])
-def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets):
+def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets, defer):
     w = workloads.gated_inputs(2, 3000, 512, z_mean=z_mean, dtype=torch.bfloat16, device=cuda, seed=P,
                                resets=resets, seg_lo=100, seg_hi=900)
     whole, whole_f = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg, return_final_state=True)
-    got, got_f = emulate(w, P)
+    got, got_f = emulate(w, P, defer)
     g, wh = host(got), host(whole)
     assert np.abs(g - wh).max() <= 2e-2 * np.abs(wh).max()
     assert np.mean(g == wh) >= 0.99
     assert np.abs(host(got_f) - host(whole_f)).max() <= 1e-5 * np.abs(host(whole_f)).max() + 1e-6
+
+
+def test_deferred_tiles_are_the_rewritten_ones(cuda):
+    """A rank > 0 leaves unwritten exactly the leading tiles whose product of a
+    before them exceeds 2^-24 on some channel of the tile (128 channels x 128
+    tokens for bf16): the tiles the fix-up rewrites."""
+    w = workloads.gated_inputs(2, 4096, 512, z_mean=5.0, dtype=torch.bfloat16, device=cuda, seed=4, resets=None)
+    out = torch.full_like(w.x, float("nan"))
+    loc = sp.local_scan(w.x, w.z, w.g, rank=1, out=out)
+    torch.cuda.synchronize()
+    L, CB = 128, 128
+    B, T, C = w.x.shape
+    unwritten = torch.isnan(out).view(B, T // L, L, C // CB, CB).any(4).any(2)  # [B, chunk, channel block]
+    want = (loc.tile_prod.view(B, T // L, C // CB, CB) > 2.0 ** -24).any(3)
+    assert torch.equal(unwritten, want)
+    assert want[:, 0].all() and not want[:, -1].any()  # chunk 0 always, the last (of 32) never here
+    whole = nk.gated_scan(w.x, w.z, w.g)
+    keep = ~unwritten.repeat_interleave(L, 1).repeat_interleave(CB, 2)
+    assert torch.equal(out[keep], whole[keep])  # the written tiles need no correction: rank 1 of a 1-slice scan
 
 
 def test_emulated_ranks_fp32_exact_carry(cuda):
