@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--no-side", action="store_true", help="skip the sequence-parallel and decode side runs")
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "assoc", "prologue",
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "ssd-conv", "assoc", "prologue",
                                                "assoc-step", "assoc-long"],
                     default="prefill",
                     help="with --profile: which kernel's workload to run (one GPU)")
@@ -630,7 +630,9 @@ def profile_side_case(args, dev, nk, sp, workloads):
     verify + commit graph of 256 sequences x 4 drafted tokens; ``sp-fixup``
     scans the 8 slices of a B=1, T=65536, C=4096 sequence, stacks their
     summaries as the all-gather would and fixes up the last slice; ``ssd-norm``
-    runs the SSD scan with the RMSNorm kernel after it, ``assoc`` the
+    runs the SSD scan with the RMSNorm kernel after it, ``ssd-conv`` the scan
+    with the conv + SiLU folded in (inputs as in-projection chunks) and the
+    RMSNorm kernel after it, ``assoc`` the
     associative memory (feature map + tensor-core kernel) and ``prologue`` the
     conv + SiLU prologue, all at NEED's 350M shape (B=8, T=2048, d_model=832,
     memory_rank=64, bf16); ``assoc-step`` runs the memory's decode step for 256
@@ -652,6 +654,19 @@ def profile_side_case(args, dev, nk, sp, workloads):
         vs = torch.randn(Ns, d, device=dev, generator=g0).to(torch.bfloat16)
         for _ in range(max(args.warmup, 3) + args.steps):
             nk.assoc_memory_step(qs, ks, vs, st, dn)
+    elif args.profile_case == "ssd-conv":  # the conv folded into the scan, inputs as in-projection chunks
+        g0 = torch.Generator(device=dev).manual_seed(1)
+        Bm, Tm, d = 8, 2048, 832
+        proj = torch.randn(Bm, Tm, 5 * d, device=dev, generator=g0).to(torch.bfloat16)
+        u, bg, cg, dt, og = proj.chunk(5, dim=-1)
+        w = (torch.randn(d, 1, 3, device=dev, generator=g0) * 0.5).to(torch.bfloat16)
+        b = (torch.randn(d, device=dev, generator=g0) * 0.1).to(torch.bfloat16)
+        dskip, nw = torch.full((d,), 0.1, device=dev), torch.ones(d, device=dev)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk.ssd_conv_scan(u, bg, cg, dt, og, dskip, 0.001, 0.2, w, b, norm_weight=nw)
+        torch.cuda.synchronize()
+        if nk.workspace_error() != 0:
+            raise RuntimeError("a device-side wait gave up")
     elif args.profile_case in ("ssd-norm", "assoc"):
         g0 = torch.Generator(device=dev).manual_seed(1)
         Bm, Tm, d = 8, 2048, 832
@@ -933,6 +948,14 @@ def run_ssd_block(dev, nk, barrier, max_over_ranks):
     def block_fused():
         return F.linear(scan_norm(F.linear(x, w_in)), w_out)
 
+    def folded(p, norm=True):  # the conv folded into the scan's tile loads, then the out_norm kernel
+        u, bg, cg, dt, og = p.chunk(5, dim=-1)
+        return nk.ssd_conv_scan(u, bg, cg, dt, og, d_skip, 0.001, 0.2, conv_w, conv_b,
+                                norm_weight=norm_w if norm else None, eps=1e-6)
+
+    def block_folded():
+        return F.linear(folded(F.linear(x, w_in)), w_out)
+
     stream = torch.cuda.current_stream(dev)
 
     def graphed(fn):
@@ -963,12 +986,17 @@ def run_ssd_block(dev, nk, barrier, max_over_ranks):
     torch_norm_us = timed(graphed(lambda: F.rms_norm(kernels(proj), (d,), norm_w, 1e-6)))
     need_block_us = timed(graphed(block_fused))
     need_norm_us = timed(graphed(lambda: scan_norm(proj)))
+    fold_us = timed(graphed(lambda: folded(proj, norm=False)))
+    fold_norm_us = timed(graphed(lambda: folded(proj)))
+    fold_block_us = timed(graphed(block_folded))
     return {"workload": "StructuredDualRetention forward, B=8, T=2048, d_model=832, bf16, random weights",
             "block_us": block_us, "prologue_and_scan_us": kernels_us, "scan_share": kernels_us / block_us,
             "block_tokens_per_s": Bm * Tm / (block_us / 1e6),
             "out_norm": {"prologue_scan_then_torch_rms_norm_us": torch_norm_us,
                          "prologue_then_scan_and_rms_norm_kernel_us": need_norm_us,
-                         "block_with_rms_norm_kernel_us": need_block_us}}
+                         "block_with_rms_norm_kernel_us": need_block_us},
+            "conv_folded": {"conv_scan_us": fold_us, "conv_scan_rms_norm_us": fold_norm_us,
+                            "block_us": fold_block_us, "block_tokens_per_s": Bm * Tm / (fold_block_us / 1e6)}}
 
 
 def run_decode(dev, nk, workloads, barrier, max_over_ranks):

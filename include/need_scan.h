@@ -163,6 +163,14 @@ typedef struct {
     int64_t seg_stride_b, seg_stride_t;
 } need_conv_args;
 
+/* need_ssd_conv_scan: the SSD block's depthwise conv, applied inside the scan. */
+typedef struct {
+    int32_t K;              /* taps, 1..4 (NEED's ssd_conv_kernel) */
+    const void* weight;     /* [C, K] taps, oldest first, the stream dtype (as need_conv_args.weight) */
+    int64_t w_stride_c, w_stride_k;
+    const void* bias;       /* [C] or null, the stream dtype */
+} need_ssd_conv;
+
 /* need_rms_norm: RMSNorm over the C channels of nb x T rows. */
 typedef struct {
     int32_t dtype;          /* x and out: NEED_BF16, NEED_F16 or NEED_F32 */
@@ -302,6 +310,18 @@ NEED_API int need_rms_norm(const need_norm_args* args, need_stream_t stream);
  * Workspace as for need_ssd_scan. */
 NEED_API int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, int32_t weight_dtype,
                                     double eps, need_stream_t stream);
+
+/* need_ssd_scan with the block's input prologue folded in
+ * (need_core.py:1620-1629: u = F.silu(dwconv(u)[..., :T]), then ssd_scan):
+ * in[2] holds the RAW u (in_proj's u chunk).  Each tile applies the causal
+ * depthwise conv + SiLU to its rows as they land, with need_ssd_conv_silu's
+ * arithmetic and resets bit for bit, and the scan and its D*u epilogue use the
+ * result, so `out` equals need_ssd_conv_silu followed by need_ssd_scan without
+ * the intermediate round trip through HBM.  With norm_weight (non-null) the
+ * block's out_norm follows as in need_ssd_scan_rms_norm.  16-bit dtypes; nh == 1.
+ * Replaces need_core.py's dwconv + F.silu + need_kernels.ssd_scan sequence. */
+NEED_API int need_ssd_conv_scan(const need_scan_args* args, const need_ssd_conv* conv, const void* norm_weight,
+                                int32_t weight_dtype, double eps, need_stream_t stream);
 
 /* need_kernels.recurrent_retention_scan (need_kernels.py:342-345):
  * args->form == NEED_FORM_RETENTION. */

@@ -73,6 +73,12 @@ class NeedConvArgs(Structure):
     ]
 
 
+class NeedSsdConv(Structure):
+    _fields_ = [
+        ("K", c_int32), ("weight", c_void_p), ("w_stride_c", c_int64), ("w_stride_k", c_int64), ("bias", c_void_p),
+    ]
+
+
 class NeedNormArgs(Structure):
     _fields_ = [
         ("dtype", c_int32), ("weight_dtype", c_int32), ("nb", c_int64), ("T", c_int64), ("C", c_int64),
@@ -118,6 +124,8 @@ SIGNATURES = {
     "need_affine_recurrence_scan_backward": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan": (c_int32, [POINTER(NeedScanArgs), c_void_p]),
     "need_ssd_scan_rms_norm": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_double, c_void_p]),
+    "need_ssd_conv_scan": (c_int32, [POINTER(NeedScanArgs), POINTER(NeedSsdConv), c_void_p, c_int32, c_double,
+                                     c_void_p]),
     "need_rms_norm": (c_int32, [POINTER(NeedNormArgs), c_void_p]),
     "need_assoc_memory_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int32]),
     "need_assoc_memory": (c_int32, [POINTER(NeedAssocArgs), c_void_p]),

@@ -40,7 +40,6 @@ using GatedCfg = ScanCfg<FORM_GATED, T, T, false, sizeof(T) == 2 ? NEED_GATED16_
 // CTAs per SM) measured fastest of 9 shapes at NEED's model shape (B=8, T=2048,
 // C=832: 47.5 us against 56.2 us for 64 x 128 x 8 warps) and at B=16, T=4096,
 // C=1024 (190 against 213.7 us).
-template <typename T>
 #ifndef NEED_SSD16_L
 #define NEED_SSD16_L 64
 #endif
@@ -50,8 +49,15 @@ template <typename T>
 #ifndef NEED_SSD16_CB
 #define NEED_SSD16_CB 64
 #endif
+template <typename T>
 using SsdCfg = ScanCfg<FORM_SSD, T, T, false, sizeof(T) == 2 ? NEED_SSD16_L : 16, sizeof(T) == 2 ? NEED_SSD16_NW : 4,
                        sizeof(T) == 2 ? NEED_SSD16_CB : 256>;
+// The 16-bit SSD scan with the block's conv + SiLU folded into its tile loads.
+template <typename T, int KC>
+using SsdConvCfg = ScanCfg<FORM_SSD, T, T, false, NEED_SSD16_L, NEED_SSD16_NW, NEED_SSD16_CB, KC>;
+static_assert(SsdConvCfg<bf16, 3>::L == SsdCfg<bf16>::L && SsdConvCfg<bf16, 3>::CBW == SsdCfg<bf16>::CBW &&
+                  SsdConvCfg<bf16, 3>::R == SsdCfg<bf16>::R,
+              "the folded-conv scan shares the SSD plan's tiles, tensor maps and workspace");
 
 #ifndef NEED_AFF16_L
 #define NEED_AFF16_L 128
@@ -469,6 +475,50 @@ int need_ssd_scan_rms_norm(const need_scan_args* args, const void* norm_weight, 
                                args->out_stride_b, args->out_stride_t, args->nb, args->T, args->C, norm_weight,
                                weight_dtype, eps, stream))
         return rc;
+    return ok();
+}
+
+int need_ssd_conv_scan(const need_scan_args* args, const need_ssd_conv* conv, const void* norm_weight,
+                       int32_t weight_dtype, double eps, need_stream_t stream) {
+    if (args == nullptr || conv == nullptr) return fail(NEED_ERR_INVALID, "null argument");
+    if (args->dtype != NEED_BF16 && args->dtype != NEED_F16)
+        return fail(NEED_ERR_UNSUPPORTED, "the folded conv takes bf16 or f16 data");
+    if (conv->K < 1 || conv->K > kConvHalo + 1)
+        return fail(NEED_ERR_UNSUPPORTED, "K=%d taps (1..%d supported)", conv->K, kConvHalo + 1);
+    if (conv->weight == nullptr) return fail(NEED_ERR_INVALID, "conv weight is null");
+    if (args->nh != 1) return fail(NEED_ERR_UNSUPPORTED, "the folded conv takes nh == 1");
+    if (norm_weight != nullptr) {
+        if (weight_dtype != NEED_F32 && weight_dtype != args->dtype)
+            return fail(NEED_ERR_UNSUPPORTED, "norm weight dtype %d must be fp32 or the stream dtype %d",
+                        weight_dtype, args->dtype);
+        if (!(eps >= 0.0)) return fail(NEED_ERR_INVALID, "eps must be >= 0");
+    }
+    Plan pl;
+    ScanParams P;
+    if (int rc = prepare(args, NEED_FORM_SSD, &pl, &P)) return rc;
+    // the raw u rows before each warp's rows: a box of kConvHalo rows of in[2]
+    if (int rc = encode_view(&P.tm_halo, args->in[2], args->dtype, args->nb, args->nh, args->T, args->C, pl.CB,
+                             kConvHalo, 2))
+        return rc;
+    P.conv_w = conv->weight;
+    P.cwsc = conv->w_stride_c;
+    P.cwsk = conv->w_stride_k;
+    P.conv_b = conv->bias;
+    int rc = NEED_OK;
+    const bool b16 = args->dtype == NEED_BF16;
+    switch (conv->K) {  // the tap count is compiled in
+        case 1: rc = b16 ? launch_cfg<SsdConvCfg<bf16, 1>>(P, stream) : launch_cfg<SsdConvCfg<f16, 1>>(P, stream); break;
+        case 2: rc = b16 ? launch_cfg<SsdConvCfg<bf16, 2>>(P, stream) : launch_cfg<SsdConvCfg<f16, 2>>(P, stream); break;
+        case 3: rc = b16 ? launch_cfg<SsdConvCfg<bf16, 3>>(P, stream) : launch_cfg<SsdConvCfg<f16, 3>>(P, stream); break;
+        default: rc = b16 ? launch_cfg<SsdConvCfg<bf16, 4>>(P, stream) : launch_cfg<SsdConvCfg<f16, 4>>(P, stream); break;
+    }
+    if (rc) return rc;
+    if (norm_weight != nullptr) {
+        if (int r2 = rms_norm_rows(args->dtype, args->out, args->out_stride_b, args->out_stride_t, args->out,
+                                   args->out_stride_b, args->out_stride_t, args->nb, args->T, args->C, norm_weight,
+                                   weight_dtype, eps, stream))
+            return r2;
+    }
     return ok();
 }
 

@@ -70,6 +70,8 @@ constexpr uint32_t kTmaPolls = 1u << 22;
 // the carry entering the slice changes no state above fp32 resolution of the
 // carry.  The local scan (sp_defer) and the fix-up's preparation both use it.
 constexpr float kFixTau = 0x1p-24f;
+// Raw input rows a folded SSD conv sees before a warp's first row: up to 4 taps.
+constexpr int kConvHalo = 3;
 #ifndef NEED_P1_UNROLL
 #define NEED_P1_UNROLL 2
 #endif
@@ -79,12 +81,17 @@ constexpr float kFixTau = 0x1p-24f;
 constexpr int kPhase1Unroll = NEED_P1_UNROLL;  // rows per unrolled step of phase 1
 constexpr int kPhase2Unroll = NEED_P2_UNROLL;  // and of phase 2
 // registers per thread the occupancy bound plans for
+// resident CTAs per SM the folded-conv SSD scan is compiled for
+#ifndef NEED_CONV_MINB
+#define NEED_CONV_MINB 4
+#endif
 #ifndef NEED_REG_BUDGET
 #define NEED_REG_BUDGET 112
 #endif
 
 struct ScanParams {
     CUtensorMap tm[5];  // streamed inputs (64-byte aligned members)
+    CUtensorMap tm_halo;  // CONV: the raw u rows just before each warp's rows
     int32_t nb, nh, T, C;
     int32_t ncb, nchains, nchunks, ntiles;
     void* out;
@@ -102,6 +109,12 @@ struct ScanParams {
     float* tile_carry;
     uint32_t* hdr;
     uint32_t lb_polls;  // look-back polls before a wait gives up
+    // CONV: the SSD block's causal depthwise conv + SiLU applied to the raw u
+    // (in[2]) as it lands: weight [C, K::CONVK] (element strides cwsc, cwsk)
+    // and optional bias [C], both in the stream dtype
+    const void* conv_w;
+    int64_t cwsc, cwsk;
+    const void* conv_b;
     // Local scan of a sequence-parallel slice after the first: tiles whose
     // entering product of a exceeds kFixTau on some channel skip phase 2 (their
     // outputs are written by the fix-up, which rewrites exactly those tiles).
@@ -322,7 +335,7 @@ struct Row8 {
 // over channels (ROWDEC), tokens per tile L, row warps NW, channels per tile CBW.
 // A lane owns 8 channels; a row of a tile takes LPR = CBW/8 lanes, so a warp
 // works on SS = 32/LPR rows side by side.
-template <int FORM_, typename TS_, typename TD_, bool ROWDEC_, int L_, int NW_, int CBW_ = 256>
+template <int FORM_, typename TS_, typename TD_, bool ROWDEC_, int L_, int NW_, int CBW_ = 256, int CONVK_ = 0>
 struct ScanCfg {
     static constexpr int FORM = FORM_;
     using TS = TS_;  // streamed dtype (inputs other than a separate decay, and the output)
@@ -364,14 +377,28 @@ struct ScanCfg {
     static constexpr int OFF_HIN = OFF_AGG + (AGG_SLOT < 0 ? AGG_BYTES : 0);
     static constexpr int OFF_ROWDEC = OFF_HIN + NW * CBW * 4;  // fp32 state entering each warp's rows
     static constexpr int OFF_RESET = OFF_ROWDEC + (ROWDEC ? L * 4 : 0);
-    static constexpr int OFF_MISC = OFF_RESET + ((L + 15) / 16) * 16;
+    // CONV (16-bit SSD): per warp the kConvHalo raw u rows before its rows (a
+    // TMA box, 128-byte aligned) and the reset flags of rows wr0-kConvHalo ..
+    // wr0+R-1 (32 bytes)
+    static constexpr int CONVK = CONVK_;  // taps of the folded conv (0: none)
+    static constexpr bool CONV = CONVK > 0;
+    static_assert(CONVK >= 0 && CONVK <= kConvHalo + 1, "1 .. kConvHalo + 1 taps");
+    static_assert(!CONV || (FORM == FORM_SSD && Ops<TS>::BYTES == 2), "the conv fold is for 16-bit SSD");
+    static_assert(!CONV || R + kConvHalo <= 32, "a warp loads its conv reset flags one per lane");
+    static_assert(!CONV || kConvHalo <= RS, "a thread's window rows lie in its own or the previous row group");
+    static constexpr int OFF_HALO =
+        CONV ? (((OFF_RESET + ((L + 15) / 16) * 16) + 127) / 128) * 128 : OFF_RESET + ((L + 15) / 16) * 16;
+    static constexpr int HALO_WARP_BYTES = kConvHalo * CBW * Ops<TS>::BYTES;
+    static constexpr int OFF_CRESET = OFF_HALO + (CONV ? NW * HALO_WARP_BYTES : 0);
+    static constexpr int OFF_MISC = OFF_CRESET + (CONV ? NW * 32 : 0);
     static constexpr int SMEM = OFF_MISC + (NW + 1) * 8 + 16 + 128;  // mbarriers, misc, alignment slack
     // resident CTAs per SM: bounded by shared memory (228 KB per SM, 1 KB
     // reserved per CTA) and by a register budget per thread
     static constexpr int MINB_SMEM = (228 * 1024) / (SMEM + 1024);
     static constexpr int MINB_REGS = 65536 / (NT * NEED_REG_BUDGET);
     static constexpr int MINB_CAP = MINB_REGS < 1 ? 1 : (MINB_REGS > 8 ? 8 : MINB_REGS);
-    static constexpr int MINB = MINB_SMEM < 1 ? 1 : (MINB_SMEM < MINB_CAP ? MINB_SMEM : MINB_CAP);
+    static constexpr int MINB_PLAIN = MINB_SMEM < 1 ? 1 : (MINB_SMEM < MINB_CAP ? MINB_SMEM : MINB_CAP);
+    static constexpr int MINB = CONV ? (NEED_CONV_MINB < MINB_SMEM ? NEED_CONV_MINB : MINB_SMEM) : MINB_PLAIN;
 };
 
 template <class K>
@@ -381,6 +408,110 @@ __device__ __forceinline__ unsigned char* slot_ptr(unsigned char* base, int k) {
     for (int j = 0; j < 5; ++j)
         if (j < k) off += K::slot_bytes(j);
     return base + off;
+}
+
+// ------------------------------------------------------------------ folded conv
+// CONV: as the rows land, the raw u in the tile's u slot (slot 2) becomes
+// u = SiLU(round(conv(raw))) rounded to the stream dtype, the arithmetic of
+// prologue.cu's conv_silu_kernel bit for bit: the taps accumulated oldest
+// first by fp32 fma onto the bias, rounded, SiLU with the scan's 16-bit
+// sigmoid, rounded.  Rows before the sequence start read as 0 (the halo box's
+// zero fill); a reset at row t (a segment start) hides every row before t from
+// the taps of rows >= t.  A pass between the rows' arrival and phase 1 does
+// it (merged into phase 1's row loop it measured slower: 72.5 against 67.7 us
+// at B=8, T=2048, C=832); the rows before a thread's first row come from the
+// previous row group of its warp or, for the first, from the warp's halo.
+// This lane's tap weights by distance back from the current row (0 past
+// K::CONVK) and biases, as fp32 pairs; loaded before the tile lands.
+struct ConvTaps {
+    float2 wb[kConvHalo + 1][4], bs[4];
+};
+template <class K>
+__device__ __forceinline__ void conv_taps(const ScanParams& p, int v, int c0, ConvTaps& ct) {
+    using TS = typename K::TS;
+    constexpr int kc = K::CONVK;
+    const TS* w = static_cast<const TS*>(p.conv_w);
+    const TS* bias = static_cast<const TS*>(p.conv_b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int ca = c0 + chan<false>(2 * i, v), cb = ca + 1;
+        const bool oa = ca < p.C, ob = cb < p.C;
+        ct.bs[i] = make_float2(bias != nullptr && oa ? to_f(bias[ca]) : 0.0f,
+                               bias != nullptr && ob ? to_f(bias[cb]) : 0.0f);
+#pragma unroll
+        for (int back = 0; back <= kConvHalo; ++back) {
+            const int64_t j = kc - 1 - back;  // tap index (oldest first)
+            ct.wb[back][i] = make_float2(back < kc && oa ? to_f(w[ca * p.cwsc + j * p.cwsk]) : 0.0f,
+                                         back < kc && ob ? to_f(w[cb * p.cwsc + j * p.cwsk]) : 0.0f);
+        }
+    }
+}
+
+// One output row of the folded conv for this lane's 8 channels: jr is the
+// row's index in the thread's window numbering (its rows are kConvHalo ..
+// kConvHalo+RS-1), win[] the raw rows jr-3 .. jr-1 (oldest first), raw the
+// row itself; taps from rows before `lastres` are outside the row's segment.
+template <class K>
+__device__ __forceinline__ void conv_row(const ConvTaps& ct, int jr, int lastres,
+                                         const typename Ops<typename K::TS>::P (&win)[kConvHalo][4],
+                                         const typename Ops<typename K::TS>::P (&raw)[4],
+                                         typename Ops<typename K::TS>::P (&o)[4]) {
+    using TS = typename K::TS;
+    using OS = Ops<TS>;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 acc = ct.bs[i];
+#pragma unroll
+        for (int back = K::CONVK - 1; back >= 0; --back) {
+            {
+                const float2 x = jr - back >= lastres ? widen(back == 0 ? raw[i] : win[kConvHalo - back][i])
+                                                      : splat2(0.0f);
+                acc = ffma2(ct.wb[back][i], x, acc);
+            }
+        }
+        const float2 a = widen(OS::pack(acc.x, acc.y));
+        const float2 y = fmul2(a, sig2<TS>(a));
+        o[i] = OS::pack(y.x, y.y);
+    }
+}
+
+// The folded conv over this thread's rows r0 .. r0+RS-1 of the u slot, in
+// place: all window rows are read first (one warp barrier), then each row is
+// rewritten.
+template <class K>
+__device__ __forceinline__ void conv_fold(const ScanParams& p, unsigned char* base, int warp, int q, int v, int wr0,
+                                          const ConvTaps& ct) {
+    using TS = typename K::TS;
+    using PS = typename Ops<TS>::P;
+    constexpr int RS = K::RS, CBW = K::CBW, H = kConvHalo;
+    const int r0 = wr0 + q * RS;
+    TS* slot = reinterpret_cast<TS*>(slot_ptr<K>(base, 2));
+    const TS* halo = reinterpret_cast<const TS*>(base + K::OFF_HALO + warp * K::HALO_WARP_BYTES);
+    const uint8_t* rsf = base + K::OFF_CRESET + warp * 32 + q * RS;  // flag of window row jr: rsf[jr]
+    PS raw[RS + H][4];  // window row jr = row r0 - H + jr
+#pragma unroll
+    for (int jr = 0; jr < RS + H; ++jr) {
+        const int r = r0 - H + jr;
+        Row8<TS, false>::lds(r >= wr0 ? slot + r * CBW : halo + (r - wr0 + H) * CBW, v, raw[jr]);
+    }
+    __syncwarp();
+    int lastres = 0;  // taps from window rows >= lastres are inside the current row's segment
+#pragma unroll
+    for (int jr = 1; jr < H; ++jr)
+        if (rsf[jr]) lastres = jr;
+#pragma unroll
+    for (int jo = 0; jo < RS; ++jo) {
+        const int jr = H + jo;
+        if (rsf[jr]) lastres = jr;
+        PS win[H][4], o[4];
+#pragma unroll
+        for (int jw = 0; jw < H; ++jw)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) win[jw][i] = raw[jo + jw][i];
+        conv_row<K>(ct, jr, lastres, win, raw[jr], o);
+        Row8<TS, false>::sts(slot + (r0 + jo) * CBW, v, o);
+    }
+    __syncwarp();
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -697,12 +828,17 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
             uint32_t bytes = 0;
 #pragma unroll
             for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
+            if constexpr (K::CONV) bytes += K::HALO_WARP_BYTES;
             mbar_arrive_expect_tx(&s_bar[warp], bytes);
 #pragma unroll
             for (int k = 0; k < K::NIN; ++k)
                 tma_load_4d(slot_ptr<K>(base, k) + wr0 * (K::slot_bytes(k) / L), &p.tm[k], c0,
                             REV ? p.T - t0 - wr0 - R : t0 + wr0, hi, bi,
                             &s_bar[warp]);
+            // the raw u rows before this warp's rows (a negative row reads the zero fill)
+            if constexpr (K::CONV)
+                tma_load_4d(base + K::OFF_HALO + warp * K::HALO_WARP_BYTES, &p.tm_halo, c0, t0 + wr0 - kConvHalo,
+                            hi, bi, &s_bar[warp]);
         }
         // this warp's reset flags and per-row decay while its rows are in flight
         if (lane < R) {
@@ -721,10 +857,23 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 s_rowdec[r] = d;
             }
         }
+        if constexpr (K::CONV) {  // reset flags of rows wr0-kConvHalo .. wr0+R-1, for the conv's window
+            if (lane < R + kConvHalo) {
+                const int t = t0 + wr0 - kConvHalo + lane;
+                uint8_t rs = 0;
+                if (p.seg != nullptr && t >= 0 && t < p.T) rs = p.seg[bi * p.sgb + (int64_t)t * p.sgt] != 0;
+                base[K::OFF_CRESET + warp * 32 + lane] = rs;
+            }
+        }
         __syncwarp();
+        ConvTaps ct;
+        if constexpr (K::CONV) conv_taps<K>(p, v, c0, ct);  // in flight while the rows land
         if (nvalid > wr0 && !mbar_wait_bounded(&s_bar[warp], par, kTmaPolls)) {
             atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
             mbar_wait_bounded(&s_bar[warp], par, kTmaPolls);
+        }
+        if constexpr (K::CONV) {
+            if (nvalid > wr0) conv_fold<K>(p, base, warp, q, v, wr0, ct);  // warp-uniform
         }
 
         // shared-memory row of virtual row r (REV: mirrored inside this warp's rows)

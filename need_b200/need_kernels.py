@@ -645,6 +645,70 @@ def ssd_scan_rms_norm(u: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tenso
     return out if out.dtype == u.dtype else out.to(u.dtype)
 
 
+def ssd_conv_scan(u_raw: torch.Tensor, b_gate: torch.Tensor, c_gate: torch.Tensor, dt_raw: torch.Tensor,
+                  out_gate: torch.Tensor, d_skip: torch.Tensor, dt_min: float, dt_max: float,
+                  conv_weight: torch.Tensor, conv_bias: Optional[torch.Tensor] = None, *,
+                  norm_weight: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                  seg_start: Optional[torch.Tensor] = None, h0: Optional[torch.Tensor] = None,
+                  h_final: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``ssd_scan(ssd_conv_silu(u_raw, conv_weight, conv_bias), ...)`` -- and with
+    ``norm_weight`` the block's ``out_norm`` after it -- in one kernel whose
+    tiles apply the causal depthwise conv + SiLU to ``u_raw`` as they land
+    (need_core.py:1620-1629, ``need_ssd_conv_scan``).  Bit-identical to the
+    two-kernel sequence :func:`ssd_conv_silu` then :func:`ssd_scan` (or
+    :func:`ssd_scan_rms_norm`), without the conv output's round trip through
+    HBM.  bf16 / f16 [B, T, D] inputs, D a multiple of 8; ``conv_weight`` is
+    the Conv1d weight [D, 1, K] (or [D, K]), K <= 4; ``seg_start`` resets both
+    the conv window and the scan."""
+    b, t, d = u_raw.shape
+    tensors = (u_raw, b_gate, c_gate, dt_raw, out_gate)
+    _require_cuda(*tensors, d_skip, conv_weight, conv_bias, norm_weight)
+    _no_grad(*tensors, d_skip, conv_weight, conv_bias, norm_weight)
+    ts = u_raw.dtype
+    if ts not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"ssd_conv_scan takes bf16 or f16 data; got {ts}")
+    if d % 8 != 0:
+        raise ValueError(f"ssd_conv_scan needs D to be a multiple of 8; got {d}")
+    if u_raw.numel() == 0:
+        return torch.empty_like(u_raw)
+    xs = [_bt_c_tensor(x if x.dtype == ts else x.to(ts), n)
+          for x, n in zip(tensors, ("u_raw", "b_gate", "c_gate", "dt_raw", "out_gate"))]
+    out = torch.empty((b, t, d), dtype=ts, device=u_raw.device)
+    ds = d_skip.to(device=u_raw.device, dtype=torch.float32).reshape(-1).contiguous()
+    cw = conv_weight.reshape(d, -1).to(ts)
+    cv = abi.NeedSsdConv()
+    cv.K = cw.shape[1]
+    cv.weight, cv.w_stride_c, cv.w_stride_k = cw.data_ptr(), cw.stride(0), cw.stride(1)
+    keep = [cw, ds]
+    if conv_bias is not None:
+        cb = conv_bias.to(ts).reshape(-1).contiguous()
+        cv.bias = cb.data_ptr()
+        keep.append(cb)
+    wptr, wdt = None, abi.F32
+    if norm_weight is not None:
+        if norm_weight.numel() != d:
+            raise ValueError(f"norm_weight must have D={d} elements; got {tuple(norm_weight.shape)}")
+        w = norm_weight.reshape(-1)
+        if w.dtype not in (torch.float32, ts):
+            w = w.float()
+        w = w.contiguous()
+        if w.data_ptr() % 16:
+            w = w.clone()
+        wptr, wdt = w.data_ptr(), _DT[w.dtype]
+        keep.append(w)
+    a = abi.NeedScanArgs()
+    _fill_common(a, abi.FORM_SSD, ts, b, 1, t, d, out)
+    xu, xbg, xcg, xdt, xog = xs
+    for k, x in enumerate((xdt, xbg, xu, xcg, xog)):
+        a.in_[k] = abi.NeedView(x.data_ptr(), x.stride(0), 0, x.stride(1))
+    a.d_skip = ds.data_ptr()
+    a.dt_min, a.dt_max = float(dt_min), float(dt_max)
+    keep += _fill_state(a, u_raw.device, b, 1, d, seg_start, h0, h_final)
+    _launch("need_ssd_conv_scan", a, u_raw.device, extra=(ctypes.byref(cv), wptr, wdt, float(eps)))
+    del keep
+    return out
+
+
 # --------------------------------------------------------------------------
 # matrix-state associative memory  (need_core.py:1960-2001)
 # --------------------------------------------------------------------------

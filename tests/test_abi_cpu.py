@@ -48,6 +48,7 @@ def test_struct_layout_matches_header(tmp_path):
         "need_view": (abi.NeedView, [f[0] for f in abi.NeedView._fields_]),
         "need_segment_args": (abi.NeedSegmentArgs, [f[0] for f in abi.NeedSegmentArgs._fields_]),
         "need_conv_args": (abi.NeedConvArgs, [f[0] for f in abi.NeedConvArgs._fields_]),
+        "need_ssd_conv": (abi.NeedSsdConv, [f[0] for f in abi.NeedSsdConv._fields_]),
         "need_assoc_args": (abi.NeedAssocArgs, [f[0] for f in abi.NeedAssocArgs._fields_]),
         "need_norm_args": (abi.NeedNormArgs, [f[0] for f in abi.NeedNormArgs._fields_]),
         "need_assoc_step_args": (abi.NeedAssocStepArgs, [f[0] for f in abi.NeedAssocStepArgs._fields_]),
@@ -110,6 +111,17 @@ def test_argument_errors_return_status(lib):
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), None, abi.F32, 1e-6, None) == abi.ERR_INVALID
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F16, 1e-6, None) == abi.ERR_UNSUPPORTED
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F32, -1.0, None) == abi.ERR_INVALID
+    cv = abi.NeedSsdConv()
+    cv.K, cv.weight = 3, 256
+    assert lib.need_ssd_conv_scan(None, ctypes.byref(cv), None, abi.F32, 1e-6, None) == abi.ERR_INVALID
+    assert lib.need_ssd_conv_scan(ctypes.byref(s), None, None, abi.F32, 1e-6, None) == abi.ERR_INVALID
+    cv.K = 5
+    assert lib.need_ssd_conv_scan(ctypes.byref(s), ctypes.byref(cv), None, abi.F32, 1e-6, None) == abi.ERR_UNSUPPORTED
+    cv.K, s.dtype = 3, abi.F32
+    assert lib.need_ssd_conv_scan(ctypes.byref(s), ctypes.byref(cv), None, abi.F32, 1e-6, None) == abi.ERR_UNSUPPORTED
+    s.dtype = abi.BF16
+    assert lib.need_ssd_conv_scan(ctypes.byref(s), ctypes.byref(cv), ctypes.byref(w), abi.F16, 1e-6,
+                                  None) == abi.ERR_UNSUPPORTED  # norm weight dtype
     s.T = 0
     assert lib.need_ssd_scan_rms_norm(ctypes.byref(s), ctypes.byref(w), abi.F32, 1e-6, None) == abi.ERR_INVALID
     n = abi.NeedNormArgs()
