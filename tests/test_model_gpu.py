@@ -147,3 +147,64 @@ def test_need_model_forward_through_the_drop_in(cuda):
         print(f"logits vs the reference's Triton path: max rel {terr:.3e}, rel L2 {tl2:.3e} "
               f"(the reference's own torch path vs its Triton path: {rerr:.3e}, {rl2:.3e})")
     assert err <= BF16_TOL, f"logits differ from the reference's: max rel {err}"
+
+
+def test_ssd_block_patched_with_the_folded_conv(cuda):
+    """The maintainer's patch: StructuredDualRetention.forward under no_grad as
+    in_proj -> ssd_conv_scan (the conv + SiLU folded into the scan, then the
+    out_norm kernel) -> out, with need_b200.need_kernels bound for the rest
+    of the model.  Every one of the 14 blocks is compared with the reference's
+    own block forward (torch path) on the input the reference's forward gave
+    it, within the bf16 budget; then the whole forward runs with the patch."""
+    need_core, ref_nk, config_for_size = reference_modules()
+    from need_b200 import need_kernels as nk
+
+    model, _ = build_model(need_core, config_for_size, cuda)
+    gen = torch.Generator(device=cuda).manual_seed(6)
+    ids = torch.randint(0, model.cfg.vocab_size, (B, T), device=cuda, generator=gen)
+    SDR = need_core.StructuredDualRetention
+    original = SDR.forward
+
+    def patched(self, x):
+        if torch.is_grad_enabled():
+            return original(self, x)
+        u, bg, cg, dt, og = self.in_proj(x).chunk(5, dim=-1)
+        y = nk.ssd_conv_scan(u, bg, cg, dt, og, self.D, self.cfg.ssd_dt_min, self.cfg.ssd_dt_max,
+                             self.dwconv.weight, self.dwconv.bias,
+                             norm_weight=self.out_norm.weight, eps=self.out_norm.eps)
+        return self.out(y)
+
+    blocks = [m for m in model.modules() if isinstance(m, SDR)]
+    assert len(blocks) == 14
+    seen = []
+    hooks = [m.register_forward_pre_hook(lambda m, a: seen.append((m, a[0].detach().clone()))) for m in blocks]
+    saved_binding, saved_triton = need_core.need_kernels, ref_nk.HAS_TRITON
+    try:
+        need_core.need_kernels = ref_nk
+        ref_nk.HAS_TRITON = False
+        want = forward_logits(model, ids)
+        for h in hooks:
+            h.remove()
+        worst = 0.0
+        for i, (m, x) in enumerate(seen):
+            with torch.no_grad(), torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                ref_y = original(m, x)
+                need_core.need_kernels = nk
+                got_y = patched(m, x)
+                need_core.need_kernels = ref_nk
+            e, _ = rel(got_y.float(), ref_y.float())
+            worst = max(worst, e)
+            assert e <= BF16_TOL, f"block {i}: max rel {e}"
+        need_core.need_kernels = nk
+        SDR.forward = patched
+        got = forward_logits(model, ids)
+    finally:
+        SDR.forward = original
+        need_core.need_kernels = saved_binding
+        ref_nk.HAS_TRITON = saved_triton
+    assert nk.workspace_error() == 0
+    assert torch.isfinite(got).all()
+    err, l2 = rel(got, want)
+    print(f"\nper-block (patched vs the reference's block): worst max rel {worst:.3e}; "
+          f"logits: max rel {err:.3e}, rel L2 {l2:.3e}")
+    assert err <= BF16_TOL, f"logits differ from the reference's: max rel {err}"
