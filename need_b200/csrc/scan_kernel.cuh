@@ -868,6 +868,14 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         __syncwarp();
         ConvTaps ct;
         if constexpr (K::CONV) conv_taps<K>(p, v, c0, ct);  // in flight while the rows land
+        PS dsp[4];  // SSD: the epilogue's D for this lane's channels, loaded while the rows land
+        if constexpr (K::FORM == FORM_SSD) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int ca = c0 + chan<SPLIT>(2 * i, v), cb = c0 + chan<SPLIT>(2 * i + 1, v);
+                dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
+            }
+        }
         if (nvalid > wr0 && !mbar_wait_bounded(&s_bar[warp], par, kTmaPolls)) {
             atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
             mbar_wait_bounded(&s_bar[warp], par, kTmaPolls);
@@ -1024,14 +1032,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         const int64_t ostep = REV ? -p.ost : p.ost;  // REV: rows are written in decreasing t
         TS* orow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh +
                    (int64_t)(REV ? p.T - 1 - t0 - r0 : t0 + r0) * p.ost + c0;
-        PS dsp[4];
-        if constexpr (K::FORM == FORM_SSD) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int ca = c0 + chan<SPLIT>(2 * i, v), cb = c0 + chan<SPLIT>(2 * i + 1, v);
-                dsp[i] = OS::pack(ca < p.C ? p.dskip[ca] : 0.0f, cb < p.C ? p.dskip[cb] : 0.0f);
-            }
-        }
         // output row r: advances the state and forms the epilogue in o
         auto step = [&](int r, PS (&o)[4]) {
             float2 a[4], b[4];
