@@ -92,6 +92,7 @@ struct Plan {
     bool dstream = false, split = false;
     int (*launch)(const ScanParams&, cudaStream_t) = nullptr;
     int (*launch_fix)(const ScanParams&, cudaStream_t) = nullptr;   // gated form only
+    int (*launch_defer)(const ScanParams&, cudaStream_t) = nullptr; // gated form only
     int (*launch_rev)(const ScanParams&, cudaStream_t) = nullptr;   // affine form only
 };
 
@@ -103,6 +104,18 @@ int launch_cfg(const ScanParams& prm, cudaStream_t s) {
     scan_kernel<K><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch");
+    return NEED_OK;
+}
+
+// The local scan of a sequence-parallel slice after the first (DEFER), one tile per CTA.
+template <class K>
+int launch_defer_cfg(const ScanParams& prm, cudaStream_t s) {
+    static std::atomic<uint64_t> smem_done{0};
+    cudaError_t e = ensure_smem(scan_kernel<K, false, false, true>, K::SMEM, smem_done);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(scan_kernel, deferred)");
+    scan_kernel<K, false, false, true><<<prm.ntiles, K::NT, K::SMEM, s>>>(prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scan_kernel launch (deferred)");
     return NEED_OK;
 }
 
@@ -157,7 +170,10 @@ Plan plan_of() {
     p.dstream = K::HAS_DSTREAM;
     p.split = K::SPLIT;
     p.launch = &launch_cfg<K>;
-    if constexpr (K::FORM == FORM_GATED) p.launch_fix = &launch_fix_cfg<K>;
+    if constexpr (K::FORM == FORM_GATED) {
+        p.launch_fix = &launch_fix_cfg<K>;
+        p.launch_defer = &launch_defer_cfg<K>;
+    }
     if constexpr (K::FORM == FORM_AFFINE) p.launch_rev = &launch_rev_cfg<K>;
     return p;
 }
@@ -534,8 +550,8 @@ int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t s
     Plan pl;
     ScanParams P;
     if (int rc = prepare(args, NEED_FORM_GATED, &pl, &P)) return rc;
-    P.sp_defer = rank > 0 ? 1 : 0;
-    if (int rc = pl.launch(P, stream)) return rc;
+    if (rank > 0 && pl.launch_defer == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no deferring scan for dtype %d", args->dtype);
+    if (int rc = rank > 0 ? pl.launch_defer(P, stream) : pl.launch(P, stream)) return rc;
     return ok();
 }
 

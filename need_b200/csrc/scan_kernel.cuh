@@ -68,7 +68,7 @@ constexpr uint32_t kTmaPolls = 1u << 22;
 // A sequence-parallel fix-up rewrites a tile while the product of a before it
 // (from the slice start) exceeds 2^-24 on some channel of the tile: past that
 // the carry entering the slice changes no state above fp32 resolution of the
-// carry.  The local scan (sp_defer) and the fix-up's preparation both use it.
+// carry.  The local scan (scan_kernel<..., DEFER>) and the fix-up's preparation both use it.
 constexpr float kFixTau = 0x1p-24f;
 // Raw input rows a folded SSD conv sees before a warp's first row: up to 4 taps.
 constexpr int kConvHalo = 3;
@@ -115,10 +115,6 @@ struct ScanParams {
     const void* conv_w;
     int64_t cwsc, cwsk;
     const void* conv_b;
-    // Local scan of a sequence-parallel slice after the first: tiles whose
-    // entering product of a exceeds kFixTau on some channel skip phase 2 (their
-    // outputs are written by the fix-up, which rewrites exactly those tiles).
-    int32_t sp_defer;
     // sequence-parallel fix-up (scan_kernel<K, true>): the local scan's
     // per-tile entering product and state, the carry entering the slice per
     // (sequence, channel) in .x, and the list of tiles to rewrite (fix_count
@@ -526,7 +522,10 @@ __device__ __forceinline__ void conv_fold(const ScanParams& p, unsigned char* ba
 // output rows are mirrored.  The caller passes the decay already shifted by
 // one row (a'_t = a_{t+1}, a'_{T-1} = 0): a tensor map based at row 1 with
 // T-1 rows, or, for a decay per row, a guarded load of row t+1.
-template <class K, bool FIX = false, bool REV = false>
+// DEFER = true: the local scan of a sequence-parallel slice after the first --
+// tiles whose entering product of a exceeds kFixTau on some channel skip
+// phase 2 (the fix-up writes their outputs; it rewrites exactly those tiles).
+template <class K, bool FIX = false, bool REV = false, bool DEFER = false>
 __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_constant__ ScanParams p) {
     using TS = typename K::TS;
     using TD = typename K::TD;
@@ -544,7 +543,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     uint8_t* s_reset = base + K::OFF_RESET;
     uint64_t* s_bar = reinterpret_cast<uint64_t*>(base + K::OFF_MISC);  // one per row warp
     uint64_t* s_p1 = s_bar + NW;  // all row warps have written their maps
-    uint32_t* s_defer = reinterpret_cast<uint32_t*>(s_p1 + 1);  // this tile skips phase 2 (sp_defer)
+    uint32_t* s_defer = reinterpret_cast<uint32_t*>(s_p1 + 1);  // DEFER: this tile skips phase 2
     // warp w's maps: 4 pairs x 32 lanes of (A pair, B pair); lane = (row group, channel vector)
     auto agg4 = [&](int w) { return reinterpret_cast<float4*>(s_agg + w * K::AGG_STRIDE); };
 
@@ -657,7 +656,6 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                                : 0.0f;
             }
             if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
-            if (lane == 0) *s_defer = 0u;
             float2 TA[NP], TB[NP];
             pass(h, TA, TB, true, false);
         } else if (warp == K::LB) {
@@ -697,17 +695,17 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 }
             }
             ulonglong2* const my_agg = p.agg + (int64_t)tile * CBW;
-            // sp_defer: with the product before this tile known, does some channel
+            // DEFER: with the product before this tile known, does some channel
             // still exceed kFixTau (then the fix-up writes the outputs)?  Written to
             // s_defer before the row warps are released.
             auto set_defer = [&]() {
-                bool d = false;
-                if (p.sp_defer) {
+                if constexpr (DEFER) {
+                    bool d = false;
 #pragma unroll
                     for (int k = 0; k < NE; ++k) d |= (c0 + lbchan(k) < p.C) && carryP[k] > kFixTau;
+                    d = __any_sync(0xffffffffu, d);
+                    if (lane == 0) *s_defer = d ? 1u : 0u;
                 }
-                d = __any_sync(0xffffffffu, d);
-                if (lane == 0) *s_defer = d ? 1u : 0u;
             };
             auto publish_agg = [&]() {
 #pragma unroll
@@ -1017,7 +1015,7 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         named_sync(1, K::NT);  // the look-back warp has put this warp's entering state in s_hin
 
         // ---------------------------------------------------------- phase 2
-        if (*s_defer == 0u) {  // else the sequence-parallel fix-up writes this tile
+        if (!DEFER || *s_defer == 0u) {  // else the sequence-parallel fix-up writes this tile
         float2 h[4];
         {
             const float4 h0 = *reinterpret_cast<const float4*>(s_hin + warp * CBW + chan<SPLIT>(0, v));
