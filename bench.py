@@ -628,8 +628,9 @@ def run_sp(dev, world, rank, barrier, max_over_ranks, sp, workloads):
 def profile_side_case(args, dev, nk, sp, workloads):
     """One-GPU workloads of the other kernels, for ncu: ``decode`` replays the
     verify + commit graph of 256 sequences x 4 drafted tokens; ``sp-fixup``
-    scans the 8 slices of a B=1, T=65536, C=4096 sequence, stacks their
-    summaries as the all-gather would and fixes up the last slice; ``ssd-norm``
+    scans the last of 8 slices of the B=4, T=65536, C=4096 workload (the
+    deferring local scan of rank 7) and fixes it up, the earlier ranks' maps
+    stood in for by its own; ``ssd-norm``
     runs the SSD scan with the RMSNorm kernel after it, ``ssd-conv`` the scan
     with the conv + SiLU folded in (inputs as in-projection chunks) and the
     RMSNorm kernel after it, ``assoc`` the
@@ -700,13 +701,14 @@ def profile_side_case(args, dev, nk, sp, workloads):
             nk.ragged_verify(pool, w.cu_k, (w.z, w.g, w.x), out=(y, sk))
             nk.commit_states(pool, sk, w.cu_k, w.accept)
     else:
+        # the last of 8 slices of the sequence-parallel workload (B=4, T=65536,
+        # C=4096): its deferring local scan, then its fix-up; the 7 earlier
+        # ranks' maps are stood in for by this slice's own (the same
+        # statistics), so only one slice is held on the device
         P, T = 8, 65536
-        locs = []
-        for r in range(P):
-            w = workloads.long_sp(dev, B=1, T=T, H=32, D=128, seed=7, t_begin=r * T // P, t_end=(r + 1) * T // P)
-            locs.append((w, sp.local_scan(w.x, w.z, w.g)))
-        gathered = torch.stack([loc.summary for _, loc in locs])
-        last = locs[-1][1]
+        w = workloads.long_sp(dev, B=4, T=T, H=32, D=128, seed=7, t_begin=(P - 1) * T // P, t_end=T)
+        last = sp.local_scan(w.x, w.z, w.g, rank=P - 1)
+        gathered = torch.stack([last.summary.clone() for _ in range(P)])
         for _ in range(max(args.warmup, 3) + args.steps):
             sp.fixup(last, gathered, P, P - 1)
     torch.cuda.synchronize()
