@@ -52,9 +52,10 @@ def _lib():
         lib.ora_assoc_memory.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i64, i32, i32]
         lib.ora_assoc_step.argtypes = [p, p, p, p, p, p, p, i64, i64, i64, i32]
         lib.ora_conv_step.argtypes = [p, p, p, p, p, i64, i64, i64, i32]
+        lib.ora_conv_silu.argtypes = [p, p, p, p, p, i64, i64, i64, i64, i32]
         for fn in ("ora_round", "ora_affine_scan", "ora_affine_scan_seq", "ora_gated_prep",
                    "ora_ssd_prep", "ora_ssd_epilogue", "ora_stream_step", "ora_rms_norm", "ora_assoc_memory", "ora_assoc_step",
-                   "ora_conv_step"):
+                   "ora_conv_step", "ora_conv_silu"):
             getattr(lib, fn).restype = None
         del f
         _LIB = lib
@@ -246,6 +247,24 @@ def conv_step(hist, u, w, bias=None, *, dtype: str = "bf16"):
     b = None if bias is None else _f32(bias).reshape(-1)
     _lib().ora_conv_step(_ptr(h), _ptr(_f32(u)), _ptr(w), _ptr(b), _ptr(ua), n, c, k, MODE[dtype])
     return h, ua
+
+
+def conv_silu(u, w, bias=None, seg=None, *, dtype: str = "bf16"):
+    """The SSD block's prologue over whole sequences, ``silu(dwconv(u)[..., :T])``
+    (need_core.py:1620-1623), in the model dtype as the reference computes it
+    on CPU: the fp32 conv (bias + taps, oldest first) rounded once, then SiLU
+    in fp32 rounded once.  u: [N, T, C]; w: [C, K] or [C, 1, K]; bias: [C];
+    seg: optional [N, T] reset mask (rows before a segment start read as 0)."""
+    uu = _f32(u)
+    n, t, c = uu.shape
+    ww = _f32(w).reshape(c, -1)
+    k = ww.shape[1]
+    b = None if bias is None else _f32(bias).reshape(-1)
+    sg = None if seg is None else np.ascontiguousarray(seg, dtype=np.uint8)
+    out = np.empty((n, t, c), np.float32)
+    _lib().ora_conv_silu(_ptr(uu), _ptr(ww), _ptr(b), None if sg is None else sg.ctypes.data, _ptr(out),
+                         n, t, c, k, MODE[dtype])
+    return out
 
 
 def ragged_verify(form: str, states, cu_k, p0, p1, p2, p3=None, p4=None, dskip=None,

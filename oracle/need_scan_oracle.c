@@ -552,6 +552,35 @@ ORA_API void ora_conv_step(float* hist, const float* u, const float* w, const fl
         }
 }
 
+/* The SSD block's input prologue over a whole sequence (need_core.py:1620-1623):
+ *   u_conv = dwconv(u)[..., :T]   (nn.Conv1d(C, C, K, padding=K-1, groups=C))
+ *   u_act  = F.silu(u_conv)
+ * in the model dtype as the reference computes it on CPU: per (t, c) the
+ * bias plus the K taps w[c, j] * u[t-K+1+j, c] (oldest first) summed in fp32
+ * and rounded once, then SiLU in fp32 (x / (1 + exp(-x))) rounded once; rows
+ * before t = 0 are zero.  With seg (optional [N, T]) rows before the segment
+ * start of t are zero too (a reset the reference's module has no input for).
+ * u, out [N, T, C]; w [C, K]; bias [C] or NULL. */
+ORA_API void ora_conv_silu(const float* u, const float* w, const float* bias, const uint8_t* seg, float* out,
+                           int64_t N, int64_t T, int64_t C, int64_t K, int mode) {
+    for (int64_t n = 0; n < N; ++n) {
+        int64_t start = 0; /* first row of the current segment */
+        for (int64_t t = 0; t < T; ++t) {
+            if (seg && seg[n * T + t]) start = t;
+            for (int64_t c = 0; c < C; ++c) {
+                float acc = bias ? bias[c] : 0.0f;
+                for (int64_t j = 0; j < K; ++j) {
+                    const int64_t tt = t - (K - 1) + j;
+                    const float x = (tt >= 0 && tt >= start) ? u[(n * T + tt) * C + c] : 0.0f;
+                    acc = fmaf(w[c * K + j], x, acc);
+                }
+                const float uc = rnd(acc, mode);
+                out[(n * T + t) * C + c] = rnd(uc / (1.0f + expf(-uc)), mode);
+            }
+        }
+    }
+}
+
 ORA_API void ora_stream_step(int form, float* state, const float* p0, const float* p1,
                              const float* p2, const float* p3, const float* p4,
                              const float* dskip, float* y, int64_t N, int64_t C,

@@ -91,6 +91,9 @@ CASES = {
     # the SSD step with its depthwise conv (K=3): raw u in p2, the conv history
     # [s, c, 2] each sequence carries, the conv weight [c, 3] and bias [c]
     "stream_ssd_conv_bf16": dict(kind="stream", form="ssd_conv", seed=9, s=6, c=64, kmax=4, dtype="bf16"),
+    # the SSD block's prologue over whole sequences: u_act = silu(dwconv(u)[..., :T]),
+    # captured from StructuredDualRetention.forward (K=3 taps, bias)
+    "ssd_prologue_bf16": dict(kind="prologue", seed=16, n=2, t=203, c=48, k=3, dtype="bf16"),
     # SelectiveRetention's step: decay per head (4 heads of 16 channels), k, v, q
     "stream_retention_bf16": dict(kind="stream", form="retention", seed=15, s=5, c=64, kmax=4, dtype="bf16"),
 }
@@ -180,6 +183,14 @@ def stream_case(seed: int, form: str, s: int, c: int, kmax: int, dtype: str):
     return out
 
 
+def prologue_case(seed: int, n: int, t: int, c: int, k: int, dtype: str):
+    rs = np.random.RandomState(seed)
+    u = cast(rs.standard_normal((n, t, c)), dtype)
+    w = cast(0.6 * rs.standard_normal((c, k)), dtype)   # the Conv1d weight [c, 1, k] in the model dtype
+    b = cast(0.2 * rs.standard_normal(c), dtype)
+    return {"u": u, "conv_w": w, "conv_b": b}
+
+
 def make_inputs(name: str):
     spec = dict(CASES[name])
     kind = spec.pop("kind")
@@ -197,6 +208,8 @@ def make_inputs(name: str):
         return assoc_step_case(**spec)
     if kind == "stream":
         return stream_case(**spec)
+    if kind == "prologue":
+        return prologue_case(**spec)
     raise KeyError(kind)
 
 

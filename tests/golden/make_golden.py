@@ -22,6 +22,7 @@ guards against drift).  Reference entry points used (file:line in NEED):
   the one-token formula of                  need_core.py:6420-6428
   NeedModel._stream_retention_step with     need_core.py:6410-6431 and its conv step
     _stream_depthwise_conv1d_step           need_core.py:6395-6409
+  StructuredDualRetention.forward's prologue  need_core.py:1618-1626 (dwconv + F.silu)
 
 The gated form (decay = sigmoid(z), update = (1 - decay)*(sigmoid(g)*x)) is the
 gate arithmetic of need_kernels.py:330-336 with a sigmoid decay; it is built
@@ -205,6 +206,44 @@ def ref_stream_ssd_conv(inp, dtype):
     return {"y": ys, "states_k": sk, "hist_k": hk}
 
 
+def ref_prologue(inp, dtype):
+    """The SSD block's prologue through the reference's own
+    StructuredDualRetention.forward (need_core.py:1618-1629): in_proj is
+    replaced by the sequence's five chunks (u, then zeros), the module is cast
+    to the model dtype, and the activated u that forward hands to
+    need_kernels.ssd_scan (need_core.py:1624-1626) is captured."""
+    dt = TD[dtype]
+    n, t, c = inp["u"].shape
+    taps = inp["conv_w"].shape[1]
+    cfg = need_core.NeedConfig(d_model=c, n_heads=2, n_layers=1, block_size=256, ssd_conv_kernel=taps,
+                               ssd_dt_min=0.001, ssd_dt_max=0.2)
+    assert cfg.fused_ssd_scan, "the capture needs the fused ssd_scan call"
+    mod = need_core.StructuredDualRetention(cfg).eval()
+    with torch.no_grad():
+        mod.dwconv.weight.copy_(torch.from_numpy(inp["conv_w"]).view(c, 1, taps))
+        mod.dwconv.bias.copy_(torch.from_numpy(inp["conv_b"]))
+    mod = mod.to(dt)
+    u = T(inp["u"], dtype)
+    feed = _Feed()
+    feed.chunks = torch.cat([u, torch.zeros(n, t, 4 * c, dtype=dt)], dim=-1)
+    feed.forward = lambda x: feed.chunks
+    mod.in_proj = feed
+    captured = {}
+
+    def capture(u_act, *args, **kwargs):
+        captured["u_act"] = u_act.clone()
+        return torch.zeros_like(u_act)
+
+    saved = need_core.need_kernels
+    need_core.need_kernels = types.SimpleNamespace(ssd_scan=capture, rms_norm=need_kernels.rms_norm)
+    try:
+        with torch.no_grad():
+            mod(torch.zeros(n, t, c, dtype=dt))
+    finally:
+        need_core.need_kernels = saved
+    return {"u_act": npf(captured["u_act"])}
+
+
 def check_module_stream_step():
     """The formula above against the real StructuredDualRetention.stream_step."""
     torch.manual_seed(0)
@@ -334,6 +373,8 @@ def main():
             out = ref_assoc(inp, dtype)
         elif kind == "assoc_step":
             out = ref_assoc_step(inp, dtype)
+        elif kind == "prologue":
+            out = ref_prologue(inp, dtype)
         elif spec["form"] == "ssd_conv":
             out = ref_stream_ssd_conv(inp, dtype)
         else:

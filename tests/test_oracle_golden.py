@@ -199,3 +199,12 @@ def test_stream_step_with_conv_history():
                                      dskip=inp["dskip"], dtype="bf16", conv_hist=inp["hist"],
                                      conv_w=inp["conv_w"], conv_b=inp["conv_b"])
     assert np.array_equal(y, g["y"]) and np.array_equal(sk, g["states_k"]) and np.array_equal(hk, g["hist_k"])
+
+
+def test_ssd_prologue():
+    """The SSD block's prologue over whole sequences (K=3 taps, bias), bit for
+    bit against the activated u that StructuredDualRetention.forward hands to
+    ssd_scan (need_core.py:1618-1626)."""
+    inp, g = load("ssd_prologue_bf16")
+    got = oracle.conv_silu(inp["u"], inp["conv_w"], inp["conv_b"], dtype="bf16")
+    assert np.array_equal(got, g["u_act"])

@@ -76,3 +76,32 @@ def test_conv_silu_with_resets(cuda):
     seg[1, ::7] = 1
     got = nk.ssd_conv_silu(u.to(cuda), w.to(cuda), b.to(cuda), seg_start=seg.to(cuda))
     compare(got, reference(u, w, b, seg), torch.bfloat16)
+
+
+def test_conv_silu_and_the_fold_against_the_reference_fixture(cuda):
+    """Against the activated u captured from the reference's own
+    StructuredDualRetention.forward (tests/golden/ssd_prologue_bf16.npz, which
+    the oracle reproduces bit for bit): the prologue kernel, and the conv that
+    ssd_conv_scan folds into the scan (bit-identical to the prologue kernel, so
+    its scan of the fixture's u_act equals ssd_scan of the kernel's)."""
+    import os
+    import sys
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, here)
+    import cases  # noqa: E402
+    inp = cases.make_inputs("ssd_prologue_bf16")
+    want = torch.from_numpy(np.load(os.path.join(here, "ssd_prologue_bf16.npz"))["u_act"])
+    u = torch.from_numpy(inp["u"]).to(torch.bfloat16).to(cuda)
+    n, t, c = u.shape
+    w = torch.from_numpy(inp["conv_w"]).to(torch.bfloat16).view(c, 1, -1).to(cuda)
+    b = torch.from_numpy(inp["conv_b"]).to(torch.bfloat16).to(cuda)
+    got = nk.ssd_conv_silu(u, w, b)
+    compare(got, want.to(torch.bfloat16), torch.bfloat16)
+    gen = torch.Generator(device=cuda).manual_seed(2)
+    bg, cg, dt, og = (torch.randn(n, t, c, device=cuda, generator=gen).to(torch.bfloat16) for _ in range(4))
+    d = torch.full((c,), 0.1, device=cuda)
+    fold = nk.ssd_conv_scan(u, bg, cg, dt, og, d, 0.001, 0.2, w, b)
+    assert torch.equal(fold, nk.ssd_scan(got, bg, cg, dt, og, d, 0.001, 0.2))
+    # a u_act one unit off moves the state of every later token, so only the tolerance applies here
+    via_fixture = nk.ssd_scan(want.to(torch.bfloat16).to(cuda), bg, cg, dt, og, d, 0.001, 0.2).float()
+    assert (fold.float() - via_fixture).abs().max() <= TOL[torch.bfloat16] * via_fixture.abs().max()
