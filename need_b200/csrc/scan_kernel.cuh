@@ -512,9 +512,9 @@ __device__ __forceinline__ void conv_fold(const ScanParams& p, unsigned char* ba
 
 // ------------------------------------------------------------------ the kernel
 // FIX = false: the scan, one tile per CTA.  FIX = true: the sequence-parallel
-// fix-up -- the same tile pipeline over the leading fix_chunks chunks of a
-// slice, each tile entered from its known corrected state (no look-back),
-// CTAs striding over those tiles.
+// fix-up -- the same tile pipeline over the fix_count tiles of fix_list (the
+// leading tiles of each chain of a slice), each tile entered from its known
+// corrected state (no look-back), the resident CTAs striding over the list.
 // REV = true (AFFINE only, no resets): the scan runs from t = T-1 down to 0,
 // h_t = a'_t h_{t+1} + b_t -- the adjoint recurrence of the backward pass.
 // Tiles, rows and the look-back work in reversed ("virtual") time tau =
