@@ -52,7 +52,7 @@
 extern "C" {
 #endif
 
-#define NEED_SCAN_ABI_VERSION 1
+#define NEED_SCAN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define NEED_API __attribute__((visibility("default")))
@@ -130,6 +130,10 @@ typedef struct {
                               first use; reusable by later calls on the same stream without
                               clearing; never used by two launches at once */
     size_t workspace_bytes;
+    uint32_t* sp_list;     /* sequence parallelism, the slice's list of the tiles its fix-up
+                              rewrites: need_sp_list_size(...) words, written by
+                              need_sp_local_scan (rank > 0) and read by need_sp_fixup (GATED);
+                              unused (may be null) elsewhere */
 } need_scan_args;
 
 /* Token dtypes of a packed stream (the packer writes uint16 or uint32,
@@ -464,9 +468,14 @@ NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* st
  * `tile_carry` required), as need_gated_scan.  For rank > 0 the tiles that
  * need_sp_fixup will rewrite -- those whose product of a before them exceeds
  * 2^-24 on some channel -- are scanned for their maps but their outputs are
- * not written: call need_sp_fixup on the same args before reading `out`.
+ * not written, and are listed in args->sp_list: call need_sp_fixup with the
+ * same args before reading `out`.
  * Replaces no reference interface (the reference has no distributed scan). */
 NEED_API int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t stream);
+
+/* Words of need_scan_args.sp_list for a GATED slice of this shape: a count
+ * (4 words) and one tile id per tile; 0 for an unknown dtype. */
+NEED_API size_t need_sp_list_size(int32_t dtype, int64_t nb, int64_t nh, int64_t T, int64_t C);
 
 /* After a rank scanned its T-slice from a zero state (with `summary`,
  * `tile_prod` and `tile_carry` requested) and gathered every rank's summary
@@ -475,12 +484,10 @@ NEED_API int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_s
  * re-scanned from the corrected fp32 state tile_carry + tile_prod * carry, with
  * the scan's own arithmetic, and their outputs rewritten; later tiles are left
  * as they are (their correction is below fp32 resolution of the carry).
- * GATED: a tile is rewritten while tile_prod exceeds 2^-24 on some channel of
- * it (the tiles need_sp_local_scan leaves unwritten).  AFFINE: while the
+ * GATED: the tiles need_sp_local_scan listed in args->sp_list (tile_prod
+ * above 2^-24 on some channel), in one launch.  AFFINE: every tile whose
  * correction is non-zero on some channel.  It also corrects h_final / summary
- * when given.  `args` is the description the local scan got; for GATED the
- * workspace must also hold 128 B + nb*nh*C*8 B + (chains + tiles) * 4 B, which
- * need_scan_workspace_size always covers. */
+ * when given. */
 NEED_API int need_sp_fixup(const need_scan_args* args, const float* all_summary, int32_t nranks,
                   int32_t rank, need_stream_t stream);
 

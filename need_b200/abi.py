@@ -13,7 +13,7 @@ from ctypes import (POINTER, Structure, c_char_p, c_double, c_int32, c_int64, c_
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_lib", "libneed_scan.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # need_status
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3, 4
@@ -38,6 +38,7 @@ class NeedScanArgs(Structure):
         ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
         ("summary", c_void_p), ("tile_prod", c_void_p), ("tile_carry", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("sp_list", c_void_p),
     ]
 
 
@@ -140,6 +141,7 @@ SIGNATURES = {
     "need_commit_states": (c_int32, [c_int32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
     "need_sp_local_scan": (c_int32, [POINTER(NeedScanArgs), c_int32, c_void_p]),
+    "need_sp_list_size": (c_size_t, [c_int32, c_int64, c_int64, c_int64, c_int64]),
     "need_sp_fixup": (c_int32, [POINTER(NeedScanArgs), c_void_p, c_int32, c_int32, c_void_p]),
 }
 

@@ -378,41 +378,40 @@ int run(const need_scan_args* a, int form, cudaStream_t s) {
     return ok();
 }
 
-}  // namespace
+// The words of a slice's sequence-parallel list: the count (4 words, 16-byte
+// aligned entries after it) and up to ntiles tile ids.
+constexpr int64_t kSpListHead = 4;
 
-namespace need {
-// Tiles of the gated scan of `a`: channels per tile, chains (sequence x channel
-// block) and chunks.  0, or a status for a dtype without a kernel.
-int gated_geometry(const need_scan_args* a, int* cbw, int64_t* nchains, int64_t* nchunks) {
-    Plan pl;
-    if (!select_plan(NEED_FORM_GATED, a->dtype, a->dtype, 0, &pl))
-        return fail(NEED_ERR_UNSUPPORTED, "no kernel for dtype %d", a->dtype);
-    const Geometry g = geometry(pl, a->nb, a->nh, a->T, a->C);
-    *cbw = pl.CB;
-    *nchains = g.nchains;
-    *nchunks = g.nchunks;
+// Points P's sequence-parallel list at args->sp_list.
+int sp_list_of(const need_scan_args* a, ScanParams* P) {
+    if (a->sp_list == nullptr) return fail(NEED_ERR_INVALID, "sp_list is null (need_sp_list_size words)");
+    if (reinterpret_cast<uintptr_t>(a->sp_list) % 4 != 0) return fail(NEED_ERR_INVALID, "sp_list is not 4-byte aligned");
+    P->sp_count = a->sp_list;
+    P->sp_list = a->sp_list + kSpListHead;
     return NEED_OK;
 }
 
-// The gated scan kernel in fix-up mode over the slice described by `a`, whose
-// tile_prod / tile_carry the local scan filled: it rewrites the fix_count
-// tiles of fix_list (sp.cu prepares them and fix_carry).  Writes only the
+}  // namespace
+
+namespace need {
+// The gated scan kernel in fix-up mode over the slice described by `a`: it
+// rewrites the tiles that the deferring local scan listed in a->sp_list,
+// entering each from the local scan's tile_prod / tile_carry and
+// the carry it composes from all_summary [nranks][nb*nh][C] (ranks < rank);
+// the chain's first tile also corrects h_final and summary.  Writes only the
 // rewritten tiles' outputs.
-int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_count,
-                       const uint32_t* fix_list, cudaStream_t stream) {
+int gated_fixup_launch(const need_scan_args* a, const float* all_summary, int32_t rank, cudaStream_t stream) {
     Plan pl;
     ScanParams P;
     if (int rc = prepare(a, NEED_FORM_GATED, &pl, &P)) return rc;
     if (pl.launch_fix == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no fix-up kernel for dtype %d", a->dtype);
+    if (int rc = sp_list_of(a, &P)) return rc;
     P.fix_tile_prod = a->tile_prod;
     P.fix_tile_carry = a->tile_carry;
-    P.fix_carry = fix_carry;
-    P.fix_count = fix_count;
-    P.fix_list = fix_list;
+    P.fix_all_summary = reinterpret_cast<const float2*>(all_summary);
+    P.fix_rank = rank;
     P.tile_prod = nullptr;
     P.tile_carry = nullptr;
-    P.h_final = nullptr;
-    P.summary = nullptr;
     P.h0 = nullptr;
     return pl.launch_fix(P, stream);
 }
@@ -550,9 +549,23 @@ int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t s
     Plan pl;
     ScanParams P;
     if (int rc = prepare(args, NEED_FORM_GATED, &pl, &P)) return rc;
-    if (rank > 0 && pl.launch_defer == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no deferring scan for dtype %d", args->dtype);
-    if (int rc = rank > 0 ? pl.launch_defer(P, stream) : pl.launch(P, stream)) return rc;
+    if (rank == 0) {  // every output is written; no list
+        if (int rc = pl.launch(P, stream)) return rc;
+        return ok();
+    }
+    if (pl.launch_defer == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no deferring scan for dtype %d", args->dtype);
+    if (int rc = sp_list_of(args, &P)) return rc;
+    const cudaError_t e = cudaMemsetAsync(P.sp_count, 0, sizeof(uint32_t), stream);  // the list starts empty
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(sequence-parallel list)");
+    if (int rc = pl.launch_defer(P, stream)) return rc;
     return ok();
+}
+
+size_t need_sp_list_size(int32_t dtype, int64_t nb, int64_t nh, int64_t T, int64_t C) {
+    Plan pl;
+    if (!select_plan(NEED_FORM_GATED, dtype, dtype, 0, &pl)) return 0;
+    if (nb < 1 || nh < 1 || T < 1 || C < 1) return size_t(kSpListHead);
+    return size_t(kSpListHead + geometry(pl, nb, nh, T, C).ntiles);
 }
 
 int need_gated_scan(const need_scan_args* args, need_stream_t stream) { return run(args, NEED_FORM_GATED, stream); }

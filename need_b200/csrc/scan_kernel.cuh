@@ -50,9 +50,8 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 
 // workspace header words (uint32)
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
-// word 8: tiles a sequence-parallel fix-up rewrites (entries of its list)
-// word 9: blocks of the fix-up's preparation that are done (the last builds the list)
-enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_FIX_COUNT = 8, WS_FIX_TICKET = 9, WS_HDR_WORDS = 32 };
+// word 3: the error word
+enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_HDR_WORDS = 32 };
 enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
 
 // look-back polls before a wait gives up (each poll is an L2 round trip plus a
@@ -115,15 +114,18 @@ struct ScanParams {
     const void* conv_w;
     int64_t cwsc, cwsk;
     const void* conv_b;
-    // sequence-parallel fix-up (scan_kernel<K, true>): the local scan's
-    // per-tile entering product and state, the carry entering the slice per
-    // (sequence, channel) in .x, and the list of tiles to rewrite (fix_count
-    // entries of fix_list, tile ids as the scan numbers them)
+    // Sequence parallelism.  sp_list / sp_count: the tiles a slice's fix-up
+    // rewrites (tile ids as the scan numbers them); the deferring local scan
+    // (scan_kernel<K, false, false, true>) appends every tile it defers, the
+    // fix-up (scan_kernel<K, true>) reads the first *sp_count entries.
+    uint32_t* sp_list;
+    uint32_t* sp_count;
+    // The fix-up: the local scan's per-tile entering product and state, the
+    // gathered slice maps [nranks][nb*nh][C] (prod a, h_end) and this rank.
     const float* fix_tile_prod;
     const float* fix_tile_carry;
-    const float2* fix_carry;
-    const uint32_t* fix_count;
-    const uint32_t* fix_list;
+    const float2* fix_all_summary;
+    int32_t fix_rank;
     ulonglong2* agg;   // [ntiles][8][CBW/8] tagged (A, B): the tile's map
     ulonglong2* incl;  // [ntiles][8][CBW/8] tagged (prod, h): state after the tile
 };
@@ -561,15 +563,15 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         fence_barrier_init();
     }
     __syncthreads();
-    const int ntl = FIX ? min(p.ntiles, static_cast<int>(*p.fix_count)) : p.ntiles;
+    const int ntl = FIX ? min(p.ntiles, static_cast<int>(*p.sp_count)) : p.ntiles;
     const int stride = FIX ? static_cast<int>(gridDim.x) : p.ntiles;
     uint32_t par = 0;  // mbarrier phase of this CTA's current tile
     // FIX: entry `item` of the list names the tile; the next entry is read one tile ahead
     int next_tile = static_cast<int>(blockIdx.x);
-    if (FIX && next_tile < ntl) next_tile = static_cast<int>(p.fix_list[next_tile]);
+    if (FIX && next_tile < ntl) next_tile = static_cast<int>(p.sp_list[next_tile]);
     for (int item = static_cast<int>(blockIdx.x); item < ntl; item += stride, par ^= 1u) {
         const int tile = next_tile;
-        if (FIX && item + stride < ntl) next_tile = static_cast<int>(p.fix_list[item + stride]);
+        if (FIX && item + stride < ntl) next_tile = static_cast<int>(p.sp_list[item + stride]);
         const int chunk = tile / p.nchains;
         const int chain = tile - chunk * p.nchains;
         const int seq = chain / p.ncb;
@@ -644,16 +646,43 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
 
         if (FIX && warp == K::LB) {
             // ------------------------------------------------------ fix-up carry
-            // The state entering this tile of the slice: the local scan's state plus
-            // the carry entering the slice times the product of a before the tile.
+            // The carry entering the slice, composed from the gathered maps of the
+            // ranks before this one (8 maps in flight at a time, identity maps past
+            // the last); the state entering this tile of the slice is the local
+            // scan's state plus that carry times the product of a before the tile.
+            // The chain's first tile also writes the slice's corrected final state
+            // and summary.
+            const int64_t nsc = (int64_t)p.nb * p.nh * p.C;
+            float carry[NE];
+#pragma unroll
+            for (int k = 0; k < NE; ++k) carry[k] = 0.0f;
+            for (int j0 = 0; j0 < p.fix_rank; j0 += 8) {
+#pragma unroll
+                for (int k = 0; k < NE; ++k) {
+                    const int c = c0 + lbchan(k);
+                    float2 m[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        m[j] = (j0 + j < p.fix_rank && c < p.C)
+                                   ? p.fix_all_summary[(j0 + j) * nsc + (int64_t)seq * p.C + c]
+                                   : make_float2(1.0f, 0.0f);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) carry[k] = fmaf(m[j].x, carry[k], m[j].y);
+                }
+            }
             const int64_t ti0 = ((int64_t)seq * p.nchunks + chunk) * p.C;
             float h[NE];
 #pragma unroll
             for (int k = 0; k < NE; ++k) {
                 const int c = c0 + lbchan(k);
-                h[k] = c < p.C ? fmaf(p.fix_tile_prod[ti0 + c], p.fix_carry[(int64_t)seq * p.C + c].x,
-                                      p.fix_tile_carry[ti0 + c])
-                               : 0.0f;
+                h[k] = c < p.C ? fmaf(p.fix_tile_prod[ti0 + c], carry[k], p.fix_tile_carry[ti0 + c]) : 0.0f;
+                if (chunk == 0 && c < p.C) {
+                    const float2 mine = p.fix_all_summary[p.fix_rank * nsc + (int64_t)seq * p.C + c];
+                    const float hl = fmaf(mine.x, carry[k], mine.y);
+                    if (p.h_final != nullptr) p.h_final[(int64_t)seq * p.C + c] = hl;
+                    if (p.summary != nullptr)
+                        reinterpret_cast<float2*>(p.summary)[(int64_t)seq * p.C + c] = make_float2(mine.x, hl);
+                }
             }
             if (!mbar_wait_bounded(s_p1, par, kTmaPolls)) atomicOr(&p.hdr[WS_ERROR], ERR_TMA);
             float2 TA[NP], TB[NP];
@@ -704,7 +733,10 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
 #pragma unroll
                     for (int k = 0; k < NE; ++k) d |= (c0 + lbchan(k) < p.C) && carryP[k] > kFixTau;
                     d = __any_sync(0xffffffffu, d);
-                    if (lane == 0) *s_defer = d ? 1u : 0u;
+                    if (lane == 0) {
+                        *s_defer = d ? 1u : 0u;
+                        if (d) p.sp_list[atomicAdd(p.sp_count, 1u)] = static_cast<uint32_t>(tile);  // for the fix-up
+                    }
                 }
             };
             auto publish_agg = [&]() {

@@ -17,12 +17,12 @@
 // kFixTau = 2^-24 on some channel of the tile (then the correction entering it
 // exceeds 2^-24 * |carry| there); with decays in (0, 1) only the leading
 // ~log(2^-24)/log(mean a) tokens of a slice are touched.  The rule does not
-// depend on the carry, so the local scan (need_sp_local_scan) leaves exactly
-// those tiles unwritten.  fix_prepare_kernel composes the carries, counts the
-// tiles of each chain (sequence x channel block) and lists them; the scan
-// kernel in fix-up mode (TMA tiles, the row warps' two-phase scan) rewrites
-// the listed tiles, its resident CTAs striding over the list.  The affine form
-// uses fixup_kernel: one warp per tile walks the rows in order, rewriting every
+// depend on the carry, so the local scan (need_sp_local_scan) decides it per
+// tile, leaves those tiles' outputs unwritten and lists them in its workspace.
+// The scan kernel in fix-up mode (TMA tiles, the row warps' two-phase scan)
+// then rewrites the listed tiles, its resident CTAs striding over the list,
+// each composing the carry from the gathered maps.  The affine form uses
+// fixup_kernel: one warp per tile walks the rows in order, rewriting every
 // tile whose correction is non-zero (its decays may exceed 1).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -182,110 +182,10 @@ __global__ void __launch_bounds__(128) fixup_kernel(const FixParams p) {
     }
 }
 
-// One block per chain (sequence x channel block of the gated tile, 32..256
-// channels), one thread per channel: the carry entering this slice, composed from the gathered maps
-// of the ranks before it; the slice's final state and summary; and the number
-// of leading chunks whose product before them exceeds kFixTau on some channel
-// of the chain (counts[chain]).  The last block to finish lists the tiles to
-// rewrite, chain by chain (tile id = chunk * nchains + chain, as the scan
-// numbers them), into list[0 .. hdr[WS_FIX_COUNT]).  hdr[WS_FIX_TICKET] must
-// be 0 at launch (a zero-filled workspace); the last block leaves it 0, and
-// every launch runs to its end (no wait in it), so the next launch finds it 0.
-__global__ void __launch_bounds__(256) fix_prepare_kernel(int32_t C, int32_t cbw, int32_t ncb, int32_t nchains,
-                                                          int32_t nchunks, int32_t rank, int64_t nsc,
-                                                          const float2* all_summary, const float* tile_prod,
-                                                          float* h_final, float2* summary, float2* fix_carry,
-                                                          uint32_t* counts, uint32_t* list, uint32_t* hdr) {
-    __shared__ int s_count;
-    __shared__ bool s_last;
-    __shared__ uint32_t s_warp[8];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int chain = blockIdx.x;
-    const int64_t seq = chain / ncb;
-    const int64_t c = int64_t(chain - seq * ncb) * cbw + tid;
-    if (tid == 0) s_count = 0;
-    __syncthreads();
-    if (tid < cbw && c < C) {
-        const int64_t i = seq * C + c;
-        // the first 8 chunks' products, this slice's map and up to 8 ranks' maps
-        // are independent loads: all in flight together
-        const float* tp = tile_prod + seq * nchunks * C + c;
-        float pr[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) pr[j] = j < nchunks ? tp[int64_t(j) * C] : 0.0f;
-        const float2 mine = all_summary[rank * nsc + i];
-        float carry = 0.0f;
-        for (int j0 = 0; j0 < rank; j0 += 8) {
-            float2 m[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)  // past the last rank: the identity map (1, 0)
-                m[j] = j0 + j < rank ? all_summary[(j0 + j) * nsc + i] : make_float2(1.0f, 0.0f);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) carry = fmaf(m[j].x, carry, m[j].y);
-        }
-        fix_carry[i] = make_float2(carry, 0.0f);
-        const float hl = fmaf(mine.x, carry, mine.y);
-        if (h_final != nullptr) h_final[i] = hl;
-        if (summary != nullptr) summary[i] = make_float2(mine.x, hl);
-        // tile_prod only shrinks along the slice: the count is the first chunk
-        // at or below kFixTau, found 8 chunks (8 independent loads) at a time
-        int k = 0;
-        for (int k0 = 0; k0 < nchunks; k0 += 8) {
-            if (k0 > 0) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) pr[j] = k0 + j < nchunks ? tp[int64_t(k0 + j) * C] : 0.0f;
-            }
-            int j = 0;
-            while (j < 8 && pr[j] > kFixTau) ++j;
-            k = k0 + j;
-            if (j < 8) break;
-        }
-        k = min(k, nchunks);
-        if (k > 0) atomicMax(&s_count, k);
-    }
-    __syncthreads();
-    if (tid == 0) {
-        counts[chain] = static_cast<uint32_t>(s_count);
-        __threadfence();
-        s_last = atomicAdd(&hdr[WS_FIX_TICKET], 1u) == static_cast<uint32_t>(nchains) - 1u;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // the last block: an exclusive scan of the counts, blockDim chains at a time
-    uint32_t done = 0;
-    for (int base = 0; base < nchains; base += blockDim.x) {
-        const int ch = base + tid;
-        const uint32_t n = ch < nchains ? __ldcg(&counts[ch]) : 0u;
-        uint32_t incl = n;
-#pragma unroll
-        for (int d = 1; d < 32; d *= 2) {
-            const uint32_t o = __shfl_up_sync(0xffffffffu, incl, d);
-            if (lane >= d) incl += o;
-        }
-        if (lane == 31) s_warp[warp] = incl;
-        __syncthreads();
-        uint32_t before = done;
-        for (int w = 0; w < warp; ++w) before += s_warp[w];
-        uint32_t total = done;
-        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += s_warp[w];
-        const uint32_t pos = before + incl - n;
-        for (uint32_t k = 0; k < n; ++k) list[pos + k] = k * static_cast<uint32_t>(nchains) + static_cast<uint32_t>(ch);
-        __syncthreads();  // s_warp is rewritten by the next round
-        done = total;
-    }
-    if (tid == 0) {
-        hdr[WS_FIX_COUNT] = done;
-        hdr[WS_FIX_TICKET] = 0u;
-    }
-}
-
 }  // namespace
 
 namespace need {
-int gated_geometry(const need_scan_args* a, int* cbw, int64_t* nchains, int64_t* nchunks);
-int gated_fixup_launch(const need_scan_args* a, const float2* fix_carry, const uint32_t* fix_count,
-                       const uint32_t* fix_list, cudaStream_t stream);
+int gated_fixup_launch(const need_scan_args* a, const float* all_summary, int32_t rank, cudaStream_t stream);
 }
 
 extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, int32_t nranks, int32_t rank,
@@ -312,32 +212,9 @@ extern "C" int need_sp_fixup(const need_scan_args* a, const float* all_summary, 
     if (rank == 0) return ok();  // no carry enters the first slice
 
     if (gated) {
-        // The gated form re-scans the listed tiles with the scan kernel itself
-        // (fix-up mode); its scratch is the caller's scan workspace: the header,
-        // fix_carry [nb*nh*C], the per-chain counts and the list of tiles.
-        int cbw = 0;
-        int64_t nchains = 0, nchunks = 0;
-        if (int rc = gated_geometry(a, &cbw, &nchains, &nchunks)) return rc;
-        if (cbw > 256 || cbw % 32 != 0)
-            return fail(NEED_ERR_UNSUPPORTED, "fix-up preparation takes tiles of 32..256 channels (got %d)", cbw);
-        const int64_t nsc = a->nb * a->nh * a->C;
-        const size_t off_counts = size_t(WS_HDR_WORDS) * 4 + size_t(nsc) * sizeof(float2);
-        const size_t off_list = off_counts + size_t(nchains) * 4;
-        const size_t need = off_list + size_t(nchains) * size_t(nchunks) * 4;
-        if (a->workspace == nullptr || !aligned16(a->workspace) || a->workspace_bytes < need)
-            return fail(NEED_ERR_WORKSPACE, "the fix-up needs a scan workspace of at least %zu bytes", need);
-        unsigned char* ws = static_cast<unsigned char*>(a->workspace);
-        uint32_t* hdr = reinterpret_cast<uint32_t*>(ws);
-        float2* fix_carry = reinterpret_cast<float2*>(ws + WS_HDR_WORDS * 4);
-        uint32_t* counts = reinterpret_cast<uint32_t*>(ws + off_counts);
-        uint32_t* list = reinterpret_cast<uint32_t*>(ws + off_list);
-        fix_prepare_kernel<<<static_cast<unsigned>(nchains), static_cast<unsigned>(cbw), 0, stream>>>(
-            int32_t(a->C), cbw, int32_t((a->C + cbw - 1) / cbw), int32_t(nchains), int32_t(nchunks), rank, nsc,
-            reinterpret_cast<const float2*>(all_summary), a->tile_prod, a->h_final,
-            reinterpret_cast<float2*>(a->summary), fix_carry, counts, list, hdr);
-        const cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return cuda_fail(e, "fix_prepare_kernel launch");
-        if (int rc = gated_fixup_launch(a, fix_carry, hdr + WS_FIX_COUNT, list, stream)) return rc;
+        // The gated form re-scans the tiles its deferring local scan listed in
+        // a->sp_list, with the scan kernel itself (fix-up mode), in one launch.
+        if (int rc = gated_fixup_launch(a, all_summary, rank, stream)) return rc;
         return ok();
     }
 

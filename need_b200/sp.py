@@ -41,6 +41,7 @@ class LocalScan:
     tile_prod: torch.Tensor  # [B, nchunks, C] fp32: product of a before each tile
     tile_carry: torch.Tensor  # [B, nchunks, C] fp32: local state entering each tile
     h_final: torch.Tensor    # [B, C] fp32
+    sp_list: torch.Tensor    # int32: the count, 3 spare words, then the ids of the tiles the fix-up rewrites
     keep: List[torch.Tensor] = field(default_factory=list)
 
 
@@ -81,8 +82,11 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
     a.summary = summary.data_ptr()
     a.tile_prod = tile_prod.data_ptr()
     a.tile_carry = tile_carry.data_ptr()
+    # the tiles the fix-up rewrites, listed by the local scan of a rank > 0
+    sp_list = torch.empty(lib.need_sp_list_size(a.dtype, B, 1, T, C), dtype=torch.int32, device=dev)
+    a.sp_list = sp_list.data_ptr()
     nk._launch("need_sp_local_scan", a, dev, extra=(int(rank),))
-    return LocalScan(a, out, summary, tile_prod, tile_carry, hf, keep)
+    return LocalScan(a, out, summary, tile_prod, tile_carry, hf, sp_list, keep)
 
 
 def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> None:

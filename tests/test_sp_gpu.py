@@ -72,6 +72,12 @@ def test_deferred_tiles_are_the_rewritten_ones(cuda):
     want = (loc.tile_prod.view(B, T // L, C // CB, CB) > 2.0 ** -24).any(3)
     assert torch.equal(unwritten, want)
     assert want[:, 0].all() and not want[:, -1].any()  # chunk 0 always, the last (of 32) never here
+    # and they are the tiles the local scan listed for the fix-up (tile = chunk * chains + chain)
+    n = int(loc.sp_list[0])
+    listed = sorted(loc.sp_list[4:4 + n].tolist())
+    nchains = B * (C // CB)
+    expect = sorted(k * nchains + b * (C // CB) + cb for b, k, cb in torch.nonzero(want).tolist())
+    assert listed == expect
     whole = nk.gated_scan(w.x, w.z, w.g)
     keep = ~unwritten.repeat_interleave(L, 1).repeat_interleave(CB, 2)
     assert torch.equal(out[keep], whole[keep])  # the written tiles need no correction: rank 1 of a 1-slice scan
