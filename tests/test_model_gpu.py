@@ -59,9 +59,10 @@ def reference_modules():
     return need_core, need_kernels, config_for_size
 
 
-def build_model(need_core, config_for_size, dev):
+def build_model(need_core, config_for_size, dev, **overrides):
     cfg, _ = config_for_size.model_config_for_params(350_000_000, block_size=T)
     cfg["image_2d_scan"] = False
+    cfg.update(overrides)
     torch.manual_seed(0)
     with torch.device(dev):
         model = need_core.NeedModel(need_core.NeedConfig(**cfg))
@@ -208,3 +209,114 @@ def test_ssd_block_patched_with_the_folded_conv(cuda):
     print(f"\nper-block (patched vs the reference's block): worst max rel {worst:.3e}; "
           f"logits: max rel {err:.3e}, rel L2 {l2:.3e}")
     assert err <= BF16_TOL, f"logits differ from the reference's: max rel {err}"
+
+
+def test_need_model_training_step_through_the_drop_in(cuda):
+    """NEED's training path: with gradients on, every StructuredDualRetention
+    block computes its gates as torch ops and calls
+    need_kernels.affine_recurrence_scan under autograd (need_core.py:1630-1638),
+    whose backward here is the reversed-time scan kernel.
+
+    The reference arm runs that scan as the reference's own differentiable
+    chunked torch scan (_chunked_affine_recurrence_scan, need_kernels.py:
+    177-226: its CPU path, and its CUDA path when associative_scan is
+    missing), not its CUDA associative_scan route (:245-262): on this torch
+    that route returns the right states and update gradient but loses the
+    decay gradient (relative error 1.0 against float64 autograd at
+    2 x 1024 x 832, where the chunked scan and this library's kernel are
+    within 3e-3).  Everything else comes from the reference.  One forward, a
+    cross-entropy of the logits against targets ~ U[0, vocab) (the model's own
+    loss path calls binary_cross_entropy, which torch refuses under autocast),
+    and the backward over 2 x 1024 tokens, in training mode with the preset's
+    dropout set to 0 (the model's cuDNN RNN runs backward only in training
+    mode; no other module draws random numbers at these settings), bf16
+    autocast, with the reference's need_kernels (torch path) and with the
+    drop-in.  All 14 forward scans and 14 adjoint
+    scans must run in libneed_scan.so; the loss must agree to 1e-3 relative,
+    the whole gradient (every parameter, one vector) within 2e-2 relative L2,
+    and the gradient of every parameter of the 14 SSD blocks within 5e-2
+    relative L2 (bf16 roundings of the gates compound through 14 layers and
+    the backward).  Parameters elsewhere are checked only through the whole
+    vector: some get gradients near zero, where a relative error says
+    nothing."""
+    need_core, ref_nk, config_for_size = reference_modules()
+    from need_b200 import need_kernels as nk
+
+    model, _ = build_model(need_core, config_for_size, cuda, dropout=0.0)
+    model.train()
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    bt, tt = 2, 1024
+    ids = torch.randint(0, model.cfg.vocab_size, (bt, tt), device=cuda, generator=gen)
+    targets = torch.randint(0, model.cfg.vocab_size, (bt, tt), device=cuda, generator=gen)
+
+    def step(binding):
+        need_core.need_kernels = binding
+        model.zero_grad(set_to_none=True)
+        with torch.enable_grad(), torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            logits = model(ids)[0]
+        loss = torch.nn.functional.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1))
+        loss.backward()
+        torch.cuda.synchronize()
+        return float(loss.detach()), {n: p.grad.float().clone() for n, p in model.named_parameters()
+                                      if p.grad is not None}
+
+    calls = {"forward": 0, "adjoint": 0}
+    adjoint = nk._affine_adjoint
+
+    def counted_adjoint(*a, **k):
+        calls["adjoint"] += 1
+        return adjoint(*a, **k)
+
+    class Counting:
+        def __getattr__(self, name):
+            fn = getattr(nk, name)
+            if name != "affine_recurrence_scan":
+                return fn
+
+            def counted(*a, **k):
+                calls["forward"] += 1
+                return fn(*a, **k)
+            return counted
+
+    class ReferenceChunked:
+        """The reference's module with its differentiable chunked scan."""
+
+        def __getattr__(self, name):
+            if name == "affine_recurrence_scan":
+                return lambda decay, update, *, dim=1, backend="auto": ref_nk._chunked_affine_recurrence_scan(
+                    torch.broadcast_to(decay, update.shape), update, dim=dim)
+            return getattr(ref_nk, name)
+
+    saved_binding, saved_triton = need_core.need_kernels, ref_nk.HAS_TRITON
+    try:
+        ref_nk.HAS_TRITON = False
+        want_loss, want = step(ReferenceChunked())
+        nk._affine_adjoint = counted_adjoint
+        got_loss, got = step(Counting())
+    finally:
+        nk._affine_adjoint = adjoint
+        need_core.need_kernels = saved_binding
+        ref_nk.HAS_TRITON = saved_triton
+    assert calls == {"forward": 14, "adjoint": 14}, calls
+    assert nk.workspace_error() == 0
+    assert set(got) == set(want)
+    lerr = abs(got_loss - want_loss) / abs(want_loss)
+    names = sorted(got)
+    gv = torch.cat([got[n].flatten() for n in names])
+    wv = torch.cat([want[n].flatten() for n in names])
+    gerr = float((gv - wv).norm() / wv.norm())
+    ssd = tuple(name + "." for name, m in model.named_modules() if isinstance(m, need_core.StructuredDualRetention))
+    assert len(ssd) == 14
+    worst, worst_name, nssd = 0.0, "", 0
+    for name in names:
+        if not name.startswith(ssd):
+            continue
+        nssd += 1
+        e = float((got[name] - want[name]).norm() / want[name].norm().clamp_min(1e-30))
+        if e > worst:
+            worst, worst_name = e, name
+    print(f"\nloss {got_loss:.6f} vs {want_loss:.6f} (rel {lerr:.2e}); whole gradient rel L2 {gerr:.3e} "
+          f"over {len(names)} tensors; worst of the {nssd} SSD-block tensors {worst:.3e} ({worst_name})")
+    assert lerr <= 1e-3
+    assert gerr <= 2e-2
+    assert worst <= 5e-2, worst_name
