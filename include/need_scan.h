@@ -249,7 +249,9 @@ NEED_API size_t need_scan_workspace_size(int32_t form, int32_t dtype, int32_t de
                                 int64_t C);
 
 /* Reads (and clears) the workspace's device-side error word: bit 0 = a look-back
- * wait gave up, bit 1 = a tile load (or tensor-core) wait gave up.
+ * wait gave up, bit 1 = a tile load (or tensor-core) wait gave up, bit 2 = a
+ * sequence-parallel fix-up found a tile id outside the slice in sp_list (its
+ * local scan did not run as a rank > 0) and skipped it.
  * Synchronises `stream`. */
 NEED_API int need_workspace_error(void* workspace, uint32_t* error_out, need_stream_t stream);
 

@@ -549,7 +549,11 @@ int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t s
     Plan pl;
     ScanParams P;
     if (int rc = prepare(args, NEED_FORM_GATED, &pl, &P)) return rc;
-    if (rank == 0) {  // every output is written; no list
+    if (rank == 0) {  // every output is written; the list (when given) is left empty
+        if (args->sp_list != nullptr) {
+            const cudaError_t e = cudaMemsetAsync(args->sp_list, 0, sizeof(uint32_t), stream);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(sequence-parallel list)");
+        }
         if (int rc = pl.launch(P, stream)) return rc;
         return ok();
     }

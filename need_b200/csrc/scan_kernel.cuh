@@ -52,7 +52,7 @@ enum { FORM_AFFINE = 0, FORM_GATED = 1, FORM_SSD = 2, FORM_RETENTION = 3 };
 // words 0-1: one 64-bit word {launch epoch (high), CTAs started (low)}
 // word 3: the error word
 enum { WS_LAUNCH = 0, WS_ERROR = 3, WS_HDR_WORDS = 32 };
-enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u };
+enum { ERR_LOOKBACK = 1u, ERR_TMA = 2u, ERR_SP_LIST = 4u };
 
 // look-back polls before a wait gives up (each poll is an L2 round trip plus a
 // 64 ns sleep: a few seconds at most); need_test_set_lookback_polls lowers it
@@ -572,6 +572,13 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
     for (int item = static_cast<int>(blockIdx.x); item < ntl; item += stride, par ^= 1u) {
         const int tile = next_tile;
         if (FIX && item + stride < ntl) next_tile = static_cast<int>(p.sp_list[item + stride]);
+        if (FIX && static_cast<unsigned>(tile) >= static_cast<unsigned>(p.ntiles)) {
+            // not a tile of this slice (a list no deferring local scan wrote):
+            // report it and skip, leaving the barriers' phase where it was
+            if (threadIdx.x == 0) atomicOr(&p.hdr[WS_ERROR], ERR_SP_LIST);
+            par ^= 1u;
+            continue;
+        }
         const int chunk = tile / p.nchains;
         const int chain = tile - chunk * p.nchains;
         const int seq = chain / p.ncb;

@@ -42,6 +42,7 @@ class LocalScan:
     tile_carry: torch.Tensor  # [B, nchunks, C] fp32: local state entering each tile
     h_final: torch.Tensor    # [B, C] fp32
     sp_list: torch.Tensor    # int32: the count, 3 spare words, then the ids of the tiles the fix-up rewrites
+    rank: int = 0            # the rank the local scan ran as
     keep: List[torch.Tensor] = field(default_factory=list)
 
 
@@ -86,12 +87,17 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
     sp_list = torch.empty(lib.need_sp_list_size(a.dtype, B, 1, T, C), dtype=torch.int32, device=dev)
     a.sp_list = sp_list.data_ptr()
     nk._launch("need_sp_local_scan", a, dev, extra=(int(rank),))
-    return LocalScan(a, out, summary, tile_prod, tile_carry, hf, sp_list, keep)
+    return LocalScan(a, out, summary, tile_prod, tile_carry, hf, sp_list, int(rank), keep)
 
 
 def fixup(loc: LocalScan, all_summary: torch.Tensor, nranks: int, rank: int) -> None:
     """Step 3: add the carry from ranks < rank to ``loc.out``, ``loc.h_final`` and
-    ``loc.summary``.  ``all_summary`` is [nranks, B, C, 2] fp32 on this device."""
+    ``loc.summary``.  ``all_summary`` is [nranks, B, C, 2] fp32 on this device.
+    The local scan must have run as a rank > 0 (it lists the tiles this
+    rewrites); a rank-0 slice needs no fix-up."""
+    if rank > 0 and loc.rank == 0:
+        raise ValueError(f"the fix-up of rank {rank} needs its slice's local scan run as a rank > 0 "
+                         "(local_scan(..., rank=rank)); this one ran as rank 0")
     all_summary = all_summary.contiguous()
     dev = loc.out.device
     a = loc.args

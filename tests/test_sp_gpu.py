@@ -22,9 +22,9 @@ def host(t):
     return t.detach().float().cpu().numpy()
 
 
-def emulate(w, P, defer=True):
-    """Ranks 0..P-1 on one device.  With ``defer`` each rank's local scan is
-    told its rank (ranks > 0 leave the tiles the fix-up rewrites unwritten),
+def emulate(w, P):
+    """Ranks 0..P-1 on one device.  Each rank's local scan is told its rank
+    (ranks > 0 leave the tiles the fix-up rewrites unwritten and list them),
     into outputs filled with NaN beforehand, so an output neither the local
     scan nor the fix-up writes stays NaN."""
     T = w.x.shape[1]
@@ -34,8 +34,7 @@ def emulate(w, P, defer=True):
         sl = slice(bounds[r], bounds[r + 1])
         seg = None if w.seg is None else w.seg[:, sl].contiguous()
         out = torch.full_like(w.x[:, sl], float("nan"))
-        locs.append(sp.local_scan(w.x[:, sl], w.z[:, sl], w.g[:, sl], seg_start=seg, rank=r if defer else 0,
-                                  out=out))
+        locs.append(sp.local_scan(w.x[:, sl], w.z[:, sl], w.g[:, sl], seg_start=seg, rank=r, out=out))
     gathered = torch.stack([loc.summary for loc in locs])
     for r, loc in enumerate(locs):
         sp.fixup(loc, gathered, P, r)
@@ -44,14 +43,13 @@ def emulate(w, P, defer=True):
     return got, locs[-1].h_final
 
 
-@pytest.mark.parametrize("defer", [True, False])
 @pytest.mark.parametrize("P", [2, 3, 8])
 @pytest.mark.parametrize("z_mean,resets", [(5.0, None), (2.0, "uniform"), (8.0, None)])
-def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets, defer):
+def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets):
     w = workloads.gated_inputs(2, 3000, 512, z_mean=z_mean, dtype=torch.bfloat16, device=cuda, seed=P,
                                resets=resets, seg_lo=100, seg_hi=900)
     whole, whole_f = nk.gated_scan(w.x, w.z, w.g, seg_start=w.seg, return_final_state=True)
-    got, got_f = emulate(w, P, defer)
+    got, got_f = emulate(w, P)
     g, wh = host(got), host(whole)
     assert np.abs(g - wh).max() <= 2e-2 * np.abs(wh).max()
     assert np.mean(g == wh) >= 0.99
@@ -81,6 +79,47 @@ def test_deferred_tiles_are_the_rewritten_ones(cuda):
     whole = nk.gated_scan(w.x, w.z, w.g)
     keep = ~unwritten.repeat_interleave(L, 1).repeat_interleave(CB, 2)
     assert torch.equal(out[keep], whole[keep])  # the written tiles need no correction: rank 1 of a 1-slice scan
+
+
+def test_fixup_needs_a_listing_local_scan(cuda):
+    """A fix-up of rank 1 on a slice scanned as rank 0 (no list of tiles) is
+    refused on the host; launched through the C ABI anyway, the fix-up finds
+    the list the rank-0 scan emptied and rewrites nothing."""
+    import ctypes
+    from need_b200 import abi
+    w = workloads.gated_inputs(1, 512, 128, z_mean=5.0, dtype=torch.bfloat16, device=cuda, seed=3, resets=None)
+    loc = sp.local_scan(w.x, w.z, w.g, rank=0)
+    before = loc.out.clone()
+    gathered = torch.stack([loc.summary, loc.summary])
+    with pytest.raises(ValueError):
+        sp.fixup(loc, gathered, 2, 1)
+    lib = abi.load()
+    a = loc.args
+    ws = nk.workspace(cuda, lib.need_scan_workspace_size(a.form, a.dtype, a.decay_dtype, 0, a.nb, a.nh, a.T, a.C))
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    abi.check("need_sp_fixup", lib.need_sp_fixup(ctypes.byref(a), gathered.data_ptr(), 2, 1,
+                                                 torch.cuda.current_stream(cuda).cuda_stream))
+    torch.cuda.synchronize()
+    assert int(loc.sp_list[0]) == 0
+    assert torch.equal(loc.out, before)
+    assert nk.workspace_error() == 0
+
+
+def test_fixup_skips_tile_ids_outside_the_slice(cuda):
+    """The fix-up checks every listed id against the slice's tile count before
+    using it: a list holding 3 ids outside the slice (one past the end, far
+    past it, negative as int32) rewrites nothing and reports bit 2 of the
+    workspace's error word.  Only the list's first 3 entries are read."""
+    w = workloads.gated_inputs(1, 512, 128, z_mean=5.0, dtype=torch.bfloat16, device=cuda, seed=5, resets=None)
+    loc = sp.local_scan(w.x, w.z, w.g, rank=1, out=torch.zeros_like(w.x))  # deferred tiles stay 0
+    ntiles = loc.sp_list.numel() - 4
+    loc.sp_list[0] = 3
+    loc.sp_list[4:7] = torch.tensor([ntiles, ntiles + 1000, -5], dtype=torch.int32, device=cuda)
+    before = loc.out.clone()
+    sp.fixup(loc, torch.stack([loc.summary, loc.summary]), 2, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(loc.out, before)
+    assert nk.workspace_error() & 4
 
 
 def test_emulated_ranks_fp32_exact_carry(cuda):
