@@ -131,9 +131,9 @@ typedef struct {
                               clearing; never used by two launches at once */
     size_t workspace_bytes;
     uint32_t* sp_list;     /* sequence parallelism, the slice's list of the tiles its fix-up
-                              rewrites: need_sp_list_size(...) words, written by
-                              need_sp_local_scan (rank > 0) and read by need_sp_fixup (GATED);
-                              unused (may be null) elsewhere */
+                              rewrites, written by need_sp_local_scan and read by need_sp_fixup
+                              (GATED); unused (may be null) elsewhere */
+    uint64_t sp_list_words; /* its size in 32-bit words, >= need_sp_list_size(...) */
 } need_scan_args;
 
 /* Token dtypes of a packed stream (the packer writes uint16 or uint32,

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 from ctypes import (POINTER, Structure, c_char_p, c_double, c_int32, c_int64, c_size_t, c_uint32,
-                    c_void_p)
+                    c_void_p, c_uint64)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_lib", "libneed_scan.so")
@@ -38,7 +38,7 @@ class NeedScanArgs(Structure):
         ("seg_start", c_void_p), ("seg_stride_b", c_int64), ("seg_stride_t", c_int64),
         ("summary", c_void_p), ("tile_prod", c_void_p), ("tile_carry", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
-        ("sp_list", c_void_p),
+        ("sp_list", c_void_p), ("sp_list_words", c_uint64),
     ]
 
 

@@ -382,10 +382,14 @@ int run(const need_scan_args* a, int form, cudaStream_t s) {
 // aligned entries after it) and up to ntiles tile ids.
 constexpr int64_t kSpListHead = 4;
 
-// Points P's sequence-parallel list at args->sp_list.
+// Points P's sequence-parallel list at args->sp_list (checked for its size).
 int sp_list_of(const need_scan_args* a, ScanParams* P) {
     if (a->sp_list == nullptr) return fail(NEED_ERR_INVALID, "sp_list is null (need_sp_list_size words)");
     if (reinterpret_cast<uintptr_t>(a->sp_list) % 4 != 0) return fail(NEED_ERR_INVALID, "sp_list is not 4-byte aligned");
+    const uint64_t need = uint64_t(kSpListHead) + uint64_t(P->ntiles);
+    if (a->sp_list_words < need)
+        return fail(NEED_ERR_WORKSPACE, "sp_list holds %llu words, needs %llu (need_sp_list_size)",
+                    (unsigned long long)a->sp_list_words, (unsigned long long)need);
     P->sp_count = a->sp_list;
     P->sp_list = a->sp_list + kSpListHead;
     return NEED_OK;

@@ -85,7 +85,7 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
     a.tile_carry = tile_carry.data_ptr()
     # the tiles the fix-up rewrites, listed by the local scan of a rank > 0
     sp_list = torch.empty(lib.need_sp_list_size(a.dtype, B, 1, T, C), dtype=torch.int32, device=dev)
-    a.sp_list = sp_list.data_ptr()
+    a.sp_list, a.sp_list_words = sp_list.data_ptr(), sp_list.numel()
     nk._launch("need_sp_local_scan", a, dev, extra=(int(rank),))
     return LocalScan(a, out, summary, tile_prod, tile_carry, hf, sp_list, int(rank), keep)
 

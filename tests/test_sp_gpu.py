@@ -105,6 +105,23 @@ def test_fixup_needs_a_listing_local_scan(cuda):
     assert nk.workspace_error() == 0
 
 
+def test_undersized_list_is_refused(cuda):
+    """need_sp_local_scan and need_sp_fixup check sp_list_words against the
+    slice's tile count before launching."""
+    import ctypes
+    from need_b200 import abi
+    w = workloads.gated_inputs(1, 512, 128, z_mean=5.0, dtype=torch.bfloat16, device=cuda, seed=6, resets=None)
+    loc = sp.local_scan(w.x, w.z, w.g, rank=1)
+    lib = abi.load()
+    a = loc.args
+    a.sp_list_words = 4  # the count only: no room for the tiles
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    assert lib.need_sp_local_scan(ctypes.byref(a), 1, stream) == abi.ERR_WORKSPACE
+    assert b"sp_list" in lib.need_last_error()
+    gathered = torch.stack([loc.summary, loc.summary])
+    assert lib.need_sp_fixup(ctypes.byref(a), gathered.data_ptr(), 2, 1, stream) == abi.ERR_WORKSPACE
+
+
 def test_fixup_skips_tile_ids_outside_the_slice(cuda):
     """The fix-up checks every listed id against the slice's tile count before
     using it: a list holding 3 ids outside the slice (one past the end, far
