@@ -499,10 +499,12 @@ def run_need_model(dev, nk):
     """NEED's own model at config 5: the ~350M preset (config_for_size.py,
     block_size raised to 2048), seeded N(0, 0.02) weights, eval, bf16 autocast
     (the reference's inference setting), one forward over 8 x 2048 random token
-    ids.  Timed three ways on this B200: with the reference's kernels (Triton),
-    with this repository's need_kernels bound in their place (every ssd_scan on
-    libneed_scan.so), and the time the drop-in's 14 scan calls take inside that
-    forward (CUDA events around each call)."""
+    ids.  Timed on this B200: with the reference's kernels (Triton), with this
+    repository's need_kernels bound in their place (every ssd_scan on
+    libneed_scan.so), the time the drop-in's 14 scan calls take inside that
+    forward (CUDA events around each call), and with every
+    StructuredDualRetention.forward replaced by the fused patch (in_proj ->
+    ssd_conv_scan with the out_norm -> out)."""
     import torch
     ref_nk = reference_kernels()
     if ref_nk is None:
@@ -551,16 +553,31 @@ def run_need_model(dev, nk):
                 scan_events.append(ev)
                 return y
             return wrapped
+    sdr = need_core.StructuredDualRetention
+    original = sdr.forward
+
+    def patched(self, x):  # the fused block of the integration notes (no-grad path)
+        if torch.is_grad_enabled():
+            return original(self, x)
+        u, bg, cg, dt, og = self.in_proj(x).chunk(5, dim=-1)
+        y = nk.ssd_conv_scan(u, bg, cg, dt, og, self.D, self.cfg.ssd_dt_min, self.cfg.ssd_dt_max,
+                             self.dwconv.weight, self.dwconv.bias,
+                             norm_weight=self.out_norm.weight, eps=self.out_norm.eps)
+        return self.out(y)
     try:
         need_core.need_kernels = ref_nk
         ref_ms = timed()
         need_core.need_kernels = nk
         our_ms = timed()
+        sdr.forward = patched
+        patched_ms = timed()
+        sdr.forward = original
         need_core.need_kernels = Timed()
         forward()
         torch.cuda.synchronize()
         scan_ms = sum(a.elapsed_time(b) for a, b in scan_events)
     finally:
+        sdr.forward = original
         need_core.need_kernels = saved
     params = sum(p.numel() for p in model.parameters())
     del model
@@ -568,7 +585,8 @@ def run_need_model(dev, nk):
                         f"{cfg['n_layers']} layers), B={Bm}, T={Tm}, bf16 autocast, random weights",
             "reference_kernels_ms": ref_ms, "drop_in_ms": our_ms,
             "drop_in_tokens_per_s": Bm * Tm / (our_ms / 1e3), "reference_tokens_per_s": Bm * Tm / (ref_ms / 1e3),
-            "scan_calls": len(scan_events), "scan_ms": scan_ms, "scan_share": scan_ms / our_ms}
+            "scan_calls": len(scan_events), "scan_ms": scan_ms, "scan_share": scan_ms / our_ms,
+            "fused_block_patch_ms": patched_ms, "fused_block_patch_tokens_per_s": Bm * Tm / (patched_ms / 1e3)}
 
 
 def reference_cpu_torch(nthreads: int):
