@@ -92,6 +92,16 @@ def test_with_out_norm(cuda, wdtype):
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_partial_channel_block(cuda, dtype):
+    """C=200: three full 64-channel tiles and one of 8 channels, with resets."""
+    args = inputs(2, 333, 200, dtype, 3, seed=40, device=cuda)
+    seg = resets(2, 333, cuda)
+    want = two_kernels(*args, seg=seg)
+    got = nk.ssd_conv_scan(*args[:6], 0.001, 0.2, args[6], args[7], seg_start=seg)
+    assert torch.equal(got, want)
+
+
 def test_single_token_and_short_sequences(cuda):
     for T in (1, 2, 3, 17, 64, 65):
         args = inputs(2, T, 64, torch.bfloat16, 3, seed=T, device=cuda)
