@@ -399,8 +399,8 @@ int sp_list_of(const need_scan_args* a, ScanParams* P) {
 
 namespace need {
 // The gated scan kernel in fix-up mode over the slice described by `a`: it
-// rewrites the tiles that the deferring local scan listed in a->sp_list,
-// entering each from the local scan's tile_prod / tile_carry and
+// rewrites the tiles that the deferring local scan listed in a->sp_list (and
+// whose rounded updates b it left in their output rows), entering each from the local scan's tile_prod / tile_carry and
 // the carry it composes from all_summary [nranks][nb*nh][C] (ranks < rank);
 // the chain's first tile also corrects h_final and summary.  Writes only the
 // rewritten tiles' outputs.
@@ -410,6 +410,9 @@ int gated_fixup_launch(const need_scan_args* a, const float* all_summary, int32_
     if (int rc = prepare(a, NEED_FORM_GATED, &pl, &P)) return rc;
     if (pl.launch_fix == nullptr) return fail(NEED_ERR_UNSUPPORTED, "no fix-up kernel for dtype %d", a->dtype);
     if (int rc = sp_list_of(a, &P)) return rc;
+    // the rounded updates b the deferring local scan left in the listed tiles' output rows
+    const need_view ov{a->out, a->out_stride_b, a->out_stride_h, a->out_stride_t};
+    if (int rc = encode_view(&P.tm[3], ov, a->dtype, a->nb, a->nh, a->T, a->C, pl.CB, pl.R, 3)) return rc;
     P.fix_tile_prod = a->tile_prod;
     P.fix_tile_carry = a->tile_carry;
     P.fix_all_summary = reinterpret_cast<const float2*>(all_summary);

@@ -861,7 +861,15 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         const int wr0 = warp * R;                              // this warp's first row
         const int r0 = wr0 + q * RS;                           // this thread's first row
         const int rend = max(0, min(RS, nvalid - r0));         // this thread's rows inside T
-        if (lane == 0 && nvalid > wr0) {
+        if (lane == 0 && nvalid > wr0 && FIX && K::FORM == FORM_GATED) {
+            // the gated fix-up: z, and the rounded b the deferring local scan left in
+            // the tile's output rows (p.tm[3]); the input gate's slot is not loaded
+            mbar_arrive_expect_tx(&s_bar[warp], (K::slot_bytes(0) + K::slot_bytes(2)) / NW);
+            tma_load_4d(slot_ptr<K>(base, 0) + wr0 * (K::slot_bytes(0) / L), &p.tm[0], c0, t0 + wr0, hi, bi,
+                        &s_bar[warp]);
+            tma_load_4d(slot_ptr<K>(base, 2) + wr0 * (K::slot_bytes(2) / L), &p.tm[3], c0, t0 + wr0, hi, bi,
+                        &s_bar[warp]);
+        } else if (lane == 0 && nvalid > wr0) {
             uint32_t bytes = 0;
 #pragma unroll
             for (int k = 0; k < K::NIN; ++k) bytes += K::slot_bytes(k) / NW;
@@ -954,8 +962,9 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                 TS* s1 = reinterpret_cast<TS*>(slot_ptr<K>(base, 1)) + srow(r) * CBW;
                 TS* s2 = reinterpret_cast<TS*>(slot_ptr<K>(base, 2)) + srow(r) * CBW;
                 PS p0[4], p1[4], p2[4], ap[4], bp[4];
+                constexpr bool FIXB = FIX && K::FORM == FORM_GATED;  // slot 2 holds b itself
                 Row8<TS, SPLIT>::lds(s0, v, p0);
-                Row8<TS, SPLIT>::lds(s1, v, p1);
+                if constexpr (!FIXB) Row8<TS, SPLIT>::lds(s1, v, p1);
                 Row8<TS, SPLIT>::lds(s2, v, p2);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -969,8 +978,12 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
                         dec = exp2_pair<TS>(make_float2(-dt.x, -dt.y));
                     }
                     ap[i] = OS::pack(dec.x, dec.y);
-                    const float2 g = sig2<TS>(widen(p1[i]));
-                    bp[i] = OS::mul(OS::sub(OS::one(), ap[i]), OS::mul(OS::pack(g.x, g.y), p2[i]));
+                    if constexpr (FIXB) {
+                        bp[i] = p2[i];
+                    } else {
+                        const float2 g = sig2<TS>(widen(p1[i]));
+                        bp[i] = OS::mul(OS::sub(OS::one(), ap[i]), OS::mul(OS::pack(g.x, g.y), p2[i]));
+                    }
                 }
                 if (reset) {  // uniform across the row group: one branch per row
 #pragma unroll
@@ -1054,7 +1067,21 @@ __global__ void __launch_bounds__(K::NT, K::MINB) scan_kernel(const __grid_const
         named_sync(1, K::NT);  // the look-back warp has put this warp's entering state in s_hin
 
         // ---------------------------------------------------------- phase 2
-        if (!DEFER || *s_defer == 0u) {  // else the sequence-parallel fix-up writes this tile
+        const bool run_phase2 = !DEFER || *s_defer == 0u;
+        if constexpr (DEFER) {
+            if (!run_phase2) {
+                // a deferred tile: its rounded updates b (slot 2, written by phase 1)
+                // go to its output rows, where the fix-up reads them back
+                TS* brow = reinterpret_cast<TS*>(p.out) + bi * p.osb + hi * p.osh + (int64_t)(t0 + r0) * p.ost + c0;
+                const bool okb0 = c0 + chan<SPLIT>(0, v) < p.C, okb1 = c0 + chan<SPLIT>(4, v) < p.C;
+                for (int j = 0; j < rend; ++j, brow += p.ost) {
+                    PS bq[4];
+                    Row8<TS, SPLIT>::lds(reinterpret_cast<const TS*>(slot_ptr<K>(base, 2)) + (r0 + j) * CBW, v, bq);
+                    Row8<TS, SPLIT>::stg(brow, v, bq, okb0, okb1);
+                }
+            }
+        }
+        if (run_phase2) {  // else the sequence-parallel fix-up writes this tile
         float2 h[4];
         {
             const float4 h0 = *reinterpret_cast<const float4*>(s_hin + warp * CBW + chan<SPLIT>(0, v));

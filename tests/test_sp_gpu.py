@@ -57,28 +57,36 @@ def test_emulated_ranks_match_whole_sequence(cuda, P, z_mean, resets):
 
 
 def test_deferred_tiles_are_the_rewritten_ones(cuda):
-    """A rank > 0 leaves unwritten exactly the leading tiles whose product of a
-    before them exceeds 2^-24 on some channel of the tile (128 channels x 128
-    tokens for bf16): the tiles the fix-up rewrites."""
+    """A rank > 0 defers exactly the leading tiles whose product of a before
+    them exceeds 2^-24 on some channel of the tile (128 channels x 128 tokens
+    for bf16): it lists them for the fix-up and leaves in their output rows
+    the rounded updates b = (1 - a) * (sigmoid(g) * x) the fix-up re-scans
+    from; every other tile holds its outputs."""
     w = workloads.gated_inputs(2, 4096, 512, z_mean=5.0, dtype=torch.bfloat16, device=cuda, seed=4, resets=None)
     out = torch.full_like(w.x, float("nan"))
     loc = sp.local_scan(w.x, w.z, w.g, rank=1, out=out)
     torch.cuda.synchronize()
+    assert not torch.isnan(out).any()
     L, CB = 128, 128
     B, T, C = w.x.shape
-    unwritten = torch.isnan(out).view(B, T // L, L, C // CB, CB).any(4).any(2)  # [B, chunk, channel block]
-    want = (loc.tile_prod.view(B, T // L, C // CB, CB) > 2.0 ** -24).any(3)
-    assert torch.equal(unwritten, want)
+    want = (loc.tile_prod.view(B, T // L, C // CB, CB) > 2.0 ** -24).any(3)  # [B, chunk, channel block]
     assert want[:, 0].all() and not want[:, -1].any()  # chunk 0 always, the last (of 32) never here
-    # and they are the tiles the local scan listed for the fix-up (tile = chunk * chains + chain)
+    # the listed tiles (tile = chunk * chains + chain)
     n = int(loc.sp_list[0])
     listed = sorted(loc.sp_list[4:4 + n].tolist())
     nchains = B * (C // CB)
     expect = sorted(k * nchains + b * (C // CB) + cb for b, k, cb in torch.nonzero(want).tolist())
     assert listed == expect
+    deferred = want.repeat_interleave(L, 1).repeat_interleave(CB, 2)
+    # deferred tiles: b in the model dtype (need_kernels.py:330-336 with a sigmoid decay)
+    decay = torch.sigmoid(w.z)
+    b_ref = (1.0 - decay) * (torch.sigmoid(w.g) * w.x)
+    got_b, want_b = out[deferred].float(), b_ref[deferred].float()
+    assert (got_b - want_b).abs().max() <= 2e-2 * want_b.abs().max()
+    assert (got_b == want_b).float().mean() >= 0.99
+    # the other tiles need no correction at rank 1 of a one-slice scan: the whole scan's outputs
     whole = nk.gated_scan(w.x, w.z, w.g)
-    keep = ~unwritten.repeat_interleave(L, 1).repeat_interleave(CB, 2)
-    assert torch.equal(out[keep], whole[keep])  # the written tiles need no correction: rank 1 of a 1-slice scan
+    assert torch.equal(out[~deferred], whole[~deferred])
 
 
 def test_fixup_needs_a_listing_local_scan(cuda):
