@@ -469,9 +469,10 @@ NEED_API int need_commit_states(int32_t dtype, int64_t nseq, int64_t C, void* st
  * rank's T-slice from a zero state (form GATED; `summary`, `tile_prod` and
  * `tile_carry` required), as need_gated_scan.  For rank > 0 the tiles that
  * need_sp_fixup will rewrite -- those whose product of a before them exceeds
- * 2^-24 on some channel -- are scanned for their maps but their outputs are
- * not written, and are listed in args->sp_list: call need_sp_fixup with the
- * same args before reading `out`.
+ * 2^-24 on some channel -- are scanned for their maps, listed in
+ * args->sp_list, and their output rows receive the tile's rounded updates
+ * b = (1 - a) * (sigmoid(g) * x) instead of outputs (the fix-up re-scans from
+ * them): call need_sp_fixup with the same args before reading `out`.
  * Replaces no reference interface (the reference has no distributed scan). */
 NEED_API int need_sp_local_scan(const need_scan_args* args, int32_t rank, need_stream_t stream);
 
@@ -487,7 +488,8 @@ NEED_API size_t need_sp_list_size(int32_t dtype, int64_t nb, int64_t nh, int64_t
  * the scan's own arithmetic, and their outputs rewritten; later tiles are left
  * as they are (their correction is below fp32 resolution of the carry).
  * GATED: the tiles need_sp_local_scan listed in args->sp_list (tile_prod
- * above 2^-24 on some channel), in one launch.  AFFINE: every tile whose
+ * above 2^-24 on some channel), in one launch, from their decay logits in[0]
+ * and the updates b the local scan left in `out`.  AFFINE: every tile whose
  * correction is non-zero on some channel.  It also corrects h_final / summary
  * when given. */
 NEED_API int need_sp_fixup(const need_scan_args* args, const float* all_summary, int32_t nranks,

@@ -18,10 +18,11 @@
 // exceeds 2^-24 * |carry| there); with decays in (0, 1) only the leading
 // ~log(2^-24)/log(mean a) tokens of a slice are touched.  The rule does not
 // depend on the carry, so the local scan (need_sp_local_scan) decides it per
-// tile, leaves those tiles' outputs unwritten and lists them in its workspace.
-// The scan kernel in fix-up mode (TMA tiles, the row warps' two-phase scan)
-// then rewrites the listed tiles, its resident CTAs striding over the list,
-// each composing the carry from the gathered maps.  The affine form uses
+// tile, lists those tiles (args->sp_list) and leaves their rounded updates b
+// in their output rows.  The scan kernel in fix-up mode (TMA tiles, the row
+// warps' two-phase scan) then rewrites the listed tiles from their decay
+// logits and those b, its resident CTAs striding over the list, each
+// composing the carry from the gathered maps.  The affine form uses
 // fixup_kernel: one warp per tile walks the rows in order, rewriting every
 // tile whose correction is non-zero (its decays may exceed 1).
 #include <cuda_bf16.h>

@@ -5,8 +5,9 @@ step:
 
 1. each rank scans its slice from a zero state with ``need_sp_local_scan``,
    also recording the slice map (prod a, h at the slice end) per channel and
-   the product of ``a`` at every tile start; a rank after the first leaves
-   the outputs of the leading tiles that step 3 rewrites unwritten;
+   the product of ``a`` at every tile start; a rank after the first lists
+   the leading tiles that step 3 rewrites and leaves their rounded updates b
+   in their output rows;
 2. the slice maps (``[B, C, 2]`` fp32 per rank, 2*B*C*4 bytes) are
    all-gathered with NCCL into local memory;
 3. ``need_sp_fixup`` composes the maps of ranks < r into the carry entering
@@ -51,8 +52,9 @@ def local_scan(x: torch.Tensor, decay_logit: torch.Tensor, gate_logit: torch.Ten
                out: Optional[torch.Tensor] = None) -> LocalScan:
     """Scan this rank's [B, T_r, C] slice from a zero state (step 1).
 
-    With ``rank > 0`` the leading tiles that :func:`fixup` rewrites are not
-    written here: ``out`` is complete only after the fix-up.  With ``rank == 0``
+    With ``rank > 0`` the leading tiles that :func:`fixup` rewrites hold their
+    rounded updates b here, not outputs: ``out`` is complete only after the
+    fix-up.  With ``rank == 0``
     (the default) every output is written.  ``out``: an optional [B, T_r, C]
     tensor of the input dtype to write into (rows 16-byte aligned)."""
     nk._require_cuda(x, decay_logit, gate_logit)
