@@ -86,6 +86,19 @@ def test_sizes_and_chunk_lengths(lib):
     assert lib.need_scan_chunk_len(abi.FORM_AFFINE, abi.BF16, abi.F16, 0) == -1  # unsupported mix
 
 
+def test_sequence_parallel_list_size_and_errors(lib):
+    """need_sp_list_size: a 4-word count plus one word per gated tile; the
+    local scan's argument errors come back before any CUDA call."""
+    ntiles = 4 * (4096 // 128) * (8192 // 128)  # B=4, C=4096 (128-channel tiles), T=8192 (128-token chunks)
+    assert lib.need_sp_list_size(abi.BF16, 4, 1, 8192, 4096) == 4 + ntiles
+    assert lib.need_sp_list_size(7, 4, 1, 8192, 4096) == 0  # unknown dtype
+    a = abi.NeedScanArgs()
+    assert lib.need_sp_local_scan(None, 1, None) == abi.ERR_INVALID
+    assert lib.need_sp_local_scan(ctypes.byref(a), -1, None) == abi.ERR_INVALID
+    assert lib.need_sp_local_scan(ctypes.byref(a), 1, None) == abi.ERR_INVALID  # no summary / tile records
+    assert b"summary" in lib.need_last_error()
+
+
 def test_argument_errors_return_status(lib):
     a = abi.NeedScanArgs()
     assert lib.need_gated_scan(None, None) == abi.ERR_INVALID
