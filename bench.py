@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--no-side", action="store_true", help="skip the sequence-parallel and decode side runs")
     ap.add_argument("--profile", action="store_true",
                     help="only the warm-up and timed steps (for ncu): no clock heat loop, e2e, side runs or CPU leg")
-    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "ssd-conv", "assoc", "prologue",
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "sp-fixup", "ssd-norm", "ssd-conv", "backward", "assoc", "prologue",
                                                "assoc-step", "assoc-long"],
                     default="prefill",
                     help="with --profile: which kernel's workload to run (one GPU)")
@@ -651,7 +651,8 @@ def profile_side_case(args, dev, nk, sp, workloads):
     stood in for by its own; ``ssd-norm``
     runs the SSD scan with the RMSNorm kernel after it, ``ssd-conv`` the scan
     with the conv + SiLU folded in (inputs as in-projection chunks) and the
-    RMSNorm kernel after it, ``assoc`` the
+    RMSNorm kernel after it, ``backward`` the reversed-time adjoint scan of the
+    affine backward at the prefill shape (B=16, T=4096, C=1024 bf16), ``assoc`` the
     associative memory (feature map + tensor-core kernel) and ``prologue`` the
     conv + SiLU prologue, all at NEED's 350M shape (B=8, T=2048, d_model=832,
     memory_rank=64, bf16); ``assoc-step`` runs the memory's decode step for 256
@@ -673,6 +674,16 @@ def profile_side_case(args, dev, nk, sp, workloads):
         vs = torch.randn(Ns, d, device=dev, generator=g0).to(torch.bfloat16)
         for _ in range(max(args.warmup, 3) + args.steps):
             nk.assoc_memory_step(qs, ks, vs, st, dn)
+    elif args.profile_case == "backward":  # the affine scan's adjoint, as its autograd backward runs it
+        g0 = torch.Generator(device=dev).manual_seed(21)
+        shape = (16, 4096, 1024)  # the prefill shape
+        decay = torch.sigmoid(torch.randn(shape, device=dev, generator=g0) + 4.0).to(torch.bfloat16)
+        g = torch.randn(shape, device=dev, generator=g0).to(torch.bfloat16)
+        for _ in range(max(args.warmup, 3) + args.steps):
+            nk._affine_adjoint(decay, g, 1)
+        torch.cuda.synchronize()
+        if nk.workspace_error() != 0:
+            raise RuntimeError("a device-side wait gave up")
     elif args.profile_case == "ssd-conv":  # the conv folded into the scan, inputs as in-projection chunks
         g0 = torch.Generator(device=dev).manual_seed(1)
         Bm, Tm, d = 8, 2048, 832
